@@ -1,0 +1,92 @@
+// common.cuh — shared host-side helpers of libremora_b200.so: status/error
+// reporting, descriptor access, the context with its per-stream workspace.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/remora_b200.h"
+
+namespace remora {
+
+// ---------------------------------------------------------------- errors --
+void set_error(const char *fmt, ...);
+int fail(int code, const char *fmt, ...);
+
+#define REMORA_CUDA_TRY(expr)                                                  \
+  do {                                                                         \
+    cudaError_t err_ = (expr);                                                 \
+    if (err_ != cudaSuccess)                                                   \
+      return ::remora::fail(REMORA_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,   \
+                            cudaGetErrorString(err_), __FILE__, __LINE__);     \
+  } while (0)
+
+#define REMORA_TRY(expr)                                                       \
+  do {                                                                         \
+    int st_ = (expr);                                                          \
+    if (st_ != REMORA_OK) return st_;                                          \
+  } while (0)
+
+// ----------------------------------------------------------- descriptors --
+// A rank-N descriptor is {allocated, aligned, offset, sizes[N], strides[N]};
+// this view reads any rank from its base pointer.
+struct DescView {
+  char *aligned = nullptr;
+  int64_t offset = 0;
+  int rank = 0;
+  int64_t sizes[REMORA_MAX_RANK] = {0};
+  int64_t strides[REMORA_MAX_RANK] = {0};
+
+  int64_t numel() const {
+    int64_t n = 1;
+    for (int d = 0; d < rank; ++d) n *= sizes[d];
+    return n;
+  }
+  // Address of the logical first element for an element size.
+  char *data(int esize) const { return aligned + offset * esize; }
+  bool contiguous() const {
+    int64_t expect = 1;
+    for (int d = rank - 1; d >= 0; --d) {
+      if (sizes[d] != 1 && strides[d] != expect) return false;
+      expect *= sizes[d];
+    }
+    return true;
+  }
+};
+
+int read_desc(const void *desc, int rank, DescView *out, const char *what);
+int dtype_size(int dtype);
+
+// -------------------------------------------------------------- context --
+// Per-stream scratch owned by the library (fold partials, scan tile status,
+// split-K partials) plus a device error word that bounded waits set.
+struct Workspace {
+  void *buf = nullptr;
+  size_t bytes = 0;
+  int *err = nullptr; // device word: nonzero after a bounded wait ran out
+};
+
+}  // namespace remora
+
+struct RemoraB200Ctx {
+  int device = 0;
+  int sm_count = 148;
+  std::mutex mu;
+  std::map<cudaStream_t, remora::Workspace> ws;
+};
+
+namespace remora {
+// Returns a workspace of at least `bytes` for `stream` (grown on demand).
+int get_workspace(RemoraB200Ctx *ctx, cudaStream_t stream, size_t bytes,
+                  Workspace **out);
+int check_ctx(RemoraB200Ctx *ctx);
+
+constexpr int kMaxFoldBlocks = 1184;  // 148 SMs x 8
+}  // namespace remora

@@ -1,0 +1,60 @@
+"""Shared test configuration.
+
+Tests marked ``gpu`` need a B200 and the built library; everything else runs
+on a CPU-only machine.  GPU tests fail (they do not skip) when no CUDA device
+is present, so a run that was meant to exercise the device cannot pass
+silently without it.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+GOLDEN = ROOT / "tests" / "golden"
+for p in (str(ROOT), str(ROOT / "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config: pytest.Config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a B200 GPU and libremora_b200.so")
+
+
+def golden(name: str) -> dict[str, np.ndarray]:
+    with np.load(GOLDEN / f"{name}.npz") as f:
+        return {k: f[k] for k in f.files}
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("GPU test run without a CUDA device")
+    major, _ = torch.cuda.get_device_capability(0)
+    if major != 10:
+        raise RuntimeError(f"GPU tests need an sm_100 device, found sm_{major}x")
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="session")
+def oracle_mod():
+    import oracle as oracle_module
+
+    oracle_module.lib()
+    return oracle_module
+
+
+def to_dev(a: np.ndarray, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def to_host(t) -> np.ndarray:
+    return t.detach().cpu().numpy()

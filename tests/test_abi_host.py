@@ -1,0 +1,134 @@
+"""Host-only tests of the boundary: descriptor layout (the reference's
+tests/test_abi.py strategy), the C library's exports, the program compiler
+and its NVRTC code generation (no GPU needed)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from remora_b200 import _lib as L
+from remora_b200.abi import (DESCRIPTORS, descriptor_rank, descriptor_shape, descriptor_strides, element_strides,
+                             make_memref_descriptor, numpy_descriptor)
+from remora_b200.errors import RemoraB200Error, RemoraLimitError
+from remora_b200.program import (BinaryExpr, CmpExpr, ConstantExpr, InputExpr, LogicExpr, SelectExpr, UnaryExpr,
+                                 compile_program, const, from_reference_expr, stable_bce, x)
+
+
+def test_descriptor_sizes_and_field_order():
+    for rank, cls in DESCRIPTORS.items():
+        assert ctypes.sizeof(cls) == 24 + 16 * rank
+        names = [f[0] for f in cls._fields_]
+        assert names[:3] == ["allocated", "aligned", "offset"]
+        assert names[3:3 + rank] == [f"size{d}" for d in range(rank)]
+        assert names[3 + rank:] == [f"stride{d}" for d in range(rank)]
+        assert descriptor_rank(cls) == rank
+
+
+def test_descriptor_from_views():
+    base = np.arange(60, dtype=np.float32).reshape(3, 4, 5)
+    d = numpy_descriptor(base)
+    assert descriptor_shape(d) == (3, 4, 5) and descriptor_strides(d) == (20, 5, 1) and d.offset == 0
+    v = base[1:, ::2, ::-1]
+    d = numpy_descriptor(v)
+    assert descriptor_shape(d) == v.shape
+    assert descriptor_strides(d) == element_strides(v) == (20, 10, -1)
+    assert d.offset == 20 + 4 and d.aligned == base.ctypes.data
+    t = base.transpose(2, 0, 1)
+    assert descriptor_strides(numpy_descriptor(t)) == (1, 20, 5)
+
+
+def test_descriptor_rejects_bad_input():
+    with pytest.raises(RemoraB200Error):
+        make_memref_descriptor(0, [2, -1], [1, 1])
+    with pytest.raises(RemoraB200Error):
+        make_memref_descriptor(0, [2, 2], [1])
+    with pytest.raises(RemoraB200Error):
+        make_memref_descriptor(0, [1] * 11, [1] * 11)
+
+
+def _header_symbols() -> set[str]:
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(remora_b200_\w+)\s*\(", text))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = L.lib()
+    declared = _header_symbols()
+    assert declared, "no entry points found in include/*.h"
+    missing = sorted(n for n in declared if not hasattr(lib, n))
+    assert not missing, f"declared but not exported: {missing}"
+    assert b"sm_100a" in lib.remora_b200_version()
+
+
+def test_header_struct_sizes_match_ctypes():
+    # RemoraMapProgram: 5 int32 + 8 int32 + 48 x 16-byte instructions
+    assert ctypes.sizeof(L.RemoraMapInstr) == 16
+    assert ctypes.sizeof(L.RemoraMapProgram) == 4 * 5 + 4 * 8 + 16 * 48
+    assert ctypes.sizeof(L.RemoraScanSpec) == 24
+
+
+def test_compile_program_cse_and_limits():
+    y = BinaryExpr("+", BinaryExpr("*", x(0), const(2.5)), const(1.0))
+    chain = SelectExpr(CmpExpr(">", y, const(0.5)), y, const(0.0))
+    p = compile_program(chain, 1)
+    # y is computed once: input, 2.5, mul, 1.0, add, 0.5, cmp, 0.0, select
+    assert p.n_instr == 9 and p.result == 8
+    deep = x(0)
+    for _ in range(30):
+        deep = BinaryExpr("+", deep, ConstantExpr(float(_)))
+    with pytest.raises(RemoraLimitError):
+        compile_program(deep, 1)
+    with pytest.raises(RemoraB200Error):
+        compile_program(x(2), 1)
+
+
+def test_from_reference_expr_by_shape():
+    # stand-ins with the reference's class names and fields
+    def mk(name, **kw):
+        return type(name, (), {"__init__": lambda self: self.__dict__.update(kw)})()
+
+    node = mk("F32BinaryExpr", op="+", left=mk("F32InputExpr", index=0), right=mk("F32ConstantExpr", value=1.0))
+    assert from_reference_expr(node) == BinaryExpr("+", InputExpr(0), ConstantExpr(1.0))
+
+
+@pytest.mark.parametrize("case", ["chain", "i32", "bool", "bce", "div", "cmp_bool_out", "sqrt"])
+def test_generated_kernels_compile_for_sm100a(case):
+    y = BinaryExpr("+", BinaryExpr("*", x(0), const(2.5)), const(1.0))
+    progs = {
+        "chain": (compile_program(SelectExpr(CmpExpr(">", y, const(0.5)), y, const(0.0)), 1), L.FOLD_ADD),
+        "i32": (compile_program(BinaryExpr("*", x(0), BinaryExpr("-", x(1), const(3))), 2, compute="i32"), L.FOLD_MUL),
+        "bool": (compile_program(LogicExpr("||", x(0), x(1)), 2, compute="bool"), -1),
+        "bce": (compile_program(stable_bce(x(0), x(1)), 2), L.FOLD_ADD),
+        "div": (compile_program(BinaryExpr("/", x(0), x(1)), 2, compute="f32", in_dtypes=["i32", "i32"]), L.FOLD_ADD),
+        "cmp_bool_out": (compile_program(CmpExpr("<=", x(0), const(0.0)), 1, out="bool"), -1),
+        "sqrt": (compile_program(UnaryExpr("sqrt", x(0)), 1), L.FOLD_ADD),
+    }
+    prog, fold_op = progs[case]
+    buf = ctypes.create_string_buffer(1 << 18)
+    st = L.lib().remora_b200_jit_check(ctypes.byref(prog), fold_op, buf, len(buf))
+    assert st == 0, L.last_error()
+    src = buf.value.decode()
+    assert "remora_map_vec" in src and "remora_map_strided" in src
+    if fold_op >= 0:
+        assert "remora_fold_cell_vec" in src and "remora_fold_all" in src
+    # no unrounded f32 arithmetic that the compiler could contract into FMA
+    body = src.split("remora_expr(")[1].split("return")[0]
+    assert "fmaf" not in body
+
+
+def test_jit_check_rejects_bad_programs():
+    p = compile_program(BinaryExpr("+", x(0), x(1)), 2)
+    p.code[2].a = 40  # read an unwritten register
+    assert L.lib().remora_b200_jit_check(ctypes.byref(p), -1, None, 0) == L.ERR_ARG
+    assert "before it is written" in L.last_error()
+    p = compile_program(UnaryExpr("exp", x(0)), 1, compute="i32")
+    assert L.lib().remora_b200_jit_check(ctypes.byref(p), -1, None, 0) == L.ERR_UNSUPPORTED
