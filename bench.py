@@ -199,12 +199,12 @@ def run_ours(args) -> None:
         for k in range(ROTATE):
             call(k)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = ClockSampler(local) if rank == 0 and not args.profile else None
     if sampler:
         sampler.start()
     # keep the GPU busy ~1 s before the timed region so clocks are steady and
     # the sampler sees the load that the timed region runs under
-    t_end = time.time() + 1.0
+    t_end = time.time() + (0.0 if args.profile else 1.0)
     while time.time() < t_end:
         for k in range(ROTATE):
             call(k)
@@ -228,6 +228,12 @@ def run_ours(args) -> None:
     ms = t0.elapsed_time(t1)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     clocks = sampler.stop() if sampler else None
+    if args.profile:
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"profile_run": wl.name, "ms": ms, "steps": args.steps}), flush=True)
+        return
 
     # e2e: host buffers through the C ABI, pinned host memory, copies inside
     # the timed region every step
@@ -376,6 +382,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="warm-up and timed steps only (no soak, e2e or CPU baseline): the ncu capture command")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
