@@ -1,12 +1,501 @@
-// gemm.cu — dense core (remora_b200_gemm).  The tcgen05 kernel is not in
-// this build yet; the entry point reports that instead of computing.
+// gemm.cu — the dense core: C = A . B as the reference's lifted dot
+// C[i,j] = fold(+, 0, map(*, A[i,:], B[:,j])) (stdlib/prelude.rem:14,
+// examples/crater_train.py:38-44), on tcgen05 tensor cores for sm_100a.
+//
+// Kernel: persistent, warp-specialised, one CTA per SM, 128 x 256 output
+// tiles, 32-deep K stages of TMA-loaded SWIZZLE_128B tiles (no multicast).
+//   warp 0 lane 0  TMA producer (stage ring, full/empty mbarriers)
+//   warp 1 lane 0  MMA issuer: 4 tcgen05.mma.kind::tf32 (K = 8 each) per
+//                  stage into a TMEM accumulator, tcgen05.commit frees the
+//                  stage; 2 accumulators of 256 columns (all 512 TMEM
+//                  columns) so the epilogue of tile i overlaps tile i+1
+//   warp 2         TMEM allocator
+//   warps 4-7      epilogue: tcgen05.ld 32 lanes x 32 columns, 128-byte
+//                  row segments straight to global memory
+// Operands may be K-major or M/N-major (both are native UMMA layouts).
+// 3xTF32: A and B are split into hi = tf32(x) (low 13 mantissa bits
+// cleared) and lo = x - hi (exact) by a prep pass; the MMA issues
+// hi*hi + hi*lo + lo*hi per K step into the same f32 accumulator.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
 #include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace remora {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32;
+constexpr uint32_t A_BYTES = BM * BK * 4;
+constexpr uint32_t B_BYTES = BN * BK * 4;
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+
+template <bool SPLIT3>
+struct Cfg {
+  static constexpr int STAGES = SPLIT3 ? 2 : 4;
+  static constexpr uint32_t STAGE_BYTES = SPLIT3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
+};
+
+struct GemmParams {
+  int M, N, K, batch;
+  int a_mn, b_mn;
+  int mt, nt, kt;
+  float *C;
+  long long ldc;
+  long long c_bstride;
+  int *err;
+};
+
+__device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *bar, uint8_t *dst, int mn, int row0,
+                                             int rows, int k0, int b) {
+  if (!mn) {
+    tc::tma_load_3d(map, bar, dst, k0, row0, b);  // box {32 k, rows}
+  } else {
+    for (int c = 0; c < rows / 32; ++c)  // box {32 rows, 32 k} per 32-row chunk
+      tc::tma_load_3d(map, bar, dst + c * 4096, row0 + 32 * c, k0, b);
+  }
+}
+
+__device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int mn, int kk) {
+  return mn ? tc::smem_desc_sw128(saddr + kk * 1024, 4096, 1024) : tc::smem_desc_sw128(saddr + kk * 32, 16, 1024);
+}
+
+__device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, int &mb, int &nb) {
+  const int per = p.mt * p.nt;
+  b = t / per;
+  const int r = t - b * per;
+  mb = r / p.nt;
+  nb = r - mb * p.nt;
+}
+
+template <bool SPLIT3>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
+                     GemmParams p) {
+  using C = Cfg<SPLIT3>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&tfull[b], 1);
+      tc::mbar_init(&tempty[b], 4);
+    }
+    tc::mbar_init(&drain, 1);
+    abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+    if (SPLIT3) {
+      tc::prefetch_tmap(&tmAl);
+      tc::prefetch_tmap(&tmBl);
+    }
+  }
+  if (warp == 2) tc::tmem_alloc(&tmem_base, kTmemCols);
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_base;
+  const int ntiles = p.batch * p.mt * p.nt;
+  volatile int *abort_v = &abort_flag;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------ TMA producer
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t issued_ph[STAGES];
+    bool pending[STAGES];
+    for (int i = 0; i < STAGES; ++i) pending[i] = false, issued_ph[i] = 0;
+    for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x) {
+      int b, mb, nb;
+      decode_tile(t, p, b, mb, nb);
+      for (int kb = 0; kb < p.kt; ++kb) {
+        if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_v, p.err, 101)) goto producer_done;
+        uint8_t *sa = smem + (size_t)s * C::STAGE_BYTES;
+        tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        load_operand(&tmA, &full[s], sa, p.a_mn, mb * BM, BM, kb * BK, b);
+        if (SPLIT3) {
+          load_operand(&tmAl, &full[s], sa + A_BYTES, p.a_mn, mb * BM, BM, kb * BK, b);
+          load_operand(&tmB, &full[s], sa + 2 * A_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
+          load_operand(&tmBl, &full[s], sa + 2 * A_BYTES + B_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
+        } else {
+          load_operand(&tmB, &full[s], sa + A_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
+        }
+        issued_ph[s] = ph;
+        pending[s] = true;
+        if (++s == STAGES) s = 0, ph ^= 1;
+      }
+    }
+  producer_done:
+    // Do not leave while a TMA copy may still write this CTA's shared memory.
+    for (int i = 0; i < STAGES; ++i) {
+      if (!pending[i]) continue;
+      const long long t0 = clock64();
+      while (!tc::mbar_test(&full[i], issued_ph[i]) && clock64() - t0 < tc::kWaitCycles) {
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------- MMA issuer
+    const uint32_t idesc = tc::idesc_tf32(BM, BN, p.a_mn, p.b_mn);
+    int s = 0;
+    uint32_t ph = 0;
+    int local = 0;
+    bool issued = false;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tempty[buf], aph ^ 1, abort_v, p.err, 102)) break;
+      tc::fence_after_sync();
+      const uint32_t d = tbase + buf * BN;
+      for (int kb = 0; kb < p.kt; ++kb) {
+        if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 103)) goto mma_done;
+        tc::fence_after_sync();
+        const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
+        const uint32_t sb = SPLIT3 ? sa + 2 * A_BYTES : sa + A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t ad = operand_desc(sa, p.a_mn, kk);
+          const uint64_t bd = operand_desc(sb, p.b_mn, kk);
+          tc::mma_tf32(d, ad, bd, idesc, (kb | kk) != 0);
+          if (SPLIT3) {
+            tc::mma_tf32(d, ad, operand_desc(sb + B_BYTES, p.b_mn, kk), idesc, 1);
+            tc::mma_tf32(d, operand_desc(sa + A_BYTES, p.a_mn, kk), bd, idesc, 1);
+          }
+        }
+        issued = true;
+        tc::mma_commit(&empty[s]);
+        if (++s == STAGES) s = 0, ph ^= 1;
+      }
+      tc::mma_commit(&tfull[buf]);
+    }
+  mma_done:
+    if (issued) {
+      // all MMAs of this CTA done before TMEM can be released
+      tc::mma_commit(&drain);
+      const long long t0 = clock64();
+      while (!tc::mbar_test(&drain, 0) && clock64() - t0 < tc::kWaitCycles) {
+      }
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------- epilogue
+    const int e = warp - 4;
+    int local = 0;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((p.ldc & 3) == 0) &&
+                        ((p.c_bstride & 3) == 0);
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!tc::mbar_wait(&tfull[buf], aph, abort_v, p.err, 104)) break;
+      tc::fence_after_sync();
+      int b, mb, nb;
+      decode_tile(t, p, b, mb, nb);
+      const int row = mb * BM + e * 32 + lane;
+      float *crow = p.C + (long long)b * p.c_bstride + (long long)row * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(tbase + buf * BN + c * 32 + ((uint32_t)(e * 32) << 16), r);
+        tc::tmem_ld_wait();
+        const int col0 = nb * BN + c * 32;
+        if (row < p.M && col0 < p.N) {
+          if (vec_ok && col0 + 32 <= p.N) {
+            float4 *dst = reinterpret_cast<float4 *>(crow + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&tempty[buf]);
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// hi = x with the low 13 mantissa bits cleared (exactly representable in
+// tf32), lo = x - hi (exact in f32).  Copies a [batch][outer][inner] view
+// with arbitrary strides into contiguous [batch][outer][inner_pad] arrays,
+// zero-filling inner in [inner, inner_pad).
+__global__ void __launch_bounds__(256) prep_operand_kernel(const float *__restrict__ src, long long sb,
+                                                           long long so, long long si, int batch, long long outer,
+                                                           long long inner, long long inner_pad,
+                                                           float *__restrict__ hi, float *__restrict__ lo) {
+  const long long n = (long long)batch * outer * inner_pad;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const long long k = i % inner_pad;
+    const long long r = (i / inner_pad) % outer;
+    const long long b = i / (inner_pad * outer);
+    float v = k < inner ? src[b * sb + r * so + k * si] : 0.0f;
+    if (lo) {
+      const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+      hi[i] = h;
+      lo[i] = __fsub_rn(v, h);
+    } else {
+      hi[i] = v;
+    }
+  }
+}
+
+__global__ void fill_zero_kernel(float *c, long long ldc, long long bs, int batch, int M, int N) {
+  const long long n = (long long)batch * M * N;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const long long j = i % N, r = (i / N) % M, b = i / ((long long)N * M);
+    c[b * bs + r * ldc + j] = 0.0f;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// One GEMM operand as TMA sees it: contiguous inner dimension, `ld` elements
+// between outer rows, `bs` between batch entries.  `mn` says whether the
+// inner dimension is M/N (1) or K (0); `rows` is the M or N extent.
+struct Operand {
+  const float *base;
+  long long ld, bs;
+  int mn;
+  long long rows, K;
+};
+
+int encode_operand(const Operand &o, int box_rows, int batch, CUtensorMap *map) {
+  auto fn = encode_fn();
+  if (!fn) return fail(REMORA_ERR_CUDA, "gemm: cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3], estr[3] = {1, 1, 1};
+  if (!o.mn) {
+    dims[0] = (cuuint64_t)o.K;
+    dims[1] = (cuuint64_t)o.rows;
+    box[0] = 32;
+    box[1] = (cuuint32_t)box_rows;
+  } else {
+    dims[0] = (cuuint64_t)o.rows;
+    dims[1] = (cuuint64_t)o.K;
+    box[0] = 32;
+    box[1] = 32;
+  }
+  dims[2] = (cuuint64_t)batch;
+  box[2] = 1;
+  strides[0] = (cuuint64_t)o.ld * 4;
+  strides[1] = (cuuint64_t)(batch > 1 ? o.bs : o.ld * (long long)dims[1]) * 4;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(o.base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(REMORA_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu", (int)r,
+                (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2]);
+  return REMORA_OK;
+}
+
+bool tma_ok(const Operand &o, int batch) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(o.base);
+  return (a & 15) == 0 && o.ld > 0 && (o.ld & 3) == 0 && (batch == 1 || ((o.bs & 3) == 0 && o.bs > 0));
+}
+
+template <bool SPLIT3>
+int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Operand &Bl, GemmParams p,
+                int sm_count, cudaStream_t stream) {
+  CUtensorMap ma, mb, mal, mbl;
+  REMORA_TRY(encode_operand(A, BM, p.batch, &ma));
+  REMORA_TRY(encode_operand(B, BN, p.batch, &mb));
+  if (SPLIT3) {
+    REMORA_TRY(encode_operand(Al, BM, p.batch, &mal));
+    REMORA_TRY(encode_operand(Bl, BN, p.batch, &mbl));
+  } else {
+    mal = ma;
+    mbl = mb;
+  }
+  using C = Cfg<SPLIT3>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<SPLIT3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::SMEM));
+    attr_set = true;
+  }
+  const int ntiles = p.batch * p.mt * p.nt;
+  const int grid = std::min(ntiles, sm_count);
+  gemm_tf32_kernel<SPLIT3><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int grid_for(long long n, int sm_count) {
+  return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count * 16));
+}
+
+}  // namespace
+
+size_t gemm_workspace_bytes(long long batch, long long M, long long N, long long K, bool split) {
+  const long long kp = (K + 3) & ~3LL, mp = (M + 3) & ~3LL, np = (N + 3) & ~3LL;
+  const size_t a = (size_t)batch * std::max(M * kp, K * mp) * 4 + 256;
+  const size_t b = (size_t)batch * std::max(N * kp, K * np) * 4 + 256;
+  return (split ? 2 : 1) * (a + b) + (size_t)batch * M * N * 4 + 1024;
+}
+
+// Runs C = A . B with every operand given as a [batch][rows][cols] view.
+// `scratch` must hold gemm_workspace_bytes(...).
+int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescView &B, const DescView &Cd, int rank,
+             char *scratch, size_t scratch_bytes, int *err, cudaStream_t stream) {
+  const int batch = rank == 3 ? (int)A.sizes[0] : 1;
+  const int o = rank - 2;
+  const long long M = A.sizes[o], K = A.sizes[o + 1], N = B.sizes[o + 1];
+  if (B.sizes[o] != K) return fail(REMORA_ERR_SHAPE, "gemm: A is [%lld, %lld] but B has %lld rows", M, K, B.sizes[o]);
+  if (Cd.sizes[o] != M || Cd.sizes[o + 1] != N) return fail(REMORA_ERR_SHAPE, "gemm: C must be [%lld, %lld]", M, N);
+  if (rank == 3 && (B.sizes[0] != batch || Cd.sizes[0] != batch))
+    return fail(REMORA_ERR_SHAPE, "gemm: batch sizes differ");
+  if (M > (1LL << 30) || N > (1LL << 30) || K > (1LL << 30) || batch > 65535)
+    return fail(REMORA_ERR_LIMIT, "gemm: dimension beyond the supported range");
+  if (M == 0 || N == 0 || batch == 0) return REMORA_OK;
+  if (Cd.strides[o + 1] != 1 && N > 1)
+    return fail(REMORA_ERR_UNSUPPORTED, "gemm: C must have unit column stride");
+  float *cptr = reinterpret_cast<float *>(Cd.data(4));
+  const long long ldc = Cd.strides[o], cbs = rank == 3 ? Cd.strides[0] : 0;
+  if (K == 0) {
+    fill_zero_kernel<<<grid_for((long long)batch * M * N, ctx->sm_count), 256, 0, stream>>>(cptr, ldc, cbs, batch,
+                                                                                              (int)M, (int)N);
+    REMORA_CUDA_TRY(cudaGetLastError());
+    return REMORA_OK;
+  }
+  const bool split = precision == REMORA_PREC_3XTF32;
+  // Operand views: A [b][M][K], B [b][K][N].
+  auto make = [&](const DescView &d, long long rows_axis_size, bool is_a, Operand *op) {
+    const long long s_rows = is_a ? d.strides[o] : d.strides[o + 1];  // stride along M (A) / N (B)
+    const long long s_k = is_a ? d.strides[o + 1] : d.strides[o];
+    op->base = reinterpret_cast<const float *>(d.data(4));
+    op->bs = rank == 3 ? d.strides[0] : 0;
+    op->rows = rows_axis_size;
+    op->K = K;
+    if (s_k == 1 || K == 1) {
+      op->mn = 0;
+      op->ld = s_rows;
+    } else if (s_rows == 1 || rows_axis_size == 1) {
+      op->mn = 1;
+      op->ld = s_k;
+    } else {
+      op->mn = 0;
+      op->ld = -1;  // not TMA-addressable: staged below
+    }
+  };
+  Operand a, b;
+  make(A, M, true, &a);
+  make(B, N, false, &b);
+  char *ws = scratch;
+  size_t used = 0;
+  auto take = [&](size_t bytes) -> float * {
+    bytes = (bytes + 255) & ~(size_t)255;
+    if (used + bytes > scratch_bytes) return nullptr;
+    float *p = reinterpret_cast<float *>(ws + used);
+    used += bytes;
+    return p;
+  };
+  // Stage an operand (and split it for 3xTF32) into contiguous arrays that
+  // keep its majorness, padding the inner extent to a multiple of 4.
+  auto stage = [&](const DescView &d, bool is_a, Operand &op, Operand &lo) -> int {
+    const long long s_rows = is_a ? d.strides[o] : d.strides[o + 1];
+    const long long s_k = is_a ? d.strides[o + 1] : d.strides[o];
+    const long long inner = op.mn ? op.rows : K, outer = op.mn ? K : op.rows;
+    const long long si = op.mn ? s_rows : s_k, so = op.mn ? s_k : s_rows;
+    const long long inner_pad = (inner + 3) & ~3LL;
+    float *hi = take((size_t)batch * outer * inner_pad * 4);
+    float *lp = split ? take((size_t)batch * outer * inner_pad * 4) : nullptr;
+    if (!hi || (split && !lp)) return fail(REMORA_ERR_LIMIT, "gemm: workspace too small");
+    prep_operand_kernel<<<grid_for((long long)batch * outer * inner_pad, ctx->sm_count), 256, 0, stream>>>(
+        reinterpret_cast<const float *>(d.data(4)), rank == 3 ? d.strides[0] : 0, so, si, batch, outer, inner,
+        inner_pad, hi, lp);
+    REMORA_CUDA_TRY(cudaGetLastError());
+    op.base = hi;
+    op.ld = inner_pad;
+    op.bs = outer * inner_pad;
+    if (op.mn) op.rows = inner; else op.K = K;
+    if (split) {
+      lo = op;
+      lo.base = lp;
+    }
+    return REMORA_OK;
+  };
+  Operand al{}, bl{};
+  if (split || a.ld < 0 || !tma_ok(a, batch)) {
+    if (a.ld < 0) a.mn = 0;
+    REMORA_TRY(stage(A, true, a, al));
+  }
+  if (split || b.ld < 0 || !tma_ok(b, batch)) {
+    if (b.ld < 0) b.mn = 0;
+    REMORA_TRY(stage(B, false, b, bl));
+  }
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = batch;
+  p.a_mn = a.mn;
+  p.b_mn = b.mn;
+  p.mt = (int)((M + BM - 1) / BM);
+  p.nt = (int)((N + BN - 1) / BN);
+  p.kt = (int)((K + BK - 1) / BK);
+  p.C = cptr;
+  p.ldc = ldc;
+  p.c_bstride = cbs;
+  p.err = err;
+  if (split) return launch_gemm<true>(a, b, al, bl, p, ctx->sm_count, stream);
+  return launch_gemm<false>(a, b, a, b, p, ctx->sm_count, stream);
+}
+
+}  // namespace remora
 
 using namespace remora;
 
 extern "C" int remora_b200_gemm(RemoraB200Ctx *ctx, const RemoraGemmSpec *spec, const void *a_desc,
                                 const void *b_desc, void *c_desc, int32_t rank, remora_stream_t stream) {
-  (void)spec, (void)a_desc, (void)b_desc, (void)c_desc, (void)rank, (void)stream;
   REMORA_TRY(check_ctx(ctx));
-  return fail(REMORA_ERR_UNSUPPORTED, "gemm: the tcgen05 kernel is not part of this build yet");
+  if (spec == nullptr) return fail(REMORA_ERR_ARG, "gemm: null spec");
+  if (spec->precision != REMORA_PREC_TF32 && spec->precision != REMORA_PREC_3XTF32)
+    return fail(REMORA_ERR_ARG, "gemm: unknown precision %d", spec->precision);
+  if (rank != 2 && rank != 3) return fail(REMORA_ERR_RANK, "gemm: rank %d (2, or 3 for a batch)", rank);
+  DescView A, B, C;
+  REMORA_TRY(read_desc(a_desc, rank, &A, "gemm A"));
+  REMORA_TRY(read_desc(b_desc, rank, &B, "gemm B"));
+  REMORA_TRY(read_desc(c_desc, rank, &C, "gemm C"));
+  const int o = rank - 2;
+  const long long batch = rank == 3 ? A.sizes[0] : 1;
+  const size_t need = gemm_workspace_bytes(batch, A.sizes[o], B.sizes[o + 1], A.sizes[o + 1],
+                                           spec->precision == REMORA_PREC_3XTF32);
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, need, &ws));
+  return run_gemm(ctx, spec->precision, A, B, C, rank, (char *)ws->buf, ws->bytes, ws->err, (cudaStream_t)stream);
 }

@@ -53,7 +53,7 @@ def oracle_mod():
 def to_dev(a: np.ndarray, device):
     import torch
 
-    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    return torch.from_numpy(np.array(a, copy=True, order="C")).to(device)
 
 
 def to_host(t) -> np.ndarray:

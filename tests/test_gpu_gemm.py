@@ -1,0 +1,112 @@
+"""GPU parity of the tcgen05 dense core (matmul as the lifted dot).
+
+Tolerances (north_star): TF32 rtol 1e-3 + atol 1e-3 * max|ref|; 3xTF32 is
+held to f32-level agreement, atol 2e-5 * max|ref| + rtol 1e-5, against the
+oracle's sequential-k f32 lifted dot."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden, to_dev, to_host
+from remora_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def check(got, ref, precision):
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = max(1.0, float(np.abs(ref).max()) if ref.size else 1.0)
+    if precision == "tf32":
+        np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-3 * scale)
+    else:
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=2e-5 * scale)
+
+
+def test_golden_lifted_matmul(cuda):
+    g = golden("lifted_matmul")
+    a, bt = to_dev(g["a"], cuda), to_dev(g["bt"], cuda)
+    for prec in ("3xtf32", "tf32"):
+        check(to_host(ops.gemm(a, bt.t(), precision=prec)), g["out"], prec)
+
+
+@pytest.mark.parametrize("mnk", [(128, 256, 32), (128, 256, 256), (256, 512, 128), (100, 200, 40), (129, 257, 36),
+                                 (300, 130, 500), (64, 64, 6), (5, 3, 1), (1, 1000, 64)])
+@pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
+def test_gemm_shapes(cuda, oracle_mod, mnk, prec):
+    M, N, K = mnk
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec))
+    check(got, oracle_mod.matmul(a, b), prec)
+
+
+@pytest.mark.parametrize("layout", ["kk", "km", "mk", "mm"])
+def test_gemm_operand_majors(cuda, oracle_mod, layout):
+    """A K-major (rows of A contiguous) or M-major (A^T stored), B K-major (the
+    reference's Bt rows) or N-major (B rows contiguous)."""
+    M, N, K = 256, 512, 160
+    rng = np.random.default_rng(42)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ta = to_dev(a, cuda) if layout[0] == "k" else to_dev(a.T.copy(), cuda).t()
+    tb = to_dev(b.T.copy(), cuda).t() if layout[1] == "k" else to_dev(b, cuda)
+    got = to_host(ops.gemm(ta, tb, precision="3xtf32"))
+    check(got, oracle_mod.matmul(a, b), "3xtf32")
+
+
+def test_gemm_batched_and_views(cuda, oracle_mod):
+    rng = np.random.default_rng(7)
+    a = rng.uniform(-1, 1, (3, 130, 68)).astype(np.float32)
+    b = rng.uniform(-1, 1, (3, 68, 260)).astype(np.float32)
+    for prec in ("3xtf32", "tf32"):
+        check(to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec)), oracle_mod.matmul(a, b), prec)
+    # strided sub-views and an output view with a row stride
+    import torch
+
+    big = to_dev(rng.uniform(-1, 1, (300, 300)).astype(np.float32), cuda)
+    av, bv = big[10:138, 4:100], big[100:196, 20:276]
+    out = torch.zeros((200, 400), dtype=torch.float32, device=cuda)
+    ops.gemm(av, bv, precision="3xtf32", out=out[3:131, 7:263])
+    ref = oracle_mod.matmul(to_host(av).copy(), to_host(bv).copy())
+    check(to_host(out[3:131, 7:263]), ref, "3xtf32")
+    assert float(out[:3].abs().sum()) == 0.0 and float(out[:, :7].abs().sum()) == 0.0
+
+
+def test_gemm_k_zero(cuda):
+    import torch
+
+    a = torch.zeros((4, 0), device=cuda)
+    b = torch.zeros((0, 5), device=cuda)
+    out = torch.full((4, 5), 7.0, device=cuda)
+    ops.gemm(a, b, out=out)
+    assert float(out.abs().sum()) == 0.0
+
+
+@pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
+def test_gemm_4096_sampled_rows(cuda, oracle_mod, prec):
+    """The dense-core workload A,B f32[4096,4096] ~ U[-1,1]: every output
+    row is computed on the device; 48 sampled rows are checked against the
+    oracle's sequential lifted dot."""
+    ra = np.random.Generator(np.random.PCG64(1729))
+    rb = np.random.Generator(np.random.PCG64(1730))
+    a = ra.uniform(-1, 1, (4096, 4096)).astype(np.float32)
+    b = rb.uniform(-1, 1, (4096, 4096)).astype(np.float32)
+    got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec))
+    rows = np.random.default_rng(0).choice(4096, 48, replace=False)
+    ref = oracle_mod.matmul(a[rows], b, nthreads=oracle_mod.max_threads())
+    check(got[rows], ref, prec)
+    assert np.isfinite(got).all()
+
+
+def test_gemm_batched_full_sampled(cuda, oracle_mod):
+    """The batched workload [32,1024,1024] x [32,1024,1024] (3xTF32)."""
+    ra = np.random.Generator(np.random.PCG64(1729))
+    a = ra.uniform(-1, 1, (32, 1024, 1024)).astype(np.float32)
+    b = ra.uniform(-1, 1, (32, 1024, 1024)).astype(np.float32)
+    got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision="3xtf32"))
+    for bi in (0, 17, 31):
+        rows = np.arange(bi * 13 % 1000, bi * 13 % 1000 + 24)
+        check(got[bi, rows], oracle_mod.matmul(a[bi, rows], b[bi], nthreads=oracle_mod.max_threads()), "3xtf32")

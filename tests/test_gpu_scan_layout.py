@@ -15,8 +15,10 @@ from remora_b200.errors import RemoraUnsupportedError
 pytestmark = pytest.mark.gpu
 
 
-def scan_close(got, ref, x):
-    bound = 1e-5 * np.abs(ref) + 2e-6 * (np.cumsum(np.abs(x.astype(np.float64)), axis=0) + 1.0)
+def scan_close(got, ref, x, right=False):
+    ax = np.abs(x.astype(np.float64))
+    mag = np.flip(np.cumsum(np.flip(ax, 0), axis=0), 0) if right else np.cumsum(ax, axis=0)
+    bound = 1e-5 * np.abs(ref) + 2e-6 * (mag + 1.0)
     assert np.all(np.abs(got.astype(np.float64) - ref) <= bound)
 
 
@@ -41,7 +43,7 @@ def test_rank1_scans(cuda, oracle_mod, n, kw):
                                   oracle_mod.scan(scan_spec(dtype="i32", init=-5, **kw), xi))
     xf = rng.uniform(-1, 1, n).astype(np.float32)
     scan_close(to_host(ops.scan(to_dev(xf, cuda), init=0.25, **kw)), oracle_mod.scan(scan_spec(init=0.25, **kw), xf),
-               xf)
+               xf, right=kw.get("right", False))
 
 
 @pytest.mark.parametrize("shape", [(5, 3), (1000, 1), (4096, 16), (3, 300000), (257, 7, 5)])
@@ -62,7 +64,9 @@ def test_scan_mul_and_determinism(cuda):
     a = to_host(ops.scan(d, op="*", init=1.0))
     b = to_host(ops.scan(d, op="*", init=1.0))
     np.testing.assert_array_equal(a, b)
-    np.testing.assert_allclose(a, np.cumprod(xf.astype(np.float64)), rtol=1e-5)
+    # f32 products of values near 1 round with a bias: sequential f32 is
+    # ~1e-4 from f64 on this input, a blocked order ~3e-4
+    np.testing.assert_allclose(a, np.cumprod(xf.astype(np.float64)), rtol=1e-3)
 
 
 def test_im2col_col2im_golden_and_oracle(cuda, oracle_mod):
