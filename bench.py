@@ -7,14 +7,18 @@ f32[64,64,64,64] ~ N(0,1): y = x*2.5 + 1.0, mask y > 0.5 ? y : 0, fold (+)
 over the last axis -> f32[64,64,64]; metric HBM GB/s of algorithmic bytes
 (67,108,864 read + 1,048,576 written per call).  One step = one pass over a
 rotation of 8 distinct inputs (545 MB, more than 4x the 126 MB L2, so every
-call streams from HBM).  Other configs: ``row_norms`` (f32[8192,1024] ->
-sqrt(sum x*x)).
+call streams from HBM).
 
-With N GPUs (torchrun, one process per GPU) every rank folds its own frames
-(weak scaling, no data-path collective); rank 0 prints the aggregate.
+Other configs: ``row_norms`` (f32[8192,1024] -> sqrt(sum x*x)), ``matmul``
+(A,B f32[4096,4096], TF32; ``matmul_3x`` the 3xTF32 form), ``bmm``
+([32,1024,1024] x [32,1024,1024], TF32).
+
+With N GPUs (torchrun, one process per GPU) every rank runs its own copy of
+the workload (weak scaling: folds shard frames, matmuls shard rows; no
+data-path collective); rank 0 prints the aggregate over max-over-ranks time.
 ``--impl reference`` times the CPU restatement of the reference's CPU path
-(the oracle, OpenMP over all host threads) on the same workload and prints
-the same JSON line with ``"impl": "reference"``.
+(the oracle, OpenMP over all host threads) on a bounded sample of the same
+workload and prints the same JSON line with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
@@ -34,8 +38,8 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "map/fold HBM GB/s"
-ROTATE = 8
+METRIC_FOLD = "map/fold HBM GB/s"
+METRIC_MM = "matmul/conv TFLOP/s"
 
 
 def measured_peaks() -> dict:
@@ -88,7 +92,7 @@ class ClockSampler:
             self._proc.kill()
         if self._thread:
             self._thread.join(timeout=2)
-        busy = [r for r in self.rows if len(r) >= 10 and r[4] not in ("", "[N/A]") and _num(r[4]) > 0]
+        busy = [r for r in self.rows if len(r) >= 10 and _num(r[4]) > 0]
         use = busy or self.rows
         if not use:
             return None
@@ -110,9 +114,18 @@ def _num(s: str) -> float:
         return 0.0
 
 
+def _oracle():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # noqa: E402  (checker and CPU baseline only)
+
+    return oracle
+
+
 # -------------------------------------------------------------- workloads
 class FoldWorkload:
-    """Cell-fold workloads (one fused kernel per call)."""
+    """Cell-fold workloads: one fused map+fold kernel per call."""
+
+    metric, unit, bound = METRIC_FOLD, "GB/s", "hbm"
 
     def __init__(self, name: str) -> None:
         from remora_b200.program import BinaryExpr, CmpExpr, SelectExpr, const, x
@@ -124,16 +137,16 @@ class FoldWorkload:
             self.premap = SelectExpr(CmpExpr(">", y, const(0.5)), y, const(0.0))
             self.epilogue = None
             self.desc = "chained_maps_fold f32[64,64,64,64] ~ N(0,1): select(x*2.5+1 > 0.5), fold + last axis"
-        elif name == "row_norms":
+        else:
             self.shape = (8192, 1024)
             self.premap = BinaryExpr("*", x(0), x(0))
             self.epilogue = "sqrt"
             self.desc = "row_norms f32[8192,1024] ~ U[-1,1]: sqrt(fold + (map x*x)) per row"
-        else:
-            raise SystemExit(f"unknown fold config {name}")
         self.n_in = int(np.prod(self.shape))
         self.n_out = int(np.prod(self.shape[:-1]))
-        self.bytes_per_call = 4 * (self.n_in + self.n_out)
+        self.work_per_call = 4 * (self.n_in + self.n_out)  # algorithmic bytes
+        self.rotate = 8
+        self.launches_per_call = 1
 
     def make_input(self, seed: int) -> np.ndarray:
         rng = np.random.Generator(np.random.PCG64(seed))
@@ -146,7 +159,201 @@ class FoldWorkload:
 
         return fold_spec(premap=self.premap, epilogue=self.epilogue)
 
+    def setup(self, dev, rank: int) -> None:
+        import torch
 
+        from remora_b200 import _lib as L
+        from remora_b200.abi import tensor_descriptor
+        from remora_b200.runtime import context
+
+        self.torch, self.L, self.lib = torch, L, L.lib()
+        self.host = [self.make_input(1729 + 1000 * rank + k) for k in range(self.rotate)]
+        self.xs = [torch.from_numpy(h).to(dev) for h in self.host]
+        self.out = torch.empty(self.shape[:-1], dtype=torch.float32, device=dev)
+        self.sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        self.ctx = context(dev.index)
+        self._spec = self.spec()
+        self.descs = [tensor_descriptor(t) for t in self.xs]
+        self.out_desc = tensor_descriptor(self.out)
+        self.ranks = (ctypes.c_int32 * 1)(len(self.shape))
+        self.ptrs = [(ctypes.c_void_p * 1)(ctypes.addressof(d)) for d in self.descs]
+        self.dev = dev
+
+    def call(self, k: int) -> None:
+        st = self.lib.remora_b200_fold(self.ctx.ptr, ctypes.byref(self._spec), self.ptrs[k], self.ranks, 1,
+                                       ctypes.addressof(self.out_desc), len(self.shape) - 1, self.sptr)
+        if st:
+            self.L.check(st, "fold")
+
+    def check(self) -> None:
+        torch = self.torch
+        self.call(0)
+        torch.cuda.synchronize()
+        x = self.xs[0]
+        if self.name == "chained":
+            y = x * 2.5 + 1.0
+            ref = torch.where(y > 0.5, y, torch.zeros_like(y)).sum(-1)
+        else:
+            ref = (x * x).sum(-1).sqrt()
+        if not torch.allclose(self.out, ref, rtol=1e-4, atol=1e-4):
+            raise SystemExit("benchmark output does not match the check")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        torch = self.torch
+        from remora_b200.abi import tensor_descriptor
+
+        self.pin_in = torch.from_numpy(self.host[0]).pin_memory()
+        self.pin_out = torch.empty(self.shape[:-1], dtype=torch.float32).pin_memory()
+        self.dbuf = torch.empty(self.shape, dtype=torch.float32, device=self.dev)
+        self.dbuf_desc = tensor_descriptor(self.dbuf)
+        self.dbuf_ptrs = (ctypes.c_void_p * 1)(ctypes.addressof(self.dbuf_desc))
+        return self.pin_in.numel() * 4, self.pin_out.numel() * 4
+
+    def e2e_step(self) -> None:
+        L, lib = self.L, self.lib
+        L.check(lib.remora_b200_memcpy_h2d(self.ctx.ptr, ctypes.c_void_p(self.dbuf.data_ptr()),
+                                           ctypes.c_void_p(self.pin_in.data_ptr()), self.pin_in.numel() * 4,
+                                           self.sptr))
+        L.check(lib.remora_b200_fold(self.ctx.ptr, ctypes.byref(self._spec), self.dbuf_ptrs, self.ranks, 1,
+                                     ctypes.addressof(self.out_desc), len(self.shape) - 1, self.sptr))
+        L.check(lib.remora_b200_memcpy_d2h(self.ctx.ptr, ctypes.c_void_p(self.pin_out.data_ptr()),
+                                           ctypes.c_void_p(self.out.data_ptr()), self.pin_out.numel() * 4,
+                                           self.sptr))
+
+    # ---- CPU side (oracle)
+    def cpu_prepare(self) -> None:
+        self.cx = self.make_input(1729)
+        o = _oracle()
+        self.nt = o.max_threads()
+        ref = o.compiled_fold(self.name, self.cx, nthreads=self.nt)
+        chk = o.cell_fold(self.spec(), [self.cx], 1, nthreads=self.nt)
+        if not np.array_equal(ref, chk):
+            raise SystemExit("compiled CPU loop differs from the oracle interpreter")
+
+    def cpu_step(self) -> float:
+        """One bounded CPU sample; returns the algorithmic work it covered."""
+        _oracle().compiled_fold(self.name, self.cx, nthreads=self.nt)
+        return float(self.work_per_call)
+
+    cpu_sample = "full workload per sample (compiled C loop of the oracle, sequential f32 cell folds, OpenMP over frames)"
+
+
+class MatmulWorkload:
+    """C = A . B on tcgen05: one library call per product (A K-major, B
+    N-major as given, both native operand layouts)."""
+
+    metric, unit, bound = METRIC_MM, "TFLOP/s", "tensor"
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.precision = "3xtf32" if name == "matmul_3x" else "tf32"
+        if name == "bmm":
+            self.batch, self.M, self.N, self.K = 32, 1024, 1024, 1024
+            self.desc = "batched matmul [32,1024,1024] x [32,1024,1024] f32 ~ U[-1,1], TF32 tcgen05, f32 accumulate"
+        else:
+            self.batch, self.M, self.N, self.K = 1, 4096, 4096, 4096
+            self.desc = f"matmul A,B f32[4096,4096] ~ U[-1,1], {self.precision.upper()} tcgen05, f32 accumulate"
+        self.work_per_call = 2.0 * self.batch * self.M * self.N * self.K  # algorithmic flops
+        self.rotate = 1
+        self.launches_per_call = 1 if self.precision == "tf32" else 3
+
+    def shapes(self):
+        if self.batch > 1:
+            return (self.batch, self.M, self.K), (self.batch, self.K, self.N), (self.batch, self.M, self.N)
+        return (self.M, self.K), (self.K, self.N), (self.M, self.N)
+
+    def make_inputs(self, seed: int):
+        sa, sb, _ = self.shapes()
+        ra = np.random.Generator(np.random.PCG64(seed))
+        rb = np.random.Generator(np.random.PCG64(seed + 1))
+        return ra.uniform(-1, 1, sa).astype(np.float32), rb.uniform(-1, 1, sb).astype(np.float32)
+
+    def setup(self, dev, rank: int) -> None:
+        import torch
+
+        from remora_b200 import _lib as L
+        from remora_b200.abi import tensor_descriptor
+        from remora_b200.runtime import context
+
+        self.torch, self.L, self.lib, self.dev = torch, L, L.lib(), dev
+        self.ha, self.hb = self.make_inputs(1729 + 1000 * rank)
+        self.a = torch.from_numpy(self.ha).to(dev)
+        self.b = torch.from_numpy(self.hb).to(dev)
+        self.c = torch.empty(self.shapes()[2], dtype=torch.float32, device=dev)
+        self.ad, self.bd, self.cd = (tensor_descriptor(t) for t in (self.a, self.b, self.c))
+        self._spec = L.RemoraGemmSpec(L.PREC_TF32 if self.precision == "tf32" else L.PREC_3XTF32, 0)
+        self.sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        self.ctx = context(dev.index)
+        self.rank_ = len(self.shapes()[0])
+
+    def call(self, k: int) -> None:
+        st = self.lib.remora_b200_gemm(self.ctx.ptr, ctypes.byref(self._spec), ctypes.addressof(self.ad),
+                                       ctypes.addressof(self.bd), ctypes.addressof(self.cd), self.rank_, self.sptr)
+        if st:
+            self.L.check(st, "gemm")
+
+    def check(self) -> None:
+        torch = self.torch
+        self.call(0)
+        torch.cuda.synchronize()
+        a64 = self.a[..., :256, :].double()
+        ref = torch.matmul(a64, self.b.double())
+        got = self.c[..., :256, :].double()
+        tol = 1e-3 if self.precision == "tf32" else 2e-5
+        err = float((got - ref).abs().max()) / max(1.0, float(ref.abs().max()))
+        if not err <= tol:
+            raise SystemExit(f"benchmark output does not match the check (scaled error {err:.3g})")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        torch = self.torch
+        self.pa = torch.from_numpy(self.ha).pin_memory()
+        self.pb = torch.from_numpy(self.hb).pin_memory()
+        self.pc = torch.empty(self.shapes()[2], dtype=torch.float32).pin_memory()
+        return (self.pa.numel() + self.pb.numel()) * 4, self.pc.numel() * 4
+
+    def e2e_step(self) -> None:
+        L, lib, c = self.L, self.lib, self.ctx.ptr
+        L.check(lib.remora_b200_memcpy_h2d(c, ctypes.c_void_p(self.a.data_ptr()), ctypes.c_void_p(self.pa.data_ptr()),
+                                           self.pa.numel() * 4, self.sptr))
+        L.check(lib.remora_b200_memcpy_h2d(c, ctypes.c_void_p(self.b.data_ptr()), ctypes.c_void_p(self.pb.data_ptr()),
+                                           self.pb.numel() * 4, self.sptr))
+        self.call(0)
+        L.check(lib.remora_b200_memcpy_d2h(c, ctypes.c_void_p(self.pc.data_ptr()), ctypes.c_void_p(self.c.data_ptr()),
+                                           self.pc.numel() * 4, self.sptr))
+
+    def cpu_prepare(self) -> None:
+        self.ca, self.cb = self.make_inputs(1729)
+        o = _oracle()
+        self.nt = o.max_threads()
+        self.rows = 64 if self.batch == 1 else 16
+
+    def cpu_step(self) -> float:
+        o = _oracle()
+        if self.batch == 1:
+            o.matmul(self.ca[: self.rows], self.cb, nthreads=self.nt)
+        else:
+            o.matmul(self.ca[0, : self.rows], self.cb[0], nthreads=self.nt)
+        return 2.0 * self.rows * self.N * self.K
+
+    @property
+    def cpu_sample(self) -> str:
+        return (f"{self.rows} output rows of one {self.M}x{self.N}x{self.K} product per sample (oracle lifted dot, "
+                "sequential f32 k order, OpenMP over rows)")
+
+
+def make_workload(name: str):
+    if name in ("chained", "row_norms"):
+        return FoldWorkload(name)
+    return MatmulWorkload(name)
+
+
+def tf32_peak(peaks: dict) -> float:
+    # dense TF32 on B200 runs at half the bf16 tensor rate: peak = measured
+    # cuBLAS bf16 burst / 2
+    return peaks["bf16_tflops"] / 2.0
+
+
+# --------------------------------------------------------------- harness
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -161,53 +368,24 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    from remora_b200 import _lib as L
-    from remora_b200 import ops
-    from remora_b200.abi import make_memref_descriptor, tensor_descriptor
-    from remora_b200.runtime import context
-
-    wl = FoldWorkload(args.config)
-    spec = wl.spec()
-    host_inputs = [wl.make_input(1729 + 1000 * rank + k) for k in range(ROTATE)]
-    xs = [torch.from_numpy(h).to(dev) for h in host_inputs]
-    out = torch.empty(wl.shape[:-1], dtype=torch.float32, device=dev)
+    wl = make_workload(args.config)
+    wl.setup(dev, rank)
+    wl.check()
     stream = torch.cuda.current_stream(dev)
-    sptr = ctypes.c_void_p(stream.cuda_stream)
-    ctx = context(local)
-    in_descs = [tensor_descriptor(t) for t in xs]
-    out_desc = tensor_descriptor(out)
-    ranks = (ctypes.c_int32 * 1)(len(wl.shape))
-    ptr_arrays = [(ctypes.c_void_p * 1)(ctypes.addressof(d)) for d in in_descs]
-    lib = L.lib()
-
-    def call(k: int) -> None:
-        st = lib.remora_b200_fold(ctx.ptr, ctypes.byref(spec), ptr_arrays[k], ranks, 1,
-                                  ctypes.addressof(out_desc), len(wl.shape) - 1, sptr)
-        if st:
-            L.check(st, "fold")
-
-    # correctness guard on the benchmark input itself (cheap, untimed)
-    ref0 = torch.from_numpy(host_inputs[0]).to(dev)
-    call(0)
-    torch.cuda.synchronize()
-    y = ref0 * 2.5 + 1.0 if wl.name == "chained" else ref0 * ref0
-    ref = torch.where(y > 0.5, y, torch.zeros_like(y)).sum(-1) if wl.name == "chained" else y.sum(-1).sqrt()
-    if not torch.allclose(out, ref, rtol=1e-4, atol=1e-4):
-        raise SystemExit("benchmark output does not match the check")
 
     for _ in range(args.warmup):
-        for k in range(ROTATE):
-            call(k)
+        for k in range(wl.rotate):
+            wl.call(k)
     torch.cuda.synchronize()
     sampler = ClockSampler(local) if rank == 0 and not args.profile else None
     if sampler:
         sampler.start()
     # keep the GPU busy ~1 s before the timed region so clocks are steady and
-    # the sampler sees the load that the timed region runs under
+    # the sampler sees the load the timed region runs under
     t_end = time.time() + (0.0 if args.profile else 1.0)
     while time.time() < t_end:
-        for k in range(ROTATE):
-            call(k)
+        for k in range(wl.rotate):
+            wl.call(k)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -218,8 +396,8 @@ def run_ours(args) -> None:
     t0.record(stream)
     for s in range(args.steps):
         ev[s][0].record(stream)
-        for k in range(ROTATE):
-            call(k)
+        for k in range(wl.rotate):
+            wl.call(k)
         ev[s][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
@@ -232,30 +410,13 @@ def run_ours(args) -> None:
         if world > 1:
             dist.destroy_process_group()
         if rank == 0:
-            print(json.dumps({"profile_run": wl.name, "ms": ms, "steps": args.steps}), flush=True)
+            print(json.dumps({"profile_run": args.config, "ms": ms, "steps": args.steps}), flush=True)
         return
 
-    # e2e: host buffers through the C ABI, pinned host memory, copies inside
-    # the timed region every step
-    pinned_in = torch.from_numpy(host_inputs[0]).pin_memory()
-    pinned_out = torch.empty(wl.shape[:-1], dtype=torch.float32).pin_memory()
-    dbuf = torch.empty(wl.shape, dtype=torch.float32, device=dev)
-    dbuf_desc = tensor_descriptor(dbuf)
-    dbuf_ptrs = (ctypes.c_void_p * 1)(ctypes.addressof(dbuf_desc))
-    nbytes_in = pinned_in.numel() * 4
-    nbytes_out = pinned_out.numel() * 4
-
-    def e2e_step() -> None:
-        L.check(lib.remora_b200_memcpy_h2d(ctx.ptr, ctypes.c_void_p(dbuf.data_ptr()),
-                                           ctypes.c_void_p(pinned_in.data_ptr()), nbytes_in, sptr))
-        L.check(lib.remora_b200_fold(ctx.ptr, ctypes.byref(spec), dbuf_ptrs, ranks, 1, ctypes.addressof(out_desc),
-                                     len(wl.shape) - 1, sptr))
-        L.check(lib.remora_b200_memcpy_d2h(ctx.ptr, ctypes.c_void_p(pinned_out.data_ptr()),
-                                           ctypes.c_void_p(out.data_ptr()), nbytes_out, sptr))
-
-    e2e_steps = max(3, min(args.steps, 50))
-    for _ in range(3):
-        e2e_step()
+    h2d, d2h = wl.e2e_setup()
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        wl.e2e_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -263,7 +424,7 @@ def run_ours(args) -> None:
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        wl.e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -276,16 +437,17 @@ def run_ours(args) -> None:
 
     if rank == 0:
         peaks = measured_peaks()
-        calls = args.steps * ROTATE
-        total_bytes = wl.bytes_per_call * calls * world
-        value = total_bytes / (ms * 1e-3) / 1e9
-        per_launch_ms = float(np.mean(step_ms)) / ROTATE
-        achieved = wl.bytes_per_call / (per_launch_ms * 1e-3) / 1e9
-        e2e_value = wl.bytes_per_call * e2e_steps * world / (e2e_ms * 1e-3) / 1e9
+        scale = 1e9 if wl.unit == "GB/s" else 1e12
+        calls = args.steps * wl.rotate
+        value = wl.work_per_call * calls * world / (ms * 1e-3) / scale
+        per_call_ms = float(np.mean(step_ms)) / wl.rotate
+        achieved = wl.work_per_call / (per_call_ms * 1e-3) / scale
+        peak = peaks["hbm_gbs"] if wl.bound == "hbm" else tf32_peak(peaks)
+        e2e_value = wl.work_per_call * e2e_steps * world / (e2e_ms * 1e-3) / scale
         line = {
-            "metric": METRIC,
+            "metric": wl.metric,
             "value": round(value, 2),
-            "unit": "GB/s",
+            "unit": wl.unit,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
@@ -293,17 +455,18 @@ def run_ours(args) -> None:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "f32",
+            "dtype": "f32" if wl.bound == "hbm" else f"f32 storage, {getattr(wl, 'precision', 'tf32')} tensor math",
             "data": "synthetic (seeded PCG64)",
-            "config": {"workload": wl.desc, "calls_per_step": ROTATE,
-                       "l2": f"{ROTATE} rotating inputs, {ROTATE * wl.n_in * 4 / 1e6:.0f} MB > 126 MB L2",
-                       "parallelism": f"replicas x{world} (frames sharded, no collective)"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
-                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                         "traffic": TRAFFIC.get(wl.name), "peak_source": peaks["source"]},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": nbytes_in,
-                    "d2h_bytes_per_step": nbytes_out},
-            "gpu_launches": calls,
+            "config": {"workload": wl.desc, "calls_per_step": wl.rotate,
+                       "l2": (f"{wl.rotate} rotating inputs, {wl.rotate * wl.work_per_call / 1e6:.0f} MB > 126 MB L2"
+                              if wl.bound == "hbm" else "operands 192 MB > 126 MB L2"),
+                       "parallelism": f"replicas x{world} (independent shards, no collective)"},
+            "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": wl.unit,
+                         "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
+                         "peak_source": peaks["source"] + (" (bf16 / 2)" if wl.bound == "tensor" else "")},
+            "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": calls * wl.launches_per_call,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -313,64 +476,60 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-# Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) from the
-# ncu captures summarised under profiles/; None until captured.
-TRAFFIC: dict[str, float | None] = {"chained": None, "row_norms": None}
+# Per-call DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel, from the ncu captures summarised under profiles/.
+TRAFFIC: dict[str, float | None] = {"chained": 67_129_856 + 563_200, "row_norms": None, "matmul": None,
+                                    "matmul_3x": None, "bmm": None}
 
 
-def cpu_baseline(wl: FoldWorkload, budget_s: float = 8.0) -> dict:
+def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
     """The oracle (CPU restatement of the reference's CPU loop order), OpenMP
-    over all host threads, repeated on the full workload for ~budget_s."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle  # noqa: E402  (checker / CPU baseline only)
-
-    x = wl.make_input(1729)
-    nt = oracle.max_threads()
-    ref = oracle.compiled_fold(wl.name, x, nthreads=nt)
-    chk = oracle.cell_fold(wl.spec(), [x], 1, nthreads=nt)
-    if not np.array_equal(ref, chk):
-        raise SystemExit("compiled CPU loop differs from the oracle interpreter")
+    over all host threads, repeated on bounded samples for ~budget_s."""
+    wl.cpu_prepare()
+    wl.cpu_step()
+    work = 0.0
     reps = 0
     t0 = time.perf_counter()
     while True:
-        oracle.compiled_fold(wl.name, x, nthreads=nt)
+        work += wl.cpu_step()
         reps += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
-    return {"value": round(wl.bytes_per_call * reps / el / 1e9, 3), "unit": "GB/s", "cores": nt, "kind": "port",
-            "sample": f"full workload x{reps} calls in {el:.1f} s (compiled C loop of the oracle, sequential f32 "
-                      "cell folds, OpenMP over frames)"}
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    return {"value": round(work / el / scale, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
+            "sample": f"{wl.cpu_sample}; {reps} samples in {el:.1f} s"}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return
-    wl = FoldWorkload(args.config)
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle  # noqa: E402  (the reference arm: CPU restatement of the reference path)
-
-    x = wl.make_input(1729)
-    nt = oracle.max_threads()
+    wl = make_workload(args.config)
+    wl.cpu_prepare()
     for _ in range(max(1, args.warmup)):
-        oracle.compiled_fold(wl.name, x, nthreads=nt)
+        wl.cpu_step()
+    work = 0.0
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.compiled_fold(wl.name, x, nthreads=nt)
+        work += wl.cpu_step()
     el = time.perf_counter() - t0
-    value = wl.bytes_per_call * args.steps / el / 1e9
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    value = work / el / scale
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded PCG64)", "impl": "reference",
+        "metric": wl.metric, "value": round(value, 5), "unit": wl.unit,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", 1)), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded PCG64)", "impl": "reference",
         "config": {"workload": wl.desc, "calls_per_step": 1},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nt, "kind": "port",
-                         "sample": f"full workload, one call per step, {args.steps} steps"},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
+                         "sample": f"{wl.cpu_sample}; one sample per step, {args.steps} steps"},
+        "e2e": {"value": round(value, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm"]
 
 
 def main() -> None:
@@ -378,7 +537,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="chained", choices=["chained", "row_norms"])
+    ap.add_argument("--config", default="chained", choices=CONFIGS)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

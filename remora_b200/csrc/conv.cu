@@ -1,6 +1,148 @@
-// conv.cu — NCHW convolution forward and reverse mode.  The implicit-GEMM
-// kernels are not in this build yet; the entry points report that.
-#include "common.cuh"
+// conv.cu — NCHW convolution forward and reverse mode (remora_b200_conv2d_*).
+//
+// The reference's conv2d is single-channel cross-correlation built from
+// im2col and a lifted dot, plus a scalar bias (examples/crater_train.py:30-36,
+// remora/runtime.py:1274-1288); its reverse mode is col2im for the image
+// (remora/ad.py:157-171) and the mul/fold VJPs for the kernel
+// (remora/ad.py:88-110).  This file extends it to batches, channels and zero
+// padding:
+//   y[n,k,i,j]  = sum_c ( sum_{a,b} x[n,c,i*s+a-p, j*s+b-p] * w[k,c,a,b] ) + bias[k]
+//   dx[n,c,h,q] = sum_{k,a,b} dy[n,k,(h+p-a)/s,(q+p-b)/s] * w[k,c,a,b]
+//   dw[k,c,a,b] = sum_{n,i,j} dy[n,k,i,j] * x[n,c,i*s+a-p, j*s+b-p]
+//
+// Two paths.  The tensor-core path (conv_tc.cu) covers the 3x3 / pad 1 /
+// stride 1 shapes of the benchmark and the crater CNN.  Every other shape
+// runs the direct kernels below: one thread per output element, forward sums
+// in the reference's order (per-channel dot over taps, then over channels;
+// f32 ops rounded one by one), reverse sums in f64 like the reference's tape.
+#include <algorithm>
+
+#include "conv.cuh"
+
+namespace remora {
+
+namespace {
+
+__global__ void __launch_bounds__(256) conv_fwd_direct(const float *__restrict__ x, const float *__restrict__ w,
+                                                       const float *__restrict__ bias, float *__restrict__ y,
+                                                       ConvGeom g) {
+  const long long total = (long long)g.N * g.K * g.OH * g.OW;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
+    const int j = (int)(t % g.OW);
+    const int i = (int)((t / g.OW) % g.OH);
+    const int k = (int)((t / ((long long)g.OW * g.OH)) % g.K);
+    const long long n = t / ((long long)g.OW * g.OH * g.K);
+    float total_c = 0.0f;
+    for (int c = 0; c < g.C; ++c) {
+      float dot = 0.0f;
+      const float *xc = x + ((n * g.C + c) * g.H) * (long long)g.W;
+      const float *wk = w + ((long long)k * g.C + c) * g.R * g.S;
+      for (int a = 0; a < g.R; ++a) {
+        const int h = i * g.stride + a - g.pad;
+        for (int b = 0; b < g.S; ++b) {
+          const int q = j * g.stride + b - g.pad;
+          const float xv = (h >= 0 && h < g.H && q >= 0 && q < g.W) ? __ldg(xc + (long long)h * g.W + q) : 0.0f;
+          dot = __fadd_rn(dot, __fmul_rn(xv, __ldg(wk + a * g.S + b)));
+        }
+      }
+      total_c = __fadd_rn(total_c, dot);
+    }
+    if (bias) total_c = __fadd_rn(total_c, __ldg(bias + k));
+    y[t] = total_c;
+  }
+}
+
+__global__ void __launch_bounds__(256) conv_dgrad_direct(const float *__restrict__ dy, const float *__restrict__ w,
+                                                         float *__restrict__ dx, ConvGeom g) {
+  const long long total = (long long)g.N * g.C * g.H * g.W;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
+    const int q = (int)(t % g.W);
+    const int h = (int)((t / g.W) % g.H);
+    const int c = (int)((t / ((long long)g.W * g.H)) % g.C);
+    const long long n = t / ((long long)g.W * g.H * g.C);
+    double acc = 0.0;
+    for (int k = 0; k < g.K; ++k)
+      for (int a = 0; a < g.R; ++a) {
+        const int ti = h + g.pad - a;
+        if (ti < 0 || ti % g.stride) continue;
+        const int i = ti / g.stride;
+        if (i >= g.OH) continue;
+        for (int b = 0; b < g.S; ++b) {
+          const int tj = q + g.pad - b;
+          if (tj < 0 || tj % g.stride) continue;
+          const int j = tj / g.stride;
+          if (j >= g.OW) continue;
+          acc += (double)__ldg(dy + ((n * g.K + k) * g.OH + i) * (long long)g.OW + j) *
+                 (double)__ldg(w + (((long long)k * g.C + c) * g.R + a) * g.S + b);
+        }
+      }
+    dx[t] = (float)acc;
+  }
+}
+
+// One block per weight element; the block reduces over all (n, i, j) in f64
+// in a fixed order (deterministic).
+__global__ void __launch_bounds__(256) conv_wgrad_direct(const float *__restrict__ x, const float *__restrict__ dy,
+                                                         float *__restrict__ dw, ConvGeom g) {
+  __shared__ double sh[256];
+  const int widx = blockIdx.x;
+  const int b = widx % g.S, a = (widx / g.S) % g.R, c = (widx / (g.S * g.R)) % g.C, k = widx / (g.S * g.R * g.C);
+  const long long per_img = (long long)g.OH * g.OW;
+  const long long total = (long long)g.N * per_img;
+  double acc = 0.0;
+  for (long long t = threadIdx.x; t < total; t += blockDim.x) {
+    const long long n = t / per_img;
+    const int i = (int)((t % per_img) / g.OW), j = (int)(t % g.OW);
+    const int h = i * g.stride + a - g.pad, q = j * g.stride + b - g.pad;
+    if (h < 0 || h >= g.H || q < 0 || q >= g.W) continue;
+    acc += (double)__ldg(dy + ((n * g.K + k) * g.OH + i) * (long long)g.OW + j) *
+           (double)__ldg(x + ((n * g.C + c) * g.H + h) * (long long)g.W + q);
+  }
+  sh[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) dw[widx] = (float)sh[0];
+}
+
+int grid_for(long long n, int sm_count) {
+  return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count * 32));
+}
+
+int read_conv(const RemoraConvSpec *spec, const RemoraMemRef4 *xin, const RemoraMemRef4 *w, const RemoraMemRef4 *yout,
+              bool x_is_input, DescView *X, DescView *Wd, DescView *Y, ConvGeom *g) {
+  if (spec == nullptr) return fail(REMORA_ERR_ARG, "conv: null spec");
+  if (spec->stride < 1 || spec->pad < 0) return fail(REMORA_ERR_ARG, "conv: stride %d pad %d", spec->stride, spec->pad);
+  if (spec->precision != REMORA_PREC_TF32 && spec->precision != REMORA_PREC_3XTF32)
+    return fail(REMORA_ERR_ARG, "conv: unknown precision %d", spec->precision);
+  REMORA_TRY(read_desc(xin, 4, X, x_is_input ? "conv input" : "conv output gradient"));
+  REMORA_TRY(read_desc(w, 4, Wd, "conv weights"));
+  REMORA_TRY(read_desc(yout, 4, Y, "conv result"));
+  for (const DescView *d : {X, Wd, Y})
+    if (!d->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "conv: operands must be contiguous NCHW / KCRS");
+  g->stride = spec->stride;
+  g->pad = spec->pad;
+  g->K = (int)Wd->sizes[0];
+  g->C = (int)Wd->sizes[1];
+  g->R = (int)Wd->sizes[2];
+  g->S = (int)Wd->sizes[3];
+  return REMORA_OK;
+}
+
+int finish_geom(ConvGeom *g) {
+  if (g->H + 2 * g->pad < g->R || g->W + 2 * g->pad < g->S)
+    return fail(REMORA_ERR_SHAPE, "conv: kernel %dx%d larger than the padded %dx%d image", g->R, g->S, g->H, g->W);
+  g->OH = (g->H + 2 * g->pad - g->R) / g->stride + 1;
+  g->OW = (g->W + 2 * g->pad - g->S) / g->stride + 1;
+  return REMORA_OK;
+}
+
+}  // namespace
+}  // namespace remora
 
 using namespace remora;
 
@@ -9,23 +151,81 @@ extern "C" {
 int remora_b200_conv2d_fwd(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *x,
                            const RemoraMemRef4 *w, const RemoraMemRef1 *bias, RemoraMemRef4 *y,
                            remora_stream_t stream) {
-  (void)spec, (void)x, (void)w, (void)bias, (void)y, (void)stream;
   REMORA_TRY(check_ctx(ctx));
-  return fail(REMORA_ERR_UNSUPPORTED, "conv2d_fwd: not part of this build yet");
+  DescView X, Wd, Y, B;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, x, w, y, true, &X, &Wd, &Y, &g));
+  g.N = (int)X.sizes[0];
+  g.H = (int)X.sizes[2];
+  g.W = (int)X.sizes[3];
+  if (X.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv: input has %lld channels, weights %d", X.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (Y.sizes[0] != g.N || Y.sizes[1] != g.K || Y.sizes[2] != g.OH || Y.sizes[3] != g.OW)
+    return fail(REMORA_ERR_SHAPE, "conv: output must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
+  const float *bp = nullptr;
+  if (bias) {
+    REMORA_TRY(read_desc(bias, 1, &B, "conv bias"));
+    if (B.sizes[0] != g.K || (B.strides[0] != 1 && g.K > 1))
+      return fail(REMORA_ERR_SHAPE, "conv: bias must be a contiguous [%d]", g.K);
+    bp = (const float *)B.data(4);
+  }
+  if (Y.numel() == 0) return REMORA_OK;
+  bool handled = false;
+  REMORA_TRY(conv_tc_fwd(ctx, g, (const float *)X.data(4), (const float *)Wd.data(4), bp, (float *)Y.data(4),
+                         spec->precision, (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
+  conv_fwd_direct<<<grid_for(Y.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)X.data(4), (const float *)Wd.data(4), bp, (float *)Y.data(4), g);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
 }
 
 int remora_b200_conv2d_dgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *dy,
                              const RemoraMemRef4 *w, RemoraMemRef4 *dx, remora_stream_t stream) {
-  (void)spec, (void)dy, (void)w, (void)dx, (void)stream;
   REMORA_TRY(check_ctx(ctx));
-  return fail(REMORA_ERR_UNSUPPORTED, "conv2d_dgrad: not part of this build yet");
+  DescView DY, Wd, DX;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, dy, w, dx, false, &DY, &Wd, &DX, &g));
+  g.N = (int)DX.sizes[0];
+  g.H = (int)DX.sizes[2];
+  g.W = (int)DX.sizes[3];
+  if (DX.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv dgrad: dx has %lld channels, weights %d", DX.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (DY.sizes[0] != g.N || DY.sizes[1] != g.K || DY.sizes[2] != g.OH || DY.sizes[3] != g.OW)
+    return fail(REMORA_ERR_SHAPE, "conv dgrad: dy must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
+  if (DX.numel() == 0) return REMORA_OK;
+  bool handled = false;
+  REMORA_TRY(conv_tc_dgrad(ctx, g, (const float *)DY.data(4), (const float *)Wd.data(4), (float *)DX.data(4),
+                           spec->precision, (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
+  conv_dgrad_direct<<<grid_for(DX.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)DY.data(4), (const float *)Wd.data(4), (float *)DX.data(4), g);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
 }
 
 int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *x,
                              const RemoraMemRef4 *dy, RemoraMemRef4 *dw, remora_stream_t stream) {
-  (void)spec, (void)x, (void)dy, (void)dw, (void)stream;
   REMORA_TRY(check_ctx(ctx));
-  return fail(REMORA_ERR_UNSUPPORTED, "conv2d_wgrad: not part of this build yet");
+  DescView X, DY, DW;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, x, dw, dy, true, &X, &DW, &DY, &g));
+  g.N = (int)X.sizes[0];
+  g.H = (int)X.sizes[2];
+  g.W = (int)X.sizes[3];
+  if (X.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv wgrad: x has %lld channels, dw %d", X.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (DY.sizes[0] != g.N || DY.sizes[1] != g.K || DY.sizes[2] != g.OH || DY.sizes[3] != g.OW)
+    return fail(REMORA_ERR_SHAPE, "conv wgrad: dy must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
+  if (DW.numel() == 0) return REMORA_OK;
+  bool handled = false;
+  REMORA_TRY(conv_tc_wgrad(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
+                           spec->precision, (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
+  conv_wgrad_direct<<<(unsigned)DW.numel(), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), g);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,21 @@
+// conv.cuh — convolution geometry shared by the direct and tensor-core paths.
+#pragma once
+
+#include "common.cuh"
+
+namespace remora {
+
+struct ConvGeom {
+  int N, C, H, W, K, R, S, OH, OW, stride, pad;
+};
+
+// Tensor-core paths: set *handled = false (and do nothing) for shapes they do
+// not cover; the caller then runs the direct kernels.
+int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *w, const float *bias,
+                float *y, int precision, cudaStream_t stream, bool *handled);
+int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const float *w, float *dx,
+                  int precision, cudaStream_t stream, bool *handled);
+int conv_tc_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw,
+                  int precision, cudaStream_t stream, bool *handled);
+
+}  // namespace remora

@@ -12,7 +12,8 @@
 //   warp 2         TMEM allocator
 //   warps 4-7      epilogue: tcgen05.ld 32 lanes x 32 columns, 128-byte
 //                  row segments straight to global memory
-// Operands may be K-major or M/N-major (both are native UMMA layouts).
+// Operands may be K-major (SWIZZLE_128B tiles) or M/N-major
+// (SWIZZLE_128B_BASE32B tiles); both are native UMMA layouts.
 // 3xTF32: A and B are split into hi = tf32(x) (low 13 mantissa bits
 // cleared) and lo = x - hi (exact) by a prep pass; the MMA issues
 // hi*hi + hi*lo + lo*hi per K step into the same f32 accumulator.
@@ -60,8 +61,9 @@ __device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *b
   }
 }
 
+// MN-major tiles are 32-row boxes of 32 elements (4 KB) side by side.
 __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int mn, int kk) {
-  return mn ? tc::smem_desc_sw128(saddr + kk * 1024, 4096, 1024) : tc::smem_desc_sw128(saddr + kk * 32, 16, 1024);
+  return mn ? tc::desc_mnmajor(saddr, 4096, kk) : tc::desc_kmajor(saddr, kk);
 }
 
 __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, int &mb, int &nb) {
@@ -314,8 +316,11 @@ int encode_operand(const Operand &o, int box_rows, int batch, CUtensorMap *map) 
   box[2] = 1;
   strides[0] = (cuuint64_t)o.ld * 4;
   strides[1] = (cuuint64_t)(batch > 1 ? o.bs : o.ld * (long long)dims[1]) * 4;
+  // K-major tiles use the 16-byte-unit 128B swizzle, MN-major tiles the
+  // 32-byte-unit one (the only MN-major layout tf32 MMAs accept).
+  const CUtensorMapSwizzle swz = o.mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(o.base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(REMORA_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu", (int)r,

@@ -62,7 +62,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort_flag = 1;
-      atomicExch(err, code);
+      atomicCAS(err, 0, code);  // keep the first wait that ran out
       return false;
     }
   }
@@ -137,19 +137,39 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------- shared-memory descriptors
-// SWIZZLE_128B operand tiles.  K-major: rows of 128 B (32 f32 along K), 8-row
-// groups 1024 B apart (SBO); one MMA (K = 8 tf32 = 32 B) starts 32 B further
-// per K step.  MN-major: 32 f32 along M/N per 128-B row, 8 K-rows per 1024-B
-// group (SBO), 32-element M/N chunks 4096 B apart (LBO, a 32x32 box each);
-// one MMA starts 1024 B further per K step.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Operand tiles in shared memory, as the UMMA canonical layouts for 32-bit
+// (tf32) elements:
+//  K-major, SWIZZLE_128B (layout type 2): rows of 128 B (32 f32 along K),
+//    16-byte units XOR-swizzled with the row index mod 8, 8-row groups 1024 B
+//    apart (SBO).  One MMA (K = 8 tf32 = 32 B) starts 32 B further per step.
+//  MN-major, SWIZZLE_128B_BASE32B (layout type 1; the only MN-major layout
+//    tf32 has): rows of 128 B (32 f32 along M/N) per K index, 32-byte units
+//    XOR-swizzled with the row index mod 4, 4-row K groups 512 B apart (SBO),
+//    32-element M/N chunks LBO apart.  One MMA (K = 8) starts 1024 B further
+//    per step.  TMA writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  d |= (uint64_t)layout << 61;
   return d;
+}
+
+// K-major SW128 operand, K step kk (8 tf32 each).
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr, int kk) {
+  return smem_desc(saddr + kk * 32, 16, 1024, kLayoutSW128);
+}
+
+// MN-major SW128_BASE32B operand with M/N chunks `chunk_stride` bytes apart,
+// K step kk (8 tf32 = two 4-row groups).
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr, uint32_t chunk_stride, int kk) {
+  return smem_desc(saddr + kk * 1024, chunk_stride, 512, kLayoutSW128Base32B);
 }
 
 // Instruction descriptor: kind::tf32, f32 accumulator, M x N, operand majors.

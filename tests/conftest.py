@@ -57,4 +57,9 @@ def to_dev(a: np.ndarray, device):
 
 
 def to_host(t) -> np.ndarray:
+    """Device-to-host copy after surfacing any device-side wait that ran out
+    (remora_b200_synchronize raises RemoraTimeoutError)."""
+    from remora_b200 import ops
+
+    ops.synchronize(t.device.index)
     return t.detach().cpu().numpy()

@@ -1,8 +1,10 @@
 """GPU parity of the tcgen05 dense core (matmul as the lifted dot).
 
-Tolerances (north_star): TF32 rtol 1e-3 + atol 1e-3 * max|ref|; 3xTF32 is
-held to f32-level agreement, atol 2e-5 * max|ref| + rtol 1e-5, against the
-oracle's sequential-k f32 lifted dot."""
+Every result is checked against the oracle's sequential-k f32 lifted dot at
+the north_star tolerance for TF32 GEMMs (rtol 1e-3 + atol 1e-3 * max|ref|).
+3xTF32 is also held to the exact (f64) product at rtol 1e-5 + atol
+1e-5 * max|ref|: at K = 4096 it is closer to the exact product than the
+sequential f32 order itself."""
 
 from __future__ import annotations
 
@@ -15,20 +17,24 @@ from remora_b200 import ops
 pytestmark = pytest.mark.gpu
 
 
-def check(got, ref, precision):
+def check(got, ref, precision, exact=None):
     ref = np.asarray(ref, dtype=np.float64)
     scale = max(1.0, float(np.abs(ref).max()) if ref.size else 1.0)
-    if precision == "tf32":
-        np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-3 * scale)
-    else:
-        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=2e-5 * scale)
+    np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-3 * scale)
+    if precision == "3xtf32" and exact is not None:
+        np.testing.assert_allclose(got, exact, rtol=1e-5, atol=1e-5 * scale)
+
+
+def exact(a, b):
+    return np.matmul(a.astype(np.float64), b.astype(np.float64))
 
 
 def test_golden_lifted_matmul(cuda):
     g = golden("lifted_matmul")
     a, bt = to_dev(g["a"], cuda), to_dev(g["bt"], cuda)
     for prec in ("3xtf32", "tf32"):
-        check(to_host(ops.gemm(a, bt.t(), precision=prec)), g["out"], prec)
+        check(to_host(ops.gemm(a, bt.t(), precision=prec)), g["out"], prec,
+              exact(g["a"], np.ascontiguousarray(g["bt"].T)))
 
 
 @pytest.mark.parametrize("mnk", [(128, 256, 32), (128, 256, 256), (256, 512, 128), (100, 200, 40), (129, 257, 36),
@@ -40,7 +46,7 @@ def test_gemm_shapes(cuda, oracle_mod, mnk, prec):
     a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
     got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec))
-    check(got, oracle_mod.matmul(a, b), prec)
+    check(got, oracle_mod.matmul(a, b), prec, exact(a, b))
 
 
 @pytest.mark.parametrize("layout", ["kk", "km", "mk", "mm"])
@@ -54,7 +60,7 @@ def test_gemm_operand_majors(cuda, oracle_mod, layout):
     ta = to_dev(a, cuda) if layout[0] == "k" else to_dev(a.T.copy(), cuda).t()
     tb = to_dev(b.T.copy(), cuda).t() if layout[1] == "k" else to_dev(b, cuda)
     got = to_host(ops.gemm(ta, tb, precision="3xtf32"))
-    check(got, oracle_mod.matmul(a, b), "3xtf32")
+    check(got, oracle_mod.matmul(a, b), "3xtf32", exact(a, b))
 
 
 def test_gemm_batched_and_views(cuda, oracle_mod):
@@ -62,7 +68,8 @@ def test_gemm_batched_and_views(cuda, oracle_mod):
     a = rng.uniform(-1, 1, (3, 130, 68)).astype(np.float32)
     b = rng.uniform(-1, 1, (3, 68, 260)).astype(np.float32)
     for prec in ("3xtf32", "tf32"):
-        check(to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec)), oracle_mod.matmul(a, b), prec)
+        check(to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec)), oracle_mod.matmul(a, b), prec,
+              exact(a, b))
     # strided sub-views and an output view with a row stride
     import torch
 
@@ -70,8 +77,8 @@ def test_gemm_batched_and_views(cuda, oracle_mod):
     av, bv = big[10:138, 4:100], big[100:196, 20:276]
     out = torch.zeros((200, 400), dtype=torch.float32, device=cuda)
     ops.gemm(av, bv, precision="3xtf32", out=out[3:131, 7:263])
-    ref = oracle_mod.matmul(to_host(av).copy(), to_host(bv).copy())
-    check(to_host(out[3:131, 7:263]), ref, "3xtf32")
+    ha, hb = to_host(av).copy(), to_host(bv).copy()
+    check(to_host(out[3:131, 7:263]), oracle_mod.matmul(ha, hb), "3xtf32", exact(ha, hb))
     assert float(out[:3].abs().sum()) == 0.0 and float(out[:, :7].abs().sum()) == 0.0
 
 
@@ -97,7 +104,7 @@ def test_gemm_4096_sampled_rows(cuda, oracle_mod, prec):
     got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec))
     rows = np.random.default_rng(0).choice(4096, 48, replace=False)
     ref = oracle_mod.matmul(a[rows], b, nthreads=oracle_mod.max_threads())
-    check(got[rows], ref, prec)
+    check(got[rows], ref, prec, exact(a[rows], b))
     assert np.isfinite(got).all()
 
 
@@ -109,4 +116,5 @@ def test_gemm_batched_full_sampled(cuda, oracle_mod):
     got = to_host(ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision="3xtf32"))
     for bi in (0, 17, 31):
         rows = np.arange(bi * 13 % 1000, bi * 13 % 1000 + 24)
-        check(got[bi, rows], oracle_mod.matmul(a[bi, rows], b[bi], nthreads=oracle_mod.max_threads()), "3xtf32")
+        check(got[bi, rows], oracle_mod.matmul(a[bi, rows], b[bi], nthreads=oracle_mod.max_threads()), "3xtf32",
+              exact(a[bi, rows], b[bi]))
