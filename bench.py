@@ -11,7 +11,10 @@ call streams from HBM).
 
 Other configs: ``row_norms`` (f32[8192,1024] -> sqrt(sum x*x)), ``matmul``
 (A,B f32[4096,4096], TF32; ``matmul_3x`` the 3xTF32 form), ``bmm``
-([32,1024,1024] x [32,1024,1024], TF32).
+([32,1024,1024] x [32,1024,1024], TF32), ``conv`` / ``conv_dgrad`` /
+``conv_wgrad`` (x [256,16,64,64] * w [32,16,3,3], pad 1), ``cnn`` (crater-CNN
+SGD step, global batch 4096, data parallel over N ranks with an NCCL
+gradient allreduce: strong scaling; 3xTF32, ``cnn_tf32`` the TF32 form).
 
 With N GPUs (torchrun, one process per GPU) every rank runs its own copy of
 the workload (weak scaling: folds shard frames, matmuls shard rows; no
@@ -341,9 +344,211 @@ class MatmulWorkload:
                 "sequential f32 k order, OpenMP over rows)")
 
 
+class ConvWorkload:
+    """The im2col-conv layer x [256,16,64,64] * w [32,16,3,3], pad 1, stride 1:
+    forward (``conv``), input gradient (``conv_dgrad``) and weight gradient
+    (``conv_wgrad``) from a seeded N(0,1) cotangent.  Metric TFLOP/s; the
+    layer is HBM-bound (about 48 flop/B), so the roofline is HBM GB/s of
+    algorithmic bytes."""
+
+    metric, unit = METRIC_MM, "TFLOP/s"
+    bound = "hbm"
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.kind = {"conv": "fwd", "conv_dgrad": "dgrad", "conv_wgrad": "wgrad"}[name]
+        self.N, self.C, self.H, self.W, self.K = 256, 16, 64, 64, 32
+        self.work_per_call = 2.0 * self.N * self.H * self.W * self.K * self.C * 9  # 9,663,676,416 flop
+        x_b = 4 * self.N * self.C * self.H * self.W
+        y_b = 4 * self.N * self.K * self.H * self.W
+        w_b = 4 * self.K * self.C * 9
+        self.bytes_per_call = x_b + y_b + w_b  # each direction reads two of x/y/w and writes the third
+        self.rotate = 1
+        self.launches_per_call = 1
+        self.precision = "tf32"
+        self.desc = (f"conv2d {self.kind} x[256,16,64,64] ~ N(0,1) * w[32,16,3,3] ~ N(0,sqrt(2/144)), pad 1, "
+                     "TF32 tcgen05 implicit GEMM" if self.kind != "wgrad" else
+                     "conv2d wgrad x[256,16,64,64], dy[256,32,64,64] ~ N(0,1) -> dw[32,16,3,3]")
+
+    def make_inputs(self, seed: int):
+        rx = np.random.Generator(np.random.PCG64(seed))
+        x = rx.standard_normal((self.N, self.C, self.H, self.W), dtype=np.float32)
+        w = (np.random.Generator(np.random.PCG64(2718)).standard_normal((self.K, self.C, 3, 3))
+             * np.sqrt(2 / 144)).astype(np.float32)
+        dy = np.random.Generator(np.random.PCG64(seed + 2)).standard_normal((self.N, self.K, self.H, self.W),
+                                                                            dtype=np.float32)
+        return x, w, dy
+
+    def setup(self, dev, rank: int) -> None:
+        import torch
+
+        from remora_b200 import _lib as L
+        from remora_b200.abi import tensor_descriptor
+        from remora_b200.runtime import context
+
+        self.torch, self.L, self.lib, self.dev = torch, L, L.lib(), dev
+        self.hx, self.hw, self.hdy = self.make_inputs(1729 + 1000 * rank)
+        self.x, self.w, self.dy = (torch.from_numpy(a).to(dev) for a in (self.hx, self.hw, self.hdy))
+        self.y = torch.empty_like(self.dy)
+        self.dx = torch.empty_like(self.x)
+        self.dw = torch.empty_like(self.w)
+        self.d = {k: tensor_descriptor(getattr(self, k)) for k in ("x", "w", "dy", "y", "dx", "dw")}
+        self._spec = L.RemoraConvSpec(1, 1, L.PREC_TF32, 0)
+        self.sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        self.ctx = context(dev.index)
+
+    def call(self, k: int) -> None:
+        a = lambda n: ctypes.addressof(self.d[n])  # noqa: E731
+        lib, c, s = self.lib, self.ctx.ptr, ctypes.byref(self._spec)
+        if self.kind == "fwd":
+            st = lib.remora_b200_conv2d_fwd(c, s, a("x"), a("w"), None, a("y"), self.sptr)
+        elif self.kind == "dgrad":
+            st = lib.remora_b200_conv2d_dgrad(c, s, a("dy"), a("w"), a("dx"), self.sptr)
+        else:
+            st = lib.remora_b200_conv2d_wgrad(c, s, a("x"), a("dy"), a("dw"), self.sptr)
+        if st:
+            self.L.check(st, "conv")
+
+    def check(self) -> None:
+        torch = self.torch
+        self.call(0)
+        torch.cuda.synchronize()
+        import torch.nn.functional as F
+
+        x64, w64, dy64 = self.x[:2].double(), self.w.double(), self.dy[:2].double()
+        if self.kind == "fwd":
+            got, ref = self.y[:2].double(), F.conv2d(x64, w64, padding=1)
+        elif self.kind == "dgrad":
+            got, ref = self.dx[:2].double(), F.conv_transpose2d(dy64, w64, padding=1)
+        else:
+            got = self.dw.double()
+            ref = torch.nn.grad.conv2d_weight(self.x.double(), self.w.shape, self.dy.double(), padding=1)
+        err = float((got - ref).abs().max()) / max(1.0, float(ref.abs().max()))
+        if not err <= 1e-3:
+            raise SystemExit(f"benchmark output does not match the check (scaled error {err:.3g})")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        torch = self.torch
+        ins = {"fwd": ("x", "w"), "dgrad": ("dy", "w"), "wgrad": ("x", "dy")}[self.kind]
+        outn = {"fwd": "y", "dgrad": "dx", "wgrad": "dw"}[self.kind]
+        self.pin_in = [(getattr(self, n), torch.from_numpy(getattr(self, "h" + n)).pin_memory()) for n in ins]
+        self.pin_out = (getattr(self, outn), torch.empty(getattr(self, outn).shape).pin_memory())
+        return sum(p.numel() * 4 for _, p in self.pin_in), self.pin_out[1].numel() * 4
+
+    def e2e_step(self) -> None:
+        L, lib, c = self.L, self.lib, self.ctx.ptr
+        for dev_t, pin in self.pin_in:
+            L.check(lib.remora_b200_memcpy_h2d(c, ctypes.c_void_p(dev_t.data_ptr()), ctypes.c_void_p(pin.data_ptr()),
+                                               pin.numel() * 4, self.sptr))
+        self.call(0)
+        dev_t, pin = self.pin_out
+        L.check(lib.remora_b200_memcpy_d2h(c, ctypes.c_void_p(pin.data_ptr()), ctypes.c_void_p(dev_t.data_ptr()),
+                                           pin.numel() * 4, self.sptr))
+
+    def cpu_prepare(self) -> None:
+        self.cx, self.cw, self.cdy = self.make_inputs(1729)
+        self.nt = _oracle().max_threads()
+
+    def cpu_step(self) -> float:
+        o = _oracle()
+        if self.kind == "fwd":
+            o.conv2d_fwd(self.cx[:1], self.cw, None, nthreads=self.nt)
+        elif self.kind == "dgrad":
+            o.conv2d_dgrad(self.cdy[:1], self.cw, (1, self.C, self.H, self.W), nthreads=self.nt)
+        else:
+            o.conv2d_wgrad(self.cx[:1], self.cdy[:1], self.cw.shape, nthreads=self.nt)
+        return self.work_per_call / self.N
+
+    cpu_sample = "one image of the batch per sample (oracle conv in the reference's order, OpenMP over channels)"
+
+
+class CnnWorkload:
+    """One SGD step of the crater CNN on a global batch of 4096 synthetic
+    64x64 images (data parallel: each of N ranks takes 4096/N, one NCCL
+    allreduce of the 529,217-float gradient per step).  Metric samples/s of
+    the whole job; the step is one CUDA graph."""
+
+    metric, unit, bound = "CNN train samples/s", "samples/s", "tensor"
+    scaling = "strong"
+    GLOBAL = 4096
+    FLOPS_PER_SAMPLE = 33.8e6  # forward + backward, all layers
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.rotate = 1
+        self.precision = "tf32" if name == "cnn_tf32" else "3xtf32"
+        self.desc = (f"crater CNN train step ({self.precision}), global batch 4096 of 64x64 synthetic images (noise 0.1, 1-3 rims r 4-16 "
+                     "on positives, 50/50): conv3x3 1->16+ReLU, pool, conv3x3 16->32+ReLU, pool, dense 8192->64+ReLU, "
+                     "dense 64->1, sigmoid BCE, SGD lr 0.01")
+
+    def setup(self, dev, rank: int) -> None:
+        import torch
+
+        from remora_b200 import crater
+        from remora_b200.cnn import CraterCNN
+
+        from remora_b200.cnn import process_group_allreduce, shard
+
+        world = getattr(self, "world", 1)
+        self.torch, self.dev = torch, dev
+        lo, hi = shard(self.GLOBAL, world, rank)
+        self.B = hi - lo
+        self.work_per_call = float(self.B)  # samples per rank per step; x world in the harness
+        self.himg, self.hlab = crater.make_batch(self.B, start=lo)
+        self.x = torch.from_numpy(self.himg).to(dev)
+        self.y = torch.from_numpy(self.hlab).to(dev)
+        allreduce = process_group_allreduce() if world > 1 else None
+        self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision)
+        self.net.step(self.x, self.y)  # eager step: compiles map programs, sizes workspaces
+        self.net.capture(self.x, self.y)
+        self.launches_per_call = 16
+
+    def call(self, k: int) -> None:
+        self.net.replay()
+
+    def close(self) -> None:
+        self.net.graph = None
+        self.torch.cuda.synchronize()
+
+    def check(self) -> None:
+        self.torch.cuda.synchronize()
+        if not bool(self.torch.isfinite(self.net.params).all()):
+            raise SystemExit("non-finite parameters after the warm-up steps")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        torch = self.torch
+        self.pin_x = torch.from_numpy(self.himg).pin_memory()
+        self.pin_y = torch.from_numpy(self.hlab).pin_memory()
+        self.pin_loss = torch.empty(self.B, dtype=torch.float32).pin_memory()
+        return (self.pin_x.numel() + self.pin_y.numel()) * 4, 4
+
+    def e2e_step(self) -> None:
+        self.x.copy_(self.pin_x, non_blocking=True)
+        self.y.copy_(self.pin_y, non_blocking=True)
+        self.net.replay()
+        self.pin_loss[:1].copy_(self.net.loss_b[:1], non_blocking=True)  # the step's result read back
+
+    def cpu_prepare(self) -> None:
+        from remora_b200 import crater
+
+        self.cparams = crater.init_params()
+        self.cimg, self.clab = crater.make_batch(32)
+        self.nt = _oracle().max_threads()
+
+    def cpu_step(self) -> float:
+        _oracle().cnn_step(self.cparams, self.cimg, self.clab, batch_total=32, nthreads=self.nt)
+        return 32.0
+
+    cpu_sample = "32 samples per SGD step (oracle CNN step: forward, backward, update; OpenMP over images)"
+
+
 def make_workload(name: str):
     if name in ("chained", "row_norms"):
         return FoldWorkload(name)
+    if name in ("cnn", "cnn_tf32"):
+        return CnnWorkload(name)
+    if name.startswith("conv"):
+        return ConvWorkload(name)
     return MatmulWorkload(name)
 
 
@@ -369,6 +574,7 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     wl = make_workload(args.config)
+    wl.world = world
     wl.setup(dev, rank)
     wl.check()
     stream = torch.cuda.current_stream(dev)
@@ -408,6 +614,8 @@ def run_ours(args) -> None:
     clocks = sampler.stop() if sampler else None
     if args.profile:
         if world > 1:
+            getattr(wl, "close", lambda: None)()
+            dist.barrier()
             dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"profile_run": args.config, "ms": ms, "steps": args.steps}), flush=True)
@@ -437,12 +645,22 @@ def run_ours(args) -> None:
 
     if rank == 0:
         peaks = measured_peaks()
-        scale = 1e9 if wl.unit == "GB/s" else 1e12
+        scale = {"GB/s": 1e9, "TFLOP/s": 1e12, "samples/s": 1.0}[wl.unit]
         calls = args.steps * wl.rotate
         value = wl.work_per_call * calls * world / (ms * 1e-3) / scale
         per_call_ms = float(np.mean(step_ms)) / wl.rotate
-        achieved = wl.work_per_call / (per_call_ms * 1e-3) / scale
-        peak = peaks["hbm_gbs"] if wl.bound == "hbm" else tf32_peak(peaks)
+        # roofline of the dominant kernel: algorithmic bytes for HBM-bound
+        # work, algorithmic flops for tensor-bound work
+        if wl.unit == "samples/s":
+            # the whole step against the dense TF32 rate: model flops per step
+            roof_unit, peak = "TFLOP/s", tf32_peak(peaks)
+            achieved = wl.work_per_call * wl.FLOPS_PER_SAMPLE / (per_call_ms * 1e-3) / 1e12
+        elif wl.bound == "hbm":
+            roof_unit, peak = "GB/s", peaks["hbm_gbs"]
+            achieved = getattr(wl, "bytes_per_call", wl.work_per_call) / (per_call_ms * 1e-3) / 1e9
+        else:
+            roof_unit, peak = "TFLOP/s", tf32_peak(peaks)
+            achieved = wl.work_per_call / (per_call_ms * 1e-3) / 1e12
         e2e_value = wl.work_per_call * e2e_steps * world / (e2e_ms * 1e-3) / scale
         line = {
             "metric": wl.metric,
@@ -453,15 +671,16 @@ def run_ours(args) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None,
-            "dtype": "f32" if wl.bound == "hbm" else f"f32 storage, {getattr(wl, 'precision', 'tf32')} tensor math",
+            "dtype": "f32" if not hasattr(wl, "precision") else f"f32 storage, {wl.precision} tensor math",
             "data": "synthetic (seeded PCG64)",
             "config": {"workload": wl.desc, "calls_per_step": wl.rotate,
                        "l2": (f"{wl.rotate} rotating inputs, {wl.rotate * wl.work_per_call / 1e6:.0f} MB > 126 MB L2"
-                              if wl.bound == "hbm" else "operands 192 MB > 126 MB L2"),
-                       "parallelism": f"replicas x{world} (independent shards, no collective)"},
-            "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": wl.unit,
+                              if wl.unit == "GB/s" else "operands larger than the 126 MB L2"),
+                       "parallelism": (f"dp{world} (NCCL gradient allreduce)" if wl.unit == "samples/s" else
+                                       f"replicas x{world} (independent shards, no collective)")},
+            "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": roof_unit,
                          "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
                          "peak_source": peaks["source"] + (" (bf16 / 2)" if wl.bound == "tensor" else "")},
             "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": h2d,
@@ -473,13 +692,16 @@ def run_ours(args) -> None:
             line["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
+        getattr(wl, "close", lambda: None)()  # graphs holding NCCL calls go before the process group
+        dist.barrier()
         dist.destroy_process_group()
 
 
 # Per-call DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernel, from the ncu captures summarised under profiles/.
-TRAFFIC: dict[str, float | None] = {"chained": 67_129_856 + 563_200, "row_norms": None, "matmul": None,
-                                    "matmul_3x": None, "bmm": None}
+TRAFFIC: dict[str, float | None] = {"chained": 67_129_856 + 563_200, "row_norms": None,
+                                    "matmul": 337_164_032 + 62_405_376, "matmul_3x": None, "bmm": None, "conv": None,
+                                    "conv_dgrad": None, "conv_wgrad": None, "cnn": None, "cnn_tf32": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
@@ -496,7 +718,7 @@ def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
-    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    scale = {"GB/s": 1e9, "TFLOP/s": 1e12, "samples/s": 1.0}[wl.unit]
     return {"value": round(work / el / scale, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
             "sample": f"{wl.cpu_sample}; {reps} samples in {el:.1f} s"}
 
@@ -514,12 +736,13 @@ def run_reference(args) -> None:
     for _ in range(args.steps):
         work += wl.cpu_step()
     el = time.perf_counter() - t0
-    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    scale = {"GB/s": 1e9, "TFLOP/s": 1e12, "samples/s": 1.0}[wl.unit]
     value = work / el / scale
     line = {
         "metric": wl.metric, "value": round(value, 5), "unit": wl.unit,
         "n_gpus": int(os.environ.get("WORLD_SIZE", 1)), "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(el * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded PCG64)", "impl": "reference",
         "config": {"workload": wl.desc, "calls_per_step": 1},
         "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
@@ -529,7 +752,7 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm"]
+CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm", "conv", "conv_dgrad", "conv_wgrad", "cnn", "cnn_tf32"]
 
 
 def main() -> None:

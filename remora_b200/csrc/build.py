@@ -48,7 +48,7 @@ def _host_compiler() -> list[str]:
 def _needs_rebuild(obj: Path, src: Path) -> bool:
     if not obj.exists():
         return True
-    deps = [src, *HERE.glob("*.cuh"), ROOT / "include" / "remora_b200.h"]
+    deps = [src, *HERE.glob("*.cuh"), *(ROOT / "include").glob("*.h")]
     return any(d.stat().st_mtime > obj.stat().st_mtime for d in deps if d.exists())
 
 

@@ -1,0 +1,410 @@
+// cnn.cu — fused kernels of the crater-CNN training step.
+//
+// The model (conv3x3 1->16 + ReLU, 2x2 max-pool, conv3x3 16->32 + ReLU,
+// 2x2 max-pool, dense 8192->64 + ReLU, dense 64->1, sigmoid BCE, SGD) is built
+// from the reference's formulas: ReLU as select(v > 0, v, 0) and the stable
+// BCE (examples/crater_train.py:46-54), the update p - lr * g
+// (examples/crater_train.py:249-253), and the VJPs of remora/ad.py:85-179
+// (select routes the adjoint to the taken branch, fold broadcasts it, mul
+// multiplies by the other operand).  Max-pool, batch-mean BCE and
+// multi-channel convolution have no reference counterpart.
+//
+// ReLU and max-pool commute (max of ReLUs = ReLU of the max), so every
+// pooled output keeps one byte: the index (0..3, window order (0,0) (0,1)
+// (1,0) (1,1), first maximum wins) of the element that receives its
+// gradient, or 255 when the maximum is not positive and no gradient flows.
+// The conv1 activation (B x 16 x 64 x 64) is never written to HBM: the
+// forward kernel pools it at once and the weight gradient of conv1 is
+// accumulated straight from the pooled gradient.
+#include <algorithm>
+
+#include "../../include/remora_b200_cnn.h"
+#include "common.cuh"
+
+namespace remora {
+
+namespace {
+
+constexpr uint8_t kNoGrad = 255;
+
+__device__ __forceinline__ void pool4(float v0, float v1, float v2, float v3, float *out, uint8_t *code) {
+  float m = v0;
+  int idx = 0;
+  if (v1 > m) m = v1, idx = 1;
+  if (v2 > m) m = v2, idx = 2;
+  if (v3 > m) m = v3, idx = 3;
+  *out = m > 0.0f ? m : 0.0f;
+  *code = m > 0.0f ? (uint8_t)idx : kNoGrad;
+}
+
+// conv3x3 (1 input channel, pad 1) + bias + ReLU + 2x2 max-pool.  One thread
+// per pooled output; each conv output is the oracle's dot over taps in order
+// (f32 ops rounded one by one), then + bias.
+__global__ void __launch_bounds__(256) conv1_relu_pool_kernel(const float *__restrict__ x,
+                                                              const float *__restrict__ w,
+                                                              const float *__restrict__ bias,
+                                                              float *__restrict__ p, uint8_t *__restrict__ code,
+                                                              int B, int K, int H, int W) {
+  const int OH = H / 2, OW = W / 2;
+  const long long total = (long long)B * K * OH * OW;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
+    const int j = (int)(t % OW), i = (int)((t / OW) % OH);
+    const int k = (int)((t / ((long long)OW * OH)) % K);
+    const long long b = t / ((long long)OW * OH * K);
+    const float *xb = x + b * (long long)H * W;
+    float patch[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int h = 2 * i + a - 1, q = 2 * j + c - 1;
+        patch[a][c] = (h >= 0 && h < H && q >= 0 && q < W) ? __ldg(xb + h * W + q) : 0.0f;
+      }
+    float wk[9];
+#pragma unroll
+    for (int u = 0; u < 9; ++u) wk[u] = __ldg(w + k * 9 + u);
+    const float bk = __ldg(bias + k);
+    float v[4];
+#pragma unroll
+    for (int di = 0; di < 2; ++di)
+#pragma unroll
+      for (int dj = 0; dj < 2; ++dj) {
+        float dot = 0.0f;
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+          for (int c = 0; c < 3; ++c) dot = __fadd_rn(dot, __fmul_rn(patch[di + a][dj + c], wk[a * 3 + c]));
+        v[di * 2 + dj] = __fadd_rn(__fadd_rn(0.0f, dot), bk);
+      }
+    pool4(v[0], v[1], v[2], v[3], p + t, code + t);
+  }
+}
+
+// ReLU + 2x2 max-pool of an NCHW tensor (the conv2 activation, bias added).
+__global__ void __launch_bounds__(256) relu_pool_kernel(const float *__restrict__ a, float *__restrict__ p,
+                                                        uint8_t *__restrict__ code, long long planes, int H, int W) {
+  const int OH = H / 2, OW = W / 2;
+  const long long total = planes * OH * OW;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
+    const int j = (int)(t % OW), i = (int)((t / OW) % OH);
+    const long long pl = t / ((long long)OW * OH);
+    const float *ap = a + (pl * H + 2 * i) * W + 2 * j;
+    const float2 r0 = *reinterpret_cast<const float2 *>(ap);
+    const float2 r1 = *reinterpret_cast<const float2 *>(ap + W);
+    pool4(r0.x, r0.y, r1.x, r1.y, p + t, code + t);
+  }
+}
+
+// Adjoint of ReLU + max-pool: the pooled gradient goes to the recorded
+// element, every other element of the window gets 0.
+__global__ void __launch_bounds__(256) unpool_kernel(const float *__restrict__ dp, const uint8_t *__restrict__ code,
+                                                     float *__restrict__ da, long long planes, int H, int W) {
+  const int OH = H / 2, OW = W / 2;
+  const long long total = planes * OH * OW;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
+    const int j = (int)(t % OW), i = (int)((t / OW) % OH);
+    const long long pl = t / ((long long)OW * OH);
+    const uint8_t c = code[t];
+    const float g = dp[t];
+    float2 r0 = make_float2(0.f, 0.f), r1 = make_float2(0.f, 0.f);
+    if (c == 0) r0.x = g;
+    else if (c == 1) r0.y = g;
+    else if (c == 2) r1.x = g;
+    else if (c == 3) r1.y = g;
+    float *ap = da + (pl * H + 2 * i) * W + 2 * j;
+    *reinterpret_cast<float2 *>(ap) = r0;
+    *reinterpret_cast<float2 *>(ap + W) = r1;
+  }
+}
+
+// Dense 64 -> 1 on the ReLU'd hidden layer, the stable BCE and its gradient.
+// One warp per sample.  loss[b] = bce(z, y); dz[b] = (sigmoid(z) - y) * inv.
+__global__ void __launch_bounds__(256) dense_bce_kernel(const float *__restrict__ h, const float *__restrict__ w4,
+                                                        const float *__restrict__ b4, const float *__restrict__ y,
+                                                        float *__restrict__ z_out, float *__restrict__ loss,
+                                                        float *__restrict__ dz, int B, int D, float inv) {
+  const int lane = threadIdx.x & 31;
+  const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long b = warp; b < B; b += nwarps) {
+    float acc = 0.0f;
+    for (int o = lane; o < D; o += 32) acc = __fadd_rn(acc, __fmul_rn(__ldg(w4 + o), h[b * D + o]));
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
+    if (lane == 0) {
+      const float z = __fadd_rn(acc, __ldg(b4));
+      const float yy = y[b];
+      const float pos = z > 0.0f ? z : 0.0f;
+      const float absz = z > 0.0f ? z : __fsub_rn(0.0f, z);
+      const float l = __fadd_rn(pos, __fadd_rn(__fmul_rn(-1.0f, __fmul_rn(z, yy)),
+                                               logf(__fadd_rn(1.0f, expf(__fsub_rn(0.0f, absz))))));
+      float s;
+      if (z > 0.0f) {
+        s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+      } else {
+        const float e = expf(z);
+        s = __fdiv_rn(e, __fadd_rn(1.0f, e));
+      }
+      z_out[b] = z;
+      loss[b] = l;
+      dz[b] = __fmul_rn(__fsub_rn(s, yy), inv);
+    }
+  }
+}
+
+// Backward of dense 64 -> 1 and the hidden ReLU.  Block o: dw4[o] =
+// sum_b dz[b] h[b,o] (fixed order), dh[b,o] = h[b,o] > 0 ? dz[b] w4[o] : 0;
+// block D (one extra) sums db4 = sum_b dz[b].
+__global__ void __launch_bounds__(256) dense_bwd_kernel(const float *__restrict__ h, const float *__restrict__ w4,
+                                                        const float *__restrict__ dz, float *__restrict__ dh,
+                                                        float *__restrict__ dw4, float *__restrict__ db4, int B,
+                                                        int D) {
+  __shared__ double sh[256];
+  const int o = blockIdx.x;
+  double acc = 0.0;
+  if (o < D) {
+    const float wo = __ldg(w4 + o);
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+      const float hv = h[(long long)b * D + o];
+      const float g = dz[b];
+      acc += (double)g * (double)hv;
+      dh[(long long)b * D + o] = hv > 0.0f ? __fmul_rn(g, wo) : 0.0f;
+    }
+  } else {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) acc += (double)dz[b];
+  }
+  sh[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (o < D) dw4[o] = (float)sh[0];
+    else *db4 = (float)sh[0];
+  }
+}
+
+// conv1 weight and bias gradients straight from the pooled gradient: each
+// pooled output with a recorded element (h, q) contributes
+// dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  Block
+// (k, slice) accumulates a slice of the batch into f64 partials
+// part[(k * slices + slice) * 10 + {0..8: taps, 9: bias}].
+__global__ void __launch_bounds__(256) conv1_wgrad_pool_kernel(const float *__restrict__ x,
+                                                               const float *__restrict__ dp,
+                                                               const uint8_t *__restrict__ code,
+                                                               double *__restrict__ part, int B, int K, int H, int W,
+                                                               int slices) {
+  __shared__ double sh[10][256];
+  const int k = blockIdx.x / slices, slice = blockIdx.x % slices;
+  const int OH = H / 2, OW = W / 2;
+  const long long per_img = (long long)OH * OW;
+  const int b0 = (int)((long long)B * slice / slices), b1 = (int)((long long)B * (slice + 1) / slices);
+  double acc[10];
+#pragma unroll
+  for (int u = 0; u < 10; ++u) acc[u] = 0.0;
+  const long long n = (long long)(b1 - b0) * per_img;
+  for (long long t = threadIdx.x; t < n; t += blockDim.x) {
+    const int b = b0 + (int)(t / per_img);
+    const long long pix = t % per_img;
+    const long long idx = ((long long)b * K + k) * per_img + pix;
+    const uint8_t c = code[idx];
+    if (c == kNoGrad) continue;
+    const double g = (double)dp[idx];
+    const int i = (int)(pix / OW), j = (int)(pix % OW);
+    const int h = 2 * i + (c >> 1), q = 2 * j + (c & 1);
+    const float *xb = x + (long long)b * H * W;
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+      for (int bb = 0; bb < 3; ++bb) {
+        const int hh = h + a - 1, qq = q + bb - 1;
+        if (hh >= 0 && hh < H && qq >= 0 && qq < W) acc[a * 3 + bb] += g * (double)__ldg(xb + hh * W + qq);
+      }
+    acc[9] += g;
+  }
+#pragma unroll
+  for (int u = 0; u < 10; ++u) sh[u][threadIdx.x] = acc[u];
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s)
+#pragma unroll
+      for (int u = 0; u < 10; ++u) sh[u][threadIdx.x] += sh[u][threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x < 10) part[(long long)blockIdx.x * 10 + threadIdx.x] = sh[threadIdx.x][0];
+}
+
+__global__ void conv1_wgrad_finish_kernel(const double *__restrict__ part, float *__restrict__ dw,
+                                          float *__restrict__ db, int K, int slices) {
+  const int k = blockIdx.x, u = threadIdx.x;
+  if (u >= 10) return;
+  double s = 0.0;
+  for (int sl = 0; sl < slices; ++sl) s += part[((long long)k * slices + sl) * 10 + u];
+  if (u < 9) dw[k * 9 + u] = (float)s;
+  else db[k] = (float)s;
+}
+
+int grid_for(long long n, int sm_count) {
+  return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count * 32));
+}
+
+int need4(const void *desc, DescView *v, const char *what) {
+  REMORA_TRY(read_desc(desc, 4, v, what));
+  if (!v->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "%s must be contiguous", what);
+  return REMORA_OK;
+}
+
+}  // namespace
+
+}  // namespace remora
+
+using namespace remora;
+
+extern "C" {
+
+int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, const RemoraMemRef4 *w,
+                                const RemoraMemRef1 *bias, RemoraMemRef4 *pooled, RemoraMemRef4 *code,
+                                remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView X, Wd, Bd, P, C;
+  REMORA_TRY(need4(x, &X, "conv1 input"));
+  REMORA_TRY(need4(w, &Wd, "conv1 weights"));
+  REMORA_TRY(read_desc(bias, 1, &Bd, "conv1 bias"));
+  REMORA_TRY(need4(pooled, &P, "pooled output"));
+  REMORA_TRY(need4(code, &C, "pool codes"));
+  const int B = (int)X.sizes[0], H = (int)X.sizes[2], W = (int)X.sizes[3], K = (int)Wd.sizes[0];
+  if (X.sizes[1] != 1 || Wd.sizes[1] != 1 || Wd.sizes[2] != 3 || Wd.sizes[3] != 3 || (H | W) & 1)
+    return fail(REMORA_ERR_SHAPE, "conv1_relu_pool: needs x [B,1,H,W] (H, W even) and w [K,1,3,3]");
+  if (Bd.sizes[0] != K || P.sizes[0] != B || P.sizes[1] != K || P.sizes[2] != H / 2 || P.sizes[3] != W / 2)
+    return fail(REMORA_ERR_SHAPE, "conv1_relu_pool: pooled output must be [B,K,H/2,W/2]");
+  for (int d = 0; d < 4; ++d)
+    if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "conv1_relu_pool: codes must match pooled shape");
+  if (P.numel() == 0) return REMORA_OK;
+  conv1_relu_pool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)X.data(4), (const float *)Wd.data(4), (const float *)Bd.data(4), (float *)P.data(4),
+      (uint8_t *)C.data(1), B, K, H, W);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *a, RemoraMemRef4 *pooled, RemoraMemRef4 *code,
+                          remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView A, P, C;
+  REMORA_TRY(need4(a, &A, "relu_pool input"));
+  REMORA_TRY(need4(pooled, &P, "relu_pool output"));
+  REMORA_TRY(need4(code, &C, "relu_pool codes"));
+  const int H = (int)A.sizes[2], W = (int)A.sizes[3];
+  if ((H | W) & 1 || P.sizes[0] != A.sizes[0] || P.sizes[1] != A.sizes[1] || P.sizes[2] != H / 2 ||
+      P.sizes[3] != W / 2)
+    return fail(REMORA_ERR_SHAPE, "relu_pool: output must be [N,C,H/2,W/2] with H, W even");
+  for (int d = 0; d < 4; ++d)
+    if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "relu_pool: codes must match pooled shape");
+  if (P.numel() == 0) return REMORA_OK;
+  relu_pool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)A.data(4), (float *)P.data(4), (uint8_t *)C.data(1), A.sizes[0] * A.sizes[1], H, W);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_unpool(RemoraB200Ctx *ctx, const RemoraMemRef4 *dpooled, const RemoraMemRef4 *code,
+                       RemoraMemRef4 *da, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView P, C, A;
+  REMORA_TRY(need4(dpooled, &P, "unpool gradient"));
+  REMORA_TRY(need4(code, &C, "unpool codes"));
+  REMORA_TRY(need4(da, &A, "unpool output"));
+  const int H = (int)A.sizes[2], W = (int)A.sizes[3];
+  if ((H | W) & 1 || P.sizes[0] != A.sizes[0] || P.sizes[1] != A.sizes[1] || P.sizes[2] != H / 2 ||
+      P.sizes[3] != W / 2)
+    return fail(REMORA_ERR_SHAPE, "unpool: gradient must be [N,C,H/2,W/2] of the [N,C,H,W] output");
+  for (int d = 0; d < 4; ++d)
+    if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "unpool: codes must match the pooled shape");
+  if (P.numel() == 0) return REMORA_OK;
+  unpool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)P.data(4), (const uint8_t *)C.data(1), (float *)A.data(4), A.sizes[0] * A.sizes[1], H, W);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const RemoraMemRef1 *w, const RemoraMemRef1 *b,
+                          const RemoraMemRef1 *y, RemoraMemRef1 *z, RemoraMemRef1 *loss, RemoraMemRef1 *dz,
+                          float grad_scale, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView Hd, Wd, Bd, Y, Z, Lo, Dz;
+  REMORA_TRY(read_desc(h, 2, &Hd, "hidden"));
+  REMORA_TRY(read_desc(w, 1, &Wd, "dense weights"));
+  REMORA_TRY(read_desc(b, 1, &Bd, "dense bias"));
+  REMORA_TRY(read_desc(y, 1, &Y, "labels"));
+  REMORA_TRY(read_desc(z, 1, &Z, "logits"));
+  REMORA_TRY(read_desc(loss, 1, &Lo, "losses"));
+  REMORA_TRY(read_desc(dz, 1, &Dz, "logit gradients"));
+  for (const DescView *d : {&Hd, &Wd, &Bd, &Y, &Z, &Lo, &Dz})
+    if (!d->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "dense_bce: operands must be contiguous");
+  const int B = (int)Hd.sizes[0], D = (int)Hd.sizes[1];
+  if (Wd.sizes[0] != D || Bd.sizes[0] != 1 || Y.sizes[0] != B || Z.sizes[0] != B || Lo.sizes[0] != B ||
+      Dz.sizes[0] != B)
+    return fail(REMORA_ERR_SHAPE, "dense_bce: shapes must be h [B,D], w [D], b [1], y/z/loss/dz [B]");
+  if (B == 0) return REMORA_OK;
+  dense_bce_kernel<<<grid_for((long long)B * 32, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)Hd.data(4), (const float *)Wd.data(4), (const float *)Bd.data(4), (const float *)Y.data(4),
+      (float *)Z.data(4), (float *)Lo.data(4), (float *)Dz.data(4), B, D, grad_scale);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const RemoraMemRef1 *w,
+                               const RemoraMemRef1 *dz, RemoraMemRef2 *dh, RemoraMemRef1 *dw, RemoraMemRef1 *db,
+                               remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView Hd, Wd, Dz, Dh, Dw, Db;
+  REMORA_TRY(read_desc(h, 2, &Hd, "hidden"));
+  REMORA_TRY(read_desc(w, 1, &Wd, "dense weights"));
+  REMORA_TRY(read_desc(dz, 1, &Dz, "logit gradients"));
+  REMORA_TRY(read_desc(dh, 2, &Dh, "hidden gradients"));
+  REMORA_TRY(read_desc(dw, 1, &Dw, "weight gradients"));
+  REMORA_TRY(read_desc(db, 1, &Db, "bias gradient"));
+  for (const DescView *d : {&Hd, &Wd, &Dz, &Dh, &Dw, &Db})
+    if (!d->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "dense_relu_bwd: operands must be contiguous");
+  const int B = (int)Hd.sizes[0], D = (int)Hd.sizes[1];
+  if (Wd.sizes[0] != D || Dz.sizes[0] != B || Dh.sizes[0] != B || Dh.sizes[1] != D || Dw.sizes[0] != D ||
+      Db.sizes[0] != 1)
+    return fail(REMORA_ERR_SHAPE, "dense_relu_bwd: shapes must be h/dh [B,D], w/dw [D], dz [B], db [1]");
+  dense_bwd_kernel<<<D + 1, 256, 0, (cudaStream_t)stream>>>(
+      (const float *)Hd.data(4), (const float *)Wd.data(4), (const float *)Dz.data(4), (float *)Dh.data(4),
+      (float *)Dw.data(4), (float *)Db.data(4), B, D);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, const RemoraMemRef4 *dpooled,
+                                   const RemoraMemRef4 *code, RemoraMemRef4 *dw, RemoraMemRef1 *db,
+                                   remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView X, P, C, Dw, Db;
+  REMORA_TRY(need4(x, &X, "conv1 input"));
+  REMORA_TRY(need4(dpooled, &P, "pooled gradient"));
+  REMORA_TRY(need4(code, &C, "pool codes"));
+  REMORA_TRY(need4(dw, &Dw, "conv1 weight gradient"));
+  REMORA_TRY(read_desc(db, 1, &Db, "conv1 bias gradient"));
+  const int B = (int)X.sizes[0], H = (int)X.sizes[2], W = (int)X.sizes[3], K = (int)Dw.sizes[0];
+  if (X.sizes[1] != 1 || Dw.sizes[1] != 1 || Dw.sizes[2] != 3 || Dw.sizes[3] != 3 || Db.sizes[0] != K ||
+      P.sizes[0] != B || P.sizes[1] != K || P.sizes[2] != H / 2 || P.sizes[3] != W / 2)
+    return fail(REMORA_ERR_SHAPE, "conv1_wgrad_pooled: x [B,1,H,W], dpooled/codes [B,K,H/2,W/2], dw [K,1,3,3]");
+  const int slices = std::max(1, std::min(B, (ctx->sm_count * 4 + K - 1) / std::max(K, 1)));
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)K * slices * 10 * sizeof(double) + 256, &ws));
+  double *part = reinterpret_cast<double *>(ws->buf);
+  conv1_wgrad_pool_kernel<<<K * slices, 256, 0, (cudaStream_t)stream>>>(
+      (const float *)X.data(4), (const float *)P.data(4), (const uint8_t *)C.data(1), part, B, K, H, W, slices);
+  conv1_wgrad_finish_kernel<<<K, 32, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4), (float *)Db.data(4), K,
+                                                                slices);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+}  // extern "C"

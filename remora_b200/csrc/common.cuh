@@ -70,7 +70,13 @@ int dtype_size(int dtype);
 struct Workspace {
   void *buf = nullptr;
   size_t bytes = 0;
-  int *err = nullptr; // device word: nonzero after a bounded wait ran out
+  // 256-byte device block, zeroed at creation: word 0 is the error word
+  // (nonzero after a bounded wait ran out); word 16 is the whole-array
+  // fold's block ticket, which only that kernel touches and which it
+  // returns to zero when it finishes.  The large buffer `buf` is scratch
+  // that every call may overwrite.
+  int *err = nullptr;
+  unsigned int *fold_ticket() const { return reinterpret_cast<unsigned int *>(err + 16); }
 };
 
 }  // namespace remora

@@ -17,6 +17,7 @@
 // f32 ops rounded one by one), reverse sums in f64 like the reference's tape.
 #include <algorithm>
 
+#include "../../include/remora_b200_cnn.h"
 #include "conv.cuh"
 
 namespace remora {
@@ -109,9 +110,158 @@ __global__ void __launch_bounds__(256) conv_wgrad_direct(const float *__restrict
   if (threadIdx.x == 0) dw[widx] = (float)sh[0];
 }
 
+// Weight (and optionally bias) gradient of a 3x3 / pad 1 / stride 1 conv.
+// Work items are bands of RB output rows of one image; a block stages the
+// band's dy rows and the RB+2 input rows (zero-padded border columns) in
+// shared memory.  Thread (kp, c) owns dw[2kp..2kp+1][c][0..2][0..2]: it walks
+// the band row by row with a 3x3 window of inputs in registers (one new
+// column of three inputs and two dy values per pixel for 18 FMAs).  Each
+// block keeps its sums in registers over all its items and writes one f32
+// partial per weight; a second kernel adds the partials in block order in
+// f64 (deterministic).
+template <int RB, int W>
+__global__ void __launch_bounds__(512) conv_wgrad3x3_tiled(const float *__restrict__ x, const float *__restrict__ dy,
+                                                           float *__restrict__ part, ConvGeom g, int with_bias) {
+  extern __shared__ float sm[];
+  const int C = g.C, K = g.K;
+  constexpr int XW = W + 2;
+  const int xplane = (RB + 2) * XW + 1;  // odd stride: conflict-free across c
+  float *xs = sm;                        // [C][RB+2][W+2]
+  float *ds = sm + C * xplane;           // [K][RB][W]
+  const int kp = threadIdx.x / C, c = threadIdx.x % C;
+  const int bands = (g.H + RB - 1) / RB;
+  const long long items = (long long)g.N * bands;
+  float acc0[9], acc1[9], bsum0 = 0.f, bsum1 = 0.f;
+#pragma unroll
+  for (int u = 0; u < 9; ++u) acc0[u] = acc1[u] = 0.f;
+  for (long long it = blockIdx.x; it < items; it += gridDim.x) {
+    const int n = (int)(it / bands), band = (int)(it % bands), r0 = band * RB;
+    __syncthreads();
+    for (int e = threadIdx.x; e < C * (RB + 2) * XW; e += blockDim.x) {
+      const int cc = e / ((RB + 2) * XW), rem = e % ((RB + 2) * XW), rr = rem / XW, col = rem % XW;
+      const int h = r0 + rr - 1, q = col - 1;
+      xs[cc * xplane + rr * XW + col] =
+          (h >= 0 && h < g.H && q >= 0 && q < W) ? __ldg(x + (((long long)n * C + cc) * g.H + h) * W + q) : 0.f;
+    }
+    for (int e = threadIdx.x; e < K * RB * W; e += blockDim.x) {
+      const int k = e / (RB * W), rem = e % (RB * W), rr = rem / W, col = rem % W;
+      const int h = r0 + rr;
+      ds[e] = h < g.H ? __ldg(dy + (((long long)n * K + k) * g.H + h) * W + col) : 0.f;
+    }
+    __syncthreads();
+    const float *xc = xs + c * xplane;
+    const float *d0p = ds + (2 * kp) * RB * W, *d1p = d0p + RB * W;
+    for (int i = 0; i < RB; ++i) {
+      float w0[3], w1[3];
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        w0[r] = xc[(i + r) * XW];
+        w1[r] = xc[(i + r) * XW + 1];
+      }
+#pragma unroll 4
+      for (int j = 0; j < W; ++j) {
+        float w2[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) w2[r] = xc[(i + r) * XW + j + 2];
+        const float d0 = d0p[i * W + j], d1 = d1p[i * W + j];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+          acc0[r * 3 + 0] = fmaf(d0, w0[r], acc0[r * 3 + 0]);
+          acc0[r * 3 + 1] = fmaf(d0, w1[r], acc0[r * 3 + 1]);
+          acc0[r * 3 + 2] = fmaf(d0, w2[r], acc0[r * 3 + 2]);
+          acc1[r * 3 + 0] = fmaf(d1, w0[r], acc1[r * 3 + 0]);
+          acc1[r * 3 + 1] = fmaf(d1, w1[r], acc1[r * 3 + 1]);
+          acc1[r * 3 + 2] = fmaf(d1, w2[r], acc1[r * 3 + 2]);
+          w0[r] = w1[r];
+          w1[r] = w2[r];
+        }
+        bsum0 += d0;
+        bsum1 += d1;
+      }
+    }
+  }
+  float *pb = part + (long long)blockIdx.x * (K * C * 9 + K);
+#pragma unroll
+  for (int u = 0; u < 9; ++u) {
+    pb[((2 * kp) * C + c) * 9 + u] = acc0[u];
+    pb[((2 * kp + 1) * C + c) * 9 + u] = acc1[u];
+  }
+  if (with_bias && c == 0) {
+    pb[K * C * 9 + 2 * kp] = bsum0;
+    pb[K * C * 9 + 2 * kp + 1] = bsum1;
+  }
+}
+
+__global__ void wgrad_finish(const float *__restrict__ part, int nblocks, int stride, int nw, int nb,
+                             float *__restrict__ dw, float *__restrict__ db) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nw + nb) return;
+  double s = 0.0;
+  for (int b = 0; b < nblocks; ++b) s += (double)part[(long long)b * stride + e];
+  if (e < nw) dw[e] = (float)s;
+  else db[e - nw] = (float)s;
+}
+
+// Bias gradient db[k] = sum over n and pixels of dy[n,k,:,:]; one block per
+// channel, f64, fixed order.
+__global__ void __launch_bounds__(256) bias_grad_direct(const float *__restrict__ dy, float *__restrict__ db,
+                                                        int N, int K, long long pix) {
+  __shared__ double sh[256];
+  const int k = blockIdx.x;
+  double acc = 0.0;
+  for (long long t = threadIdx.x; t < (long long)N * pix; t += blockDim.x) {
+    const long long n = t / pix, p = t % pix;
+    acc += (double)dy[(n * K + k) * pix + p];
+  }
+  sh[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) db[k] = (float)sh[0];
+}
+
 int grid_for(long long n, int sm_count) {
   return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count * 32));
 }
+
+}  // namespace
+
+// dw (and db when non-null) of a 3x3 / pad 1 / stride 1 conv with the
+// register-tiled kernel; *handled = false for shapes it does not take.
+int conv_wgrad3x3(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw, float *db,
+                  cudaStream_t stream, bool *handled) {
+  *handled = false;
+  if (!(g.R == 3 && g.S == 3 && g.pad == 1 && g.stride == 1 && g.K % 2 == 0)) return REMORA_OK;
+  const int threads = (g.K / 2) * g.C;
+  if (threads > 512 || threads % 32) return REMORA_OK;
+  constexpr int RB = 4;
+  int W = g.W;
+  if (W != 32 && W != 64) return REMORA_OK;
+  const size_t smem = ((size_t)g.C * ((RB + 2) * (W + 2) + 1) + (size_t)g.K * RB * W) * sizeof(float);
+  if (smem > 200 * 1024) return REMORA_OK;
+  const int blocks = std::max(1, std::min<int>(ctx->sm_count * 2, g.N * ((g.H + RB - 1) / RB)));
+  const int nw = g.K * g.C * 9, nb = g.K;
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, stream, (size_t)blocks * (nw + nb) * sizeof(float) + 256, &ws));
+  float *part = reinterpret_cast<float *>(ws->buf);
+  if (W == 64) {
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(conv_wgrad3x3_tiled<RB, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+    conv_wgrad3x3_tiled<RB, 64><<<blocks, threads, smem, stream>>>(x, dy, part, g, db != nullptr);
+  } else {
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(conv_wgrad3x3_tiled<RB, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+    conv_wgrad3x3_tiled<RB, 32><<<blocks, threads, smem, stream>>>(x, dy, part, g, db != nullptr);
+  }
+  wgrad_finish<<<(nw + nb + 255) / 256, 256, 0, stream>>>(part, blocks, nw + nb, nw, db ? nb : 0, dw, db);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  *handled = true;
+  return REMORA_OK;
+}
+
+namespace {
 
 int read_conv(const RemoraConvSpec *spec, const RemoraMemRef4 *xin, const RemoraMemRef4 *w, const RemoraMemRef4 *yout,
               bool x_is_input, DescView *X, DescView *Wd, DescView *Y, ConvGeom *g) {
@@ -219,11 +369,40 @@ int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, con
     return fail(REMORA_ERR_SHAPE, "conv wgrad: dy must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
   if (DW.numel() == 0) return REMORA_OK;
   bool handled = false;
-  REMORA_TRY(conv_tc_wgrad(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
-                           spec->precision, (cudaStream_t)stream, &handled));
+  REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), nullptr,
+                           (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
   conv_wgrad_direct<<<(unsigned)DW.numel(), 256, 0, (cudaStream_t)stream>>>(
       (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), g);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *x,
+                                  const RemoraMemRef4 *dy, RemoraMemRef4 *dw, RemoraMemRef1 *db,
+                                  remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView X, DY, DW, DB;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, x, dw, dy, true, &X, &DW, &DY, &g));
+  REMORA_TRY(read_desc(db, 1, &DB, "conv bias gradient"));
+  g.N = (int)X.sizes[0];
+  g.H = (int)X.sizes[2];
+  g.W = (int)X.sizes[3];
+  if (X.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv wgrad: x has %lld channels, dw %d", X.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (DY.sizes[0] != g.N || DY.sizes[1] != g.K || DY.sizes[2] != g.OH || DY.sizes[3] != g.OW)
+    return fail(REMORA_ERR_SHAPE, "conv wgrad: dy must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
+  if (DB.sizes[0] != g.K || (DB.strides[0] != 1 && g.K > 1))
+    return fail(REMORA_ERR_SHAPE, "conv wgrad: db must be a contiguous [%d]", g.K);
+  bool handled = false;
+  REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
+                           (float *)DB.data(4), (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
+  conv_wgrad_direct<<<(unsigned)DW.numel(), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), g);
+  bias_grad_direct<<<g.K, 256, 0, (cudaStream_t)stream>>>((const float *)DY.data(4), (float *)DB.data(4), g.N, g.K,
+                                                          (long long)g.OH * g.OW);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }

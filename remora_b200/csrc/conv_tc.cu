@@ -13,10 +13,11 @@
 // further — a descriptor offset, no data movement.  Weights stay resident
 // in shared memory for the whole kernel in the same MN-major form.
 //
-// Roles (288 threads): warps 0-3 load and shift the input rows (generic
-// stores + fence.proxy.async, then an mbarrier arrive), warp 8 lane 0 issues
+// Roles (416 threads): warps 0-7 load and shift the input rows (all of a
+// tile's 128-bit loads in flight at once, then generic stores +
+// fence.proxy.async and an mbarrier arrive), warp 12 lane 0 issues
 // 9 * CIN/8 tcgen05.mma (M=128, N=32, K=8) per 128-pixel block into a TMEM
-// accumulator, warps 4-7 read TMEM (32 lanes x 32 channels per warp), add
+// accumulator, warps 8-11 read TMEM (32 lanes x 32 channels per warp), add
 // the bias and store NCHW rows (for one channel a warp writes 32 consecutive
 // pixels).  Two TMEM accumulators and up to two input stages overlap load,
 // MMA and epilogue of consecutive tiles.  Input gradient: the same kernel
@@ -42,6 +43,8 @@ struct ConvCfg {
   static constexpr size_t SMEM = W_BYTES + (size_t)STAGES * STAGE_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * MT * 32 <= 64 ? 64 : 128;
   static constexpr int NVEC = CIN * ROWS * (IMG_W / 4);
+  static constexpr int NV = NVEC / 256;  // 16-byte loads per loader thread per tile
+  static_assert(NVEC % 256 == 0, "loads split evenly over the 256 loader threads");
   static_assert(PIX % IMG_W == 0, "tile must hold whole rows");
   static_assert(COPY_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1 KB aligned operand regions");
   static_assert(CIN % 8 == 0, "K steps of 8 channels");
@@ -58,7 +61,9 @@ struct ConvTCParams {
   int *err;
 };
 
-constexpr int kConvThreads = 288;
+// warps 0-7 load, 8-11 epilogue (lane quarters 0-3), 12 MMA + TMEM alloc
+constexpr int kConvThreads = 416;
+constexpr int kLoaders = 256;
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
@@ -83,7 +88,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv3x3_tc_kernel(ConvTCParam
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      tc::mbar_init(&afull[s], 128);
+      tc::mbar_init(&afull[s], kLoaders);
       tc::mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -108,49 +113,56 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv3x3_tc_kernel(ConvTCParam
     *reinterpret_cast<float *>(wsm + off) = v;
   }
   fence_proxy_async_smem();
-  if (warp == 8) tc::tmem_alloc(&tmem_base, Cf::TMEM_COLS);
+  if (warp == 12) tc::tmem_alloc(&tmem_base, Cf::TMEM_COLS);
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const int ntiles = p.N * p.tiles_per_img;
   volatile int *abort_v = &abort_flag;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // --------------------------------------------- input rows -> 3 copies
+    // All of a tile's loads go to registers first, before the stage is known
+    // to be free, so their latency overlaps the previous tile's MMAs.
     const uint32_t stg_u = tc::smem_u32(stg);
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int st = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1;
-      if (!tc::mbar_wait(&aempty[st], ph ^ 1, abort_v, p.err, 201)) break;
       const int n = t / p.tiles_per_img, oh0 = (t % p.tiles_per_img) * Cf::TH;
-      const uint32_t base = stg_u + st * Cf::STAGE_BYTES;
-#pragma unroll 4
-      for (int v0 = warp * 32; v0 < Cf::NVEC; v0 += 128) {
-        const int v = v0 + lane;
+      float4 val[Cf::NV];
+#pragma unroll
+      for (int u = 0; u < Cf::NV; ++u) {
+        const int v = u * kLoaders + warp * 32 + lane;
         const int q = v % (IMG_W / 4), rl = v / (IMG_W / 4);
         const int c = rl / Cf::ROWS, r = rl % Cf::ROWS;
         const int ih = oh0 - 1 + r;
-        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v < Cf::NVEC && ih >= 0 && ih < p.H)
-          val = __ldg(reinterpret_cast<const float4 *>(p.x + (((long long)n * CIN + c) * p.H + ih) * IMG_W) + q);
-        float left = __shfl_up_sync(0xffffffffu, val.w, 1);
-        float right = __shfl_down_sync(0xffffffffu, val.x, 1);
+        val[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ih >= 0 && ih < p.H)
+          val[u] = __ldg(reinterpret_cast<const float4 *>(p.x + (((long long)n * CIN + c) * p.H + ih) * IMG_W) + q);
+      }
+      if (!tc::mbar_wait(&aempty[st], ph ^ 1, abort_v, p.err, 201)) break;
+      const uint32_t base = stg_u + st * Cf::STAGE_BYTES;
+#pragma unroll
+      for (int u = 0; u < Cf::NV; ++u) {
+        const int v = u * kLoaders + warp * 32 + lane;
+        const int q = v % (IMG_W / 4), rl = v / (IMG_W / 4);
+        const int c = rl / Cf::ROWS, r = rl % Cf::ROWS;
+        float left = __shfl_up_sync(0xffffffffu, val[u].w, 1);
+        float right = __shfl_down_sync(0xffffffffu, val[u].x, 1);
         if (q == 0) left = 0.0f;
         if (q == IMG_W / 4 - 1) right = 0.0f;
-        if (v < Cf::NVEC) {
-          const int px = r * IMG_W + 4 * q;
-          const uint32_t off = (px >> 5) * Cf::LBO + (c >> 2) * 512 + (c & 3) * 128 +
-                               ((((px & 31) >> 3) ^ (c & 3)) << 5) + ((px & 7) ? 16 : 0);
-          st_shared_v4(base + off, left, val.x, val.y, val.z);                      // column - 1
-          st_shared_v4(base + Cf::COPY_BYTES + off, val.x, val.y, val.z, val.w);    // column
-          st_shared_v4(base + 2 * Cf::COPY_BYTES + off, val.y, val.z, val.w, right);  // column + 1
-        }
+        const int px = r * IMG_W + 4 * q;
+        const uint32_t off = (px >> 5) * Cf::LBO + (c >> 2) * 512 + (c & 3) * 128 +
+                             ((((px & 31) >> 3) ^ (c & 3)) << 5) + ((px & 7) ? 16 : 0);
+        st_shared_v4(base + off, left, val[u].x, val[u].y, val[u].z);                       // column - 1
+        st_shared_v4(base + Cf::COPY_BYTES + off, val[u].x, val[u].y, val[u].z, val[u].w);  // column
+        st_shared_v4(base + 2 * Cf::COPY_BYTES + off, val[u].y, val[u].z, val[u].w, right);  // column + 1
       }
       fence_proxy_async_smem();
       tc::mbar_arrive(&afull[st]);
     }
-  } else if (warp == 8 && lane == 0) {
+  } else if (warp == 12 && lane == 0) {
     // ---------------------------------------------------------- MMA issue
     const uint32_t idesc = tc::idesc_tf32(128, 32, 1, 1);
     const uint32_t stg_u = tc::smem_u32(stg), w_u = tc::smem_u32(wsm);
@@ -192,9 +204,9 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv3x3_tc_kernel(ConvTCParam
       while (!tc::mbar_test(&drain, 0) && clock64() - t0 < tc::kWaitCycles) {
       }
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ----------------------------------------------------------- epilogue
-    const int q = warp - 4;
+    const int q = warp - 8;
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -222,7 +234,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv3x3_tc_kernel(ConvTCParam
     }
   }
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 12) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tbase, Cf::TMEM_COLS);
   }

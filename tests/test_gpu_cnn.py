@@ -1,0 +1,98 @@
+"""GPU parity of the crater-CNN training step against the oracle's step
+(oracle/oracle.c:oracle_cnn_step) on the same seeded images and parameters.
+
+3xTF32 mode (split-precision GEMMs, exact-order conv kernels; the default)
+is held to rtol 1e-4 + atol 1e-4 * max|ref| per gradient tensor, inside the
+1e-3 gradient tolerance.  Plain TF32 (10-bit mantissa operands in conv2 and
+the dense GEMMs) does not meet 1e-3 on every tensor: the first layer's weight
+gradient, a sum over every pixel of the batch with heavy cancellation, comes
+out at ~3e-2 * max|ref| (measured on B200).  Its test pins the loss at 1e-3
+and every gradient at 5e-2 * max|ref|, the bound of that mode."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import to_host
+from remora_b200 import crater
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(cuda, oracle_mod, batch, precision, steps=1):
+    import torch
+
+    from remora_b200.cnn import CraterCNN
+
+    params = crater.init_params()
+    imgs, labels = crater.make_batch(batch)
+    net = CraterCNN(cuda, batch, lr=0.01, params=params, precision=precision)
+    xi, yi = torch.from_numpy(imgs).to(cuda), torch.from_numpy(labels).to(cuda)
+    ref_params = params.copy()
+    for _ in range(steps):
+        net.forward_backward(xi, yi)
+        grads = to_host(net.grads).copy()
+        loss = net.loss()
+        net.update()
+        ref_loss, ref_grads = oracle_mod.cnn_step(ref_params, imgs, labels, lr=0.01,
+                                                  nthreads=oracle_mod.max_threads())
+    return loss, grads, to_host(net.params), ref_loss, ref_grads, ref_params
+
+
+def _compare(grads, ref, tol):
+    for name, (a, b, _) in crater.offsets().items():
+        r = ref[a:b].astype(np.float64)
+        scale = max(float(np.abs(r).max()), 1e-12)
+        err = float(np.abs(grads[a:b] - r).max()) / scale
+        assert err <= tol, f"{name}: scaled error {err:.3g} > {tol}"
+
+
+@pytest.mark.parametrize("batch", [2, 8])
+def test_cnn_step_3xtf32_matches_oracle(cuda, oracle_mod, batch):
+    loss, grads, params, ref_loss, ref_grads, ref_params = _run(cuda, oracle_mod, batch, "3xtf32")
+    assert abs(loss - ref_loss) <= 1e-5 * max(1.0, abs(ref_loss))
+    _compare(grads, ref_grads, 1e-4)
+    np.testing.assert_allclose(params, ref_params, rtol=1e-5, atol=1e-6)
+
+
+def test_cnn_step_tf32_matches_oracle(cuda, oracle_mod):
+    loss, grads, params, ref_loss, ref_grads, ref_params = _run(cuda, oracle_mod, 16, "tf32")
+    assert abs(loss - ref_loss) <= 1e-3 * max(1.0, abs(ref_loss))
+    _compare(grads, ref_grads, 5e-2)
+    np.testing.assert_allclose(params, ref_params, rtol=1e-3, atol=1e-4)
+
+
+def test_cnn_training_reduces_loss_and_graph_replay(cuda):
+    """A few hundred samples, several SGD steps: the loss falls (the
+    reference's own training test, tests/test_crater_train.py:6-19, asks for
+    the final loss below 0.95x the first); a captured CUDA-graph step gives
+    the same parameters as the eager step."""
+    import torch
+
+    from remora_b200.cnn import CraterCNN
+
+    imgs, labels = crater.make_batch(256)
+    xi, yi = torch.from_numpy(imgs).to(cuda), torch.from_numpy(labels).to(cuda)
+    net = CraterCNN(cuda, 256, lr=0.05)
+    losses = []
+    for _ in range(30):
+        net.forward_backward(xi, yi)
+        losses.append(net.loss())
+        net.update()
+    assert all(np.isfinite(losses))
+    assert losses[-1] < 0.95 * losses[0], losses
+    assert np.isfinite(to_host(net.params)).all()
+    # graph replay == eager step
+    a = CraterCNN(cuda, 256, lr=0.05)
+    b = CraterCNN(cuda, 256, lr=0.05)
+    a.step(xi, yi)
+    b.step(xi, yi)
+    b.capture(xi, yi)  # records (and runs) one step
+    a.step(xi, yi)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_host(a.params), to_host(b.params))
+    b.replay()
+    a.step(xi, yi)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(to_host(a.params), to_host(b.params))

@@ -251,3 +251,22 @@ def test_array_fold_and_golden(cuda, oracle_mod):
     init = np.zeros(16, np.float32)
     close(to_host(ops.array_fold(to_dev(big, cuda), to_dev(init, cuda))),
           big.astype(np.float64).sum(0), rtol=1e-4)
+
+
+def test_whole_fold_after_other_scratch_users(cuda):
+    """Calls that stage data through the shared per-stream scratch (a 3xTF32
+    GEMM's split operands, a scan's carries) between whole-array folds must
+    not disturb the fold's block ticket."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    xs = rng.uniform(0, 1, 1 << 20).astype(np.float32)
+    d = to_dev(xs, cuda)
+    ref = float(np.sum(xs.astype(np.float64)))
+    a = torch.rand(300, 200, device=cuda)
+    for _ in range(3):
+        ops.gemm(a, a.t(), precision="3xtf32")
+        ops.scan(d)
+        got = float(to_host(ops.fold(d, mode="all")))
+        assert abs(got - ref) <= 1e-5 * ref
+        assert float(to_host(ops.fold(to_dev(np.arange(1, 5, dtype=np.float32), cuda), mode="all"))) == 10.0
