@@ -277,6 +277,26 @@ int remora_b200_scan(RemoraB200Ctx *ctx, const RemoraScanSpec *spec,
                      const void *in_desc, void *out_desc, int32_t rank,
                      remora_stream_t stream);
 
+/* The same scans as remora_b200_scan, for callers that cannot allocate
+   device memory: callers whose device memory is owned entirely by another
+   allocator (a host framework's memory pool that has reserved the GPU), and
+   callers on a latency-critical path where cudaMalloc, which may synchronise
+   the device, is not acceptable.  This entry point allocates nothing: its
+   scratch (tile aggregates and carries) is one fixed 1 MiB array in device
+   memory that every GPU loading the library holds until the process exits.
+   Limits: a rank-1 scan may have at most 268,304,384 elements (larger scans
+   return REMORA_ERR_LIMIT before any work is queued); input and output must
+   be contiguous (strided views return REMORA_ERR_UNSUPPORTED).  The first
+   call on a device looks up the array's device address (cudaGetSymbolAddress)
+   and caches it; make that first call before any stream capture.  Every call
+   on a device shares the array: calls that overlap on the GPU (different
+   streams, or different threads) race and give wrong results; serialise
+   them.  The array keeps the previous call's contents; nothing in it needs
+   to start at zero.  No counterpart in the reference. */
+int remora_b200_scan_noalloc(RemoraB200Ctx *ctx, const RemoraScanSpec *spec,
+                             const void *in_desc, void *out_desc, int32_t rank,
+                             remora_stream_t stream);
+
 /* Dense core: C = A . B as the lifted dot
    C[i,j] = fold(+, 0, map(*, A[i,:], B[:,j])) (stdlib/prelude.rem:14,
    examples/crater_train.py:38-44), rank 2 or batched rank 3, f32 storage,

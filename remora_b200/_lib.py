@@ -147,6 +147,7 @@ _PROTOTYPES: dict[str, tuple] = {
     ),
     "remora_b200_array_fold": (_I32, [_VP, ctypes.POINTER(RemoraFoldSpec), _VP, _I32, _VP, _VP, _VP]),
     "remora_b200_scan": (_I32, [_VP, ctypes.POINTER(RemoraScanSpec), _VP, _VP, _I32, _VP]),
+    "remora_b200_scan_noalloc": (_I32, [_VP, ctypes.POINTER(RemoraScanSpec), _VP, _VP, _I32, _VP]),
     "remora_b200_gemm": (_I32, [_VP, ctypes.POINTER(RemoraGemmSpec), _VP, _VP, _VP, _I32, _VP]),
     "remora_b200_conv2d_fwd": (_I32, [_VP, ctypes.POINTER(RemoraConvSpec), _VP, _VP, _VP, _VP, _VP]),
     "remora_b200_conv2d_dgrad": (_I32, [_VP, ctypes.POINTER(RemoraConvSpec), _VP, _VP, _VP, _VP]),

@@ -412,6 +412,73 @@ extern "C" int remora_b200_array_fold(RemoraB200Ctx *ctx, const RemoraFoldSpec *
   return REMORA_OK;
 }
 
+// ---- scan without any allocation: the tile aggregates and carries live in
+// one fixed-size device array instead of the library's cached workspace.
+namespace remora {
+namespace {
+
+// Every GPU that loads the library holds this array until the process exits.
+constexpr size_t kNoAllocScanBytes = (size_t)1 << 20;
+__device__ __align__(256) unsigned char g_noalloc_scan_scratch[kNoAllocScanBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the fixed scratch on `device` (which must be current).
+// Host code cannot use the array's name as a device address; the address is
+// looked up once per device and cached.
+int noalloc_scratch(int device, void **out) {
+  if (device < 0 || device >= kMaxDevices) return fail(REMORA_ERR_ARG, "scan_noalloc: device %d", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scan_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(REMORA_ERR_CUDA, "scan_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return REMORA_OK;
+}
+
+}  // namespace
+}  // namespace remora
+
+extern "C" int remora_b200_scan_noalloc(RemoraB200Ctx *ctx, const RemoraScanSpec *spec, const void *in_desc,
+                                        void *out_desc, int32_t rank, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView in, out;
+  REMORA_TRY(validate_scan(spec, in_desc, out_desc, rank, &in, &out));
+  if (!in.contiguous() || !out.contiguous())
+    return fail(REMORA_ERR_UNSUPPORTED,
+                "scan_noalloc: input and output must be contiguous (a strided view would need a staging copy)");
+  const int64_t N = in.sizes[0];
+  const int64_t C = N ? in.numel() / N : 0;
+  // Rank >= 2: fewer row segments so their carries fit the fixed scratch.
+  int sm = ctx->sm_count;
+  size_t need = 0;
+  if (N > 0 && C > 0) {
+    if (C == 1) {
+      need = scan_scratch_bytes(N, 1, sm);
+    } else {
+      sm = std::max<int>(1, std::min<int>(sm, (int)((kNoAllocScanBytes - 256) / (8 * 2048))));
+      const int64_t nseg = std::max<int64_t>(1, std::min<int64_t>(N, (int64_t)sm * 2048 / C));
+      need = nseg == 1 ? 0 : scan_scratch_bytes(N, C, sm);
+    }
+  }
+  if (need > kNoAllocScanBytes) {
+    const long long max_tiles = (long long)((kNoAllocScanBytes - 256) / 8) & ~63LL;
+    return fail(REMORA_ERR_LIMIT,
+                "scan_noalloc: a rank-1 scan of %lld elements needs %zu bytes of scratch; the fixed scratch holds "
+                "%zu bytes, i.e. at most %lld elements",
+                (long long)N, need, kNoAllocScanBytes, max_tiles * kTile);
+  }
+  void *scratch = nullptr;
+  REMORA_TRY(noalloc_scratch(ctx->device, &scratch));
+  return run_scan(*spec, in, out, static_cast<char *>(scratch), kNoAllocScanBytes, sm, (cudaStream_t)stream);
+}
+
 extern "C" int remora_b200_scan(RemoraB200Ctx *ctx, const RemoraScanSpec *spec, const void *in_desc,
                                 void *out_desc, int32_t rank, remora_stream_t stream) {
   REMORA_TRY(check_ctx(ctx));
