@@ -10,8 +10,6 @@
 // are two-level and deterministic: fixed per-block ranges, fixed-order
 // combine of the block partials by the last block to finish.
 #include <algorithm>
-#include <set>
-#include <utility>
 
 #include "jit.cuh"
 
@@ -28,6 +26,11 @@ __device__ __forceinline__ float cvt_f(unsigned char v) { return v ? 1.0f : 0.0f
 __device__ __forceinline__ int cvt_i(float v) { return (int)v; }
 __device__ __forceinline__ int cvt_i(int v) { return v; }
 __device__ __forceinline__ int cvt_i(unsigned char v) { return v ? 1 : 0; }
+// Programmatic dependent launch: wait until the previous kernel in the
+// stream has finished and its writes are visible, then let the next one be
+// scheduled onto SMs as ours drain.  No-ops without the launch attribute.
+#define PDL_PROLOGUE() do { asm volatile("griddepcontrol.wait;" ::: "memory"); \
+                            asm volatile("griddepcontrol.launch_dependents;" :::); } while (0)
 )";
 
 const char *ctype(int dtype) {
@@ -86,6 +89,7 @@ std::string map_module_source(const RemoraMapProgram &p, const int *modes) {
   // ---- vectorised kernel: FULL inputs as 4-vectors, BCAST (divisor a
   // multiple of 4) as one element per vector, SCALAR hoisted.
   s += "extern \"C\" __global__ void __launch_bounds__(256) remora_map_vec(MapVecArgs a) {\n";
+  s += "  PDL_PROLOGUE();\n";
   s += "  const i64 nv = a.n >> 2;\n  const i64 step = (i64)gridDim.x * blockDim.x;\n";
   for (int k = 0; k < n; ++k) {
     if (modes[k] == IN_SCALAR)
@@ -160,6 +164,7 @@ std::string map_module_source(const RemoraMapProgram &p, const int *modes) {
 
   // ---- general strided kernel (views, negative strides, broadcasting).
   s += "extern \"C\" __global__ void __launch_bounds__(256) remora_map_strided(MapStridedArgs a) {\n";
+  s += "  PDL_PROLOGUE();\n";
   s += "  const i64 step = (i64)gridDim.x * blockDim.x;\n";
   s += "  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += step) {\n";
   s += "    i64 rem = i, off_o = 0;\n";
@@ -196,22 +201,6 @@ struct FoldCellArgs {
   int32_t init_i;
 };
 
-struct FoldBulkArgs {
-  void *out;
-  int64_t rows;
-  int64_t L;
-  const void *in[2];
-  float init_f;
-  int32_t init_i;
-  int64_t rows_per_tile;
-  int64_t ntiles;
-  int *err;
-};
-
-// Cell folds of at least this many input bytes take the TMA-staged kernel;
-// smaller ones are launch-bound and keep the register-streaming kernel.
-constexpr int64_t kFoldBulkMinBytes = 1 << 20;
-
 struct FoldAllArgs {
   void *out;
   int64_t n;
@@ -222,15 +211,6 @@ struct FoldAllArgs {
   float init_f;
   int32_t init_i;
 };
-
-// TMA-staged cell fold: warps per block, pipeline depth, and the bytes of
-// one input that one stage holds (two inputs share the same budget).
-constexpr int kFoldBulkWarps = 8;
-constexpr int kFoldBulkStages = 3;
-constexpr int fold_bulk_tile(int n_in) { return n_in == 2 ? 2048 : 4096; }
-constexpr size_t fold_bulk_smem(int n_in) {
-  return (size_t)kFoldBulkWarps * kFoldBulkStages * fold_bulk_tile(n_in) * n_in;
-}
 
 std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U) {
   const bool f = sp.dtype == REMORA_F32;
@@ -281,9 +261,16 @@ std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U)
   s += "struct FoldCellArgs { void* out; i64 rows; i64 L; const void* in[2]; float init_f; int init_i; };\n";
   s += "struct FoldAllArgs { void* out; i64 n; i64 per_block; const void* in[2]; void* partials; unsigned int* counter; float init_f; int init_i; };\n";
 
+  {
+    int lu = 0, lg = 0;
+    while ((1 << lu) < U) ++lu;
+    while ((1 << lg) < G) ++lg;
+    s += "#define HS " + std::to_string(std::min(lu, lg)) + "\n";  // halving steps of the butterfly
+  }
   // ---- cell fold, 128-bit loads (L % 4 == 0, 16-byte aligned rows)
   s += R"(
 extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_vec(FoldCellArgs a) {
+  PDL_PROLOGUE();
   const int lane = threadIdx.x & 31, sub = lane & (G - 1), grp = lane / G;
   const i64 warp = (i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const i64 nwarps = (i64)gridDim.x * (blockDim.x >> 5);
@@ -309,115 +296,37 @@ extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_vec(FoldCellA
     s += std::string("          acc[u] = acc_op(acc[u], ELEM(") + cvt + "(va[u]." + c + "), " + cvt + "(vb[u]." + c + ")));\n";
   s += "        }\n      }\n    }\n";
   s += R"(
+    // Butterfly over the G lanes of a group for its U rows at once: the
+    // first HS steps halve the rows a lane holds (it keeps one half and
+    // sends the other), the rest are plain xor steps.  Each partial sum
+    // pairs the same lanes in the same order as a separate butterfly per
+    // row would, so the totals are the same bit for bit, with
+    // U/2 + U/4 + ... + log2(G/U)... shuffles instead of U * log2(G).
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      ACC v = acc[u];
+    for (int step = 0; step < HS; ++step) {
+      const int o = G >> (step + 1), h = U >> step;
+      const bool up = (lane & o) != 0;
 #pragma unroll
-      for (int o = G / 2; o > 0; o >>= 1) v = acc_op(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (sub == 0 && r0 + u < a.rows) put(a.out, r0 + u, v, )" + init_arg + R"();
+      for (int j = 0; j < h / 2; ++j) {
+        const ACC send = up ? acc[j] : acc[j + h / 2];
+        const ACC keep = up ? acc[j + h / 2] : acc[j];
+        acc[j] = acc_op(keep, __shfl_xor_sync(0xffffffffu, send, o));
+      }
     }
-  }
-}
-)";
-
-  // ---- cell fold, TMA-staged: every warp streams its own tiles of whole
-  // rows into shared memory with cp.async.bulk (FB_STAGES deep, one
-  // mbarrier per stage) and folds them from there, so each SM keeps up to
-  // 16 warps x FB_STAGES x FB_TILE bytes of HBM reads in flight with few
-  // registers.  Rows are folded exactly as in remora_fold_cell_vec (lane
-  // `sub` sums float4 columns sub, sub+G, ...; then an xor-shuffle tree), so
-  // both kernels give bit-identical results.  Waits are bounded: a wait
-  // that runs out records code 301 in the error word and the warp drains
-  // its copies still in flight before it returns.
-  s += "#define NIN " + std::to_string(n_in) + "\n#define FB_TILE " + std::to_string(fold_bulk_tile(n_in)) +
-       "\n#define FB_STAGES " + std::to_string(kFoldBulkStages) + "\n#define FB_WARPS " +
-       std::to_string(kFoldBulkWarps) + "\n";
-  s += "struct FoldBulkArgs { void* out; i64 rows; i64 L; const void* in[2]; float init_f; int init_i; "
-       "i64 rows_per_tile; i64 ntiles; int* err; };\n";
-  s += R"(
-__device__ __forceinline__ unsigned fb_saddr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ bool fb_try(unsigned bar, unsigned parity) {
-  unsigned ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-  return ok != 0u;
-}
-__device__ __forceinline__ bool fb_wait(unsigned bar, unsigned parity) {
-  if (fb_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!fb_try(bar, parity))
-    if (clock64() - t0 > 4000000000LL) return false;
-  return true;
-}
-extern "C" __global__ void __launch_bounds__(FB_WARPS * 32) remora_fold_cell_bulk(FoldBulkArgs a) {
-  extern __shared__ __align__(128) unsigned char fb_smem[];
-  __shared__ __align__(8) u64 fb_bar[FB_WARPS][FB_STAGES];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & (G - 1), grp = lane / G;
-  unsigned char* stage0 = fb_smem + (size_t)w * FB_STAGES * FB_TILE * NIN;
-  if (lane == 0) {
-    for (int s = 0; s < FB_STAGES; ++s)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(fb_saddr(&fb_bar[w][s])) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncwarp();
-  const i64 W = (i64)gridDim.x * FB_WARPS;
-  const i64 first = (i64)blockIdx.x * FB_WARPS + w;
-  const i64 nt = first < a.ntiles ? (a.ntiles - first + W - 1) / W : 0;
-  const i64 rowB = a.L * 4, nv = a.L >> 2, R = a.rows_per_tile;
-  // tile k of this warp: rows [t*R, min(t*R+R, rows)), t = first + k*W
-  auto issue = [&](i64 k) {
-    const i64 r0 = (first + k * W) * R;
-    const i64 nr = a.rows - r0 < R ? a.rows - r0 : R;
-    const unsigned bytes = (unsigned)(nr * rowB);
-    const int s = (int)(k % FB_STAGES);
-    const unsigned bar = fb_saddr(&fb_bar[w][s]);
-    unsigned char* dst = stage0 + (size_t)s * FB_TILE * NIN;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes * NIN) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 :: "r"(fb_saddr(dst)), "l"((const char*)a.in[0] + r0 * rowB), "r"(bytes), "r"(bar) : "memory");
-#if NIN == 2
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 :: "r"(fb_saddr(dst + FB_TILE)), "l"((const char*)a.in[1] + r0 * rowB), "r"(bytes), "r"(bar) : "memory");
-#endif
-  };
-  if (lane == 0)
-    for (i64 k = 0; k < nt && k < FB_STAGES; ++k) issue(k);
-  i64 k = 0;
-  bool ok = true;
-  for (; k < nt; ++k) {
-    const int s = (int)(k % FB_STAGES);
-    const bool got = fb_wait(fb_saddr(&fb_bar[w][s]), (unsigned)((k / FB_STAGES) & 1));
-    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-    const unsigned char* src = stage0 + (size_t)s * FB_TILE * NIN;
-    const i64 r0 = (first + k * W) * R;
-    const i64 nr = a.rows - r0 < R ? a.rows - r0 : R;
-    for (i64 i0 = 0; i0 < nr; i0 += 32 / G) {
-      const i64 i = i0 + grp;
-      ACC acc = IDENT;
-      if (i < nr) {
-)";
-  s += "        const " + inV + "* pa = (const " + inV + "*)(src + i * rowB);\n";
-  if (n_in == 2) s += "        const " + inV1 + "* pb = (const " + inV1 + "*)(src + FB_TILE + i * rowB);\n";
-  s += "        for (i64 c = sub; c < nv; c += G) {\n          const " + inV + " va = pa[c];\n";
-  if (n_in == 2) s += "          const " + inV1 + " vb = pb[c];\n";
-  else s += "          const " + inV + " vb = va;\n";
-  for (const char *c : {"x", "y", "z", "w"})
-    s += std::string("          acc = acc_op(acc, ELEM(") + cvt + "(va." + c + "), " + cvt + "(vb." + c + ")));\n";
-  s += "        }\n      }\n";
-  s += R"(
 #pragma unroll
-      for (int o = G / 2; o > 0; o >>= 1) acc = acc_op(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-      if (sub == 0 && i < nr) put(a.out, r0 + i, acc, )" + init_arg + R"();
+    for (int o = G >> (HS + 1); o > 0; o >>= 1) {
+#pragma unroll
+      for (int j = 0; j < (U >> HS); ++j) acc[j] = acc_op(acc[j], __shfl_xor_sync(0xffffffffu, acc[j], o));
     }
-    __syncwarp();
-    if (lane == 0 && k + FB_STAGES < nt) issue(k + FB_STAGES);
-  }
-  if (!ok && lane == 0) {
-    atomicCAS(a.err, 0, 301);
-    // drain: the copies of tiles k .. k+FB_STAGES-1 may still be in flight
-    for (i64 j = k; j < nt && j < k + FB_STAGES; ++j)
-      if (!fb_wait(fb_saddr(&fb_bar[w][j % FB_STAGES]), (unsigned)((j / FB_STAGES) & 1))) break;
+    if ((sub & ((G >> HS) - 1)) == 0) {
+      int u0 = 0;
+#pragma unroll
+      for (int step = 0; step < HS; ++step)
+        if (lane & (G >> (step + 1))) u0 += U >> (step + 1);
+#pragma unroll
+      for (int j = 0; j < (U >> HS); ++j)
+        if (r0 + u0 + j < a.rows) put(a.out, r0 + u0 + j, acc[j], )" + init_arg + R"();
+    }
   }
 }
 )";
@@ -425,6 +334,7 @@ extern "C" __global__ void __launch_bounds__(FB_WARPS * 32) remora_fold_cell_bul
   // ---- cell fold, scalar loads (any L, any 4-byte alignment)
   s += R"(
 extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_scalar(FoldCellArgs a) {
+  PDL_PROLOGUE();
   const int lane = threadIdx.x & 31, sub = lane & (G - 1), grp = lane / G;
   const i64 warp = (i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const i64 nwarps = (i64)gridDim.x * (blockDim.x >> 5);
@@ -448,12 +358,36 @@ extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_scalar(FoldCe
   s += R"(        }
       }
     }
+    // Butterfly over the G lanes of a group for its U rows at once: the
+    // first HS steps halve the rows a lane holds (it keeps one half and
+    // sends the other), the rest are plain xor steps.  Each partial sum
+    // pairs the same lanes in the same order as a separate butterfly per
+    // row would, so the totals are the same bit for bit, with
+    // U/2 + U/4 + ... + log2(G/U)... shuffles instead of U * log2(G).
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      ACC v = acc[u];
+    for (int step = 0; step < HS; ++step) {
+      const int o = G >> (step + 1), h = U >> step;
+      const bool up = (lane & o) != 0;
 #pragma unroll
-      for (int o = G / 2; o > 0; o >>= 1) v = acc_op(v, __shfl_xor_sync(0xffffffffu, v, o));
-      if (sub == 0 && r0 + u < a.rows) put(a.out, r0 + u, v, )" + init_arg + R"();
+      for (int j = 0; j < h / 2; ++j) {
+        const ACC send = up ? acc[j] : acc[j + h / 2];
+        const ACC keep = up ? acc[j + h / 2] : acc[j];
+        acc[j] = acc_op(keep, __shfl_xor_sync(0xffffffffu, send, o));
+      }
+    }
+#pragma unroll
+    for (int o = G >> (HS + 1); o > 0; o >>= 1) {
+#pragma unroll
+      for (int j = 0; j < (U >> HS); ++j) acc[j] = acc_op(acc[j], __shfl_xor_sync(0xffffffffu, acc[j], o));
+    }
+    if ((sub & ((G >> HS) - 1)) == 0) {
+      int u0 = 0;
+#pragma unroll
+      for (int step = 0; step < HS; ++step)
+        if (lane & (G >> (step + 1))) u0 += U >> (step + 1);
+#pragma unroll
+      for (int j = 0; j < (U >> HS); ++j)
+        if (r0 + u0 + j < a.rows) put(a.out, r0 + u0 + j, acc[j], )" + init_arg + R"();
     }
   }
 }
@@ -474,6 +408,7 @@ __device__ __forceinline__ ACC block_reduce(ACC v, ACC* sh) {
   return t;
 }
 extern "C" __global__ void __launch_bounds__(256) remora_fold_all(FoldAllArgs a) {
+  PDL_PROLOGUE();
   __shared__ ACC sh[32];
   __shared__ int is_last;
   const i64 beg = (i64)blockIdx.x * a.per_block;
@@ -528,21 +463,23 @@ int pow2_floor(int64_t v) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Opts a JIT kernel into more than 48 KB of dynamic shared memory, once per
-// kernel and device.
-int allow_dynamic_smem(cudaKernel_t k, int device, size_t bytes) {
-  static std::mutex mu;
-  static std::set<std::pair<const void *, int>> done;
-  std::lock_guard<std::mutex> lock(mu);
-  if (done.count({(const void *)k, device})) return REMORA_OK;
-  REMORA_CUDA_TRY(cudaFuncSetAttribute((const void *)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-  done.insert({(const void *)k, device});
-  return REMORA_OK;
-}
-
+// Every JIT kernel starts with PDL_PROLOGUE, so it may be launched as a
+// programmatic dependent of the previous kernel in the stream: its blocks
+// are scheduled while that kernel's last blocks drain, which hides most of
+// the launch gap between back-to-back HBM-bound kernels.
 int launch(cudaKernel_t k, int grid, int block, void *args_struct, cudaStream_t stream) {
   void *params[] = {args_struct};
-  cudaError_t e = cudaLaunchKernel((const void *)k, dim3(grid), dim3(block), params, 0, stream);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, (const void *)k, params);
   if (e != cudaSuccess) return fail(REMORA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   return REMORA_OK;
 }
@@ -737,33 +674,6 @@ int run_fold(RemoraB200Ctx *ctx, const RemoraFoldSpec &sp, const DescView *ins_i
     cudaKernel_t kern;
     REMORA_TRY(jit_kernel_keyed(key, vec ? "remora_fold_cell_vec" : "remora_fold_cell_scalar",
                                 [&]() { return fold_module_source(sp, n_in, G, U); }, &kern));
-    const int64_t row_bytes = L * 4;
-    if (vec && rows > 0 && row_bytes <= fold_bulk_tile(n_in) &&
-        rows * row_bytes * n_in >= kFoldBulkMinBytes) {
-      cudaKernel_t bulk;
-      REMORA_TRY(jit_kernel_keyed(key, "remora_fold_cell_bulk",
-                                  [&]() { return fold_module_source(sp, n_in, G, U); }, &bulk));
-      const size_t smem = fold_bulk_smem(n_in);
-      REMORA_TRY(allow_dynamic_smem(bulk, ctx->device, smem));
-      FoldBulkArgs b{};
-      b.out = dst;
-      b.rows = rows;
-      b.L = L;
-      b.in[0] = src[0];
-      b.in[1] = src[1];
-      b.init_f = sp.init_f;
-      b.init_i = sp.init_i;
-      b.rows_per_tile = fold_bulk_tile(n_in) / row_bytes;
-      b.ntiles = (rows + b.rows_per_tile - 1) / b.rows_per_tile;
-      b.err = err;
-      const int64_t grid = std::max<int64_t>(
-          1, std::min<int64_t>((b.ntiles + kFoldBulkWarps - 1) / kFoldBulkWarps, (int64_t)ctx->sm_count * 2));
-      void *params[] = {&b};
-      REMORA_CUDA_TRY(cudaLaunchKernel((const void *)bulk, dim3((unsigned)grid), dim3(kFoldBulkWarps * 32), params,
-                                       smem, stream));
-      if (!out_contig) REMORA_TRY(copy_from_contiguous(dst, out_in, out_es, stream, ctx->sm_count));
-      return REMORA_OK;
-    }
     FoldCellArgs a{};
     a.out = dst;
     a.rows = rows;

@@ -270,3 +270,32 @@ def test_whole_fold_after_other_scratch_users(cuda):
         got = float(to_host(ops.fold(d, mode="all")))
         assert abs(got - ref) <= 1e-5 * ref
         assert float(to_host(ops.fold(to_dev(np.arange(1, 5, dtype=np.float32), cuda), mode="all"))) == 10.0
+
+
+@pytest.mark.parametrize("L,n_in", [(4, 1), (64, 1), (100, 1), (1020, 1), (1024, 1), (12, 2), (512, 2)])
+def test_fold_rows_independent_of_launch_geometry(cuda, oracle_mod, L, n_in):
+    """A row's total depends only on the row: a ~3 MiB fold (grid-stride
+    launch, ragged last row block) equals the concatenation of the folds of
+    its ~200 KiB row blocks (single-pass launches) bit for bit, and the
+    oracle within the fold tolerance."""
+    import torch
+
+    rng = np.random.default_rng(L + 100 * n_in)
+    rows = max(4096, ((3 << 20) // (4 * L * n_in)) | 1)  # ~3 MiB, odd row count: ragged last row block
+    xs = [rng.standard_normal((rows, L)).astype(np.float32) for _ in range(n_in)]
+    expr, kw = (CHAIN, {}) if n_in == 1 else (stable_bce(x(0), x(1)), {})
+    if n_in == 2:
+        xs[1] = (xs[1] > 0).astype(np.float32)
+    dev = [to_dev(a, cuda) for a in xs]
+    big = to_host(ops.fold(*dev, premap=expr, **kw))
+    step = max(1, (200 << 10) // (4 * L * n_in))
+    parts = [to_host(ops.fold(*[d[i:i + step] for d in dev], premap=expr, **kw)) for i in range(0, rows, step)]
+    np.testing.assert_array_equal(big, np.concatenate(parts))
+    ref = oracle_mod.cell_fold(fold_spec(premap=expr, n_inputs=n_in), xs, 1, nthreads=oracle_mod.max_threads())
+    close(big, ref)
+    # i32 (exact) through the same path
+    if n_in == 1:
+        xi = rng.integers(-1000, 1000, (rows, L)).astype(np.int32)
+        np.testing.assert_array_equal(to_host(ops.fold(to_dev(xi, cuda), init=3)),
+                                      oracle_mod.cell_fold(fold_spec(dtype="i32", init=3), [xi], 1))
+    torch.cuda.synchronize()
