@@ -1,9 +1,14 @@
 // conv.cuh — convolution geometry shared by the direct and tensor-core paths.
 #pragma once
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace remora {
+
+// cuTensorMapEncodeTiled from the driver (gemm.cu), or null.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 struct ConvGeom {
   int N, C, H, W, K, R, S, OH, OW, stride, pad;

@@ -1,27 +1,36 @@
 // conv_tc.cu — tcgen05 implicit-GEMM convolution for 3x3 / pad 1 / stride 1
 // (the benchmark layer [256,16,64,64] * [32,16,3,3] and the crater CNN's
-// second layer), forward and input gradient.
+// second layer), forward and input gradient, TF32 and 3xTF32.
 //
-// GEMM view of one tile: M = 128-pixel blocks of the output (TH rows x W
-// columns of one image), N = 32 output channels (zero-padded weights when
-// there are fewer), K = input channels, accumulated over the 9 taps.
-// im2col never touches HBM: the loader warps stage the TH+2 input rows of
-// the tile once per channel and write them to shared memory three times,
-// shifted by -1, 0, +1 columns (zero at the image border).  Each copy is an
-// MN-major SWIZZLE_128B_BASE32B operand (32 pixels per 128-byte row, one row
-// per channel), so the A operand of tap (r, s) is copy s starting r*W pixels
-// further — a descriptor offset, no data movement.  Weights stay resident
-// in shared memory for the whole kernel in the same MN-major form.
+// GEMM view of one tile: M = output pixels of TH rows of one image, N = the
+// output channels (16 or 32, zero-padded weights above COUT), K = input
+// channels, accumulated over the 9 taps.  im2col never touches HBM and is
+// never materialised: shared memory holds the tile's TH+2 input rows ONCE,
+// as a K-major "interleaved" UMMA operand (layout SWIZZLE_NONE): 16-byte
+// rows of 4 channels of one pixel, one plane per 4 channels, rows of the
+// image PW = W + 1 positions apart with one zero column between them.
+// Output pixel (i, w) is GEMM row m = i * PW + w, and tap (r, s) reads
+// operand row m + r * PW + s: every tap is the same operand at another
+// 16-byte-aligned start address (a descriptor offset), and the zero column
+// is the left pad of one row and the right pad of the one before.  Rows
+// m with m % PW == W are discarded in the epilogue.
 //
-// Roles (416 threads): warps 0-7 load and shift the input rows (all of a
-// tile's 128-bit loads in flight at once, then generic stores +
-// fence.proxy.async and an mbarrier arrive), warp 12 lane 0 issues
-// 9 * CIN/8 tcgen05.mma (M=128, N=32, K=8) per 128-pixel block into a TMEM
-// accumulator, warps 8-11 read TMEM (32 lanes x 32 channels per warp), add
-// the bias and store NCHW rows (for one channel a warp writes 32 consecutive
-// pixels).  Two TMEM accumulators and up to two input stages overlap load,
-// MMA and epilogue of consecutive tiles.  Input gradient: the same kernel
-// on dY with w'[c][k][r][s] = w[k][c][2-r][2-s].
+// Roles (448 threads):
+//   warp 0 lane 0    TMA: one tiled load per tile of the raw NCHW rows
+//                    [CIN][TH+2][W] (rows outside the image read as zero)
+//   warp 1           TMEM allocation; lane 0 issues the MMAs
+//                    (M = 128, N = NOUT, K = 8) into a TMEM accumulator
+//   warps 2-5        epilogue: TMEM -> registers -> NCHW rows (+ bias)
+//   warps 6-13       transform: raw rows -> the interleaved operand (and,
+//                    for 3xTF32, its hi/lo split)
+// Raw stages, operand stages and two accumulators let TMA, transform, MMA
+// and epilogue of consecutive tiles overlap.  Input gradient: the same
+// kernel on dY with w'[c][k][r][s] = w[k][c][2-r][2-s].
+// 3xTF32: hi = x with the low 13 mantissa bits cleared, lo = x - hi, for
+// activations and weights; the MMA adds hi*hi + hi*lo + lo*hi into one
+// f32 accumulator.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 #include "conv.cuh"
@@ -31,27 +40,43 @@ namespace remora {
 
 namespace {
 
-template <int CIN, int IMG_W, int MT, int STAGES>
+constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
+
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
 struct ConvCfg {
-  static constexpr int PIX = 128 * MT;
-  static constexpr int TH = PIX / IMG_W;
-  static constexpr int ROWS = TH + 2;
-  static constexpr uint32_t LBO = CIN * 128;  // bytes between 32-pixel chunks
-  static constexpr uint32_t COPY_BYTES = (uint32_t)ROWS * IMG_W * CIN * 4;
-  static constexpr uint32_t STAGE_BYTES = 3 * COPY_BYTES;
-  static constexpr uint32_t W_BYTES = 9 * CIN * 128;
-  static constexpr size_t SMEM = W_BYTES + (size_t)STAGES * STAGE_BYTES + 1024;
-  static constexpr uint32_t TMEM_COLS = 2 * MT * 32 <= 64 ? 64 : 128;
-  static constexpr int NVEC = CIN * ROWS * (IMG_W / 4);
-  static constexpr int NV = NVEC / 256;  // 16-byte loads per loader thread per tile
-  static_assert(NVEC % 256 == 0, "loads split evenly over the 256 loader threads");
-  static_assert(PIX % IMG_W == 0, "tile must hold whole rows");
-  static_assert(COPY_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "1 KB aligned operand regions");
-  static_assert(CIN % 8 == 0, "K steps of 8 channels");
+  static constexpr int PW = W + 1;                     // padded row pitch (positions)
+  static constexpr int ROWS = TH + 2;                  // input rows per tile
+  static constexpr int MB = (TH * PW + 127) / 128;     // 128-row M blocks per tile
+  static constexpr int NPOS0 = MB * 128 + 2 * PW + 2;  // positions any tap reads
+  // planes start one 16-byte bank group apart (NPOS = 1 mod 8)
+  static constexpr int NPOS = ((NPOS0 + 7) / 8) * 8 + 1;
+  static constexpr uint32_t PLANE = NPOS * 16;  // bytes of one 4-channel plane
+  static constexpr int NPL = CIN / 4;
+  static constexpr uint32_t A_COPY = NPL * PLANE;
+  static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT3 ? 2 : 1));
+  static constexpr uint32_t RAW_BYTES = CIN * ROWS * W * 4;
+  static constexpr uint32_t RAW_STAGE = align1k(RAW_BYTES);
+  static constexpr uint32_t BPLANE = NOUT * 16;
+  static constexpr uint32_t W_COPY = 9 * NPL * BPLANE;
+  static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT3 ? 2 : 1));
+  static constexpr uint32_t STG_BYTES = align1k(CG * TH * W * 4);  // one channel group of the output tile
+  static constexpr uint32_t OFF_RAW = W_REGION;
+  static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
+  static constexpr uint32_t OFF_STG = OFF_A + A_ST * A_STAGE;
+  static constexpr size_t SMEM = (size_t)OFF_STG + STG_BYTES + 1024;
+  static constexpr int ACC_COLS = MB * NOUT;  // TMEM columns of one accumulator
+  static constexpr int ITEMS = NPL * ROWS * (W / 4);
+  static constexpr int KSTEPS = CIN / 8;
+  static_assert(CIN % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
+  static_assert((CG == 8 || CG == 16 || CG == 32) && NOUT % CG == 0, "channel group");
+  static_assert(CG <= 256 && TH <= 256, "TMA store box dims");
+  static_assert(2 * ACC_COLS <= 512, "two accumulators fit TMEM");
+  static_assert(SMEM <= 232448, "shared memory per block");
+  static_assert(ROWS <= 256 && W <= 256 && CIN <= 256, "TMA box dims");
+  static_assert(PLANE / 16 < 16384 && BPLANE / 16 < 16384, "descriptor offsets");
 };
 
 struct ConvTCParams {
-  const float *x;
   const float *w;
   const float *bias;
   float *y;
@@ -61,217 +86,413 @@ struct ConvTCParams {
   int *err;
 };
 
-// warps 0-7 load, 8-11 epilogue (lane quarters 0-3), 12 MMA + TMEM alloc
-constexpr int kConvThreads = 416;
-constexpr int kLoaders = 256;
+// warp roles
+constexpr int kConvThreads = 448;
+constexpr int kTransformWarp0 = 6, kTransformWarps = 8;
+constexpr int kTransformThreads = kTransformWarps * 32;
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int CIN, int IMG_W, int MT, int STAGES>
-__global__ void __launch_bounds__(kConvThreads, 1) conv3x3_tc_kernel(ConvTCParams p) {
-  using Cf = ConvCfg<CIN, IMG_W, MT, STAGES>;
+__device__ __forceinline__ float tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+// (x, y, z, w) rotated left by r in 0..3
+__device__ __forceinline__ float4 rotl4(float4 v, int r) {
+  if (r & 1) v = make_float4(v.y, v.z, v.w, v.x);
+  if (r & 2) v = make_float4(v.z, v.w, v.x, v.y);
+  return v;
+}
+
+__device__ __forceinline__ float comp(const float4 &v, int j) {
+  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 32 lanes x 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+
+template <int CG>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[CG]) {
+  if constexpr (CG == 32) tc::tmem_ld_32x32b_x32(taddr, r);
+  else if constexpr (CG == 16) tmem_ld_32x32b_x16(taddr, r);
+  else tmem_ld_32x32b_x8(taddr, r);
+}
+
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// TMA tile store from shared memory (no multicast), and its bulk-group
+// completion: .read = the source may be overwritten, plain = the writes
+// are performed.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// K-major interleaved (SWIZZLE_NONE) operand: 8-row groups 128 B apart
+// (SBO), the two 4-element K chunks of one MMA `lbo` bytes apart.
+__device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lbo) {
+  return tc::smem_desc(saddr, lbo, 128, 0);
+}
+
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy,
+                      ConvTCParams p) {
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  uint8_t *wsm = smem;
-  uint8_t *stg = smem + Cf::W_BYTES;
-  __shared__ __align__(8) uint64_t afull[STAGES], aempty[STAGES], tfull[2], tempty[2], drain;
+  __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], afull[A_ST], aempty[A_ST], tfull[2], tempty[2],
+      sfull, sfree, drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ float bias_s[32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t s_base = tc::smem_u32(smem);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      tc::mbar_init(&afull[s], kLoaders);
+    for (int s = 0; s < RAW_ST; ++s) {
+      tc::mbar_init(&rfull[s], 1);
+      tc::mbar_init(&rempty[s], kTransformWarps);
+    }
+    for (int s = 0; s < A_ST; ++s) {
+      tc::mbar_init(&afull[s], kTransformWarps);
       tc::mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
       tc::mbar_init(&tempty[b], 4);
     }
+    tc::mbar_init(&sfull, 4);
+    tc::mbar_init(&sfree, 1);
     tc::mbar_init(&drain, 1);
     abort_flag = 0;
     tc::fence_barrier_init();
   }
   if (threadIdx.x < 32) bias_s[threadIdx.x] = (p.bias && (int)threadIdx.x < p.COUT) ? p.bias[threadIdx.x] : 0.0f;
-  // Resident weights, one MN-major [CIN][32] tile per tap.
-  for (int idx = threadIdx.x; idx < 9 * CIN * 32; idx += kConvThreads) {
-    const int co = idx & 31, ci = (idx >> 5) % CIN, tap = idx / (CIN * 32);
+  // Operand stages start all zero: pad columns and the tail past the last
+  // row are never written again.
+  for (uint32_t off = threadIdx.x * 16; off < A_ST * Cf::A_STAGE; off += kConvThreads * 16)
+    st_shared_v4(s_base + Cf::OFF_A + off, 0.f, 0.f, 0.f, 0.f);
+  // Resident weights: plane (tap, ci/4), row co, 16 bytes of 4 input channels.
+  for (int idx = threadIdx.x; idx < 9 * CIN * NOUT; idx += kConvThreads) {
+    const int co = idx % NOUT, ci = (idx / NOUT) % CIN, tap = idx / (NOUT * CIN);
     const int r = tap / 3, s = tap % 3;
     float v = 0.0f;
     if (co < p.COUT)
       v = p.mode == 0 ? __ldg(p.w + ((co * CIN + ci) * 3 + r) * 3 + s)
                       : __ldg(p.w + ((ci * p.COUT + co) * 3 + (2 - r)) * 3 + (2 - s));
-    const uint32_t off = tap * CIN * 128 + (ci >> 2) * 512 + (ci & 3) * 128 + (((co >> 3) ^ (ci & 3)) << 5) +
-                         (co & 7) * 4;
-    *reinterpret_cast<float *>(wsm + off) = v;
+    const uint32_t off = (uint32_t)(tap * Cf::NPL + (ci >> 2)) * Cf::BPLANE + co * 16 + (ci & 3) * 4;
+    if (SPLIT3) {
+      const float h = tf32_hi(v);
+      *reinterpret_cast<float *>(smem + off) = h;
+      *reinterpret_cast<float *>(smem + Cf::W_COPY + off) = __fsub_rn(v, h);
+    } else {
+      *reinterpret_cast<float *>(smem + off) = v;
+    }
   }
   fence_proxy_async_smem();
-  if (warp == 12) tc::tmem_alloc(&tmem_base, Cf::TMEM_COLS);
+  if (warp == 1) tc::tmem_alloc(&tmem_base, 512);
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const int ntiles = p.N * p.tiles_per_img;
   volatile int *abort_v = &abort_flag;
 
-  if (warp < 8) {
-    // --------------------------------------------- input rows -> 3 copies
-    // All of a tile's loads go to registers first, before the stage is known
-    // to be free, so their latency overlaps the previous tile's MMAs.
-    const uint32_t stg_u = tc::smem_u32(stg);
-    int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const int st = it % STAGES;
-      const uint32_t ph = (it / STAGES) & 1;
-      const int n = t / p.tiles_per_img, oh0 = (t % p.tiles_per_img) * Cf::TH;
-      float4 val[Cf::NV];
-#pragma unroll
-      for (int u = 0; u < Cf::NV; ++u) {
-        const int v = u * kLoaders + warp * 32 + lane;
-        const int q = v % (IMG_W / 4), rl = v / (IMG_W / 4);
-        const int c = rl / Cf::ROWS, r = rl % Cf::ROWS;
-        const int ih = oh0 - 1 + r;
-        val[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ih >= 0 && ih < p.H)
-          val[u] = __ldg(reinterpret_cast<const float4 *>(p.x + (((long long)n * CIN + c) * p.H + ih) * IMG_W) + q);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------- TMA producer
+      tc::prefetch_tmap(&tmx);
+      int it = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int st = it % RAW_ST;
+        const uint32_t ph = (it / RAW_ST) & 1;
+        if (!tc::mbar_wait(&rempty[st], ph ^ 1, abort_v, p.err, 201)) break;
+        const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * TH;
+        tc::mbar_arrive_expect_tx(&rfull[st], Cf::RAW_BYTES);
+        tc::tma_load_3d(&tmx, &rfull[st], smem + Cf::OFF_RAW + st * Cf::RAW_STAGE, 0, h0 - 1, n * CIN);
+        ++issued;
       }
-      if (!tc::mbar_wait(&aempty[st], ph ^ 1, abort_v, p.err, 201)) break;
-      const uint32_t base = stg_u + st * Cf::STAGE_BYTES;
-#pragma unroll
-      for (int u = 0; u < Cf::NV; ++u) {
-        const int v = u * kLoaders + warp * 32 + lane;
-        const int q = v % (IMG_W / 4), rl = v / (IMG_W / 4);
-        const int c = rl / Cf::ROWS, r = rl % Cf::ROWS;
-        float left = __shfl_up_sync(0xffffffffu, val[u].w, 1);
-        float right = __shfl_down_sync(0xffffffffu, val[u].x, 1);
-        if (q == 0) left = 0.0f;
-        if (q == IMG_W / 4 - 1) right = 0.0f;
-        const int px = r * IMG_W + 4 * q;
-        const uint32_t off = (px >> 5) * Cf::LBO + (c >> 2) * 512 + (c & 3) * 128 +
-                             ((((px & 31) >> 3) ^ (c & 3)) << 5) + ((px & 7) ? 16 : 0);
-        st_shared_v4(base + off, left, val[u].x, val[u].y, val[u].z);                       // column - 1
-        st_shared_v4(base + Cf::COPY_BYTES + off, val[u].x, val[u].y, val[u].z, val[u].w);  // column
-        st_shared_v4(base + 2 * Cf::COPY_BYTES + off, val[u].y, val[u].z, val[u].w, right);  // column + 1
-      }
-      fence_proxy_async_smem();
-      tc::mbar_arrive(&afull[st]);
-    }
-  } else if (warp == 12 && lane == 0) {
-    // ---------------------------------------------------------- MMA issue
-    const uint32_t idesc = tc::idesc_tf32(128, 32, 1, 1);
-    const uint32_t stg_u = tc::smem_u32(stg), w_u = tc::smem_u32(wsm);
-    int it = 0;
-    bool issued = false;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const int st = it % STAGES;
-      const uint32_t ph = (it / STAGES) & 1;
-      const int acc = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      if (!tc::mbar_wait(&afull[st], ph, abort_v, p.err, 202)) break;
-      if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort_v, p.err, 203)) break;
-      tc::fence_after_sync();
-      const uint32_t abase = stg_u + st * Cf::STAGE_BYTES;
-#pragma unroll 1
-      for (int mt = 0; mt < MT; ++mt) {
-        const uint32_t d = tbase + acc * (MT * 32) + mt * 32;
-        uint32_t first = 1;
-#pragma unroll
-        for (int tap = 0; tap < 9; ++tap) {
-          const int r = tap / 3, s = tap % 3;
-          const uint32_t a0 = abase + s * Cf::COPY_BYTES + ((mt * 128 + r * IMG_W) >> 5) * Cf::LBO;
-          const uint32_t b0 = w_u + tap * CIN * 128;
-#pragma unroll
-          for (int kk = 0; kk < CIN / 8; ++kk) {
-            tc::mma_tf32(d, tc::desc_mnmajor(a0, Cf::LBO, kk), tc::desc_mnmajor(b0, CIN * 128, kk), idesc,
-                         first ? 0u : 1u);
-            first = 0;
-          }
+      // Do not leave while a TMA copy may still write this CTA's shared
+      // memory: wait (bounded) for the last RAW_ST loads to land.
+      for (int j = issued > RAW_ST ? issued - RAW_ST : 0; j < issued; ++j) {
+        const long long t0 = clock64();
+        while (!tc::mbar_test(&rfull[j % RAW_ST], (j / RAW_ST) & 1) && clock64() - t0 < tc::kWaitCycles) {
         }
       }
-      issued = true;
-      tc::mma_commit(&aempty[st]);
-      tc::mma_commit(&tfull[acc]);
     }
-    if (issued) {
-      tc::mma_commit(&drain);
-      const long long t0 = clock64();
-      while (!tc::mbar_test(&drain, 0) && clock64() - t0 < tc::kWaitCycles) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------ MMA issue
+      const uint32_t idesc = tc::idesc_tf32(128, NOUT, 0, 0);
+      // Descriptors are built once; an operand at byte offset o from a base
+      // is the base descriptor plus o >> 4 (start-address field, no carry:
+      // shared-memory addresses are below 2^18).
+      const uint64_t bd_hi = desc_interleaved(s_base, Cf::BPLANE);
+      const uint64_t bd_lo = desc_interleaved(s_base + Cf::W_COPY, Cf::BPLANE);
+      int it = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        const int st = it % A_ST;
+        const uint32_t ph = (it / A_ST) & 1;
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!tc::mbar_wait(&afull[st], ph, abort_v, p.err, 202)) break;
+        if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort_v, p.err, 203)) break;
+        tc::fence_after_sync();
+        const uint32_t a_hi = s_base + Cf::OFF_A + st * Cf::A_STAGE;
+        const uint64_t ad_hi0 = desc_interleaved(a_hi, Cf::PLANE);
+        const uint64_t ad_lo0 = desc_interleaved(a_hi + Cf::A_COPY, Cf::PLANE);
+#pragma unroll 1
+        for (int mb = 0; mb < Cf::MB; ++mb) {
+          const uint32_t d = tbase + acc * Cf::ACC_COLS + mb * NOUT;
+          const uint64_t ad_hi = ad_hi0 + (uint64_t)(mb * 128), ad_lo = ad_lo0 + (uint64_t)(mb * 128);
+#pragma unroll
+          for (int tap = 0; tap < 9; ++tap) {
+#pragma unroll
+            for (int kk = 0; kk < Cf::KSTEPS; ++kk) {
+              // operand rows start (r * PW + s) positions and 2*kk planes in
+              const uint32_t a_off = (uint32_t)(((tap / 3) * Cf::PW + tap % 3) * 16 + 2 * kk * Cf::PLANE) >> 4;
+              const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + 2 * kk) * Cf::BPLANE) >> 4;
+              tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (tap | kk) != 0);
+              if (SPLIT3) {
+                tc::mma_tf32(d, ad_hi + a_off, bd_lo + b_off, idesc, 1);
+                tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc, 1);
+              }
+            }
+          }
+        }
+        issued = true;
+        tc::mma_commit(&aempty[st]);
+        tc::mma_commit(&tfull[acc]);
+      }
+      if (issued) {
+        tc::mma_commit(&drain);
+        const long long t0 = clock64();
+        while (!tc::mbar_test(&drain, 0) && clock64() - t0 < tc::kWaitCycles) {
+        }
       }
     }
-  } else if (warp >= 8 && warp < 12) {
-    // ----------------------------------------------------------- epilogue
-    const int q = warp - 8;
+  } else if (warp < kTransformWarp0) {
+    // ------------------------------------------------------------ epilogue
+    // Per group of CG output channels: TMEM -> registers (+ bias) -> the
+    // staging tile [CG][TH][W] in shared memory (for one channel the lanes
+    // write consecutive pixels), then one TMA store of the whole group into
+    // NCHW y (rows past H are clipped by the tensor map).  The staging tile
+    // is reused once the store has read it.
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const bool storer = warp == 2 && lane == 0;
+    const uint32_t stg = s_base + Cf::OFF_STG;
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    uint32_t use = 0;  // staging uses so far (one mbarrier phase each)
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aph, abort_v, p.err, 204)) break;
       tc::fence_after_sync();
-      const int n = t / p.tiles_per_img, oh0 = (t % p.tiles_per_img) * Cf::TH;
+      const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * TH;
+      for (int cg = 0; cg < NOUT / CG && cg * CG < p.COUT; ++cg, ++use) {
+        if (!tc::mbar_wait(&sfree, (use & 1) ^ 1, abort_v, p.err, 207)) {
+          ok = false;
+          break;
+        }
 #pragma unroll 1
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t r[32];
-        tc::tmem_ld_32x32b_x32(tbase + acc * (MT * 32) + mt * 32 + ((uint32_t)(q * 32) << 16), r);
-        tc::tmem_ld_wait();
-        const int px = mt * 128 + q * 32 + lane;
-        const int oh = oh0 + px / IMG_W, col = px % IMG_W;
-        if (oh < p.H) {
-          float *yp = p.y + ((long long)n * p.COUT * p.H + oh) * IMG_W + col;
+        for (int mb = 0; mb < Cf::MB; ++mb) {
+          uint32_t r[CG];
+          tmem_ld_cols<CG>(tbase + acc * Cf::ACC_COLS + mb * NOUT + cg * CG + ((uint32_t)(q * 32) << 16), r);
+          tc::tmem_ld_wait();
+          const int m = mb * 128 + q * 32 + lane;
+          const int i = m / Cf::PW, col = m % Cf::PW;
+          if (col < W && i < TH) {
 #pragma unroll
-          for (int co = 0; co < 32; ++co)
-            if (co < p.COUT) yp[(long long)co * p.H * IMG_W] = __fadd_rn(__uint_as_float(r[co]), bias_s[co]);
+            for (int c = 0; c < CG; ++c)
+              st_shared_f32(stg + (uint32_t)((c * TH + i) * W + col) * 4,
+                            __fadd_rn(__uint_as_float(r[c]), bias_s[cg * CG + c]));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&sfull);
+        bool stored = true;
+        if (storer) {
+          stored = tc::mbar_wait(&sfull, use & 1, abort_v, p.err, 208);
+          if (stored) {
+            tma_store_3d(&tmy, stg, 0, h0, n * p.COUT + cg * CG);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+            tc::mbar_arrive(&sfree);
+          }
+        }
+        __syncwarp();
+        if (__any_sync(0xffffffffu, !stored)) {
+          ok = false;
+          break;
         }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
     }
+    if (storer) bulk_wait_group0();  // the last stores have landed in global memory
+  } else {
+    // ----------------------------------------------------------- transform
+    // Item (plane c4, row j, pixel quad qd): four 16-byte reads (channels
+    // 4c4..4c4+3 of pixels 4qd..4qd+3, consecutive lanes take consecutive
+    // quads: conflict-free), a 4x4 transpose in registers, four 16-byte
+    // writes (one pixel's 4 channels each).  Each lane writes its pixels in
+    // an order rotated by (qd / 2) % 4 so the 8 lanes of a shared-memory
+    // phase hit 8 different 16-byte bank groups.
+    const int tt = threadIdx.x - kTransformWarp0 * 32;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const int rs = it % RAW_ST, as = it % A_ST;
+      const uint32_t rph = (it / RAW_ST) & 1, aph = (it / A_ST) & 1;
+      if (!tc::mbar_wait(&rfull[rs], rph, abort_v, p.err, 205)) break;
+      if (!tc::mbar_wait(&aempty[as], aph ^ 1, abort_v, p.err, 206)) break;
+      const uint32_t raw = s_base + Cf::OFF_RAW + rs * Cf::RAW_STAGE;
+      const uint32_t a_hi = s_base + Cf::OFF_A + as * Cf::A_STAGE;
+#pragma unroll 1
+      for (int item = tt; item < Cf::ITEMS; item += kTransformThreads) {
+        const int qd = item % (W / 4), j = (item / (W / 4)) % Cf::ROWS, c4 = item / ((W / 4) * Cf::ROWS);
+        const int rot = (qd >> 1) & 3;
+        float4 v[4];
+#pragma unroll
+        for (int ci = 0; ci < 4; ++ci)
+          v[ci] = rotl4(ld_shared_v4(raw + (uint32_t)(((4 * c4 + ci) * Cf::ROWS + j) * W + 4 * qd) * 4), rot);
+        const uint32_t row0 = (uint32_t)c4 * Cf::PLANE + (uint32_t)(j * Cf::PW + 1 + 4 * qd) * 16;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t dst = a_hi + row0 + (uint32_t)((jj + rot) & 3) * 16;
+          const float x0 = comp(v[0], jj), x1 = comp(v[1], jj), x2 = comp(v[2], jj), x3 = comp(v[3], jj);
+          if (SPLIT3) {
+            const float h0 = tf32_hi(x0), h1 = tf32_hi(x1), h2 = tf32_hi(x2), h3 = tf32_hi(x3);
+            st_shared_v4(dst, h0, h1, h2, h3);
+            st_shared_v4(dst + Cf::A_COPY, __fsub_rn(x0, h0), __fsub_rn(x1, h1), __fsub_rn(x2, h2),
+                         __fsub_rn(x3, h3));
+          } else {
+            st_shared_v4(dst, x0, x1, x2, x3);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&afull[as]);
+        tc::mbar_arrive(&rempty[rs]);
+      }
+    }
   }
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 1) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tbase, Cf::TMEM_COLS);
+    tc::tmem_dealloc(tbase, 512);
   }
 }
 
-template <int CIN, int IMG_W, int MT, int STAGES>
-int launch_conv(const ConvTCParams &p, int sm_count, cudaStream_t stream) {
-  using Cf = ConvCfg<CIN, IMG_W, MT, STAGES>;
-  static bool attr = false;
-  if (!attr) {
-    REMORA_CUDA_TRY(cudaFuncSetAttribute(conv3x3_tc_kernel<CIN, IMG_W, MT, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
-    attr = true;
-  }
-  ConvTCParams q = p;
-  q.tiles_per_img = (p.H + Cf::TH - 1) / Cf::TH;
-  const int ntiles = p.N * q.tiles_per_img;
-  const int grid = std::min(ntiles, sm_count);
-  conv3x3_tc_kernel<CIN, IMG_W, MT, STAGES><<<grid, kConvThreads, Cf::SMEM, stream>>>(q);
-  REMORA_CUDA_TRY(cudaGetLastError());
+// Tiled TMA view of an NCHW activation as {W, H, N*C} (innermost first),
+// box {W, box_rows, box_ch}.
+int encode_activation(const float *x, int N, int C, int H, int W, int box_rows, int box_ch, CUtensorMap *map) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return fail(REMORA_ERR_CUDA, "conv: cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N * C};
+  cuuint64_t strides[2] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4};
+  cuuint32_t box[3] = {(cuuint32_t)W, (cuuint32_t)box_rows, (cuuint32_t)box_ch};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(x), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(REMORA_ERR_CUDA, "conv: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return REMORA_OK;
 }
 
-// Picks the instantiation for (input channels, width); false if none.
-int dispatch(const ConvTCParams &p, int cin, int width, int sm_count, cudaStream_t stream, bool *handled) {
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
+int launch_conv(const float *x, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
+  if (p.COUT % CG != 0 || (reinterpret_cast<uintptr_t>(p.y) & 15) != 0) {
+    *handled = false;  // the store box would cross into the next image's channels
+    return REMORA_OK;
+  }
+  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
+  static bool attr = false;
+  if (!attr) {
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
+    attr = true;
+  }
+  CUtensorMap mx, my;
+  REMORA_TRY(encode_activation(x, p.N, CIN, p.H, W, Cf::ROWS, CIN, &mx));
+  REMORA_TRY(encode_activation(p.y, p.N, p.COUT, p.H, W, TH, CG, &my));
+  ConvTCParams q = p;
+  q.tiles_per_img = (p.H + TH - 1) / TH;
+  const int ntiles = p.N * q.tiles_per_img;
+  const int grid = std::min(ntiles, sm_count);
+  kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, my, q);
+  REMORA_CUDA_TRY(cudaGetLastError());
   *handled = true;
-  if (cin == 16 && width == 64) return launch_conv<16, 64, 2, 2>(p, sm_count, stream);
-  if (cin == 32 && width == 64) return launch_conv<32, 64, 1, 1>(p, sm_count, stream);
-  if (cin == 16 && width == 32) return launch_conv<16, 32, 2, 2>(p, sm_count, stream);
-  if (cin == 32 && width == 32) return launch_conv<32, 32, 1, 2>(p, sm_count, stream);
+  return REMORA_OK;
+}
+
+// Picks the instantiation for (input channels, width, output channels,
+// precision); *handled = false if there is none.
+int dispatch(const float *x, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+             cudaStream_t stream, bool *handled) {
   *handled = false;
+  const int nout = p.COUT <= 16 ? 16 : 32;
+  if (cin == 16 && width == 64 && nout == 32)
+    return split ? launch_conv<16, 64, 8, 32, true, 1, 1, 16>(x, p, sm_count, stream, handled)
+                 : launch_conv<16, 64, 8, 32, false, 1, 2, 16>(x, p, sm_count, stream, handled);
+  if (cin == 32 && width == 64 && nout == 16)
+    return split ? launch_conv<32, 64, 4, 16, true, 1, 1, 8>(x, p, sm_count, stream, handled)
+                 : launch_conv<32, 64, 8, 16, false, 1, 1, 8>(x, p, sm_count, stream, handled);
+  if (cin == 16 && width == 32 && nout == 32)
+    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(x, p, sm_count, stream, handled)
+                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(x, p, sm_count, stream, handled);
+  if (cin == 32 && width == 32 && nout == 16)
+    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 16>(x, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 1, 1, 16>(x, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
 bool shape_ok(const ConvGeom &g, const void *x, int precision) {
-  return precision == REMORA_PREC_TF32 && g.R == 3 && g.S == 3 && g.pad == 1 && g.stride == 1 &&
-         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && g.N > 0 && g.H > 0;
+  return (precision == REMORA_PREC_TF32 || precision == REMORA_PREC_3XTF32) && g.R == 3 && g.S == 3 &&
+         g.pad == 1 && g.stride == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && g.N > 0 && g.H > 0;
 }
 
 }  // namespace
@@ -282,8 +503,8 @@ int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const flo
   if (!shape_ok(g, x, precision) || g.K > 32) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
-  ConvTCParams p{x, w, bias, y, g.N, g.H, g.K, 0, 0, ws->err};
-  return dispatch(p, g.C, g.W, ctx->sm_count, stream, handled);
+  ConvTCParams p{w, bias, y, g.N, g.H, g.K, 0, 0, ws->err};
+  return dispatch(x, p, g.C, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count, stream, handled);
 }
 
 int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const float *w, float *dx, int precision,
@@ -293,8 +514,8 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights
-  ConvTCParams p{dy, w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
-  return dispatch(p, g.K, g.W, ctx->sm_count, stream, handled);
+  ConvTCParams p{w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
+  return dispatch(dy, p, g.K, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count, stream, handled);
 }
 
 int conv_tc_wgrad(RemoraB200Ctx *, const ConvGeom &, const float *, const float *, float *, int, cudaStream_t,

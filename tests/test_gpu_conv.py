@@ -2,9 +2,9 @@
 
 TF32 tensor-core results (3x3 / pad 1 / stride 1 shapes) are held to the
 north_star tolerance for TF32 conv and gradients, rtol 1e-3 + atol
-1e-3 * max|ref|, against the oracle; the direct path (other shapes, and any
-shape at 3xTF32 precision) computes in the oracle's order and is held to
-rtol 1e-5."""
+1e-3 * max|ref|, against the oracle; 3xTF32 (the same tensor-core kernels
+with hi/lo split operands) and the direct path (other shapes, computing in
+the oracle's order) are held to rtol 1e-5 + atol 1e-5 * max|ref|."""
 
 from __future__ import annotations
 
