@@ -37,47 +37,70 @@ __device__ __forceinline__ void pool4(float v0, float v1, float v2, float v3, fl
   *code = m > 0.0f ? (uint8_t)idx : kNoGrad;
 }
 
-// conv3x3 (1 input channel, pad 1) + bias + ReLU + 2x2 max-pool.  One thread
-// per pooled output; each conv output is the oracle's dot over taps in order
-// (f32 ops rounded one by one), then + bias.
-__global__ void __launch_bounds__(256) conv1_relu_pool_kernel(const float *__restrict__ x,
-                                                              const float *__restrict__ w,
-                                                              const float *__restrict__ bias,
-                                                              float *__restrict__ p, uint8_t *__restrict__ code,
-                                                              int B, int K, int H, int W) {
-  const int OH = H / 2, OW = W / 2;
-  const long long total = (long long)B * K * OH * OW;
-  const long long step = (long long)gridDim.x * blockDim.x;
-  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += step) {
-    const int j = (int)(t % OW), i = (int)((t / OW) % OH);
-    const int k = (int)((t / ((long long)OW * OH)) % K);
-    const long long b = t / ((long long)OW * OH * K);
-    const float *xb = x + b * (long long)H * W;
-    float patch[4][4];
+// conv3x3 (1 input channel, pad 1) + bias + ReLU + 2x2 max-pool.  One block
+// per image: the image goes to shared memory once with a zero border, each
+// thread takes four pooled positions, keeps their 4x4 input patches in
+// registers and runs all K channels over them (weights broadcast from shared
+// memory).  Each conv output is the oracle's dot over taps in order (f32 ops
+// rounded one by one), then + bias; for one channel the lanes of a warp
+// write consecutive pooled pixels.
+constexpr int kConv1Threads = 256;
+constexpr int kConv1MaxK = 32;
+
+template <int H, int W>
+__global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const float *__restrict__ x,
+                                                                        const float *__restrict__ w,
+                                                                        const float *__restrict__ bias,
+                                                                        float *__restrict__ p,
+                                                                        uint8_t *__restrict__ code, int K) {
+  constexpr int OH = H / 2, OW = W / 2, NP = OH * OW, PWD = W + 2;
+  constexpr int PER = (NP + kConv1Threads - 1) / kConv1Threads;
+  __shared__ float img[(H + 2) * PWD];
+  __shared__ float ws[kConv1MaxK * 10];
+  const long long b = blockIdx.x;
+  const float *xb = x + b * (long long)H * W;
+  for (int e = threadIdx.x; e < (H + 2) * PWD; e += kConv1Threads) {
+    const int r = e / PWD - 1, c = e % PWD - 1;
+    img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
+  }
+  for (int e = threadIdx.x; e < K * 10; e += kConv1Threads)
+    ws[e] = (e % 10) < 9 ? __ldg(w + (e / 10) * 9 + e % 10) : __ldg(bias + e / 10);
+  __syncthreads();
+  float patch[PER][4][4];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int pos = threadIdx.x + u * kConv1Threads;
+    const int i = pos / OW, j = pos % OW;
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int h = 2 * i + a - 1, q = 2 * j + c - 1;
-        patch[a][c] = (h >= 0 && h < H && q >= 0 && q < W) ? __ldg(xb + h * W + q) : 0.0f;
-      }
+      for (int c = 0; c < 4; ++c) patch[u][a][c] = pos < NP ? img[(2 * i + a) * PWD + 2 * j + c] : 0.0f;
+  }
+  float *pb = p + b * (long long)K * NP;
+  uint8_t *cb = code + b * (long long)K * NP;
+#pragma unroll 1
+  for (int k = 0; k < K; ++k) {
     float wk[9];
 #pragma unroll
-    for (int u = 0; u < 9; ++u) wk[u] = __ldg(w + k * 9 + u);
-    const float bk = __ldg(bias + k);
-    float v[4];
+    for (int t = 0; t < 9; ++t) wk[t] = ws[k * 10 + t];
+    const float bk = ws[k * 10 + 9];
 #pragma unroll
-    for (int di = 0; di < 2; ++di)
+    for (int u = 0; u < PER; ++u) {
+      const int pos = threadIdx.x + u * kConv1Threads;
+      float v[4];
 #pragma unroll
-      for (int dj = 0; dj < 2; ++dj) {
-        float dot = 0.0f;
+      for (int di = 0; di < 2; ++di)
 #pragma unroll
-        for (int a = 0; a < 3; ++a)
+        for (int dj = 0; dj < 2; ++dj) {
+          float dot = 0.0f;
 #pragma unroll
-          for (int c = 0; c < 3; ++c) dot = __fadd_rn(dot, __fmul_rn(patch[di + a][dj + c], wk[a * 3 + c]));
-        v[di * 2 + dj] = __fadd_rn(__fadd_rn(0.0f, dot), bk);
-      }
-    pool4(v[0], v[1], v[2], v[3], p + t, code + t);
+          for (int a = 0; a < 3; ++a)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) dot = __fadd_rn(dot, __fmul_rn(patch[u][di + a][dj + c], wk[a * 3 + c]));
+          v[di * 2 + dj] = __fadd_rn(__fadd_rn(0.0f, dot), bk);
+        }
+      if (pos < NP) pool4(v[0], v[1], v[2], v[3], pb + (long long)k * NP + pos, cb + (long long)k * NP + pos);
+    }
   }
 }
 
@@ -190,62 +213,74 @@ __global__ void __launch_bounds__(256) dense_bwd_kernel(const float *__restrict_
 
 // conv1 weight and bias gradients straight from the pooled gradient: each
 // pooled output with a recorded element (h, q) contributes
-// dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  Block
-// (k, slice) accumulates a slice of the batch into f64 partials
-// part[(k * slices + slice) * 10 + {0..8: taps, 9: bias}].
-__global__ void __launch_bounds__(256) conv1_wgrad_pool_kernel(const float *__restrict__ x,
-                                                               const float *__restrict__ dp,
-                                                               const uint8_t *__restrict__ code,
-                                                               double *__restrict__ part, int B, int K, int H, int W,
-                                                               int slices) {
-  __shared__ double sh[10][256];
-  const int k = blockIdx.x / slices, slice = blockIdx.x % slices;
-  const int OH = H / 2, OW = W / 2;
-  const long long per_img = (long long)OH * OW;
-  const int b0 = (int)((long long)B * slice / slices), b1 = (int)((long long)B * (slice + 1) / slices);
-  double acc[10];
-#pragma unroll
-  for (int u = 0; u < 10; ++u) acc[u] = 0.0;
-  const long long n = (long long)(b1 - b0) * per_img;
-  for (long long t = threadIdx.x; t < n; t += blockDim.x) {
-    const int b = b0 + (int)(t / per_img);
-    const long long pix = t % per_img;
-    const long long idx = ((long long)b * K + k) * per_img + pix;
-    const uint8_t c = code[idx];
-    if (c == kNoGrad) continue;
-    const double g = (double)dp[idx];
-    const int i = (int)(pix / OW), j = (int)(pix % OW);
-    const int h = 2 * i + (c >> 1), q = 2 * j + (c & 1);
-    const float *xb = x + (long long)b * H * W;
-#pragma unroll
-    for (int a = 0; a < 3; ++a)
-#pragma unroll
-      for (int bb = 0; bb < 3; ++bb) {
-        const int hh = h + a - 1, qq = q + bb - 1;
-        if (hh >= 0 && hh < H && qq >= 0 && qq < W) acc[a * 3 + bb] += g * (double)__ldg(xb + hh * W + qq);
-      }
-    acc[9] += g;
+// dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  One block
+// per image (image in shared memory with a zero border); the 16 lanes of a
+// half-warp share a channel k and stride its pooled positions, keep f32
+// sums, and combine them with a fixed shuffle tree into
+// part[(b * K + k) * 10 + {0..8: taps, 9: bias}].  The finish kernel adds
+// the per-image partials in image order in f64.
+template <int H, int W>
+__global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const float *__restrict__ x,
+                                                                         const float *__restrict__ dp,
+                                                                         const uint8_t *__restrict__ code,
+                                                                         float *__restrict__ part, int K) {
+  constexpr int OW = W / 2, NP = (H / 2) * OW, PWD = W + 2;
+  __shared__ float img[(H + 2) * PWD];
+  const long long b = blockIdx.x;
+  const float *xb = x + b * (long long)H * W;
+  for (int e = threadIdx.x; e < (H + 2) * PWD; e += kConv1Threads) {
+    const int r = e / PWD - 1, c = e % PWD - 1;
+    img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
   }
-#pragma unroll
-  for (int u = 0; u < 10; ++u) sh[u][threadIdx.x] = acc[u];
   __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
-    if ((int)threadIdx.x < s)
+  const int lane16 = threadIdx.x & 15;
+  for (int k = threadIdx.x >> 4; k < K; k += kConv1Threads / 16) {
+    float acc[10];
 #pragma unroll
-      for (int u = 0; u < 10; ++u) sh[u][threadIdx.x] += sh[u][threadIdx.x + s];
-    __syncthreads();
+    for (int u = 0; u < 10; ++u) acc[u] = 0.0f;
+    const long long base = (b * K + k) * (long long)NP;
+#pragma unroll 4
+    for (int pos = lane16; pos < NP; pos += 16) {
+      const uint8_t c0 = code[base + pos];
+      if (c0 == kNoGrad) continue;
+      const int c = c0 & 3;  // window index; anything else is not a valid code
+      const float g = dp[base + pos];
+      const int h = 2 * (pos / OW) + (c >> 1), q = 2 * (pos % OW) + (c & 1);
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int bb = 0; bb < 3; ++bb) acc[a * 3 + bb] = fmaf(g, img[(h + a) * PWD + q + bb], acc[a * 3 + bb]);
+      acc[9] += g;
+    }
+#pragma unroll
+    for (int u = 0; u < 10; ++u) {
+      float v = acc[u];
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane16 == 0) part[(b * K + k) * 10 + u] = v;
+    }
   }
-  if (threadIdx.x < 10) part[(long long)blockIdx.x * 10 + threadIdx.x] = sh[threadIdx.x][0];
 }
 
-__global__ void conv1_wgrad_finish_kernel(const double *__restrict__ part, float *__restrict__ dw,
-                                          float *__restrict__ db, int K, int slices) {
-  const int k = blockIdx.x, u = threadIdx.x;
-  if (u >= 10) return;
+// dw1, db1 = sums of the per-image partials, in image order, f64.  One block
+// per output value.
+__global__ void __launch_bounds__(256) conv1_wgrad_finish_kernel(const float *__restrict__ part,
+                                                                 float *__restrict__ dw, float *__restrict__ db,
+                                                                 int B, int K) {
+  __shared__ double sh[256];
+  const int k = blockIdx.x / 10, u = blockIdx.x % 10;
   double s = 0.0;
-  for (int sl = 0; sl < slices; ++sl) s += part[((long long)k * slices + sl) * 10 + u];
-  if (u < 9) dw[k * 9 + u] = (float)s;
-  else db[k] = (float)s;
+  for (int b = threadIdx.x; b < B; b += 256) s += (double)part[((long long)b * K + k) * 10 + u];
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (u < 9) dw[k * 9 + u] = (float)sh[0];
+    else db[k] = (float)sh[0];
+  }
 }
 
 int grid_for(long long n, int sm_count) {
@@ -284,9 +319,13 @@ int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, cons
   for (int d = 0; d < 4; ++d)
     if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "conv1_relu_pool: codes must match pooled shape");
   if (P.numel() == 0) return REMORA_OK;
-  conv1_relu_pool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
-      (const float *)X.data(4), (const float *)Wd.data(4), (const float *)Bd.data(4), (float *)P.data(4),
-      (uint8_t *)C.data(1), B, K, H, W);
+  if (!((H == 64 && W == 64) || (H == 32 && W == 32)) || K > kConv1MaxK)
+    return fail(REMORA_ERR_UNSUPPORTED, "conv1_relu_pool: images of 64x64 or 32x32 and at most %d channels",
+                kConv1MaxK);
+  auto kern = H == 64 ? conv1_relu_pool_kernel<64, 64> : conv1_relu_pool_kernel<32, 32>;
+  kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)Wd.data(4),
+                                                      (const float *)Bd.data(4), (float *)P.data(4),
+                                                      (uint8_t *)C.data(1), K);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }
@@ -395,14 +434,22 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, c
   if (X.sizes[1] != 1 || Dw.sizes[1] != 1 || Dw.sizes[2] != 3 || Dw.sizes[3] != 3 || Db.sizes[0] != K ||
       P.sizes[0] != B || P.sizes[1] != K || P.sizes[2] != H / 2 || P.sizes[3] != W / 2)
     return fail(REMORA_ERR_SHAPE, "conv1_wgrad_pooled: x [B,1,H,W], dpooled/codes [B,K,H/2,W/2], dw [K,1,3,3]");
-  const int slices = std::max(1, std::min(B, (ctx->sm_count * 4 + K - 1) / std::max(K, 1)));
+  if (!((H == 64 && W == 64) || (H == 32 && W == 32)))
+    return fail(REMORA_ERR_UNSUPPORTED, "conv1_wgrad_pooled: images of 64x64 or 32x32");
+  if (K == 0) return REMORA_OK;
+  if (B == 0) {
+    REMORA_CUDA_TRY(cudaMemsetAsync(Dw.data(4), 0, (size_t)K * 9 * 4, (cudaStream_t)stream));
+    REMORA_CUDA_TRY(cudaMemsetAsync(Db.data(4), 0, (size_t)K * 4, (cudaStream_t)stream));
+    return REMORA_OK;
+  }
   Workspace *ws = nullptr;
-  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)K * slices * 10 * sizeof(double) + 256, &ws));
-  double *part = reinterpret_cast<double *>(ws->buf);
-  conv1_wgrad_pool_kernel<<<K * slices, 256, 0, (cudaStream_t)stream>>>(
-      (const float *)X.data(4), (const float *)P.data(4), (const uint8_t *)C.data(1), part, B, K, H, W, slices);
-  conv1_wgrad_finish_kernel<<<K, 32, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4), (float *)Db.data(4), K,
-                                                                slices);
+  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * K * 10 * sizeof(float) + 256, &ws));
+  float *part = reinterpret_cast<float *>(ws->buf);
+  auto kern = H == 64 ? conv1_wgrad_pool_kernel<64, 64> : conv1_wgrad_pool_kernel<32, 32>;
+  kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)P.data(4),
+                                                      (const uint8_t *)C.data(1), part, K);
+  conv1_wgrad_finish_kernel<<<K * 10, 256, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4),
+                                                                      (float *)Db.data(4), B, K);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }

@@ -11,6 +11,8 @@ and every gradient at 5e-2 * max|ref|, the bound of that mode."""
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -96,3 +98,46 @@ def test_cnn_training_reduces_loss_and_graph_replay(cuda):
     a.step(xi, yi)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(to_host(a.params), to_host(b.params))
+
+
+@pytest.mark.parametrize("hw", [64, 32])
+def test_conv1_relu_pool_and_wgrad_layers(cuda, oracle_mod, hw):
+    """The fused first layer against the oracle's conv -> ReLU -> 2x2 max-pool
+    (bit-exact: same rounding order) and its weight/bias gradient against the
+    oracle's conv weight gradient of the unpooled, ReLU-masked cotangent."""
+    import torch
+
+    from remora_b200.cnn import _lib
+    from remora_b200.abi import tensor_descriptor
+    from remora_b200.runtime import context
+
+    lib = _lib()
+    rng = np.random.default_rng(hw)
+    B, K = 5, 16
+    x = rng.standard_normal((B, 1, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((K, 1, 3, 3)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(K) * 0.1).astype(np.float32)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    p = torch.empty((B, K, hw // 2, hw // 2), dtype=torch.float32, device=cuda)
+    code = torch.empty((B, K, hw // 2, hw // 2), dtype=torch.uint8, device=cuda)
+    keep = [tensor_descriptor(t) for t in (xd, wd, bd, p, code)]
+    ctx = context(cuda.index)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    assert lib.remora_b200_conv1_relu_pool(ctx.ptr, *[ctypes.addressof(d) for d in keep], stream) == 0
+    a1 = oracle_mod.conv2d_fwd(x, w, b)
+    a1 = np.where(a1 > 0, a1, np.float32(0))
+    np.testing.assert_array_equal(to_host(p), oracle_mod.maxpool2x2_fwd(a1))
+    # weight gradient from a pooled cotangent
+    dp = rng.standard_normal(p.shape).astype(np.float32)
+    dpd = dev(dp)
+    dw = torch.empty((K, 1, 3, 3), dtype=torch.float32, device=cuda)
+    db = torch.empty(K, dtype=torch.float32, device=cuda)
+    keep2 = [tensor_descriptor(t) for t in (xd, dpd, code, dw, db)]
+    assert lib.remora_b200_conv1_wgrad_pooled(ctx.ptr, *[ctypes.addressof(d) for d in keep2], stream) == 0
+    da = oracle_mod.maxpool2x2_bwd(a1, dp)
+    da = np.where(a1 > 0, da, np.float32(0))
+    ref_w = oracle_mod.conv2d_wgrad(x, da, (K, 1, 3, 3))
+    ref_b = da.astype(np.float64).sum(axis=(0, 2, 3))
+    np.testing.assert_allclose(to_host(dw), ref_w, rtol=1e-5, atol=1e-5 * float(np.abs(ref_w).max()))
+    np.testing.assert_allclose(to_host(db), ref_b, rtol=1e-5, atol=1e-5 * float(np.abs(ref_b).max()))
