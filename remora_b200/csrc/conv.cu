@@ -369,6 +369,9 @@ int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, con
     return fail(REMORA_ERR_SHAPE, "conv wgrad: dy must be [%d, %d, %d, %d]", g.N, g.K, g.OH, g.OW);
   if (DW.numel() == 0) return REMORA_OK;
   bool handled = false;
+  REMORA_TRY(conv_tc_wgrad_bias(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
+                                nullptr, spec->precision, (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
   REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), nullptr,
                            (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
@@ -396,6 +399,9 @@ int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec
   if (DB.sizes[0] != g.K || (DB.strides[0] != 1 && g.K > 1))
     return fail(REMORA_ERR_SHAPE, "conv wgrad: db must be a contiguous [%d]", g.K);
   bool handled = false;
+  REMORA_TRY(conv_tc_wgrad_bias(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
+                                (float *)DB.data(4), spec->precision, (cudaStream_t)stream, &handled));
+  if (handled) return REMORA_OK;
   REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
                            (float *)DB.data(4), (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;

@@ -23,6 +23,12 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
 int conv_tc_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw,
                   int precision, cudaStream_t stream, bool *handled);
 
+// Tensor-core weight gradient (and bias gradient when db is non-null) for
+// 3x3 / pad 1 / stride 1, 16 input channels, at most 32 output channels,
+// W in {32, 64}, TF32 or 3xTF32.
+int conv_tc_wgrad_bias(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw, float *db,
+                       int precision, cudaStream_t stream, bool *handled);
+
 // Register-tiled weight (and bias, when db is non-null) gradient for 3x3 /
 // pad 1 / stride 1 with K even, (K/2)*C threads <= 512, W in {32, 64}.
 int conv_wgrad3x3(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw, float *db,
