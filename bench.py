@@ -587,12 +587,23 @@ def run_ours(args) -> None:
     if sampler:
         sampler.start()
     # keep the GPU busy ~1 s before the timed region so clocks are steady and
-    # the sampler sees the load the timed region runs under
-    t_end = time.time() + (0.0 if args.profile else 1.0)
-    while time.time() < t_end:
+    # the sampler sees the load the timed region runs under.  The number of
+    # passes is agreed over the ranks first: a step may hold a collective
+    # (the CNN's gradient allreduce), so every rank must run the same count.
+    t0 = time.perf_counter()
+    for k in range(wl.rotate):
+        wl.call(k)
+    torch.cuda.synchronize()
+    one = max(time.perf_counter() - t0, 1e-6)
+    soak = 0 if args.profile else int(min(2000, max(1, 1.0 / one)))
+    if world > 1:
+        n = torch.tensor([soak], dtype=torch.int64, device=dev)
+        dist.all_reduce(n, op=dist.ReduceOp.MIN)
+        soak = int(n.item())
+    for _ in range(soak):
         for k in range(wl.rotate):
             wl.call(k)
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
