@@ -710,9 +710,10 @@ def run_ours(args) -> None:
 
 # Per-call DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernel, from the ncu captures summarised under profiles/.
-TRAFFIC: dict[str, float | None] = {"chained": 67_129_856 + 563_200, "row_norms": None,
-                                    "matmul": 337_164_032 + 62_405_376, "matmul_3x": None, "bmm": None, "conv": None,
-                                    "conv_dgrad": None, "conv_wgrad": None, "cnn": None, "cnn_tf32": None}
+TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms": None,
+                                    "matmul": 335_706_368 + 61_118_208, "matmul_3x": None, "bmm": None,
+                                    "conv": 67_154_688 + 75_236_608, "conv_dgrad": None,
+                                    "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
