@@ -40,18 +40,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 32;
+// Tiles are BM x BN_ with BN_ = 256 (the default) or 64 (for N <= 64,
+// e.g. a dense layer with 64 outputs, where a 256-wide tile would compute
+// 4x the needed products).
+constexpr int BM = 128, BK = 32;
 constexpr uint32_t A_BYTES = BM * BK * 4;
-constexpr uint32_t B_BYTES = BN * BK * 4;
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 
-template <bool SPLIT3>
+template <bool SPLIT3, int BN_>
 struct Cfg {
-  static constexpr int STAGES = SPLIT3 ? 2 : 4;
+  static constexpr int BN = BN_;
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr int STAGES = SPLIT3 ? (BN == 256 ? 2 : 4) : (BN == 256 ? 4 : 8);
   static constexpr uint32_t STAGE_BYTES = SPLIT3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory per block");
 };
+// Scratch for K-split partials: at most one 128 x 256 f32 tile per SM.
+constexpr size_t kSplitPartBytes = (size_t)148 * BM * 256 * 4 + 256;
 
 struct GemmParams {
   int M, N, K, batch;
@@ -61,7 +68,29 @@ struct GemmParams {
   long long ldc;
   long long c_bstride;
   int *err;
+  // A launch of few tiles splits each along K into `split` ranges; their
+  // BM x BN partials go to `part` ([tile][split][BM][BN]) and
+  // gemm_split_fixup adds them in split order.  split == 1: no split.
+  int split;
+  float *part;
 };
+
+// Work unit u -> tile, K-block range, and partial slot (-1: the whole tile).
+__device__ __forceinline__ void decode_unit(int u, const GemmParams &p, int &tile, int &kb0, int &kb1,
+                                            int &slot) {
+  if (p.split == 1) {
+    tile = u;
+    kb0 = 0;
+    kb1 = p.kt;
+    slot = -1;
+  } else {
+    const int part = u % p.split;
+    tile = u / p.split;
+    kb0 = (int)((long long)p.kt * part / p.split);
+    kb1 = (int)((long long)p.kt * (part + 1) / p.split);
+    slot = u;
+  }
+}
 
 __device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *bar, uint8_t *dst, int mn, int row0,
                                              int rows, int k0, int b) {
@@ -86,13 +115,15 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, 
   nb = r - mb * p.nt;
 }
 
-template <bool SPLIT3>
+template <bool SPLIT3, int BN_>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
                      GemmParams p) {
-  using C = Cfg<SPLIT3>;
+  using C = Cfg<SPLIT3, BN_>;
   constexpr int STAGES = C::STAGES;
+  constexpr int BN = C::BN;
+  constexpr uint32_t B_BYTES = C::B_BYTES;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
@@ -126,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const int ntiles = p.batch * p.mt * p.nt;
+  const int nunits = ntiles * p.split;
   volatile int *abort_v = &abort_flag;
 
   if (warp == 0 && lane == 0) {
@@ -135,10 +167,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t issued_ph[STAGES];
     bool pending[STAGES];
     for (int i = 0; i < STAGES; ++i) pending[i] = false, issued_ph[i] = 0;
-    for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x) {
+    for (int u = blockIdx.x; u < nunits && !*abort_v; u += gridDim.x) {
+      int t, kb0, kb1, slot;
+      decode_unit(u, p, t, kb0, kb1, slot);
       int b, mb, nb;
       decode_tile(t, p, b, mb, nb);
-      for (int kb = 0; kb < p.kt; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_v, p.err, 101)) goto producer_done;
         uint8_t *sa = smem + (size_t)s * C::STAGE_BYTES;
         tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
@@ -170,13 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph = 0;
     int local = 0;
     bool issued = false;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++local) {
+      int t, kb0, kb1, slot;
+      decode_unit(u, p, t, kb0, kb1, slot);
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!tc::mbar_wait(&tempty[buf], aph ^ 1, abort_v, p.err, 102)) break;
       tc::fence_after_sync();
       const uint32_t d = tbase + buf * BN;
-      for (int kb = 0; kb < p.kt; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 103)) goto mma_done;
         tc::fence_after_sync();
         const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
@@ -185,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t ad = operand_desc(sa, p.a_mn, kk);
           const uint64_t bd = operand_desc(sb, p.b_mn, kk);
-          tc::mma_tf32(d, ad, bd, idesc, (kb | kk) != 0);
+          tc::mma_tf32(d, ad, bd, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           if (SPLIT3) {
             tc::mma_tf32(d, ad, operand_desc(sb + B_BYTES, p.b_mn, kk), idesc, 1);
             tc::mma_tf32(d, operand_desc(sa + A_BYTES, p.a_mn, kk), bd, idesc, 1);
@@ -211,7 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((p.ldc & 3) == 0) &&
                         ((p.c_bstride & 3) == 0);
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++local) {
+      int t, kb0, kb1, slot;
+      decode_unit(u, p, t, kb0, kb1, slot);
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!tc::mbar_wait(&tfull[buf], aph, abort_v, p.err, 104)) break;
@@ -226,7 +264,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_ld_32x32b_x32(tbase + buf * BN + c * 32 + ((uint32_t)(e * 32) << 16), r);
         tc::tmem_ld_wait();
         const int col0 = nb * BN + c * 32;
-        if (row < p.M && col0 < p.N) {
+        if (slot >= 0) {
+          // one K range of a split tile: the whole BM x BN partial, unguarded
+          float4 *dst = reinterpret_cast<float4 *>(p.part + ((long long)slot * BM + e * 32 + lane) * BN + c * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        } else if (row < p.M && col0 < p.N) {
           if (vec_ok && col0 + 32 <= p.N) {
             float4 *dst = reinterpret_cast<float4 *>(crow + col0);
 #pragma unroll
@@ -274,6 +319,27 @@ __global__ void __launch_bounds__(256) prep_operand_kernel(const float *__restri
     } else {
       hi[i] = v;
     }
+  }
+}
+
+// C of every split tile = its partials added in split order (fixed, so the
+// result is deterministic).  One thread per element of C.
+template <int BN>
+__global__ void __launch_bounds__(256) gemm_split_fixup(const float *__restrict__ part, GemmParams p) {
+  const long long per = (long long)BM * BN;
+  const long long n = (long long)p.batch * p.mt * p.nt * per;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const int t = (int)(i / per);
+    const int r = (int)((i % per) / BN), c = (int)(i % BN);
+    int b, mb, nb;
+    decode_tile(t, p, b, mb, nb);
+    const int row = mb * BM + r, col = nb * BN + c;
+    if (row >= p.M || col >= p.N) continue;
+    const float *src = part + ((long long)t * p.split) * per + (long long)r * BN + c;
+    float v = src[0];
+    for (int s = 1; s < p.split; ++s) v = __fadd_rn(v, src[(long long)s * per]);
+    p.C[(long long)b * p.c_bstride + (long long)row * p.ldc + col] = v;
   }
 }
 
@@ -335,9 +401,11 @@ bool tma_ok(const Operand &o, int batch) {
   return (a & 15) == 0 && o.ld > 0 && (o.ld & 3) == 0 && (batch == 1 || ((o.bs & 3) == 0 && o.bs > 0));
 }
 
-template <bool SPLIT3>
+template <bool SPLIT3, int BN>
 int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Operand &Bl, GemmParams p,
                 int sm_count, cudaStream_t stream) {
+  using C = Cfg<SPLIT3, BN>;
+  p.nt = (p.N + BN - 1) / BN;
   CUtensorMap ma, mb, mal, mbl;
   REMORA_TRY(encode_operand(A, BM, p.batch, &ma));
   REMORA_TRY(encode_operand(B, BN, p.batch, &mb));
@@ -348,17 +416,32 @@ int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Ope
     mal = ma;
     mbl = mb;
   }
-  using C = Cfg<SPLIT3>;
   static bool attr_set = false;
   if (!attr_set) {
-    REMORA_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<SPLIT3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<SPLIT3, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::SMEM));
     attr_set = true;
   }
   const int ntiles = p.batch * p.mt * p.nt;
-  const int grid = std::min(ntiles, sm_count);
-  gemm_tf32_kernel<SPLIT3><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
+  // Few tiles and a long K (a dense layer's forward or weight gradient):
+  // split K so that the launch fills the SMs.
+  p.split = 1;
+  if (p.part != nullptr && 2 * ntiles <= sm_count && p.kt >= 8) {
+    const long long cap = (long long)(kSplitPartBytes - 256) / ((long long)BM * BN * 4);
+    int s = std::min(sm_count / ntiles, p.kt / 4);
+    s = (int)std::min<long long>(s, cap / ntiles);
+    if (s >= 2) p.split = s;
+  }
+  const int nunits = ntiles * p.split;
+  const int grid = std::min(nunits, sm_count);
+  gemm_tf32_kernel<SPLIT3, BN><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
   REMORA_CUDA_TRY(cudaGetLastError());
+  if (p.split > 1) {
+    const long long n = (long long)ntiles * BM * BN;
+    gemm_split_fixup<BN><<<(int)std::min<long long>((n + 255) / 256, (long long)sm_count * 16), 256, 0, stream>>>(
+        p.part, p);
+    REMORA_CUDA_TRY(cudaGetLastError());
+  }
   return REMORA_OK;
 }
 
@@ -372,7 +455,7 @@ size_t gemm_workspace_bytes(long long batch, long long M, long long N, long long
   const long long kp = (K + 3) & ~3LL, mp = (M + 3) & ~3LL, np = (N + 3) & ~3LL;
   const size_t a = (size_t)batch * std::max(M * kp, K * mp) * 4 + 256;
   const size_t b = (size_t)batch * std::max(N * kp, K * np) * 4 + 256;
-  return (split ? 2 : 1) * (a + b) + (size_t)batch * M * N * 4 + 1024;
+  return (split ? 2 : 1) * (a + b) + (size_t)batch * M * N * 4 + 1024 + kSplitPartBytes;
 }
 
 // Runs C = A . B with every operand given as a [batch][rows][cols] view.
@@ -473,14 +556,19 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   p.a_mn = a.mn;
   p.b_mn = b.mn;
   p.mt = (int)((M + BM - 1) / BM);
-  p.nt = (int)((N + BN - 1) / BN);
+  p.nt = 0;  // set by launch_gemm for its tile width
   p.kt = (int)((K + BK - 1) / BK);
   p.C = cptr;
   p.ldc = ldc;
   p.c_bstride = cbs;
   p.err = err;
-  if (split) return launch_gemm<true>(a, b, al, bl, p, ctx->sm_count, stream);
-  return launch_gemm<false>(a, b, a, b, p, ctx->sm_count, stream);
+  p.part = take(kSplitPartBytes);  // null when the workspace has no room: no split
+  const bool narrow = N <= 64;
+  if (split)
+    return narrow ? launch_gemm<true, 64>(a, b, al, bl, p, ctx->sm_count, stream)
+                  : launch_gemm<true, 256>(a, b, al, bl, p, ctx->sm_count, stream);
+  return narrow ? launch_gemm<false, 64>(a, b, a, b, p, ctx->sm_count, stream)
+                : launch_gemm<false, 256>(a, b, a, b, p, ctx->sm_count, stream);
 }
 
 }  // namespace remora

@@ -38,7 +38,8 @@ def test_golden_lifted_matmul(cuda):
 
 
 @pytest.mark.parametrize("mnk", [(128, 256, 32), (128, 256, 256), (256, 512, 128), (100, 200, 40), (129, 257, 36),
-                                 (300, 130, 500), (64, 64, 6), (5, 3, 1), (1, 1000, 64)])
+                                 (300, 130, 500), (64, 64, 6), (5, 3, 1), (1, 1000, 64),
+                                 (1000, 300, 3000), (512, 64, 8192), (64, 2048, 1024), (300, 40, 2000)])
 @pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
 def test_gemm_shapes(cuda, oracle_mod, mnk, prec):
     M, N, K = mnk
