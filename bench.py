@@ -502,7 +502,7 @@ class CnnWorkload:
         self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision)
         self.net.step(self.x, self.y)  # eager step: compiles map programs, sizes workspaces
         self.net.capture(self.x, self.y)
-        self.launches_per_call = 16
+        self.launches_per_call = 17  # kernels per step (see profiles/launches_cnn_step.md)
 
     def call(self, k: int) -> None:
         self.net.replay()

@@ -71,6 +71,33 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x,
                                    const RemoraMemRef4 *code, RemoraMemRef4 *dw,
                                    RemoraMemRef1 *db, remora_stream_t stream);
 
+/* Fused second layer: pooled = maxpool2x2(relu(conv3x3_pad1(x, w) + bias))
+   on the tensor cores (TF32 or 3xTF32 per spec), x [B,C,H,W] (C = 16,
+   W = 32), w [K,C,3,3] (K = 17..32), pooled and code [B,K,H/2,W/2]; the
+   full-resolution activation is never written.  Other shapes return
+   REMORA_ERR_UNSUPPORTED. */
+int remora_b200_conv2d_fwd_relu_pool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
+                                     const RemoraMemRef4 *x, const RemoraMemRef4 *w,
+                                     const RemoraMemRef1 *bias, RemoraMemRef4 *pooled,
+                                     RemoraMemRef4 *code, remora_stream_t stream);
+
+/* Input gradient of that layer from the pooled gradient: dx = conv2d_dgrad(
+   unpool(dpooled, code), w) with the unpooled gradient formed on the fly
+   (dpooled/code [B,K,H/2,W/2], K = 32; w [K,C,3,3], C <= 16; dx [B,C,H,W],
+   W = 32). */
+int remora_b200_conv2d_dgrad_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
+                                    const RemoraMemRef4 *dpooled,
+                                    const RemoraMemRef4 *code, const RemoraMemRef4 *w,
+                                    RemoraMemRef4 *dx, remora_stream_t stream);
+
+/* Weight and bias gradients of that layer from the pooled gradient
+   (x [B,16,H,W], W = 32; dpooled/code [B,K,H/2,W/2]; dw [K,16,3,3]; db [K]). */
+int remora_b200_conv2d_wgrad_bias_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
+                                         const RemoraMemRef4 *x,
+                                         const RemoraMemRef4 *dpooled,
+                                         const RemoraMemRef4 *code, RemoraMemRef4 *dw,
+                                         RemoraMemRef1 *db, remora_stream_t stream);
+
 /* Weight gradient plus bias gradient db[k] = sum over n, i, j of dy[n,k,i,j]
    (the fold VJP of remora/ad.py:106-110 for the broadcast bias). */
 int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,

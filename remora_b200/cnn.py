@@ -35,6 +35,9 @@ _CNN_PROTOS = {
     "remora_b200_dense_relu_bwd": [ctypes.c_void_p] * 8,
     "remora_b200_conv1_wgrad_pooled": [ctypes.c_void_p] * 7,
     "remora_b200_conv2d_wgrad_bias": [ctypes.c_void_p] * 7,
+    "remora_b200_conv2d_fwd_relu_pool": [ctypes.c_void_p] * 8,
+    "remora_b200_conv2d_dgrad_unpool": [ctypes.c_void_p] * 7,
+    "remora_b200_conv2d_wgrad_bias_unpool": [ctypes.c_void_p] * 8,
 }
 
 
@@ -96,13 +99,11 @@ class CraterCNN:
         B, f32, u8 = self.B, torch.float32, torch.uint8
         e = lambda *s, dt=f32: torch.empty(s, dtype=dt, device=self.dev)  # noqa: E731
         self.p1, self.code1 = e(B, 16, 32, 32), e(B, 16, 32, 32, dt=u8)
-        self.a2 = e(B, 32, 32, 32)
         self.p2, self.code2 = e(B, 32, 16, 16), e(B, 32, 16, 16, dt=u8)
         self.hpre, self.h = e(B, 64), e(B, 64)
         self.z, self.loss_b, self.dz = e(B), e(B), e(B)
         self.dh = e(B, 64)
         self.dp2 = e(B, 32, 16, 16)
-        self.da2 = e(B, 32, 32, 32)
         self.dp1 = e(B, 16, 32, 32)
         self.zero64 = torch.zeros(64, dtype=f32, device=self.dev)
         self.loss_sum = e(1).reshape(())
@@ -158,9 +159,10 @@ class CraterCNN:
         # forward
         self._check(lib.remora_b200_conv1_relu_pool(c, self._d(images), self._d(p["w1"]), self._d(p["b1"]),
                                                     self._d(self.p1), self._d(self.code1), s), "conv1")
-        self._check(lib.remora_b200_conv2d_fwd(c, ctypes.byref(self.conv_spec), self._d(self.p1), self._d(p["w2"]),
-                                               self._d(p["b2"]), self._d(self.a2), s), "conv2")
-        self._check(lib.remora_b200_relu_pool(c, self._d(self.a2), self._d(self.p2), self._d(self.code2), s), "pool2")
+        # conv2 + bias + ReLU + pool in one kernel: the [B,32,32,32] activation never exists
+        self._check(lib.remora_b200_conv2d_fwd_relu_pool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
+                                                         self._d(p["w2"]), self._d(p["b2"]), self._d(self.p2),
+                                                         self._d(self.code2), s), "conv2")
         p2flat = self.p2.view(B, 8192)
         self._gemm(p2flat, p["w3"].t(), self.hpre)
         self._map(self.prog_bias_relu, [self.hpre, p["b3"].unsqueeze(0).expand(B, 64)], self.h)
@@ -177,13 +179,13 @@ class CraterCNN:
         self._check(lib.remora_b200_array_fold(c, ctypes.byref(fs), self._d(self.dh), 2, self._d(self.zero64),
                                                self._d(g["b3"]), s), "db3")
         self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))
-        self._check(lib.remora_b200_unpool(c, self._d(self.dp2), self._d(self.code2), self._d(self.da2), s),
-                    "unpool2")
-        self._check(lib.remora_b200_conv2d_wgrad_bias(c, ctypes.byref(self.conv_spec), self._d(self.p1),
-                                                      self._d(self.da2), self._d(g["w2"]), self._d(g["b2"]), s),
-                    "conv2 wgrad")
-        self._check(lib.remora_b200_conv2d_dgrad(c, ctypes.byref(self.conv_spec), self._d(self.da2),
-                                                 self._d(p["w2"]), self._d(self.dp1), s), "conv2 dgrad")
+        # conv2 gradients straight from the pooled gradient and the pool codes
+        self._check(lib.remora_b200_conv2d_wgrad_bias_unpool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
+                                                             self._d(self.dp2), self._d(self.code2),
+                                                             self._d(g["w2"]), self._d(g["b2"]), s), "conv2 wgrad")
+        self._check(lib.remora_b200_conv2d_dgrad_unpool(c, ctypes.byref(self.conv_spec), self._d(self.dp2),
+                                                        self._d(self.code2), self._d(p["w2"]), self._d(self.dp1),
+                                                        s), "conv2 dgrad")
         self._check(lib.remora_b200_conv1_wgrad_pooled(c, self._d(images), self._d(self.dp1), self._d(self.code1),
                                                        self._d(g["w1"]), self._d(g["b1"]), s), "conv1 wgrad")
 

@@ -413,4 +413,104 @@ int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec
   return REMORA_OK;
 }
 
+// ---- fused conv + ReLU + 2x2 max-pool (the crater CNN's second layer) ----
+
+namespace {
+// Pooled tensor [N, C, H/2, W/2] (values) or its codes (bytes) for an
+// activation of [N, C, H, W].
+int read_pooled(const void *desc, int N, int C, int H, int W, DescView *out, const char *what) {
+  REMORA_TRY(read_desc(desc, 4, out, what));
+  if (!out->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "%s must be contiguous", what);
+  if (out->sizes[0] != N || out->sizes[1] != C || out->sizes[2] != H / 2 || out->sizes[3] != W / 2)
+    return fail(REMORA_ERR_SHAPE, "%s must be [%d, %d, %d, %d]", what, N, C, H / 2, W / 2);
+  return REMORA_OK;
+}
+}  // namespace
+
+int remora_b200_conv2d_fwd_relu_pool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *x,
+                                     const RemoraMemRef4 *w, const RemoraMemRef1 *bias, RemoraMemRef4 *pooled,
+                                     RemoraMemRef4 *code, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView X, Wd, P, Cd, B;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, x, w, pooled, true, &X, &Wd, &P, &g));
+  g.N = (int)X.sizes[0];
+  g.H = (int)X.sizes[2];
+  g.W = (int)X.sizes[3];
+  if (X.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv: input has %lld channels, weights %d", X.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (g.OH != g.H || g.OW != g.W || (g.H | g.W) & 1)
+    return fail(REMORA_ERR_SHAPE, "conv_relu_pool: needs a same-size conv on an even-sized image");
+  REMORA_TRY(read_pooled(pooled, g.N, g.K, g.H, g.W, &P, "pooled output"));
+  REMORA_TRY(read_pooled(code, g.N, g.K, g.H, g.W, &Cd, "pool codes"));
+  REMORA_TRY(read_desc(bias, 1, &B, "conv bias"));
+  if (B.sizes[0] != g.K || (B.strides[0] != 1 && g.K > 1))
+    return fail(REMORA_ERR_SHAPE, "conv: bias must be a contiguous [%d]", g.K);
+  if (P.numel() == 0) return REMORA_OK;
+  bool handled = false;
+  REMORA_TRY(conv_tc_fwd_relu_pool(ctx, g, (const float *)X.data(4), (const float *)Wd.data(4),
+                                   (const float *)B.data(4), (float *)P.data(4), (uint8_t *)Cd.data(1),
+                                   spec->precision, (cudaStream_t)stream, &handled));
+  if (!handled)
+    return fail(REMORA_ERR_UNSUPPORTED,
+                "conv_relu_pool: only the tensor-core shape 3x3 / pad 1, 16 -> 17..32 channels, width 32");
+  return REMORA_OK;
+}
+
+int remora_b200_conv2d_dgrad_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *dpooled,
+                                    const RemoraMemRef4 *code, const RemoraMemRef4 *w, RemoraMemRef4 *dx,
+                                    remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView DP, Cd, Wd, DX;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, dpooled, w, dx, false, &DP, &Wd, &DX, &g));
+  g.N = (int)DX.sizes[0];
+  g.H = (int)DX.sizes[2];
+  g.W = (int)DX.sizes[3];
+  if (DX.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv dgrad: dx has %lld channels, weights %d", DX.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (g.OH != g.H || g.OW != g.W || (g.H | g.W) & 1)
+    return fail(REMORA_ERR_SHAPE, "conv_dgrad_unpool: needs a same-size conv on an even-sized image");
+  REMORA_TRY(read_pooled(dpooled, g.N, g.K, g.H, g.W, &DP, "pooled gradient"));
+  REMORA_TRY(read_pooled(code, g.N, g.K, g.H, g.W, &Cd, "pool codes"));
+  if (DX.numel() == 0) return REMORA_OK;
+  bool handled = false;
+  REMORA_TRY(conv_tc_dgrad_unpool(ctx, g, (const float *)DP.data(4), (const uint8_t *)Cd.data(1),
+                                  (const float *)Wd.data(4), (float *)DX.data(4), spec->precision,
+                                  (cudaStream_t)stream, &handled));
+  if (!handled)
+    return fail(REMORA_ERR_UNSUPPORTED,
+                "conv_dgrad_unpool: only the tensor-core shape 3x3 / pad 1, 32 -> 16 channels, width 32");
+  return REMORA_OK;
+}
+
+int remora_b200_conv2d_wgrad_bias_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const RemoraMemRef4 *x,
+                                         const RemoraMemRef4 *dpooled, const RemoraMemRef4 *code,
+                                         RemoraMemRef4 *dw, RemoraMemRef1 *db, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView X, DP, Cd, DW, DB;
+  ConvGeom g{};
+  REMORA_TRY(read_conv(spec, x, dw, dpooled, true, &X, &DW, &DP, &g));
+  REMORA_TRY(read_desc(db, 1, &DB, "conv bias gradient"));
+  g.N = (int)X.sizes[0];
+  g.H = (int)X.sizes[2];
+  g.W = (int)X.sizes[3];
+  if (X.sizes[1] != g.C) return fail(REMORA_ERR_SHAPE, "conv wgrad: x has %lld channels, dw %d", X.sizes[1], g.C);
+  REMORA_TRY(finish_geom(&g));
+  if (g.OH != g.H || g.OW != g.W || (g.H | g.W) & 1)
+    return fail(REMORA_ERR_SHAPE, "conv_wgrad_unpool: needs a same-size conv on an even-sized image");
+  REMORA_TRY(read_pooled(dpooled, g.N, g.K, g.H, g.W, &DP, "pooled gradient"));
+  REMORA_TRY(read_pooled(code, g.N, g.K, g.H, g.W, &Cd, "pool codes"));
+  if (DB.sizes[0] != g.K || (DB.strides[0] != 1 && g.K > 1))
+    return fail(REMORA_ERR_SHAPE, "conv wgrad: db must be a contiguous [%d]", g.K);
+  bool handled = false;
+  REMORA_TRY(conv_tc_wgrad_bias_unpool(ctx, g, (const float *)X.data(4), (const float *)DP.data(4),
+                                       (const uint8_t *)Cd.data(1), (float *)DW.data(4), (float *)DB.data(4),
+                                       spec->precision, (cudaStream_t)stream, &handled));
+  if (!handled)
+    return fail(REMORA_ERR_UNSUPPORTED,
+                "conv_wgrad_unpool: only the tensor-core shape 3x3 / pad 1, 16 input channels, width 32");
+  return REMORA_OK;
+}
+
 }  // extern "C"

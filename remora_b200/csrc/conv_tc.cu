@@ -42,7 +42,18 @@ namespace {
 
 constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
+// Fusions of the crater CNN's second layer:
+//   kFuseNone    plain conv (forward or input gradient)
+//   kFusePool    forward whose epilogue applies ReLU + 2x2 max-pool and
+//                stores the pooled values and the pool codes instead of y
+//   kFuseUnpool  input gradient whose input dY is given pooled: the pooled
+//                gradient and the codes are expanded to the full-resolution
+//                dY (the adjoint of ReLU + max-pool) while the transform
+//                builds the operand
+constexpr int kFuseNone = 0, kFusePool = 1, kFuseUnpool = 2;
+constexpr uint8_t kNoGradCode = 255;
+
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
 struct ConvCfg {
   static constexpr int PW = W + 1;                     // padded row pitch (positions)
   static constexpr int ROWS = TH + 2;                  // input rows per tile
@@ -54,8 +65,13 @@ struct ConvCfg {
   static constexpr int NPL = CIN / 4;
   static constexpr uint32_t A_COPY = NPL * PLANE;
   static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT3 ? 2 : 1));
-  static constexpr uint32_t RAW_BYTES = CIN * ROWS * W * 4;
-  static constexpr uint32_t RAW_STAGE = align1k(RAW_BYTES);
+  // kFuseUnpool: the raw stage holds pooled rows: values, then codes
+  static constexpr int PROWS = TH / 2 + 2;
+  static constexpr uint32_t RAW_F32 = FUSE == kFuseUnpool ? CIN * PROWS * (W / 2) * 4 : CIN * ROWS * W * 4;
+  static constexpr uint32_t RAW_CODES = FUSE == kFuseUnpool ? CIN * PROWS * (W / 2) : 0;
+  static constexpr uint32_t RAW_BYTES = RAW_F32 + RAW_CODES;
+  static constexpr uint32_t RAW_CODE_OFF = align1k(RAW_F32);
+  static constexpr uint32_t RAW_STAGE = align1k(RAW_CODE_OFF + RAW_CODES);
   static constexpr uint32_t BPLANE = NOUT * 16;
   static constexpr uint32_t W_COPY = 9 * NPL * BPLANE;
   static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT3 ? 2 : 1));
@@ -63,13 +79,20 @@ struct ConvCfg {
   static constexpr uint32_t OFF_RAW = W_REGION;
   static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
   static constexpr uint32_t OFF_STG = OFF_A + A_ST * A_STAGE;
-  static constexpr size_t SMEM = (size_t)OFF_STG + STG_BYTES + 1024;
+  // kFusePool: pooled values and codes of one channel group
+  static constexpr int PNUM = CG * (TH / 2) * (W / 2);
+  static constexpr uint32_t PST_BYTES = FUSE == kFusePool ? align1k(PNUM * 4) : 0;
+  static constexpr uint32_t CST_BYTES = FUSE == kFusePool ? align1k(PNUM) : 0;
+  static constexpr uint32_t OFF_PST = OFF_STG + STG_BYTES;
+  static constexpr uint32_t OFF_CST = OFF_PST + PST_BYTES;
+  static constexpr size_t SMEM = (size_t)OFF_CST + CST_BYTES + 1024;
   static constexpr int ACC_COLS = MB * NOUT;  // TMEM columns of one accumulator
   static constexpr int ITEMS = NPL * ROWS * (W / 4);
   static constexpr int KSTEPS = CIN / 8;
   static_assert(CIN % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
   static_assert((CG == 8 || CG == 16 || CG == 32) && NOUT % CG == 0, "channel group");
   static_assert(CG <= 256 && TH <= 256, "TMA store box dims");
+  static_assert(FUSE == kFuseNone || (TH % 2 == 0 && W % 32 == 0), "pooled rows are 16-byte TMA boxes");
   static_assert(2 * ACC_COLS <= 512, "two accumulators fit TMEM");
   static_assert(SMEM <= 232448, "shared memory per block");
   static_assert(ROWS <= 256 && W <= 256 && CIN <= 256, "TMA box dims");
@@ -171,15 +194,19 @@ __device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lb
   return tc::smem_desc(saddr, lbo, 128, 0);
 }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy,
+                      const __grid_constant__ CUtensorMap tmx2, const __grid_constant__ CUtensorMap tmy2,
                       ConvTCParams p) {
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
+  // tmx: input rows (kFuseUnpool: pooled gradient values), tmx2: their pool
+  // codes (kFuseUnpool only); tmy: output (kFusePool: pooled values), tmy2:
+  // output pool codes (kFusePool only)
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], afull[A_ST], aempty[A_ST], tfull[2], tempty[2],
-      sfull, sfree, drain;
+      sfull, sfree, pfull, drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ float bias_s[32];
@@ -201,6 +228,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     tc::mbar_init(&sfull, 4);
     tc::mbar_init(&sfree, 1);
+    tc::mbar_init(&pfull, 4);
     tc::mbar_init(&drain, 1);
     abort_flag = 0;
     tc::fence_barrier_init();
@@ -246,8 +274,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const uint32_t ph = (it / RAW_ST) & 1;
         if (!tc::mbar_wait(&rempty[st], ph ^ 1, abort_v, p.err, 201)) break;
         const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * TH;
+        uint8_t *raw = smem + Cf::OFF_RAW + st * Cf::RAW_STAGE;
         tc::mbar_arrive_expect_tx(&rfull[st], Cf::RAW_BYTES);
-        tc::tma_load_3d(&tmx, &rfull[st], smem + Cf::OFF_RAW + st * Cf::RAW_STAGE, 0, h0 - 1, n * CIN);
+        if (FUSE == kFuseUnpool) {
+          // pooled rows h0/2 - 1 .. h0/2 + TH/2 cover input rows h0 - 1 .. h0 + TH
+          tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 / 2 - 1, n * CIN);
+          tc::tma_load_3d(&tmx2, &rfull[st], raw + Cf::RAW_CODE_OFF, 0, h0 / 2 - 1, n * CIN);
+        } else {
+          tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, n * CIN);
+        }
         ++issued;
       }
       // Do not leave while a TMA copy may still write this CTA's shared
@@ -352,7 +387,44 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&sfull);
         bool stored = true;
-        if (storer) {
+        if (FUSE == kFusePool) {
+          // ReLU + 2x2 max-pool of the staged group: every epilogue thread
+          // waits for the whole tile, pools a share of it into the pooled
+          // staging tiles, and the storer sends both with TMA.
+          stored = tc::mbar_wait(&sfull, use & 1, abort_v, p.err, 208);
+          if (stored) {
+            const uint32_t pst = s_base + Cf::OFF_PST, cst = s_base + Cf::OFF_CST;
+            for (int e = (warp - 2) * 32 + lane; e < Cf::PNUM; e += 128) {
+              const int c = e / ((TH / 2) * (W / 2)), rem = e % ((TH / 2) * (W / 2));
+              const int pi = rem / (W / 2), pj = rem % (W / 2);
+              const uint32_t a0 = stg + (uint32_t)((c * TH + 2 * pi) * W + 2 * pj) * 4;
+              float v0, v1, v2, v3;
+              asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v0), "=f"(v1) : "r"(a0) : "memory");
+              asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v2), "=f"(v3) : "r"(a0 + W * 4) : "memory");
+              float m = v0;
+              uint32_t idx = 0;
+              if (v1 > m) m = v1, idx = 1;
+              if (v2 > m) m = v2, idx = 2;
+              if (v3 > m) m = v3, idx = 3;
+              st_shared_f32(pst + (uint32_t)e * 4, m > 0.0f ? m : 0.0f);
+              asm volatile("st.shared.u8 [%0], %1;" ::"r"(cst + (uint32_t)e), "r"(m > 0.0f ? idx : (uint32_t)kNoGradCode)
+                           : "memory");
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&pfull);
+            if (storer) {
+              stored = tc::mbar_wait(&pfull, use & 1, abort_v, p.err, 209);
+              if (stored) {
+                tma_store_3d(&tmy, pst, 0, h0 / 2, n * p.COUT + cg * CG);
+                tma_store_3d(&tmy2, cst, 0, h0 / 2, n * p.COUT + cg * CG);
+                bulk_commit_group();
+                bulk_wait_group_read0();
+                tc::mbar_arrive(&sfree);
+              }
+            }
+          }
+        } else if (storer) {
           stored = tc::mbar_wait(&sfull, use & 1, abort_v, p.err, 208);
           if (stored) {
             tma_store_3d(&tmy, stg, 0, h0, n * p.COUT + cg * CG);
@@ -394,9 +466,29 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const int qd = item % (W / 4), j = (item / (W / 4)) % Cf::ROWS, c4 = item / ((W / 4) * Cf::ROWS);
         const int rot = (qd >> 1) & 3;
         float4 v[4];
+        if (FUSE == kFuseUnpool) {
+          // input row h0 - 1 + j sits in pooled row (j + 1) / 2 of the stage
+          // with row parity (j + 1) & 1; pixels 4qd .. 4qd+3 in pooled
+          // columns 2qd, 2qd + 1.  The pooled gradient goes to the recorded
+          // window element, the others get 0.
+          const int pj = (j + 1) >> 1, hp = ((j + 1) & 1) * 2;
 #pragma unroll
-        for (int ci = 0; ci < 4; ++ci)
-          v[ci] = rotl4(ld_shared_v4(raw + (uint32_t)(((4 * c4 + ci) * Cf::ROWS + j) * W + 4 * qd) * 4), rot);
+          for (int ci = 0; ci < 4; ++ci) {
+            const uint32_t e = (uint32_t)(((4 * c4 + ci) * Cf::PROWS + pj) * (W / 2) + 2 * qd);
+            float2 g;
+            uint32_t cw;
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(g.x), "=f"(g.y) : "r"(raw + e * 4) : "memory");
+            asm volatile("ld.shared.u16 %0, [%1];" : "=r"(cw) : "r"(raw + Cf::RAW_CODE_OFF + e) : "memory");
+            const uint32_t c0 = cw & 0xFF, c1 = (cw >> 8) & 0xFF;
+            v[ci] = rotl4(make_float4(c0 == (uint32_t)hp ? g.x : 0.0f, c0 == (uint32_t)(hp + 1) ? g.x : 0.0f,
+                                      c1 == (uint32_t)hp ? g.y : 0.0f, c1 == (uint32_t)(hp + 1) ? g.y : 0.0f),
+                          rot);
+          }
+        } else {
+#pragma unroll
+          for (int ci = 0; ci < 4; ++ci)
+            v[ci] = rotl4(ld_shared_v4(raw + (uint32_t)(((4 * c4 + ci) * Cf::ROWS + j) * W + 4 * qd) * 4), rot);
+        }
         const uint32_t row0 = (uint32_t)c4 * Cf::PLANE + (uint32_t)(j * Cf::PW + 1 + 4 * qd) * 16;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
@@ -428,42 +520,68 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 }
 
 // Tiled TMA view of an NCHW activation as {W, H, N*C} (innermost first),
-// box {W, box_rows, box_ch}.
-int encode_activation(const float *x, int N, int C, int H, int W, int box_rows, int box_ch, CUtensorMap *map) {
+// box {W, box_rows, box_ch}; f32, or u8 for pool codes.
+int encode_activation(const void *x, int N, int C, int H, int W, int box_rows, int box_ch, CUtensorMap *map,
+                      bool codes = false) {
   auto fn = tensor_map_encoder();
   if (!fn) return fail(REMORA_ERR_CUDA, "conv: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t es = codes ? 1 : 4;
   cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N * C};
-  cuuint64_t strides[2] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4};
+  cuuint64_t strides[2] = {(cuuint64_t)W * es, (cuuint64_t)H * W * es};
   cuuint32_t box[3] = {(cuuint32_t)W, (cuuint32_t)box_rows, (cuuint32_t)box_ch};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(x), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, codes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                  const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(REMORA_ERR_CUDA, "conv: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return REMORA_OK;
 }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG>
-int launch_conv(const float *x, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
-  if (p.COUT % CG != 0 || (reinterpret_cast<uintptr_t>(p.y) & 15) != 0) {
-    *handled = false;  // the store box would cross into the next image's channels
+// Operands of one launch: x (kFuseUnpool: the pooled gradient) and its
+// codes; y (kFusePool: the pooled output) and its codes.
+struct ConvIO {
+  const float *x;
+  const uint8_t *x_codes;
+  float *y;
+  uint8_t *y_codes;
+};
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
+int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
+  if (p.COUT % CG != 0 || !aligned16(io.y) || !aligned16(io.x) ||
+      (FUSE == kFusePool && !aligned16(io.y_codes)) || (FUSE == kFuseUnpool && !aligned16(io.x_codes))) {
+    *handled = false;  // a store box would cross into the next image's channels, or TMA cannot address it
     return REMORA_OK;
   }
-  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG>;
+  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
   static bool attr = false;
   if (!attr) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
     attr = true;
   }
-  CUtensorMap mx, my;
-  REMORA_TRY(encode_activation(x, p.N, CIN, p.H, W, Cf::ROWS, CIN, &mx));
-  REMORA_TRY(encode_activation(p.y, p.N, p.COUT, p.H, W, TH, CG, &my));
+  CUtensorMap mx, my, mx2, my2;
+  if (FUSE == kFuseUnpool) {
+    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx));
+    REMORA_TRY(encode_activation(io.x_codes, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx2, true));
+  } else {
+    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H, W, Cf::ROWS, CIN, &mx));
+    mx2 = mx;
+  }
+  if (FUSE == kFusePool) {
+    REMORA_TRY(encode_activation(io.y, p.N, p.COUT, p.H / 2, W / 2, TH / 2, CG, &my));
+    REMORA_TRY(encode_activation(io.y_codes, p.N, p.COUT, p.H / 2, W / 2, TH / 2, CG, &my2, true));
+  } else {
+    REMORA_TRY(encode_activation(io.y, p.N, p.COUT, p.H, W, TH, CG, &my));
+    my2 = my;
+  }
   ConvTCParams q = p;
   q.tiles_per_img = (p.H + TH - 1) / TH;
   const int ntiles = p.N * q.tiles_per_img;
   const int grid = std::min(ntiles, sm_count);
-  kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, my, q);
+  kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, my, mx2, my2, q);
   REMORA_CUDA_TRY(cudaGetLastError());
   *handled = true;
   return REMORA_OK;
@@ -471,22 +589,42 @@ int launch_conv(const float *x, const ConvTCParams &p, int sm_count, cudaStream_
 
 // Picks the instantiation for (input channels, width, output channels,
 // precision); *handled = false if there is none.
-int dispatch(const float *x, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
              cudaStream_t stream, bool *handled) {
   *handled = false;
   const int nout = p.COUT <= 16 ? 16 : 32;
   if (cin == 16 && width == 64 && nout == 32)
-    return split ? launch_conv<16, 64, 8, 32, true, 1, 1, 16>(x, p, sm_count, stream, handled)
-                 : launch_conv<16, 64, 8, 32, false, 1, 2, 16>(x, p, sm_count, stream, handled);
+    return split ? launch_conv<16, 64, 8, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
+                 : launch_conv<16, 64, 8, 32, false, 1, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 64 && nout == 16)
-    return split ? launch_conv<32, 64, 4, 16, true, 1, 1, 8>(x, p, sm_count, stream, handled)
-                 : launch_conv<32, 64, 8, 16, false, 1, 1, 8>(x, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 64, 4, 16, true, 1, 1, 8>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 64, 8, 16, false, 1, 1, 8>(io, p, sm_count, stream, handled);
   if (cin == 16 && width == 32 && nout == 32)
-    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(x, p, sm_count, stream, handled)
-                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(x, p, sm_count, stream, handled);
+    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
+                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 32 && nout == 16)
-    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 16>(x, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 1, 1, 16>(x, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 16>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 1, 1, 16>(io, p, sm_count, stream, handled);
+  return REMORA_OK;
+}
+
+// The fused forms of the crater CNN's second layer (16 -> 32 channels on
+// 32 x 32 images and its input gradient).
+int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+                  cudaStream_t stream, bool *handled) {
+  *handled = false;
+  if (cin == 16 && width == 32 && p.COUT > 16 && p.COUT <= 32 && p.H % 2 == 0)
+    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
+                 : launch_conv<16, 32, 16, 32, false, 1, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
+  return REMORA_OK;
+}
+
+int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+                    cudaStream_t stream, bool *handled) {
+  *handled = false;
+  if (cin == 32 && width == 32 && p.COUT <= 16 && p.H % 2 == 0)
+    return split ? launch_conv<32, 32, 8, 16, true, 2, 1, 16, kFuseUnpool>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 2, 1, 16, kFuseUnpool>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
@@ -504,7 +642,30 @@ int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const flo
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, y, g.N, g.H, g.K, 0, 0, ws->err};
-  return dispatch(x, p, g.C, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count, stream, handled);
+  return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
+                  stream, handled);
+}
+
+int conv_tc_fwd_relu_pool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *w, const float *bias,
+                          float *pooled, uint8_t *codes, int precision, cudaStream_t stream, bool *handled) {
+  *handled = false;
+  if (!shape_ok(g, x, precision) || g.K > 32) return REMORA_OK;
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
+  ConvTCParams p{w, bias, pooled, g.N, g.H, g.K, 0, 0, ws->err};
+  return dispatch_pool(ConvIO{x, nullptr, pooled, codes}, p, g.C, g.W, precision == REMORA_PREC_3XTF32,
+                       ctx->sm_count, stream, handled);
+}
+
+int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpooled, const uint8_t *codes,
+                         const float *w, float *dx, int precision, cudaStream_t stream, bool *handled) {
+  *handled = false;
+  if (!shape_ok(g, dpooled, precision) || g.C > 32) return REMORA_OK;
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
+  ConvTCParams p{w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
+  return dispatch_unpool(ConvIO{dpooled, codes, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32,
+                         ctx->sm_count, stream, handled);
 }
 
 int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const float *w, float *dx, int precision,
@@ -515,7 +676,8 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights
   ConvTCParams p{w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
-  return dispatch(dy, p, g.K, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count, stream, handled);
+  return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
+                  stream, handled);
 }
 
 int conv_tc_wgrad(RemoraB200Ctx *, const ConvGeom &, const float *, const float *, float *, int, cudaStream_t,

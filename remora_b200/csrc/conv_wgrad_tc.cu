@@ -49,7 +49,10 @@ constexpr int kWgThreads = 448;
 constexpr int kWgTransformWarp0 = 6, kWgTransformWarps = 8;
 constexpr int kWgTransformThreads = kWgTransformWarps * 32;
 
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST>
+// UNPOOL: dy is given as a pooled gradient and its 2x2 max-pool codes
+// ([COUT][H/2][W/2] each); the transform expands it (the pooled value goes
+// to the recorded window element, the others are 0).
+template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL = false>
 struct WgCfg {
   static constexpr int CPR = W / 4;     // 4-pixel chunks per image row
   static constexpr int NCH = R * CPR;   // chunks per tile
@@ -59,14 +62,17 @@ struct WgCfg {
   static constexpr uint32_t B_BYTES = NCH * B_CH;
   static constexpr uint32_t OP_STAGE = wg_align1k(A_BYTES + B_BYTES * (SPLIT3 ? 2 : 1));
   static constexpr uint32_t RAWX = kWgCin * (R + 2) * W * 4;
-  static constexpr uint32_t RAWD = 32 * R * W * 4;
+  static constexpr uint32_t RAWD = UNPOOL ? 32 * (R / 2) * (W / 2) * 4 : 32 * R * W * 4;
+  static constexpr uint32_t RAWC = UNPOOL ? 32 * (R / 2) * (W / 2) : 0;  // codes
   static constexpr uint32_t RAWX_AL = wg_align1k(RAWX);  // dy raw rows start here
-  static constexpr uint32_t RAW_STAGE = RAWX_AL + wg_align1k(RAWD);
+  static constexpr uint32_t RAWC_OFF = RAWX_AL + wg_align1k(RAWD);
+  static constexpr uint32_t RAW_STAGE = RAWC_OFF + wg_align1k(RAWC);
   static constexpr uint32_t OFF_RAW = OP_ST * OP_STAGE;
   static constexpr size_t SMEM = (size_t)OFF_RAW + (size_t)RAW_ST * RAW_STAGE + 1024;
   static constexpr int ITEMS_A = 32 * NCH;
   static constexpr int ITEMS_B = 3 * kWgCin * NCH;
   static_assert(NCH % 2 == 0, "K steps of 8 pixels");
+  static_assert(!UNPOOL || (R % 2 == 0 && W % 32 == 0), "pooled rows are 16-byte TMA boxes");
   static_assert(SMEM <= 230 * 1024, "shared memory per block");
   static_assert(kWgRowsA * kWgRowsB * 4 <= OP_STAGE, "the epilogue reuses an operand stage");
   static_assert(A_CH / 16 < 16384 && B_CH / 16 < 16384, "descriptor offsets");
@@ -110,11 +116,12 @@ __device__ __forceinline__ void wg_put(uint32_t hi, uint32_t lo, float4 v) {
   }
 }
 
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST>
+template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL>
 __global__ void __launch_bounds__(kWgThreads, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmd,
-                         WgParams p) {
-  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST>;
+                         const __grid_constant__ CUtensorMap tmc, WgParams p) {
+  // tmd: dy rows, or with UNPOOL the pooled gradient; tmc: its codes
+  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], ofull[OP_ST], oempty[OP_ST], drain, efull;
@@ -123,7 +130,8 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t s_base = tc::smem_u32(smem);
-  const uint32_t raw_bytes = Cf::RAWX + (uint32_t)p.COUT * R * W * 4;
+  const uint32_t raw_bytes = UNPOOL ? Cf::RAWX + (uint32_t)p.COUT * (R / 2) * (W / 2) * 5
+                                    : Cf::RAWX + (uint32_t)p.COUT * R * W * 4;
   if (threadIdx.x == 0) {
     for (int s = 0; s < RAW_ST; ++s) {
       tc::mbar_init(&rfull[s], 1);
@@ -167,7 +175,12 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         uint8_t *raw = smem + Cf::OFF_RAW + st * Cf::RAW_STAGE;
         tc::mbar_arrive_expect_tx(&rfull[st], raw_bytes);
         tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, n * kWgCin);
-        tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0, n * p.COUT);
+        if (UNPOOL) {
+          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0 / 2, n * p.COUT);
+          tc::tma_load_3d(&tmc, &rfull[st], raw + Cf::RAWC_OFF, 0, h0 / 2, n * p.COUT);
+        } else {
+          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0, n * p.COUT);
+        }
         ++issued;
       }
       for (int j = issued > RAW_ST ? issued - RAW_ST : 0; j < issued; ++j) {
@@ -256,7 +269,21 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         const int kc = item % Cf::NCH, co = item / Cf::NCH;
         if (co >= p.COUT) continue;
         const int hr = kc / Cf::CPR, w0 = 4 * (kc % Cf::CPR);
-        const float4 v = wg_ld4(rawd + (uint32_t)((co * R + hr) * W + w0) * 4);
+        float4 v;
+        if (UNPOOL) {
+          // row hr of the tile: pooled row hr / 2, parity hr & 1; pixels
+          // w0 .. w0+3 in pooled columns w0/2, w0/2 + 1
+          const uint32_t e = (uint32_t)((co * (R / 2) + hr / 2) * (W / 2) + w0 / 2);
+          float2 g;
+          uint32_t cw;
+          asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(g.x), "=f"(g.y) : "r"(rawd + e * 4) : "memory");
+          asm volatile("ld.shared.u16 %0, [%1];" : "=r"(cw) : "r"(rawd - Cf::RAWX_AL + Cf::RAWC_OFF + e) : "memory");
+          const uint32_t hp = (uint32_t)(hr & 1) * 2, c0 = cw & 0xFF, c1 = (cw >> 8) & 0xFF;
+          v = make_float4(c0 == hp ? g.x : 0.0f, c0 == hp + 1 ? g.x : 0.0f, c1 == hp ? g.y : 0.0f,
+                          c1 == hp + 1 ? g.y : 0.0f);
+        } else {
+          v = wg_ld4(rawd + (uint32_t)((co * R + hr) * W + w0) * 4);
+        }
         const uint32_t dst = a0 + kc * Cf::A_CH + co * 16;
         wg_put<SPLIT3>(dst, dst + 32 * 16, v);
       }
@@ -304,40 +331,49 @@ __global__ void wgrad_tc_finish(const float *__restrict__ part, int nblocks, int
   }
 }
 
-int wg_encode(const float *x, int N, int C, int H, int W, int box_rows, int box_ch, CUtensorMap *map) {
+int wg_encode(const void *x, int N, int C, int H, int W, int box_rows, int box_ch, CUtensorMap *map,
+              bool codes = false) {
   auto fn = tensor_map_encoder();
   if (!fn) return fail(REMORA_ERR_CUDA, "conv wgrad: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t es = codes ? 1 : 4;
   cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N * C};
-  cuuint64_t strides[2] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 4};
+  cuuint64_t strides[2] = {(cuuint64_t)W * es, (cuuint64_t)H * W * es};
   cuuint32_t box[3] = {(cuuint32_t)W, (cuuint32_t)box_rows, (cuuint32_t)box_ch};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(x), dims, strides, box, estr,
+  CUresult r = fn(map, codes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                  const_cast<void *>(x), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(REMORA_ERR_CUDA, "conv wgrad: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return REMORA_OK;
 }
 
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST>
-int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw, float *db,
-                 cudaStream_t stream) {
-  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST>;
-  auto kern = conv_wgrad_tc_kernel<W, R, SPLIT3, RAW_ST, OP_ST>;
+template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL = false>
+int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, const uint8_t *codes,
+                 float *dw, float *db, cudaStream_t stream) {
+  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
+  auto kern = conv_wgrad_tc_kernel<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
   static bool attr = false;
   if (!attr) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
     attr = true;
   }
-  CUtensorMap mx, md;
+  CUtensorMap mx, md, mc;
   REMORA_TRY(wg_encode(x, g.N, kWgCin, g.H, W, R + 2, kWgCin, &mx));
-  REMORA_TRY(wg_encode(dy, g.N, g.K, g.H, W, R, g.K, &md));
+  if (UNPOOL) {
+    REMORA_TRY(wg_encode(dy, g.N, g.K, g.H / 2, W / 2, R / 2, g.K, &md));
+    REMORA_TRY(wg_encode(codes, g.N, g.K, g.H / 2, W / 2, R / 2, g.K, &mc, true));
+  } else {
+    REMORA_TRY(wg_encode(dy, g.N, g.K, g.H, W, R, g.K, &md));
+    mc = md;
+  }
   const int tiles_per_img = (g.H + R - 1) / R;
   const int ntiles = g.N * tiles_per_img;
   const int grid = std::min(ntiles, ctx->sm_count);
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, (size_t)grid * 32 * kWgOutCols * sizeof(float) + 256, &ws));
   WgParams p{g.N, g.H, g.K, tiles_per_img, reinterpret_cast<float *>(ws->buf), ws->err};
-  kern<<<grid, kWgThreads, Cf::SMEM, stream>>>(mx, md, p);
+  kern<<<grid, kWgThreads, Cf::SMEM, stream>>>(mx, md, mc, p);
   const int outs = g.K * kWgOutCols;
   wgrad_tc_finish<<<(outs + 255) / 256, 256, 0, stream>>>(p.part, grid, g.K, dw, db);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -356,13 +392,29 @@ int conv_tc_wgrad_bias(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, co
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(dy) & 15)) return REMORA_OK;
   *handled = true;
   if (g.W == 32)
-    return split ? launch_wgrad<32, 2, true, 1, 2>(ctx, g, x, dy, dw, db, stream)
-                 : launch_wgrad<32, 2, false, 2, 2>(ctx, g, x, dy, dw, db, stream);
+    return split ? launch_wgrad<32, 2, true, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+                 : launch_wgrad<32, 2, false, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
   if (g.W == 64)
-    return split ? launch_wgrad<64, 1, true, 1, 2>(ctx, g, x, dy, dw, db, stream)
-                 : launch_wgrad<64, 1, false, 2, 2>(ctx, g, x, dy, dw, db, stream);
+    return split ? launch_wgrad<64, 1, true, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+                 : launch_wgrad<64, 1, false, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
   *handled = false;
   return REMORA_OK;
+}
+
+int conv_tc_wgrad_bias_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dpooled,
+                              const uint8_t *codes, float *dw, float *db, int precision, cudaStream_t stream,
+                              bool *handled) {
+  *handled = false;
+  const bool split = precision == REMORA_PREC_3XTF32;
+  if (!(precision == REMORA_PREC_TF32 || split) || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
+      g.C != kWgCin || g.K < 1 || g.K > 32 || g.N < 1 || g.H < 2 || g.H % 2 || g.OH != g.H || g.OW != g.W ||
+      g.W != 32)
+    return REMORA_OK;
+  const auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!a16(x) || !a16(dpooled) || !a16(codes)) return REMORA_OK;
+  *handled = true;
+  return split ? launch_wgrad<32, 2, true, 1, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream)
+               : launch_wgrad<32, 2, false, 2, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream);
 }
 
 }  // namespace remora

@@ -141,3 +141,61 @@ def test_conv1_relu_pool_and_wgrad_layers(cuda, oracle_mod, hw):
     ref_b = da.astype(np.float64).sum(axis=(0, 2, 3))
     np.testing.assert_allclose(to_host(dw), ref_w, rtol=1e-5, atol=1e-5 * float(np.abs(ref_w).max()))
     np.testing.assert_allclose(to_host(db), ref_b, rtol=1e-5, atol=1e-5 * float(np.abs(ref_b).max()))
+
+
+@pytest.mark.parametrize("precision", ["tf32", "3xtf32"])
+def test_fused_conv2_pool_matches_unfused(cuda, precision):
+    """conv2 + ReLU + max-pool in one kernel, and the conv2 gradients taken
+    straight from the pooled gradient, give bit for bit what the separate
+    conv2d / relu_pool / unpool calls give."""
+    import torch
+
+    from remora_b200 import _lib as L
+    from remora_b200.abi import tensor_descriptor
+    from remora_b200.cnn import _lib
+    from remora_b200.runtime import context
+
+    lib = _lib()
+    rng = np.random.default_rng(5)
+    B = 6
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    x = dev(rng.standard_normal((B, 16, 32, 32)).astype(np.float32))
+    w = dev((rng.standard_normal((32, 16, 3, 3)) * 0.1).astype(np.float32))
+    b = dev((rng.standard_normal(32) * 0.1).astype(np.float32))
+    spec = L.RemoraConvSpec(1, 1, {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32}[precision], 0)
+    ctx = context(cuda.index)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    keep = []
+
+    def d(t):
+        keep.append(tensor_descriptor(t))
+        return ctypes.addressof(keep[-1])
+
+    f32, u8 = torch.float32, torch.uint8
+    a2 = torch.empty((B, 32, 32, 32), dtype=f32, device=cuda)
+    p_ref, c_ref = torch.empty((B, 32, 16, 16), dtype=f32, device=cuda), torch.empty((B, 32, 16, 16), dtype=u8,
+                                                                                    device=cuda)
+    p_fused, c_fused = torch.empty_like(p_ref), torch.empty_like(c_ref)
+    assert lib.remora_b200_conv2d_fwd(ctx.ptr, ctypes.byref(spec), d(x), d(w), d(b), d(a2), stream) == 0
+    assert lib.remora_b200_relu_pool(ctx.ptr, d(a2), d(p_ref), d(c_ref), stream) == 0
+    assert lib.remora_b200_conv2d_fwd_relu_pool(ctx.ptr, ctypes.byref(spec), d(x), d(w), d(b), d(p_fused),
+                                                d(c_fused), stream) == 0
+    np.testing.assert_array_equal(to_host(p_fused), to_host(p_ref))
+    np.testing.assert_array_equal(to_host(c_fused), to_host(c_ref))
+    # backward from a pooled gradient
+    dp = dev(rng.standard_normal((B, 32, 16, 16)).astype(np.float32))
+    da = torch.empty((B, 32, 32, 32), dtype=f32, device=cuda)
+    assert lib.remora_b200_unpool(ctx.ptr, d(dp), d(c_ref), d(da), stream) == 0
+    dx_ref, dx_fused = torch.empty_like(x), torch.empty_like(x)
+    assert lib.remora_b200_conv2d_dgrad(ctx.ptr, ctypes.byref(spec), d(da), d(w), d(dx_ref), stream) == 0
+    assert lib.remora_b200_conv2d_dgrad_unpool(ctx.ptr, ctypes.byref(spec), d(dp), d(c_ref), d(w), d(dx_fused),
+                                               stream) == 0
+    np.testing.assert_array_equal(to_host(dx_fused), to_host(dx_ref))
+    dw_ref, dw_fused = torch.empty_like(w), torch.empty_like(w)
+    db_ref, db_fused = torch.empty_like(b), torch.empty_like(b)
+    assert lib.remora_b200_conv2d_wgrad_bias(ctx.ptr, ctypes.byref(spec), d(x), d(da), d(dw_ref), d(db_ref),
+                                             stream) == 0
+    assert lib.remora_b200_conv2d_wgrad_bias_unpool(ctx.ptr, ctypes.byref(spec), d(x), d(dp), d(c_ref),
+                                                    d(dw_fused), d(db_fused), stream) == 0
+    np.testing.assert_array_equal(to_host(dw_fused), to_host(dw_ref))
+    np.testing.assert_array_equal(to_host(db_fused), to_host(db_ref))
