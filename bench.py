@@ -149,7 +149,6 @@ class FoldWorkload:
         self.n_out = int(np.prod(self.shape[:-1]))
         self.work_per_call = 4 * (self.n_in + self.n_out)  # algorithmic bytes
         self.rotate = 8
-        self.launches_per_call = 1
 
     def make_input(self, seed: int) -> np.ndarray:
         rng = np.random.Generator(np.random.PCG64(seed))
@@ -258,7 +257,6 @@ class MatmulWorkload:
             self.desc = f"matmul A,B f32[4096,4096] ~ U[-1,1], {self.precision.upper()} tcgen05, f32 accumulate"
         self.work_per_call = 2.0 * self.batch * self.M * self.N * self.K  # algorithmic flops
         self.rotate = 1
-        self.launches_per_call = 1 if self.precision == "tf32" else 3
 
     def shapes(self):
         if self.batch > 1:
@@ -364,7 +362,6 @@ class ConvWorkload:
         w_b = 4 * self.K * self.C * 9
         self.bytes_per_call = x_b + y_b + w_b  # each direction reads two of x/y/w and writes the third
         self.rotate = 1
-        self.launches_per_call = 1
         self.precision = "tf32"
         self.desc = (f"conv2d {self.kind} x[256,16,64,64] ~ N(0,1) * w[32,16,3,3] ~ N(0,sqrt(2/144)), pad 1, "
                      "TF32 tcgen05 implicit GEMM" if self.kind != "wgrad" else
@@ -502,7 +499,8 @@ class CnnWorkload:
         self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision)
         self.net.step(self.x, self.y)  # eager step: compiles map programs, sizes workspaces
         self.net.capture(self.x, self.y)
-        self.launches_per_call = 17  # kernels per step (see profiles/launches_cnn_step.md)
+        # library kernels in one replay of the step's graph, counted at capture
+        self.graph_launches_per_call = self.net.graph_launches
 
     def call(self, k: int) -> None:
         self.net.replay()
@@ -615,6 +613,9 @@ def run_ours(args) -> None:
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    from remora_b200 import _lib as L
+
+    n_launch0 = L.launch_count()
     t0.record(stream)
     for s in range(args.steps):
         ev[s][0].record(stream)
@@ -622,6 +623,9 @@ def run_ours(args) -> None:
             wl.call(k)
         ev[s][1].record(stream)
     t1.record(stream)
+    # library kernels enqueued in the timed region: counted at each launch
+    # site, plus those a graph replay launches (counted when it was captured)
+    n_launch = L.launch_count() - n_launch0 + args.steps * wl.rotate * getattr(wl, "graph_launches_per_call", 0)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -704,7 +708,7 @@ def run_ours(args) -> None:
                              if roof_unit == "TFLOP/s" else " HBM copy")},
             "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": calls * wl.launches_per_call,
+            "gpu_launches": n_launch,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -206,6 +206,10 @@ int remora_b200_shutdown(RemoraB200Ctx *ctx);
 /* replaces the CUDAError message path (remora/runtime.py:477-491) */
 int remora_b200_last_error(char *buf, size_t n);
 const char *remora_b200_version(void);
+/* Number of kernels the library has enqueued in this process (launched, or
+   recorded into a CUDA graph under stream capture): the difference over a
+   captured region is the kernel count of one replay. */
+unsigned long long remora_b200_launch_count(void);
 /* replaces CUDARuntime.alloc / free (remora/runtime.py:270-281) */
 int remora_b200_malloc(RemoraB200Ctx *ctx, size_t nbytes, void **dptr);
 int remora_b200_free(RemoraB200Ctx *ctx, void *dptr);

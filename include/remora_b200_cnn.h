@@ -57,11 +57,14 @@ int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h,
 
 /* Backward of the dense 64 -> 1 layer on a ReLU'd hidden layer:
    dw[o] = sum_b dz[b] h[b,o], db = sum_b dz[b],
-   dh[b,o] = h[b,o] > 0 ? dz[b] * w[o] : 0 (sums in f64, fixed order). */
+   dh[b,o] = h[b,o] > 0 ? dz[b] * w[o] : 0, and, when dh_colsum is not
+   NULL, dh_colsum[o] = sum_b dh[b,o] (the gradient of the hidden layer's
+   bias).  Sums in f64, fixed order. */
 int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h,
                                const RemoraMemRef1 *w, const RemoraMemRef1 *dz,
                                RemoraMemRef2 *dh, RemoraMemRef1 *dw,
-                               RemoraMemRef1 *db, remora_stream_t stream);
+                               RemoraMemRef1 *db, RemoraMemRef1 *dh_colsum,
+                               remora_stream_t stream);
 
 /* conv1's weight and bias gradients straight from the pooled gradient and
    the pool codes (the unpooled gradient is never materialised):

@@ -128,6 +128,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "remora_b200_shutdown": (_I32, [_VP]),
     "remora_b200_last_error": (_I32, [ctypes.c_char_p, _SZ]),
     "remora_b200_version": (ctypes.c_char_p, []),
+    "remora_b200_launch_count": (ctypes.c_ulonglong, []),
     "remora_b200_malloc": (_I32, [_VP, _SZ, ctypes.POINTER(_VP)]),
     "remora_b200_free": (_I32, [_VP, _VP]),
     "remora_b200_memcpy_h2d": (_I32, [_VP, _VP, _VP, _SZ, _VP]),
@@ -192,6 +193,12 @@ def exported_symbols() -> list[str]:
     """Names of the C-ABI entry points the loaded library exports."""
     handle = lib()
     return [name for name in _PROTOTYPES if hasattr(handle, name)]
+
+
+def launch_count() -> int:
+    """Kernels the library has enqueued in this process so far (launched, or
+    recorded into a CUDA graph under stream capture)."""
+    return int(lib().remora_b200_launch_count())
 
 
 def last_error() -> str:

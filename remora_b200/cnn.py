@@ -32,7 +32,7 @@ _CNN_PROTOS = {
     "remora_b200_relu_pool": [ctypes.c_void_p] * 5,
     "remora_b200_unpool": [ctypes.c_void_p] * 5,
     "remora_b200_dense_bce": [ctypes.c_void_p] * 8 + [ctypes.c_float, ctypes.c_void_p],
-    "remora_b200_dense_relu_bwd": [ctypes.c_void_p] * 8,
+    "remora_b200_dense_relu_bwd": [ctypes.c_void_p] * 9,
     "remora_b200_conv1_wgrad_pooled": [ctypes.c_void_p] * 7,
     "remora_b200_conv2d_wgrad_bias": [ctypes.c_void_p] * 7,
     "remora_b200_conv2d_fwd_relu_pool": [ctypes.c_void_p] * 8,
@@ -105,7 +105,6 @@ class CraterCNN:
         self.dh = e(B, 64)
         self.dp2 = e(B, 32, 16, 16)
         self.dp1 = e(B, 16, 32, 32)
-        self.zero64 = torch.zeros(64, dtype=f32, device=self.dev)
         self.loss_sum = e(1).reshape(())
         # fused maps: ReLU(h + b3) with b3 broadcast over the batch, and the
         # in-place SGD update p - lr * g
@@ -170,14 +169,11 @@ class CraterCNN:
                                               self._d(labels), self._d(self.z), self._d(self.loss_b),
                                               self._d(self.dz), ctypes.c_float(1.0 / self.B_total), s), "dense_bce")
         # backward
+        # dense 64 -> 1 backward; also sums dh over the batch: the hidden bias gradient
         self._check(lib.remora_b200_dense_relu_bwd(c, self._d(self.h), self._d(p["w4"]), self._d(self.dz),
-                                                   self._d(self.dh), self._d(g["w4"]), self._d(g["b4"]), s),
-                    "dense2 bwd")
+                                                   self._d(self.dh), self._d(g["w4"]), self._d(g["b4"]),
+                                                   self._d(g["b3"]), s), "dense2 bwd")
         self._gemm(self.dh.t(), p2flat, g["w3"])
-        fs = L.RemoraFoldSpec()
-        fs.op, fs.dtype = L.FOLD_ADD, L.F32
-        self._check(lib.remora_b200_array_fold(c, ctypes.byref(fs), self._d(self.dh), 2, self._d(self.zero64),
-                                               self._d(g["b3"]), s), "db3")
         self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))
         # conv2 gradients straight from the pooled gradient and the pool codes
         self._check(lib.remora_b200_conv2d_wgrad_bias_unpool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
@@ -219,8 +215,10 @@ class CraterCNN:
         torch.cuda.current_stream(self.dev).wait_stream(side)
         torch.cuda.synchronize(self.dev)
         self.graph = torch.cuda.CUDAGraph()
+        n0 = L.launch_count()
         with torch.cuda.graph(self.graph, stream=side):
             self.step(images, labels)
+        self.graph_launches = L.launch_count() - n0  # library kernels per replay
         self._graph_keep = list(self._keep)
 
     def replay(self) -> None:

@@ -179,35 +179,47 @@ __global__ void __launch_bounds__(256) dense_bce_kernel(const float *__restrict_
 }
 
 // Backward of dense 64 -> 1 and the hidden ReLU.  Block o: dw4[o] =
-// sum_b dz[b] h[b,o] (fixed order), dh[b,o] = h[b,o] > 0 ? dz[b] w4[o] : 0;
-// block D (one extra) sums db4 = sum_b dz[b].
+// sum_b dz[b] h[b,o] (fixed order), dh[b,o] = h[b,o] > 0 ? dz[b] w4[o] : 0,
+// and (when dsum is non-null) dsum[o] = sum_b dh[b,o], the gradient of the
+// hidden layer's bias; block D (one extra) sums db4 = sum_b dz[b].  Sums in
+// f64, combined in a fixed tree order.
 __global__ void __launch_bounds__(256) dense_bwd_kernel(const float *__restrict__ h, const float *__restrict__ w4,
                                                         const float *__restrict__ dz, float *__restrict__ dh,
-                                                        float *__restrict__ dw4, float *__restrict__ db4, int B,
-                                                        int D) {
-  __shared__ double sh[256];
+                                                        float *__restrict__ dw4, float *__restrict__ db4,
+                                                        float *__restrict__ dsum, int B, int D) {
+  __shared__ double sh[2][256];
   const int o = blockIdx.x;
-  double acc = 0.0;
+  double acc = 0.0, acc2 = 0.0;
   if (o < D) {
     const float wo = __ldg(w4 + o);
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
       const float hv = h[(long long)b * D + o];
       const float g = dz[b];
       acc += (double)g * (double)hv;
-      dh[(long long)b * D + o] = hv > 0.0f ? __fmul_rn(g, wo) : 0.0f;
+      const float d = hv > 0.0f ? __fmul_rn(g, wo) : 0.0f;
+      dh[(long long)b * D + o] = d;
+      acc2 += (double)d;
     }
   } else {
     for (int b = threadIdx.x; b < B; b += blockDim.x) acc += (double)dz[b];
   }
-  sh[threadIdx.x] = acc;
+  sh[0][threadIdx.x] = acc;
+  sh[1][threadIdx.x] = acc2;
   __syncthreads();
   for (int s = 128; s > 0; s >>= 1) {
-    if ((int)threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+    if ((int)threadIdx.x < s) {
+      sh[0][threadIdx.x] += sh[0][threadIdx.x + s];
+      sh[1][threadIdx.x] += sh[1][threadIdx.x + s];
+    }
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    if (o < D) dw4[o] = (float)sh[0];
-    else *db4 = (float)sh[0];
+    if (o < D) {
+      dw4[o] = (float)sh[0][0];
+      if (dsum) dsum[o] = (float)sh[1][0];
+    } else {
+      *db4 = (float)sh[0][0];
+    }
   }
 }
 
@@ -323,6 +335,7 @@ int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, cons
     return fail(REMORA_ERR_UNSUPPORTED, "conv1_relu_pool: images of 64x64 or 32x32 and at most %d channels",
                 kConv1MaxK);
   auto kern = H == 64 ? conv1_relu_pool_kernel<64, 64> : conv1_relu_pool_kernel<32, 32>;
+  note_launch();
   kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)Wd.data(4),
                                                       (const float *)Bd.data(4), (float *)P.data(4),
                                                       (uint8_t *)C.data(1), K);
@@ -344,6 +357,7 @@ int remora_b200_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *a, RemoraMemR
   for (int d = 0; d < 4; ++d)
     if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "relu_pool: codes must match pooled shape");
   if (P.numel() == 0) return REMORA_OK;
+  note_launch();
   relu_pool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)A.data(4), (float *)P.data(4), (uint8_t *)C.data(1), A.sizes[0] * A.sizes[1], H, W);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -364,6 +378,7 @@ int remora_b200_unpool(RemoraB200Ctx *ctx, const RemoraMemRef4 *dpooled, const R
   for (int d = 0; d < 4; ++d)
     if (C.sizes[d] != P.sizes[d]) return fail(REMORA_ERR_SHAPE, "unpool: codes must match the pooled shape");
   if (P.numel() == 0) return REMORA_OK;
+  note_launch();
   unpool_kernel<<<grid_for(P.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)P.data(4), (const uint8_t *)C.data(1), (float *)A.data(4), A.sizes[0] * A.sizes[1], H, W);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -389,6 +404,7 @@ int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const Remo
       Dz.sizes[0] != B)
     return fail(REMORA_ERR_SHAPE, "dense_bce: shapes must be h [B,D], w [D], b [1], y/z/loss/dz [B]");
   if (B == 0) return REMORA_OK;
+  note_launch();
   dense_bce_kernel<<<grid_for((long long)B * 32, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)Hd.data(4), (const float *)Wd.data(4), (const float *)Bd.data(4), (const float *)Y.data(4),
       (float *)Z.data(4), (float *)Lo.data(4), (float *)Dz.data(4), B, D, grad_scale);
@@ -398,7 +414,7 @@ int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const Remo
 
 int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const RemoraMemRef1 *w,
                                const RemoraMemRef1 *dz, RemoraMemRef2 *dh, RemoraMemRef1 *dw, RemoraMemRef1 *db,
-                               remora_stream_t stream) {
+                               RemoraMemRef1 *dh_colsum, remora_stream_t stream) {
   REMORA_TRY(check_ctx(ctx));
   DescView Hd, Wd, Dz, Dh, Dw, Db;
   REMORA_TRY(read_desc(h, 2, &Hd, "hidden"));
@@ -413,9 +429,18 @@ int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const
   if (Wd.sizes[0] != D || Dz.sizes[0] != B || Dh.sizes[0] != B || Dh.sizes[1] != D || Dw.sizes[0] != D ||
       Db.sizes[0] != 1)
     return fail(REMORA_ERR_SHAPE, "dense_relu_bwd: shapes must be h/dh [B,D], w/dw [D], dz [B], db [1]");
+  float *ds = nullptr;
+  if (dh_colsum) {
+    DescView Ds;
+    REMORA_TRY(read_desc(dh_colsum, 1, &Ds, "hidden-bias gradient"));
+    if (Ds.sizes[0] != D || !Ds.contiguous())
+      return fail(REMORA_ERR_SHAPE, "dense_relu_bwd: dh_colsum must be a contiguous [%d]", D);
+    ds = (float *)Ds.data(4);
+  }
+  note_launch();
   dense_bwd_kernel<<<D + 1, 256, 0, (cudaStream_t)stream>>>(
       (const float *)Hd.data(4), (const float *)Wd.data(4), (const float *)Dz.data(4), (float *)Dh.data(4),
-      (float *)Dw.data(4), (float *)Db.data(4), B, D);
+      (float *)Dw.data(4), (float *)Db.data(4), ds, B, D);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }
@@ -446,8 +471,10 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, c
   REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * K * 10 * sizeof(float) + 256, &ws));
   float *part = reinterpret_cast<float *>(ws->buf);
   auto kern = H == 64 ? conv1_wgrad_pool_kernel<64, 64> : conv1_wgrad_pool_kernel<32, 32>;
+  note_launch();
   kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)P.data(4),
                                                       (const uint8_t *)C.data(1), part, K);
+  note_launch();
   conv1_wgrad_finish_kernel<<<K * 10, 256, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4),
                                                                       (float *)Db.data(4), B, K);
   REMORA_CUDA_TRY(cudaGetLastError());

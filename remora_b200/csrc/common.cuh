@@ -62,6 +62,11 @@ struct DescView {
 };
 
 int read_desc(const void *desc, int rank, DescView *out, const char *what);
+
+// Bumps the process-wide count of kernels this library has enqueued
+// (launched, or recorded into a graph under stream capture); every launch
+// site calls it once per kernel.
+void note_launch();
 int dtype_size(int dtype);
 
 // -------------------------------------------------------------- context --

@@ -1,6 +1,7 @@
 // context.cu — context, plumbing and error reporting of libremora_b200.so.
 // Replaces the reference's CUDARuntime (remora/runtime.py:243-340): device
 // selection, allocation, copies, memset and synchronisation.
+#include <atomic>
 #include <cstdarg>
 
 #include "common.cuh"
@@ -8,6 +9,9 @@
 namespace remora {
 
 static thread_local std::string g_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char *fmt, ...) {
   char buf[1024];
@@ -98,6 +102,8 @@ using namespace remora;
 extern "C" {
 
 const char *remora_b200_version(void) { return "remora_b200 0.1 (sm_100a)"; }
+
+unsigned long long remora_b200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int remora_b200_last_error(char *buf, size_t n) {
   if (buf == nullptr || n == 0) return REMORA_ERR_ARG;

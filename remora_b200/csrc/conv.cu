@@ -249,12 +249,15 @@ int conv_wgrad3x3(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const f
   if (W == 64) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(conv_wgrad3x3_tiled<RB, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
+    note_launch();
     conv_wgrad3x3_tiled<RB, 64><<<blocks, threads, smem, stream>>>(x, dy, part, g, db != nullptr);
   } else {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(conv_wgrad3x3_tiled<RB, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem));
+    note_launch();
     conv_wgrad3x3_tiled<RB, 32><<<blocks, threads, smem, stream>>>(x, dy, part, g, db != nullptr);
   }
+  note_launch();
   wgrad_finish<<<(nw + nb + 255) / 256, 256, 0, stream>>>(part, blocks, nw + nb, nw, db ? nb : 0, dw, db);
   REMORA_CUDA_TRY(cudaGetLastError());
   *handled = true;
@@ -324,6 +327,7 @@ int remora_b200_conv2d_fwd(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, const
   REMORA_TRY(conv_tc_fwd(ctx, g, (const float *)X.data(4), (const float *)Wd.data(4), bp, (float *)Y.data(4),
                          spec->precision, (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
+  note_launch();
   conv_fwd_direct<<<grid_for(Y.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)X.data(4), (const float *)Wd.data(4), bp, (float *)Y.data(4), g);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -348,6 +352,7 @@ int remora_b200_conv2d_dgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, con
   REMORA_TRY(conv_tc_dgrad(ctx, g, (const float *)DY.data(4), (const float *)Wd.data(4), (float *)DX.data(4),
                            spec->precision, (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
+  note_launch();
   conv_dgrad_direct<<<grid_for(DX.numel(), ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)DY.data(4), (const float *)Wd.data(4), (float *)DX.data(4), g);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -375,6 +380,7 @@ int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec, con
   REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), nullptr,
                            (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
+  note_launch();
   conv_wgrad_direct<<<(unsigned)DW.numel(), 256, 0, (cudaStream_t)stream>>>(
       (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), g);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -405,8 +411,10 @@ int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec
   REMORA_TRY(conv_wgrad3x3(ctx, g, (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4),
                            (float *)DB.data(4), (cudaStream_t)stream, &handled));
   if (handled) return REMORA_OK;
+  note_launch();
   conv_wgrad_direct<<<(unsigned)DW.numel(), 256, 0, (cudaStream_t)stream>>>(
       (const float *)X.data(4), (const float *)DY.data(4), (float *)DW.data(4), g);
+  note_launch();
   bias_grad_direct<<<g.K, 256, 0, (cudaStream_t)stream>>>((const float *)DY.data(4), (float *)DB.data(4), g.N, g.K,
                                                           (long long)g.OH * g.OW);
   REMORA_CUDA_TRY(cudaGetLastError());

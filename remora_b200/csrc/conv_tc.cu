@@ -581,6 +581,7 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
   q.tiles_per_img = (p.H + TH - 1) / TH;
   const int ntiles = p.N * q.tiles_per_img;
   const int grid = std::min(ntiles, sm_count);
+  note_launch();
   kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, my, mx2, my2, q);
   REMORA_CUDA_TRY(cudaGetLastError());
   *handled = true;

@@ -315,14 +315,19 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   }
 }
 
-// dw[co][ci][r][s] and db[co] from the per-CTA partials, f64, CTA order.
-__global__ void wgrad_tc_finish(const float *__restrict__ part, int nblocks, int cout, float *__restrict__ dw,
-                                float *__restrict__ db) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+// dw[co][ci][r][s] and db[co] from the per-CTA partials in f64: one warp
+// per value, lane l adding partials l, l+32, ... in order, then a fixed
+// shuffle tree (deterministic).
+__global__ void __launch_bounds__(256) wgrad_tc_finish(const float *__restrict__ part, int nblocks, int cout,
+                                                       float *__restrict__ dw, float *__restrict__ db) {
+  const int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (e >= cout * kWgOutCols) return;
   const int co = e / kWgOutCols, n = e % kWgOutCols;
   double s = 0.0;
-  for (int b = 0; b < nblocks; ++b) s += (double)part[((long long)b * 32 + co) * kWgOutCols + n];
+  for (int b = lane; b < nblocks; b += 32) s += (double)part[((long long)b * 32 + co) * kWgOutCols + n];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane != 0) return;
   if (n == kWgOnesRow) {
     if (db) db[co] = (float)s;
   } else {
@@ -373,9 +378,11 @@ int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const fl
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, (size_t)grid * 32 * kWgOutCols * sizeof(float) + 256, &ws));
   WgParams p{g.N, g.H, g.K, tiles_per_img, reinterpret_cast<float *>(ws->buf), ws->err};
+  note_launch();
   kern<<<grid, kWgThreads, Cf::SMEM, stream>>>(mx, md, mc, p);
   const int outs = g.K * kWgOutCols;
-  wgrad_tc_finish<<<(outs + 255) / 256, 256, 0, stream>>>(p.part, grid, g.K, dw, db);
+  note_launch();
+  wgrad_tc_finish<<<(outs * 32 + 255) / 256, 256, 0, stream>>>(p.part, grid, g.K, dw, db);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }

@@ -434,10 +434,12 @@ int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Ope
   }
   const int nunits = ntiles * p.split;
   const int grid = std::min(nunits, sm_count);
+  note_launch();
   gemm_tf32_kernel<SPLIT3, BN><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
   REMORA_CUDA_TRY(cudaGetLastError());
   if (p.split > 1) {
     const long long n = (long long)ntiles * BM * BN;
+    note_launch();
     gemm_split_fixup<BN><<<(int)std::min<long long>((n + 255) / 256, (long long)sm_count * 16), 256, 0, stream>>>(
         p.part, p);
     REMORA_CUDA_TRY(cudaGetLastError());
@@ -477,6 +479,7 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   float *cptr = reinterpret_cast<float *>(Cd.data(4));
   const long long ldc = Cd.strides[o], cbs = rank == 3 ? Cd.strides[0] : 0;
   if (K == 0) {
+    note_launch();
     fill_zero_kernel<<<grid_for((long long)batch * M * N, ctx->sm_count), 256, 0, stream>>>(cptr, ldc, cbs, batch,
                                                                                               (int)M, (int)N);
     REMORA_CUDA_TRY(cudaGetLastError());
@@ -525,6 +528,7 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
     float *hi = take((size_t)batch * outer * inner_pad * 4);
     float *lp = split ? take((size_t)batch * outer * inner_pad * 4) : nullptr;
     if (!hi || (split && !lp)) return fail(REMORA_ERR_LIMIT, "gemm: workspace too small");
+    note_launch();
     prep_operand_kernel<<<grid_for((long long)batch * outer * inner_pad, ctx->sm_count), 256, 0, stream>>>(
         reinterpret_cast<const float *>(d.data(4)), rank == 3 ? d.strides[0] : 0, so, si, batch, outer, inner,
         inner_pad, hi, lp);

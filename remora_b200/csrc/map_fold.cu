@@ -479,6 +479,7 @@ int launch(cudaKernel_t k, int grid, int block, void *args_struct, cudaStream_t 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   cudaError_t e = cudaLaunchKernelExC(&cfg, (const void *)k, params);
   if (e != cudaSuccess) return fail(REMORA_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   return REMORA_OK;

@@ -119,6 +119,7 @@ int copy_to_contiguous(const DescView &src, int esize, void *dst, cudaStream_t s
   const int64_t n = src.numel();
   if (n == 0) return REMORA_OK;
   StridedView v = make_view(src);
+  note_launch();
   if (esize == 4)
     strided_copy_kernel<uint32_t, true><<<grid_for(n, sm_count), 256, 0, stream>>>(
         (const uint32_t *)src.data(4), (uint32_t *)dst, v, n);
@@ -133,6 +134,7 @@ int copy_from_contiguous(const void *src, const DescView &dst, int esize, cudaSt
   const int64_t n = dst.numel();
   if (n == 0) return REMORA_OK;
   StridedView v = make_view(dst);
+  note_launch();
   if (esize == 4)
     strided_copy_kernel<uint32_t, false><<<grid_for(n, sm_count), 256, 0, stream>>>(
         (const uint32_t *)src, (uint32_t *)dst.data(4), v, n);
@@ -155,6 +157,7 @@ int remora_b200_memset_d32(RemoraB200Ctx *ctx, void *dst, uint32_t value, size_t
   if (count == 0) return REMORA_OK;
   if (dst == nullptr || (reinterpret_cast<uintptr_t>(dst) & 3))
     return fail(REMORA_ERR_ARG, "memset_d32: null or unaligned destination");
+  note_launch();
   memset32_kernel<<<grid_for((int64_t)count, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (uint32_t *)dst, value, (int64_t)count);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -185,6 +188,7 @@ int remora_b200_im2col(RemoraB200Ctx *ctx, const RemoraIm2colSpec *spec, const R
                 spec->kh * spec->kw);
   const int64_t n = co.numel();
   if (n == 0) return REMORA_OK;
+  note_launch();
   im2col_kernel<<<grid_for(n, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)im.data(4), im.strides[0], im.strides[1], (float *)co.data(4), co.strides[0],
       co.strides[1], oh, ow, spec->kh, spec->kw, spec->stride);
@@ -206,6 +210,7 @@ int remora_b200_col2im(RemoraB200Ctx *ctx, const RemoraIm2colSpec *spec, const R
                 spec->kh * spec->kw);
   const int64_t n = im.numel();
   if (n == 0) return REMORA_OK;
+  note_launch();
   col2im_kernel<<<grid_for(n, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
       (const float *)co.data(4), co.strides[0], co.strides[1], (float *)im.data(4), im.strides[0],
       im.strides[1], im.sizes[0], im.sizes[1], oh, ow, spec->kh, spec->kw, spec->stride);
@@ -227,16 +232,16 @@ int remora_b200_transpose(RemoraB200Ctx *ctx, int32_t dtype, const RemoraMemRef2
   dim3 block(32, 8);
   dim3 grid((unsigned)std::min<int64_t>((C + 31) / 32, 65535), (unsigned)std::min<int64_t>((R + 31) / 32, 65535));
   const int es = dtype_size(dtype);
+  if (es != 4 && es != 1) return fail(REMORA_ERR_ARG, "transpose: bad dtype %d", dtype);
+  note_launch();
   if (es == 4)
     transpose_kernel<uint32_t><<<grid, block, 0, (cudaStream_t)stream>>>(
         (const uint32_t *)a.data(4), a.strides[0], a.strides[1], (uint32_t *)b.data(4), b.strides[0],
         b.strides[1], R, C);
-  else if (es == 1)
+  else
     transpose_kernel<uint8_t><<<grid, block, 0, (cudaStream_t)stream>>>(
         (const uint8_t *)a.data(1), a.strides[0], a.strides[1], (uint8_t *)b.data(1), b.strides[0],
         b.strides[1], R, C);
-  else
-    return fail(REMORA_ERR_ARG, "transpose: bad dtype %d", dtype);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }

@@ -197,8 +197,11 @@ int scan_impl(const T *x, T *y, int64_t N, int64_t C, int right, int exclusive, 
     T *carry = agg + ((ntiles + 63) & ~int64_t(63));
     if ((size_t)(2 * ((ntiles + 63) & ~int64_t(63))) * sizeof(T) > scratch_bytes)
       return fail(REMORA_ERR_LIMIT, "scan: scratch too small");
+    note_launch();
     tile_aggregate<T, Op><<<(unsigned)ntiles, kThreads, 0, stream>>>(x, N, right, agg);
+    note_launch();
     carries_rank1<T, Op><<<1, kThreads, 0, stream>>>(agg, carry, ntiles, init);
+    note_launch();
     tile_scan<T, Op><<<(unsigned)ntiles, kThreads, 0, stream>>>(x, y, N, right, exclusive, carry);
   } else {
     const int64_t cblocks = (C + kThreads - 1) / kThreads;
@@ -209,14 +212,18 @@ int scan_impl(const T *x, T *y, int64_t N, int64_t C, int right, int exclusive, 
     nseg = (N + seg_rows - 1) / seg_rows;
     dim3 grid((unsigned)cblocks, (unsigned)nseg);
     if (nseg == 1) {
+      note_launch();
       seg_scan<T, Op><<<grid, kThreads, 0, stream>>>(x, y, N, C, seg_rows, nullptr, init, 0);
     } else {
       T *agg = reinterpret_cast<T *>(scratch);
       T *carry = agg + nseg * C;
       if ((size_t)(2 * nseg * C) * sizeof(T) > scratch_bytes)
         return fail(REMORA_ERR_LIMIT, "scan: scratch too small");
+      note_launch();
       seg_aggregate<T, Op><<<grid, kThreads, 0, stream>>>(x, N, C, seg_rows, agg);
+      note_launch();
       seg_carries<T, Op><<<(unsigned)cblocks, kThreads, 0, stream>>>(agg, carry, C, nseg, init);
+      note_launch();
       seg_scan<T, Op><<<grid, kThreads, 0, stream>>>(x, y, N, C, seg_rows, carry, init, 1);
     }
   }
@@ -332,13 +339,16 @@ int array_fold_impl(const T *x, const T *init, int64_t init_stride, T *out, int6
   int64_t nseg = std::max<int64_t>(1, std::min<int64_t>(N / 16, want_threads / std::max<int64_t>(C, 1)));
   nseg = std::min<int64_t>(nseg, 65535);
   if (nseg <= 1) {
+    note_launch();
     array_fold_direct<T, Op><<<(unsigned)cblocks, kThreads, 0, stream>>>(x, init, init_stride, out, N, C);
   } else {
     const int64_t seg_rows = (N + nseg - 1) / nseg;
     nseg = (N + seg_rows - 1) / seg_rows;
     if ((size_t)(nseg * C) * sizeof(T) > scratch_bytes) return fail(REMORA_ERR_LIMIT, "array fold: scratch");
     T *agg = reinterpret_cast<T *>(scratch);
+    note_launch();
     seg_aggregate<T, Op><<<dim3((unsigned)cblocks, (unsigned)nseg), kThreads, 0, stream>>>(x, N, C, seg_rows, agg);
+    note_launch();
     array_fold_combine<T, Op><<<(unsigned)cblocks, kThreads, 0, stream>>>(agg, init, init_stride, out, C, nseg);
   }
   REMORA_CUDA_TRY(cudaGetLastError());

@@ -69,6 +69,14 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert b"sm_100a" in lib.remora_b200_version()
 
 
+def test_launch_counter_is_exported_and_untouched_by_rejected_calls():
+    n0 = L.launch_count()
+    assert isinstance(n0, int) and n0 >= 0
+    # a call with no context is rejected before any kernel is enqueued
+    assert L.lib().remora_b200_memset_d32(None, None, 0, 16, None) != 0
+    assert L.launch_count() == n0
+
+
 def test_header_struct_sizes_match_ctypes():
     # RemoraMapProgram: 5 int32 + 8 int32 + 48 x 16-byte instructions
     assert ctypes.sizeof(L.RemoraMapInstr) == 16

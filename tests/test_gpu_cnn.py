@@ -91,7 +91,12 @@ def test_cnn_training_reduces_loss_and_graph_replay(cuda):
     a.step(xi, yi)
     b.step(xi, yi)
     b.capture(xi, yi)  # records (and runs) one step
+    from remora_b200 import _lib as L
+
+    n0 = L.launch_count()
     a.step(xi, yi)
+    # one replay launches the same library kernels as one eager step
+    assert L.launch_count() - n0 == b.graph_launches > 10
     torch.cuda.synchronize()
     np.testing.assert_array_equal(to_host(a.params), to_host(b.params))
     b.replay()
