@@ -15,13 +15,27 @@
 // is the left pad of one row and the right pad of the one before.  Rows
 // m with m % PW == W are discarded in the epilogue.
 //
-// Roles (448 threads):
+// Forward fused with ReLU + 2x2 max-pool: the operand is split by input
+// row parity into two planes per 4 channels (padded rows 2r and 2r + 1 of
+// the tile are row r of plane 0 and plane 1, pitch PW = W + 2), GEMM row m
+// = i * PW + w stands for pooled row i, and two accumulators per M block
+// hold conv rows 2i and 2i + 1: tap (r, s) of conv row 2i + a reads plane
+// (a + r) & 1 at row offset (a + r) >> 1, again a descriptor offset.  A
+// thread then holds both rows of its pooling window and the lane next to
+// it (PW even: lanes 2k, 2k + 1 are columns 2j, 2j + 1) holds the other
+// column.
+//
+// Roles (512 threads):
 //   warp 0 lane 0    TMA: one tiled load per tile of the raw NCHW rows
 //                    [CIN][TH+2][W] (rows outside the image read as zero)
 //   warp 1           TMEM allocation; lane 0 issues the MMAs
 //                    (M = 128, N = NOUT, K = 8) into a TMEM accumulator
-//   warps 2-5        epilogue: TMEM -> registers -> NCHW rows (+ bias)
-//   warps 6-13       transform: raw rows -> the interleaved operand (and,
+//   warps 2-9        epilogue: TMEM -> registers (+ bias, ReLU + pool) ->
+//                    global memory; for one channel the 32 lanes of a warp
+//                    hold consecutive pixels, so every store instruction
+//                    writes a contiguous run.  Two warps per TMEM lane
+//                    quarter split the channel groups (or the M blocks).
+//   warps 10-15      transform: raw rows -> the interleaved operand (and,
 //                    for 3xTF32, its hi/lo split)
 // Raw stages, operand stages and two accumulators let TMA, transform, MMA
 // and epilogue of consecutive tiles overlap.  Input gradient: the same
@@ -55,15 +69,18 @@ constexpr uint8_t kNoGradCode = 255;
 
 template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
 struct ConvCfg {
-  static constexpr int PW = W + 1;                     // padded row pitch (positions)
+  static constexpr bool PAR = FUSE == kFusePool;       // operand split by input row parity
+  static constexpr int NPAR = PAR ? 2 : 1;
+  static constexpr int PW = PAR ? W + 2 : W + 1;       // padded row pitch (positions)
   static constexpr int ROWS = TH + 2;                  // input rows per tile
-  static constexpr int MB = (TH * PW + 127) / 128;     // 128-row M blocks per tile
-  static constexpr int NPOS0 = MB * 128 + 2 * PW + 2;  // positions any tap reads
+  static constexpr int MROWS = PAR ? TH / 2 : TH;      // GEMM rows of pixels per tile
+  static constexpr int MB = (MROWS * PW + 127) / 128;  // 128-row M blocks per tile
+  static constexpr int NPOS0 = MB * 128 + (PAR ? PW : 2 * PW) + 2;  // positions any tap reads
   // planes start one 16-byte bank group apart (NPOS = 1 mod 8)
   static constexpr int NPOS = ((NPOS0 + 7) / 8) * 8 + 1;
   static constexpr uint32_t PLANE = NPOS * 16;  // bytes of one 4-channel plane
   static constexpr int NPL = CIN / 4;
-  static constexpr uint32_t A_COPY = NPL * PLANE;
+  static constexpr uint32_t A_COPY = NPL * NPAR * PLANE;
   static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT3 ? 2 : 1));
   // kFuseUnpool: the raw stage holds pooled rows: values, then codes
   static constexpr int PROWS = TH / 2 + 2;
@@ -75,34 +92,27 @@ struct ConvCfg {
   static constexpr uint32_t BPLANE = NOUT * 16;
   static constexpr uint32_t W_COPY = 9 * NPL * BPLANE;
   static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT3 ? 2 : 1));
-  static constexpr uint32_t STG_BYTES = align1k(CG * TH * W * 4);  // one channel group of the output tile
   static constexpr uint32_t OFF_RAW = W_REGION;
   static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
-  static constexpr uint32_t OFF_STG = OFF_A + A_ST * A_STAGE;
-  // kFusePool: pooled values and codes of one channel group
-  static constexpr int PNUM = CG * (TH / 2) * (W / 2);
-  static constexpr uint32_t PST_BYTES = FUSE == kFusePool ? align1k(PNUM * 4) : 0;
-  static constexpr uint32_t CST_BYTES = FUSE == kFusePool ? align1k(PNUM) : 0;
-  static constexpr uint32_t OFF_PST = OFF_STG + STG_BYTES;
-  static constexpr uint32_t OFF_CST = OFF_PST + PST_BYTES;
-  static constexpr size_t SMEM = (size_t)OFF_CST + CST_BYTES + 1024;
-  static constexpr int ACC_COLS = MB * NOUT;  // TMEM columns of one accumulator
+  static constexpr size_t SMEM = (size_t)OFF_A + A_ST * A_STAGE + 1024;
+  static constexpr int ACC_COLS = MB * NPAR * NOUT;  // TMEM columns of one accumulator
   static constexpr int ITEMS = NPL * ROWS * (W / 4);
   static constexpr int KSTEPS = CIN / 8;
   static_assert(CIN % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
-  static_assert((CG == 8 || CG == 16 || CG == 32) && NOUT % CG == 0, "channel group");
-  static_assert(CG <= 256 && TH <= 256, "TMA store box dims");
+  static_assert((CG == 8 || CG == 16 || CG == 32) && (NOUT == CG || NOUT == 2 * CG), "channel groups");
   static_assert(FUSE == kFuseNone || (TH % 2 == 0 && W % 32 == 0), "pooled rows are 16-byte TMA boxes");
+  static_assert(!PAR || PW % 2 == 0, "pool partners share a lane pair");
   static_assert(2 * ACC_COLS <= 512, "two accumulators fit TMEM");
   static_assert(SMEM <= 232448, "shared memory per block");
   static_assert(ROWS <= 256 && W <= 256 && CIN <= 256, "TMA box dims");
-  static_assert(PLANE / 16 < 16384 && BPLANE / 16 < 16384, "descriptor offsets");
+  static_assert(NPAR * PLANE / 16 < 16384 && BPLANE / 16 < 16384, "descriptor offsets");
 };
 
 struct ConvTCParams {
   const float *w;
   const float *bias;
-  float *y;
+  float *y;         // output, NCHW [N][COUT][H][W] (kFusePool: pooled [N][COUT][H/2][W/2])
+  uint8_t *codes;   // kFusePool: pool codes, same shape as the pooled output
   int N, H, COUT;
   int mode;  // 0: forward, w is [COUT][CIN][3][3]; 1: input gradient, w is [CIN][COUT][3][3] (forward weights)
   int tiles_per_img;
@@ -110,8 +120,10 @@ struct ConvTCParams {
 };
 
 // warp roles
-constexpr int kConvThreads = 448;
-constexpr int kTransformWarp0 = 6, kTransformWarps = 8;
+// 16 warps, four per SM sub-partition: up to 128 registers a thread
+constexpr int kConvThreads = 512;
+constexpr int kEpiWarp0 = 2, kEpiWarps = 8;
+constexpr int kTransformWarp0 = kEpiWarp0 + kEpiWarps, kTransformWarps = 6;
 constexpr int kTransformThreads = kTransformWarps * 32;
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
@@ -170,24 +182,6 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[CG]) 
   else tmem_ld_32x32b_x8(taddr, r);
 }
 
-__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-// TMA tile store from shared memory (no multicast), and its bulk-group
-// completion: .read = the source may be overwritten, plain = the writes
-// are performed.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
-               "r"(src), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_group_read0() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
 // K-major interleaved (SWIZZLE_NONE) operand: 8-row groups 128 B apart
 // (SBO), the two 4-element K chunks of one MMA `lbo` bytes apart.
 __device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lbo) {
@@ -196,17 +190,15 @@ __device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lb
 
 template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE>
 __global__ void __launch_bounds__(kConvThreads, 1)
-    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy,
-                      const __grid_constant__ CUtensorMap tmx2, const __grid_constant__ CUtensorMap tmy2,
+    conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmx2,
                       ConvTCParams p) {
   // tmx: input rows (kFuseUnpool: pooled gradient values), tmx2: their pool
-  // codes (kFuseUnpool only); tmy: output (kFusePool: pooled values), tmy2:
-  // output pool codes (kFusePool only)
+  // codes (kFuseUnpool only)
   using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], afull[A_ST], aempty[A_ST], tfull[2], tempty[2],
-      sfull, sfree, pfull, drain;
+      drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ float bias_s[32];
@@ -224,11 +216,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 4);
+      tc::mbar_init(&tempty[b], kEpiWarps);
     }
-    tc::mbar_init(&sfull, 4);
-    tc::mbar_init(&sfree, 1);
-    tc::mbar_init(&pfull, 4);
     tc::mbar_init(&drain, 1);
     abort_flag = 0;
     tc::fence_barrier_init();
@@ -313,23 +302,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort_v, p.err, 203)) break;
         tc::fence_after_sync();
         const uint32_t a_hi = s_base + Cf::OFF_A + st * Cf::A_STAGE;
-        const uint64_t ad_hi0 = desc_interleaved(a_hi, Cf::PLANE);
-        const uint64_t ad_lo0 = desc_interleaved(a_hi + Cf::A_COPY, Cf::PLANE);
+        // the two 4-channel K chunks of one MMA are NPAR planes apart
+        const uint64_t ad_hi0 = desc_interleaved(a_hi, Cf::NPAR * Cf::PLANE);
+        const uint64_t ad_lo0 = desc_interleaved(a_hi + Cf::A_COPY, Cf::NPAR * Cf::PLANE);
 #pragma unroll 1
         for (int mb = 0; mb < Cf::MB; ++mb) {
-          const uint32_t d = tbase + acc * Cf::ACC_COLS + mb * NOUT;
           const uint64_t ad_hi = ad_hi0 + (uint64_t)(mb * 128), ad_lo = ad_lo0 + (uint64_t)(mb * 128);
 #pragma unroll
-          for (int tap = 0; tap < 9; ++tap) {
+          for (int a = 0; a < Cf::NPAR; ++a) {
+            // accumulator of conv rows with parity a (one block of NOUT columns each)
+            const uint32_t d = tbase + acc * Cf::ACC_COLS + (mb * Cf::NPAR + a) * NOUT;
 #pragma unroll
-            for (int kk = 0; kk < Cf::KSTEPS; ++kk) {
-              // operand rows start (r * PW + s) positions and 2*kk planes in
-              const uint32_t a_off = (uint32_t)(((tap / 3) * Cf::PW + tap % 3) * 16 + 2 * kk * Cf::PLANE) >> 4;
-              const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + 2 * kk) * Cf::BPLANE) >> 4;
-              tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (tap | kk) != 0);
-              if (SPLIT3) {
-                tc::mma_tf32(d, ad_hi + a_off, bd_lo + b_off, idesc, 1);
-                tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc, 1);
+            for (int tap = 0; tap < 9; ++tap) {
+              const int r = tap / 3, sc = tap % 3;
+              // plane parity and row offset of the tap's input rows
+              const int pp = Cf::PAR ? (a + r) & 1 : 0, ro = Cf::PAR ? (a + r) >> 1 : r;
+#pragma unroll
+              for (int kk = 0; kk < Cf::KSTEPS; ++kk) {
+                // operand rows start (ro * PW + sc) positions into plane (4-channel group 2kk, parity pp)
+                const uint32_t a_off =
+                    (uint32_t)((ro * Cf::PW + sc) * 16 + (2 * kk * Cf::NPAR + pp) * Cf::PLANE) >> 4;
+                const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + 2 * kk) * Cf::BPLANE) >> 4;
+                tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (tap | kk) != 0);
+                if (SPLIT3) {
+                  tc::mma_tf32(d, ad_hi + a_off, bd_lo + b_off, idesc, 1);
+                  tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc, 1);
+                }
               }
             }
           }
@@ -347,103 +345,79 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
   } else if (warp < kTransformWarp0) {
     // ------------------------------------------------------------ epilogue
-    // Per group of CG output channels: TMEM -> registers (+ bias) -> the
-    // staging tile [CG][TH][W] in shared memory (for one channel the lanes
-    // write consecutive pixels), then one TMA store of the whole group into
-    // NCHW y (rows past H are clipped by the tensor map).  The staging tile
-    // is reused once the store has read it.
+    // Per M block and group of CG channels: TMEM -> registers, + bias, and
+    // straight to global memory.  Lane m of the block is GEMM row m: pixel
+    // (i, w) = (m / PW, m % PW) of the tile (kFusePool: pooled row i, conv
+    // rows 2i and 2i + 1 in the two parity accumulators); rows with w >= W
+    // or past the image are discarded.
     const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const bool storer = warp == 2 && lane == 0;
-    const uint32_t stg = s_base + Cf::OFF_STG;
+    const uint32_t tq = (uint32_t)(q * 32) << 16;
+    const long long plane_px = Cf::PAR ? (long long)(p.H / 2) * (W / 2) : (long long)p.H * W;
+    // the two warps of a lane quarter: with two channel groups each takes
+    // one group (all M blocks), with one group they alternate M blocks
+    constexpr int NCG = NOUT / CG;
+    const int half = (warp - kEpiWarp0) >> 2;
+    const int cg = NCG == 2 ? half : 0;
+    const int mb0 = NCG == 2 ? 0 : half, mbs = NCG == 2 ? 1 : 2;
+    const bool active = cg * CG < p.COUT;
+    float bias_r[CG];
+#pragma unroll
+    for (int c = 0; c < CG; ++c) bias_r[c] = bias_s[cg * CG + c];
     int it = 0;
-    uint32_t use = 0;  // staging uses so far (one mbarrier phase each)
-    bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       if (!tc::mbar_wait(&tfull[acc], aph, abort_v, p.err, 204)) break;
       tc::fence_after_sync();
       const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * TH;
-      for (int cg = 0; cg < NOUT / CG && cg * CG < p.COUT; ++cg, ++use) {
-        if (!tc::mbar_wait(&sfree, (use & 1) ^ 1, abort_v, p.err, 207)) {
-          ok = false;
-          break;
-        }
+      const uint32_t tacc = tbase + acc * Cf::ACC_COLS + tq + cg * CG;
 #pragma unroll 1
-        for (int mb = 0; mb < Cf::MB; ++mb) {
-          uint32_t r[CG];
-          tmem_ld_cols<CG>(tbase + acc * Cf::ACC_COLS + mb * NOUT + cg * CG + ((uint32_t)(q * 32) << 16), r);
+      for (int mb = mb0; mb < Cf::MB && active; mb += mbs) {
+        const int m = mb * 128 + q * 32 + lane;
+        const int i = m / Cf::PW, col = m % Cf::PW;
+        if constexpr (Cf::PAR) {
+          // ReLU + 2x2 max-pool; window order (0,0) (0,1) (1,0) (1,1), the
+          // first maximum wins, code 255 when the maximum is not positive.
+          // The even-column lane of each pair stores.  H is even, so conv
+          // row 2i + 1 exists whenever row 2i does.
+          const bool store = col < W && !(col & 1) && i < TH / 2 && h0 + 2 * i < p.H;
+          const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 / 2 + i) * (W / 2) +
+                              col / 2;
+          uint32_t top[CG], bot[CG];
+          tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NOUT, top);
+          tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NOUT, bot);
           tc::tmem_ld_wait();
-          const int m = mb * 128 + q * 32 + lane;
-          const int i = m / Cf::PW, col = m % Cf::PW;
-          if (col < W && i < TH) {
 #pragma unroll
-            for (int c = 0; c < CG; ++c)
-              st_shared_f32(stg + (uint32_t)((c * TH + i) * W + col) * 4,
-                            __fadd_rn(__uint_as_float(r[c]), bias_s[cg * CG + c]));
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&sfull);
-        bool stored = true;
-        if (FUSE == kFusePool) {
-          // ReLU + 2x2 max-pool of the staged group: every epilogue thread
-          // waits for the whole tile, pools a share of it into the pooled
-          // staging tiles, and the storer sends both with TMA.
-          stored = tc::mbar_wait(&sfull, use & 1, abort_v, p.err, 208);
-          if (stored) {
-            const uint32_t pst = s_base + Cf::OFF_PST, cst = s_base + Cf::OFF_CST;
-            for (int e = (warp - 2) * 32 + lane; e < Cf::PNUM; e += 128) {
-              const int c = e / ((TH / 2) * (W / 2)), rem = e % ((TH / 2) * (W / 2));
-              const int pi = rem / (W / 2), pj = rem % (W / 2);
-              const uint32_t a0 = stg + (uint32_t)((c * TH + 2 * pi) * W + 2 * pj) * 4;
-              float v0, v1, v2, v3;
-              asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v0), "=f"(v1) : "r"(a0) : "memory");
-              asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v2), "=f"(v3) : "r"(a0 + W * 4) : "memory");
-              float m = v0;
+          for (int c = 0; c < CG; ++c) {
+            const float v0 = __fadd_rn(__uint_as_float(top[c]), bias_r[c]);
+            const float v2 = __fadd_rn(__uint_as_float(bot[c]), bias_r[c]);
+            const float v1 = __shfl_xor_sync(0xffffffffu, v0, 1);
+            const float v3 = __shfl_xor_sync(0xffffffffu, v2, 1);
+            if (store && cg * CG + c < p.COUT) {
+              float mx = v0;
               uint32_t idx = 0;
-              if (v1 > m) m = v1, idx = 1;
-              if (v2 > m) m = v2, idx = 2;
-              if (v3 > m) m = v3, idx = 3;
-              st_shared_f32(pst + (uint32_t)e * 4, m > 0.0f ? m : 0.0f);
-              asm volatile("st.shared.u8 [%0], %1;" ::"r"(cst + (uint32_t)e), "r"(m > 0.0f ? idx : (uint32_t)kNoGradCode)
-                           : "memory");
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&pfull);
-            if (storer) {
-              stored = tc::mbar_wait(&pfull, use & 1, abort_v, p.err, 209);
-              if (stored) {
-                tma_store_3d(&tmy, pst, 0, h0 / 2, n * p.COUT + cg * CG);
-                tma_store_3d(&tmy2, cst, 0, h0 / 2, n * p.COUT + cg * CG);
-                bulk_commit_group();
-                bulk_wait_group_read0();
-                tc::mbar_arrive(&sfree);
-              }
+              if (v1 > mx) mx = v1, idx = 1;
+              if (v2 > mx) mx = v2, idx = 2;
+              if (v3 > mx) mx = v3, idx = 3;
+              p.y[o + c * plane_px] = mx > 0.0f ? mx : 0.0f;
+              p.codes[o + c * plane_px] = mx > 0.0f ? (uint8_t)idx : kNoGradCode;
             }
           }
-        } else if (storer) {
-          stored = tc::mbar_wait(&sfull, use & 1, abort_v, p.err, 208);
-          if (stored) {
-            tma_store_3d(&tmy, stg, 0, h0, n * p.COUT + cg * CG);
-            bulk_commit_group();
-            bulk_wait_group_read0();
-            tc::mbar_arrive(&sfree);
-          }
-        }
-        __syncwarp();
-        if (__any_sync(0xffffffffu, !stored)) {
-          ok = false;
-          break;
+        } else {
+          const bool store = col < W && i < TH && h0 + i < p.H;
+          const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 + i) * W + col;
+          uint32_t r[CG];
+          tmem_ld_cols<CG>(tacc + mb * NOUT, r);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < CG; ++c)
+            if (store && cg * CG + c < p.COUT) p.y[o + c * plane_px] = __fadd_rn(__uint_as_float(r[c]), bias_r[c]);
         }
       }
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&tempty[acc]);
     }
-    if (storer) bulk_wait_group0();  // the last stores have landed in global memory
   } else {
     // ----------------------------------------------------------- transform
     // Item (plane c4, row j, pixel quad qd): four 16-byte reads (channels
@@ -489,7 +463,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           for (int ci = 0; ci < 4; ++ci)
             v[ci] = rotl4(ld_shared_v4(raw + (uint32_t)(((4 * c4 + ci) * Cf::ROWS + j) * W + 4 * qd) * 4), rot);
         }
-        const uint32_t row0 = (uint32_t)c4 * Cf::PLANE + (uint32_t)(j * Cf::PW + 1 + 4 * qd) * 16;
+        // padded row j: row j of plane c4, or (row-parity split) row j / 2
+        // of plane (c4, j % 2)
+        const uint32_t row0 = (uint32_t)(c4 * Cf::NPAR + (Cf::PAR ? (j & 1) : 0)) * Cf::PLANE +
+                              (uint32_t)((Cf::PAR ? j >> 1 : j) * Cf::PW + 1 + 4 * qd) * 16;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const uint32_t dst = a_hi + row0 + (uint32_t)((jj + rot) & 3) * 16;
@@ -551,9 +528,9 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
 int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
   using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
-  if (p.COUT % CG != 0 || !aligned16(io.y) || !aligned16(io.x) ||
-      (FUSE == kFusePool && !aligned16(io.y_codes)) || (FUSE == kFuseUnpool && !aligned16(io.x_codes))) {
-    *handled = false;  // a store box would cross into the next image's channels, or TMA cannot address it
+  if (!aligned16(io.x) || (FUSE == kFuseUnpool && !aligned16(io.x_codes)) ||
+      (reinterpret_cast<uintptr_t>(io.y) & 3)) {
+    *handled = false;  // TMA cannot address the input, or the output is not f32-aligned
     return REMORA_OK;
   }
   auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
@@ -562,7 +539,7 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
     attr = true;
   }
-  CUtensorMap mx, my, mx2, my2;
+  CUtensorMap mx, mx2;
   if (FUSE == kFuseUnpool) {
     REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx));
     REMORA_TRY(encode_activation(io.x_codes, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx2, true));
@@ -570,19 +547,14 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
     REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H, W, Cf::ROWS, CIN, &mx));
     mx2 = mx;
   }
-  if (FUSE == kFusePool) {
-    REMORA_TRY(encode_activation(io.y, p.N, p.COUT, p.H / 2, W / 2, TH / 2, CG, &my));
-    REMORA_TRY(encode_activation(io.y_codes, p.N, p.COUT, p.H / 2, W / 2, TH / 2, CG, &my2, true));
-  } else {
-    REMORA_TRY(encode_activation(io.y, p.N, p.COUT, p.H, W, TH, CG, &my));
-    my2 = my;
-  }
   ConvTCParams q = p;
+  q.y = io.y;
+  q.codes = io.y_codes;
   q.tiles_per_img = (p.H + TH - 1) / TH;
   const int ntiles = p.N * q.tiles_per_img;
   const int grid = std::min(ntiles, sm_count);
   note_launch();
-  kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, my, mx2, my2, q);
+  kern<<<grid, kConvThreads, Cf::SMEM, stream>>>(mx, mx2, q);
   REMORA_CUDA_TRY(cudaGetLastError());
   *handled = true;
   return REMORA_OK;
@@ -595,8 +567,8 @@ int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool s
   *handled = false;
   const int nout = p.COUT <= 16 ? 16 : 32;
   if (cin == 16 && width == 64 && nout == 32)
-    return split ? launch_conv<16, 64, 8, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
-                 : launch_conv<16, 64, 8, 32, false, 1, 2, 16>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<16, 64, 8, 32, true, 2, 1, 16>(io, p, sm_count, stream, handled)
+                 : launch_conv<16, 64, 8, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 64 && nout == 16)
     return split ? launch_conv<32, 64, 4, 16, true, 1, 1, 8>(io, p, sm_count, stream, handled)
                  : launch_conv<32, 64, 8, 16, false, 1, 1, 8>(io, p, sm_count, stream, handled);
@@ -604,8 +576,8 @@ int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool s
     return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
                  : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 32 && nout == 16)
-    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 16>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 1, 1, 16>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 8>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 1, 1, 8>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
@@ -615,8 +587,8 @@ int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, b
                   cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 16 && width == 32 && p.COUT > 16 && p.COUT <= 32 && p.H % 2 == 0)
-    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
-                 : launch_conv<16, 32, 16, 32, false, 1, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<16, 32, 16, 32, true, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
+                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
@@ -624,8 +596,8 @@ int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width,
                     cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 32 && width == 32 && p.COUT <= 16 && p.H % 2 == 0)
-    return split ? launch_conv<32, 32, 8, 16, true, 2, 1, 16, kFuseUnpool>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 2, 1, 16, kFuseUnpool>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 32, 8, 16, true, 2, 1, 8, kFuseUnpool>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 2, 1, 8, kFuseUnpool>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
@@ -642,7 +614,7 @@ int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const flo
   if (!shape_ok(g, x, precision) || g.K > 32) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
-  ConvTCParams p{w, bias, y, g.N, g.H, g.K, 0, 0, ws->err};
+  ConvTCParams p{w, bias, y, nullptr, g.N, g.H, g.K, 0, 0, ws->err};
   return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
                   stream, handled);
 }
@@ -653,7 +625,7 @@ int conv_tc_fwd_relu_pool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x,
   if (!shape_ok(g, x, precision) || g.K > 32) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
-  ConvTCParams p{w, bias, pooled, g.N, g.H, g.K, 0, 0, ws->err};
+  ConvTCParams p{w, bias, pooled, codes, g.N, g.H, g.K, 0, 0, ws->err};
   return dispatch_pool(ConvIO{x, nullptr, pooled, codes}, p, g.C, g.W, precision == REMORA_PREC_3XTF32,
                        ctx->sm_count, stream, handled);
 }
@@ -664,7 +636,7 @@ int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpo
   if (!shape_ok(g, dpooled, precision) || g.C > 32) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
-  ConvTCParams p{w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
+  ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
   return dispatch_unpool(ConvIO{dpooled, codes, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32,
                          ctx->sm_count, stream, handled);
 }
@@ -676,7 +648,7 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights
-  ConvTCParams p{w, nullptr, dx, g.N, g.H, g.C, 1, 0, ws->err};
+  ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
   return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
                   stream, handled);
 }
