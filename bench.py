@@ -14,7 +14,9 @@ Other configs: ``row_norms`` (f32[8192,1024] -> sqrt(sum x*x)), ``matmul``
 ([32,1024,1024] x [32,1024,1024], TF32), ``conv`` / ``conv_dgrad`` /
 ``conv_wgrad`` (x [256,16,64,64] * w [32,16,3,3], pad 1), ``cnn`` (crater-CNN
 SGD step, global batch 4096, data parallel over N ranks with an NCCL
-gradient allreduce: strong scaling; 3xTF32, ``cnn_tf32`` the TF32 form).
+gradient allreduce: strong scaling; 3xTF32, ``cnn_tf32`` the TF32 form),
+``sort`` / ``grade`` / ``filter`` (the reference's C runtime helpers on
+2^26 f32 keys ~ N(0,1); filter keeps x > 0).
 
 With N GPUs (torchrun, one process per GPU) every rank runs its own copy of
 the workload (weak scaling: folds shard frames, matmuls shard rows; no
@@ -43,6 +45,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC_FOLD = "map/fold HBM GB/s"
 METRIC_MM = "matmul/conv TFLOP/s"
+METRIC_RT = "runtime helpers HBM GB/s"
 
 
 def measured_peaks() -> dict:
@@ -541,6 +544,125 @@ class CnnWorkload:
     cpu_sample = "32 samples per SGD step (oracle CNN step: forward, backward, update; OpenMP over images)"
 
 
+class RuntimeWorkload:
+    """The reference's C runtime helpers (remora/remora_rt.c) on 2^26 f32
+    keys ~ N(0,1) (268 MB, larger than L2): sort, grade, or filter (x > 0).
+    `value` counts the bytes the operation must move at least (keys in,
+    result out); the roofline counts the traffic of the implementation's
+    passes (LSD sort: 4 passes, each reading the keys twice and writing them
+    once, plus the indices for grade; filter: two reads, one write of the
+    kept half)."""
+
+    metric, unit, bound = METRIC_RT, "GB/s", "hbm"
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.n = 1 << 26
+        n = self.n
+        if name == "sort":
+            self.work_per_call = 8 * n
+            self.bytes_per_call = 4 * 12 * n
+        elif name == "grade":
+            self.work_per_call = 8 * n
+            # pass 0: 4 (count) + 4 (keys) + 8 (keys, indices out); passes 1-2:
+            # 4 + 8 + 8; pass 3: 4 + 8 + 4 (indices only)
+            self.bytes_per_call = 16 * n + 2 * 20 * n + 16 * n
+        else:
+            self.work_per_call = 4 * n + 2 * n  # read all, write the kept half
+            self.bytes_per_call = 4 * n + 4 * n + 2 * n
+        self.desc = f"{name} f32[{n}] ~ N(0,1)" + (" keeping x > 0" if name == "filter" else "")
+        self.rotate = 1
+
+    def setup(self, dev, rank: int) -> None:
+        import torch
+
+        from remora_b200 import _lib as L
+        from remora_b200.abi import tensor_descriptor
+        from remora_b200.runtime import context
+
+        self.torch, self.L, self.lib, self.dev = torch, L, L.lib(), dev
+        rng = np.random.Generator(np.random.PCG64(1729 + 1000 * rank))
+        self.host = rng.standard_normal(self.n, dtype=np.float32)
+        self.x = torch.from_numpy(self.host).to(dev)
+        self.out = torch.empty(self.n, dtype=torch.int32 if self.name == "grade" else torch.float32, device=dev)
+        self.count = torch.zeros((), dtype=torch.int64, device=dev)
+        self.ctx = context(dev.index)
+        self.sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        self.xd, self.od, self.cd = (tensor_descriptor(t) for t in (self.x, self.out, self.count))
+        self.pred = L.RemoraFilterPred(L.OP_GT, 0.0, 0, 0)
+
+    def _run(self, xd) -> None:
+        lib, a = self.lib, ctypes.addressof
+        if self.name == "sort":
+            st = lib.remora_b200_sort(self.ctx.ptr, self.L.F32, a(xd), a(self.od), 1, self.sptr)
+        elif self.name == "grade":
+            st = lib.remora_b200_grade(self.ctx.ptr, self.L.F32, a(xd), a(self.od), 1, self.sptr)
+        else:
+            st = lib.remora_b200_filter(self.ctx.ptr, self.L.F32, a(xd), None, 0, ctypes.byref(self.pred), a(self.od),
+                                        a(self.cd), self.sptr)
+        if st:
+            self.L.check(st, self.name)
+
+    def call(self, k: int) -> None:
+        self._run(self.xd)
+
+    def check(self) -> None:
+        torch = self.torch
+        self.call(0)
+        torch.cuda.synchronize()
+        if self.name == "sort":
+            ok = torch.equal(self.out, torch.sort(self.x)[0])
+        elif self.name == "grade":
+            ok = torch.equal(self.x[self.out.long()], torch.sort(self.x)[0])
+        else:
+            ref = self.x[self.x > 0]
+            ok = int(self.count.item()) == ref.numel() and torch.equal(self.out[: ref.numel()], ref)
+        if not ok:
+            raise SystemExit("benchmark output does not match the check")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        from remora_b200.abi import tensor_descriptor
+
+        torch = self.torch
+        self.pin_in = torch.from_numpy(self.host).pin_memory()
+        self.pin_out = torch.empty(self.n, dtype=self.out.dtype).pin_memory()
+        self.dbuf = torch.empty(self.n, dtype=torch.float32, device=self.dev)
+        self.dbuf_desc = tensor_descriptor(self.dbuf)
+        return self.n * 4, self.n * 4
+
+    def e2e_step(self) -> None:
+        L, lib = self.L, self.lib
+        L.check(lib.remora_b200_memcpy_h2d(self.ctx.ptr, ctypes.c_void_p(self.dbuf.data_ptr()),
+                                           ctypes.c_void_p(self.pin_in.data_ptr()), self.n * 4, self.sptr))
+        self._run(self.dbuf_desc)
+        L.check(lib.remora_b200_memcpy_d2h(self.ctx.ptr, ctypes.c_void_p(self.pin_out.data_ptr()),
+                                           ctypes.c_void_p(self.out.data_ptr()), self.n * 4, self.sptr))
+
+    # ---- CPU side: remora_rt.c itself where it was compiled, else the oracle
+    def cpu_prepare(self) -> None:
+        o = _oracle()
+        self.o = o
+        self.cn = 1 << 22
+        self.cx = np.random.Generator(np.random.PCG64(1729)).standard_normal(self.cn, dtype=np.float32)
+        self.cmask = (self.cx > 0).astype(np.int32)
+        self.cpu_kind = "reference" if o.ref_available() else "port"
+        self.nt = 1
+        src = "remora_rt.c compiled from the reference source" if self.cpu_kind == "reference" else "the oracle port"
+        self.cpu_sample = f"{self.cn} keys per sample ({src}, one thread, as remora_rt.c is sequential)"
+
+    def cpu_step(self) -> float:
+        o, ref = self.o, self.cpu_kind == "reference"
+        if self.name == "sort":
+            (o.ref_sort if ref else o.sort)(self.cx)
+        elif self.name == "grade":
+            (o.ref_grade if ref else o.grade)(self.cx)
+        elif ref:
+            o.ref_filter(self.cx, self.cmask)
+        else:
+            o.filter_(self.cx, self.cmask)
+        return float(self.work_per_call) * self.cn / self.n
+
+
 def make_workload(name: str):
     if name in ("chained", "row_norms"):
         return FoldWorkload(name)
@@ -548,6 +670,8 @@ def make_workload(name: str):
         return CnnWorkload(name)
     if name.startswith("conv"):
         return ConvWorkload(name)
+    if name in ("sort", "grade", "filter"):
+        return RuntimeWorkload(name)
     return MatmulWorkload(name)
 
 
@@ -725,7 +849,8 @@ def run_ours(args) -> None:
 TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms": None,
                                     "matmul": 335_706_368 + 61_118_208, "matmul_3x": None, "bmm": None,
                                     "conv": 67_154_688 + 75_236_608, "conv_dgrad": None,
-                                    "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None}
+                                    "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None,
+                                    "sort": None, "grade": None, "filter": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
@@ -743,7 +868,8 @@ def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
         if el >= budget_s:
             break
     scale = {"GB/s": 1e9, "TFLOP/s": 1e12, "samples/s": 1.0}[wl.unit]
-    return {"value": round(work / el / scale, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
+    return {"value": round(work / el / scale, 5), "unit": wl.unit, "cores": wl.nt,
+            "kind": getattr(wl, "cpu_kind", "port"),
             "sample": f"{wl.cpu_sample}; {reps} samples in {el:.1f} s"}
 
 
@@ -769,14 +895,16 @@ def run_reference(args) -> None:
         "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded PCG64)", "impl": "reference",
         "config": {"workload": wl.desc, "calls_per_step": 1},
-        "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": wl.nt, "kind": "port",
+        "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": wl.nt,
+                         "kind": getattr(wl, "cpu_kind", "port"),
                          "sample": f"{wl.cpu_sample}; one sample per step, {args.steps} steps"},
         "e2e": {"value": round(value, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm", "conv", "conv_dgrad", "conv_wgrad", "cnn", "cnn_tf32"]
+CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm", "conv", "conv_dgrad", "conv_wgrad", "cnn", "cnn_tf32",
+           "sort", "grade", "filter"]
 
 
 def main() -> None:

@@ -192,6 +192,17 @@ typedef struct {
   int32_t reserved_;
 } RemoraIm2colSpec;
 
+/* Filter predicate fused into the compaction: keep x where `x op literal`
+   (op one of REMORA_OP_LT .. REMORA_OP_NE; f32 comparisons are ordered, so
+   NaN compares false), the mask the reference's lowering builds with
+   arith.cmpi / arith.cmpf (remora/lowering/tensor_ops.py:2655-2706). */
+typedef struct {
+  int32_t op;
+  float lit_f;   /* literal of an f32 filter */
+  int32_t lit_i; /* literal of an i32 filter */
+  int32_t reserved_;
+} RemoraFilterPred;
+
 typedef struct RemoraB200Ctx RemoraB200Ctx;
 
 /* ------------------------------------------------------------------------ */
@@ -344,6 +355,68 @@ int remora_b200_col2im(RemoraB200Ctx *ctx, const RemoraIm2colSpec *spec,
 int remora_b200_transpose(RemoraB200Ctx *ctx, int32_t dtype,
                           const RemoraMemRef2 *in, RemoraMemRef2 *out,
                           remora_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* The C runtime helpers of the reference (remora/remora_rt.c) on the GPU.   */
+/* f32 and i32 data, as remora_rt.c; rotate and append also take bool.      */
+/* ------------------------------------------------------------------------ */
+
+/* Ascending sort of a rank-1 array, or of every row of a rank-2 array.
+   Replaces remora_sort_i32 / remora_sort_f32 (remora/remora_rt.c:42-54) and
+   the per-row aliases remora_sort_1d_* (remora/remora_rt.c:289-290) used by
+   the rank-2 lowering (remora/lowering/tensor_ops.py:2505-2570).  in and out
+   may be the same buffer.  For f32, -0.0 is placed before +0.0 (qsort leaves
+   their order open); NaNs without the sign bit go last.  Rows of up to 2^31 - 1. */
+int remora_b200_sort(RemoraB200Ctx *ctx, int32_t dtype, const void *in_desc,
+                     void *out_desc, int32_t rank, remora_stream_t stream);
+
+/* Stable ascending argsort (int32 indices; equal values keep index order,
+   -0.0 and +0.0 are equal) of a rank-1 array or of every row of a rank-2
+   array.  Replaces remora_grade_i32 / remora_grade_f32
+   (remora/remora_rt.c:56-121) and remora_grade_1d_* (:291-292). */
+int remora_b200_grade(RemoraB200Ctx *ctx, int32_t dtype, const void *in_desc,
+                      void *out_desc, int32_t rank, remora_stream_t stream);
+
+/* Stream compaction of a rank-1 array: dst[0..count) = src[i] for every i in
+   order where the flag is set; *count (a rank-0 int64 device scalar) gets
+   the number kept.  The flag is either mask[i] != 0 (mask_dtype REMORA_I32,
+   the form of remora_filter_i32 / remora_filter_f32,
+   remora/remora_rt.c:125-163, or REMORA_BOOL) or the fused predicate `pred`
+   (then mask_desc is NULL).  dst must be contiguous; elements past its
+   length are counted but not written.  Replaces the reference's n+2 buffer
+   with the count at position 0 (remora/lowering/tensor_ops.py:2707-2720,
+   remora/runtime.py:663-668) by a separate count. */
+int remora_b200_filter(RemoraB200Ctx *ctx, int32_t dtype, const void *src_desc,
+                       const void *mask_desc, int32_t mask_dtype,
+                       const RemoraFilterPred *pred, void *dst_desc,
+                       RemoraMemRef0 *count_desc, remora_stream_t stream);
+
+/* dst = src[0] repeated counts[0] times, then src[1] counts[1] times, ...
+   (rank 1; counts int32; a negative count repeats nothing).  *total (rank-0
+   int64 device scalar) gets the length of the result.  With dst_desc NULL
+   only the total is computed: remora_replicate_*_count; otherwise
+   remora_replicate_*_fill / remora_replicate_* (remora/remora_rt.c:167-285).
+   dst must be contiguous; elements past its length are not written. */
+int remora_b200_replicate(RemoraB200Ctx *ctx, int32_t dtype,
+                          const void *src_desc, const void *counts_desc,
+                          void *dst_desc, RemoraMemRef0 *total_desc,
+                          remora_stream_t stream);
+
+/* out[i, ...] = in[(i + shift) mod N, ...] along axis 0 with a non-negative
+   modulus, any rank >= 1.  Replaces remora_rotate_*_1d
+   (remora/remora_rt.c:324-358) and the rotate lowering
+   (remora/lowering/tensor_ops.py:1968-2021; interpreter np.roll(a, -shift,
+   axis=0), remora/runtime.py:1135-1139). */
+int remora_b200_rotate(RemoraB200Ctx *ctx, int32_t dtype, int64_t shift,
+                       const void *in_desc, void *out_desc, int32_t rank,
+                       remora_stream_t stream);
+
+/* out = a followed by b along axis 0 (trailing axes equal), any rank >= 1.
+   Replaces remora_append_*_1d (remora/remora_rt.c:360-388) and the append
+   lowering (remora/lowering/tensor_ops.py:2215-2263). */
+int remora_b200_append(RemoraB200Ctx *ctx, int32_t dtype, const void *a_desc,
+                       const void *b_desc, void *out_desc, int32_t rank,
+                       remora_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

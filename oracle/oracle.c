@@ -633,3 +633,99 @@ void oracle_row_norms_f32(const float *x, int64_t rows, int64_t L, float *out,
     out[r] = sqrtf(acc);
   }
 }
+
+/* ---- sort / grade / filter / replicate (remora/remora_rt.c) ---- */
+
+/* Value order of element i of a row: f32 compares as floats (so -0.0 and
+   +0.0 are equal), i32 as signed integers. */
+static int rt_less(int dtype, const void *base, int64_t a, int64_t b) {
+  if (dtype == REMORA_F32) return ((const float *)base)[a] < ((const float *)base)[b];
+  return ((const int32_t *)base)[a] < ((const int32_t *)base)[b];
+}
+
+/* Stable bottom-up merge sort of the index array idx[0..n) by the values
+   they point at. */
+static void rt_stable_order(int dtype, const void *vals, int64_t *idx, int64_t *tmp, int64_t n) {
+  for (int64_t w = 1; w < n; w *= 2) {
+    for (int64_t lo = 0; lo < n; lo += 2 * w) {
+      int64_t mid = lo + w < n ? lo + w : n, hi = lo + 2 * w < n ? lo + 2 * w : n;
+      int64_t i = lo, j = mid, k = lo;
+      while (i < mid && j < hi) tmp[k++] = rt_less(dtype, vals, idx[j], idx[i]) ? idx[j++] : idx[i++];
+      while (i < mid) tmp[k++] = idx[i++];
+      while (j < hi) tmp[k++] = idx[j++];
+    }
+    memcpy(idx, tmp, (size_t)n * sizeof(int64_t));
+  }
+}
+
+static void rt_sort_or_grade(int dtype, const void *in, void *out, int grade, int64_t rows, int64_t len,
+                             int nthreads) {
+#pragma omp parallel num_threads(nthreads)
+  {
+    int64_t *idx = (int64_t *)malloc((size_t)(len > 0 ? len : 1) * sizeof(int64_t));
+    int64_t *tmp = (int64_t *)malloc((size_t)(len > 0 ? len : 1) * sizeof(int64_t));
+#pragma omp for schedule(dynamic)
+    for (int64_t r = 0; r < rows; ++r) {
+      const char *row = (const char *)in + r * len * 4;
+      for (int64_t i = 0; i < len; ++i) idx[i] = i;
+      rt_stable_order(dtype, row, idx, tmp, len);
+      for (int64_t i = 0; i < len; ++i) {
+        if (grade) ((int32_t *)out)[r * len + i] = (int32_t)idx[i];
+        else memcpy((char *)out + (r * len + i) * 4, row + idx[i] * 4, 4);
+      }
+    }
+    free(idx);
+    free(tmp);
+  }
+}
+
+void oracle_sort(int dtype, const void *in, void *out, int64_t rows, int64_t len, int nthreads) {
+  rt_sort_or_grade(dtype, in, out, 0, rows, len, nthreads);
+}
+
+void oracle_grade(int dtype, const void *in, int32_t *out, int64_t rows, int64_t len, int nthreads) {
+  rt_sort_or_grade(dtype, in, out, 1, rows, len, nthreads);
+}
+
+static int rt_compare(int op, double x, double lit) {
+  switch (op) {
+    case REMORA_OP_LT: return x < lit;
+    case REMORA_OP_LE: return x <= lit;
+    case REMORA_OP_GT: return x > lit;
+    case REMORA_OP_GE: return x >= lit;
+    case REMORA_OP_EQ: return x == lit;
+    default: return x < lit || x > lit; /* ordered not-equal: false for NaN */
+  }
+}
+
+int64_t oracle_filter(int dtype, const void *src, const void *mask, int mask_dtype,
+                      const RemoraFilterPred *pred, int64_t n, void *dst, int64_t cap) {
+  int64_t out_n = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    int keep;
+    if (pred) {
+      if (dtype == REMORA_F32) keep = rt_compare(pred->op, ((const float *)src)[i], pred->lit_f);
+      else keep = rt_compare(pred->op, ((const int32_t *)src)[i], pred->lit_i);
+    } else if (mask_dtype == REMORA_BOOL) {
+      keep = ((const uint8_t *)mask)[i] != 0;
+    } else {
+      keep = ((const int32_t *)mask)[i] != 0;
+    }
+    if (keep) {
+      if (out_n < cap) memcpy((char *)dst + out_n * 4, (const char *)src + i * 4, 4);
+      ++out_n;
+    }
+  }
+  return out_n;
+}
+
+int64_t oracle_replicate(int dtype, const void *src, const int32_t *counts, int64_t n, void *dst, int64_t cap) {
+  (void)dtype;
+  int64_t out_n = 0;
+  for (int64_t i = 0; i < n; ++i)
+    for (int32_t r = 0; r < counts[i]; ++r) {
+      if (out_n < cap) memcpy((char *)dst + out_n * 4, (const char *)src + i * 4, 4);
+      ++out_n;
+    }
+  return out_n;
+}

@@ -15,6 +15,11 @@
  *   im2col/col2im    remora/runtime.py:1274-1305
  *   VJPs             remora/ad.py:85-179
  *   CNN formulas     examples/crater_train.py:46-54,249-253
+ *   sort / grade     remora/remora_rt.c:17-121 (interpreter: stable np.sort /
+ *                    np.argsort, remora/runtime.py:1171-1177)
+ *   filter           remora/remora_rt.c:125-163 (+ the comparison mask of
+ *                    remora/lowering/tensor_ops.py:2655-2706)
+ *   replicate        remora/remora_rt.c:167-285
  * f32 arithmetic is done as separate IEEE multiplies and adds (the file is
  * compiled with -ffp-contract=off), matching arith.mulf/arith.addf.
  */
@@ -103,6 +108,26 @@ void oracle_chained_fold_f32(const float *x, int64_t rows, int64_t L, float *out
                              int nthreads);
 void oracle_row_norms_f32(const float *x, int64_t rows, int64_t L, float *out,
                           int nthreads);
+
+/* Ascending sort of `rows` contiguous rows of `len` f32 / i32 values: a
+   stable merge sort on the numeric order (-0.0 == +0.0 keep their input
+   order, as the interpreter's stable np.sort does; qsort in remora_rt.c
+   leaves them in some order). */
+void oracle_sort(int dtype, const void *in, void *out, int64_t rows, int64_t len,
+                 int nthreads);
+/* Stable argsort per row: int32 indices, ties in index order
+   (remora_rt.c `_cmp_grade_*` breaks ties by index). */
+void oracle_grade(int dtype, const void *in, int32_t *out, int64_t rows,
+                  int64_t len, int nthreads);
+/* Keeps src[i] where the flag is set (mask != 0 for an i32 or one-byte bool
+   mask, or `src[i] op literal` for pred, ordered for f32), in order; writes
+   at most cap values and returns how many were kept. */
+int64_t oracle_filter(int dtype, const void *src, const void *mask, int mask_dtype,
+                      const RemoraFilterPred *pred, int64_t n, void *dst, int64_t cap);
+/* src[i] repeated max(counts[i], 0) times, in order; writes at most cap
+   values and returns the full length. */
+int64_t oracle_replicate(int dtype, const void *src, const int32_t *counts, int64_t n,
+                         void *dst, int64_t cap);
 
 #ifdef __cplusplus
 }

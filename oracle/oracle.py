@@ -9,6 +9,7 @@ checker and the timed CPU baseline; the product never imports it.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -20,8 +21,16 @@ LIB_PATH = HERE / "liboracle.so"
 _lib = None
 
 
+REF_DIR = HERE / "_ref"
+REF_RT_PATH = REF_DIR / "libremora_rt.so"
+REFERENCE = Path(os.environ.get("REMORA_REFERENCE", "/root/reference"))
+
+
 def build() -> Path:
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    if (REFERENCE / "remora" / "remora_rt.c").exists():
+        # The reference's own C runtime, compiled from its source into _ref/.
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REMORA_REFERENCE={REFERENCE}"], check=True)
     return LIB_PATH
 
 
@@ -217,3 +226,149 @@ def cnn_step(params: np.ndarray, images: np.ndarray, labels: np.ndarray, batch_t
     loss = lib().oracle_cnn_step(_p(params), _p(grads), _p(imgs), _p(labs), _i64(B), _i64(batch_total or B),
                                  ctypes.c_float(lr), int(apply_sgd), int(nthreads))
     return float(loss), grads
+
+
+# ---- the reference's C runtime helpers (remora/remora_rt.c) ----
+_F32, _I32, _BOOL = 0, 1, 2
+
+
+def _code(a: np.ndarray) -> int:
+    return _F32 if a.dtype == np.float32 else _I32
+
+
+class FilterPred(ctypes.Structure):
+    _fields_ = [("op", ctypes.c_int32), ("lit_f", ctypes.c_float), ("lit_i", ctypes.c_int32),
+                ("reserved_", ctypes.c_int32)]
+
+
+def sort(x: np.ndarray, nthreads: int = 1) -> np.ndarray:
+    """Ascending stable sort of a rank-1 array or of each row of a rank-2 one."""
+    x = np.ascontiguousarray(x)
+    out = np.empty_like(x)
+    rows, length = (1, x.size) if x.ndim == 1 else x.shape
+    lib().oracle_sort(_code(x), _p(x), _p(out), _i64(rows), _i64(length), int(nthreads))
+    return out
+
+
+def grade(x: np.ndarray, nthreads: int = 1) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    out = np.empty(x.shape, dtype=np.int32)
+    rows, length = (1, x.size) if x.ndim == 1 else x.shape
+    lib().oracle_grade(_code(x), _p(x), _p(out), _i64(rows), _i64(length), int(nthreads))
+    return out
+
+
+def filter_(src: np.ndarray, mask: np.ndarray | None = None, pred: tuple[int, float | int] | None = None) -> np.ndarray:
+    """filter with an i32/bool mask, or with pred = (REMORA_OP_* code, literal)."""
+    src = np.ascontiguousarray(src)
+    dst = np.empty_like(src)
+    f = lib().oracle_filter
+    f.restype = ctypes.c_int64
+    if pred is not None:
+        pr = FilterPred(pred[0], float(pred[1]), int(pred[1]), 0)
+        n = f(_code(src), _p(src), None, 0, ctypes.byref(pr), _i64(src.size), _p(dst), _i64(src.size))
+    else:
+        m = np.ascontiguousarray(mask)
+        mdt = _BOOL if m.dtype in (np.bool_, np.uint8) else _I32
+        n = f(_code(src), _p(src), _p(m), mdt, None, _i64(src.size), _p(dst), _i64(src.size))
+    return dst[:n].copy()
+
+
+def replicate(src: np.ndarray, counts: np.ndarray) -> np.ndarray:
+    src = np.ascontiguousarray(src)
+    c = np.ascontiguousarray(counts, dtype=np.int32)
+    total = int(np.clip(c, 0, None).astype(np.int64).sum())
+    dst = np.empty(max(total, 1), dtype=src.dtype)
+    f = lib().oracle_replicate
+    f.restype = ctypes.c_int64
+    n = f(_code(src), _p(src), _p(c), _i64(src.size), _p(dst), _i64(total))
+    assert n == total
+    return dst[:total].copy()
+
+
+def rotate(x: np.ndarray, shift: int) -> np.ndarray:
+    """out[i] = x[(i + shift) mod N] along axis 0 (np.roll(x, -shift, 0))."""
+    n = x.shape[0]
+    if n == 0:
+        return x.copy()
+    k = shift % n
+    return np.concatenate([x[k:], x[:k]], axis=0)
+
+
+def append(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    return np.concatenate([a, b], axis=0)
+
+
+# ---- remora_rt.c itself (compiled into _ref/ where the reference is present) ----
+_ref_rt = None
+
+
+def ref_available() -> bool:
+    return REF_RT_PATH.exists()
+
+
+def ref_rt() -> ctypes.CDLL:
+    global _ref_rt
+    if _ref_rt is None:
+        if not REF_RT_PATH.exists():
+            raise FileNotFoundError(f"{REF_RT_PATH} is not built (needs the reference source tree)")
+        _ref_rt = ctypes.CDLL(str(REF_RT_PATH))
+        for name in ("remora_filter_i32", "remora_filter_f32", "remora_replicate_i32", "remora_replicate_f32",
+                     "remora_replicate_i32_count", "remora_replicate_f32_count"):
+            getattr(_ref_rt, name).restype = ctypes.c_int64
+    return _ref_rt
+
+
+def _mr(a: np.ndarray):
+    # remora_rt.c's flattened rank-1 memref: (allocated, aligned, offset, size, stride)
+    return [_p(a), _p(a), _i64(0), _i64(a.size), _i64(1)]
+
+
+def _sfx(a: np.ndarray) -> str:
+    return "f32" if a.dtype == np.float32 else "i32"
+
+
+def ref_sort(x: np.ndarray) -> np.ndarray:
+    out = np.array(x, copy=True, order="C")
+    getattr(ref_rt(), f"remora_sort_{_sfx(x)}")(*_mr(out))
+    return out
+
+
+def ref_grade(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    out = np.empty(x.size, dtype=np.int32)
+    getattr(ref_rt(), f"remora_grade_{_sfx(x)}")(*_mr(x), *_mr(out))
+    return out
+
+
+def ref_filter(src: np.ndarray, mask: np.ndarray) -> np.ndarray:
+    src = np.ascontiguousarray(src)
+    m = np.ascontiguousarray(mask, dtype=np.int32)
+    dst = np.empty(src.size + 2, dtype=src.dtype)
+    n = getattr(ref_rt(), f"remora_filter_{_sfx(src)}")(*_mr(src), *_mr(m), *_mr(dst))
+    return dst[:n].copy()
+
+
+def ref_replicate(src: np.ndarray, counts: np.ndarray) -> tuple[int, np.ndarray]:
+    """(the count helper's total, the fill result)."""
+    src = np.ascontiguousarray(src)
+    c = np.ascontiguousarray(counts, dtype=np.int32)
+    total = getattr(ref_rt(), f"remora_replicate_{_sfx(src)}_count")(*_mr(src), *_mr(c))
+    dst = np.empty(max(1, int(np.clip(c, 0, None).sum())), dtype=src.dtype)
+    n = getattr(ref_rt(), f"remora_replicate_{_sfx(src)}")(*_mr(src), *_mr(c), *_mr(dst))
+    return int(total), dst[:n].copy()
+
+
+def ref_rotate(x: np.ndarray, shift: int) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    k = np.array([shift], dtype=np.int32)
+    out = np.empty_like(x)
+    getattr(ref_rt(), f"remora_rotate_{_sfx(x)}_1d")(*_mr(x), *_mr(k), *_mr(out))
+    return out
+
+
+def ref_append(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    out = np.empty(a.size + b.size, dtype=a.dtype)
+    getattr(ref_rt(), f"remora_append_{_sfx(a)}_1d")(*_mr(a), *_mr(b), *_mr(out))
+    return out

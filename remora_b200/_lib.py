@@ -119,6 +119,15 @@ class RemoraIm2colSpec(ctypes.Structure):
     ]
 
 
+class RemoraFilterPred(ctypes.Structure):
+    _fields_ = [
+        ("op", ctypes.c_int32),
+        ("lit_f", ctypes.c_float),
+        ("lit_i", ctypes.c_int32),
+        ("reserved_", ctypes.c_int32),
+    ]
+
+
 # ------------------------------------------------------------------ loading
 _VP = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -156,6 +165,12 @@ _PROTOTYPES: dict[str, tuple] = {
     "remora_b200_im2col": (_I32, [_VP, ctypes.POINTER(RemoraIm2colSpec), _VP, _VP, _VP]),
     "remora_b200_col2im": (_I32, [_VP, ctypes.POINTER(RemoraIm2colSpec), _VP, _VP, _VP]),
     "remora_b200_transpose": (_I32, [_VP, _I32, _VP, _VP, _VP]),
+    "remora_b200_sort": (_I32, [_VP, _I32, _VP, _VP, _I32, _VP]),
+    "remora_b200_grade": (_I32, [_VP, _I32, _VP, _VP, _I32, _VP]),
+    "remora_b200_filter": (_I32, [_VP, _I32, _VP, _VP, _I32, ctypes.POINTER(RemoraFilterPred), _VP, _VP, _VP]),
+    "remora_b200_replicate": (_I32, [_VP, _I32, _VP, _VP, _VP, _VP, _VP]),
+    "remora_b200_rotate": (_I32, [_VP, _I32, ctypes.c_int64, _VP, _VP, _I32, _VP]),
+    "remora_b200_append": (_I32, [_VP, _I32, _VP, _VP, _VP, _I32, _VP]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -259,3 +259,109 @@ def synchronize(device: int | None = None) -> None:
     dev = torch.cuda.current_device() if device is None else device
     s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     L.check(L.lib().remora_b200_synchronize(context(dev).ptr, s), "synchronize")
+
+
+# ------------------------------------------- the C runtime helpers on GPU
+_CMP = {"<": L.OP_LT, "<=": L.OP_LE, ">": L.OP_GT, ">=": L.OP_GE, "==": L.OP_EQ, "!=": L.OP_NE}
+
+
+def _sort_like(x, out, grade: bool):
+    torch = _torch()
+    _check_cuda(x)
+    if x.dim() not in (1, 2):
+        raise RemoraShapeError(f"{'grade' if grade else 'sort'} takes rank 1 or 2, got rank {x.dim()}")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.int32 if grade else x.dtype, device=x.device)
+    xd, od = tensor_descriptor(x), tensor_descriptor(out)
+    fn = L.lib().remora_b200_grade if grade else L.lib().remora_b200_sort
+    L.check(fn(_ctx(out).ptr, dtype_of(x), ctypes.addressof(xd), ctypes.addressof(od), x.dim(), _stream(out)),
+            "grade" if grade else "sort")
+    return out
+
+
+def sort(x, out=None):
+    """Ascending sort of a rank-1 array, or of every row of a rank-2 array
+    (the reference's remora_sort_* runtime helper)."""
+    return _sort_like(x, out, grade=False)
+
+
+def grade(x, out=None):
+    """Stable ascending argsort (int32), per row for rank 2 (remora_grade_*)."""
+    return _sort_like(x, out, grade=True)
+
+
+def filter(x, mask=None, *, pred: tuple[str, float | int] | None = None, out=None, count=None, sync: bool = True):
+    """Keeps x[i] where mask[i] != 0 (i32 or bool mask) or where `x[i] op lit`
+    for pred = (op, lit), in order (remora_filter_*).  With sync, returns the
+    kept values (the count is read back to the host); otherwise returns
+    (out, count) with count a device int64 scalar."""
+    torch = _torch()
+    _check_cuda(x)
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    if count is None:
+        count = torch.zeros((), dtype=torch.int64, device=x.device)
+    xd, od, cd = tensor_descriptor(x), tensor_descriptor(out), tensor_descriptor(count)
+    if (mask is None) == (pred is None):
+        raise RemoraB200Error("filter takes exactly one of mask and pred")
+    if pred is not None:
+        op, lit = pred
+        pr = L.RemoraFilterPred(_CMP[op], float(lit), int(lit), 0)
+        st = L.lib().remora_b200_filter(_ctx(out).ptr, dtype_of(x), ctypes.addressof(xd), None, 0,
+                                        ctypes.byref(pr), ctypes.addressof(od), ctypes.addressof(cd), _stream(out))
+    else:
+        _check_cuda(mask)
+        md = tensor_descriptor(mask)
+        st = L.lib().remora_b200_filter(_ctx(out).ptr, dtype_of(x), ctypes.addressof(xd), ctypes.addressof(md),
+                                        dtype_of(mask), None, ctypes.addressof(od), ctypes.addressof(cd),
+                                        _stream(out))
+    L.check(st, "filter")
+    if not sync:
+        return out, count
+    return out[: int(count.item())]
+
+
+def replicate(x, counts, out=None, *, total=None, sync: bool = True):
+    """x[0] repeated counts[0] times, then x[1] counts[1] times, ...
+    (remora_replicate_*; a negative count repeats nothing).  Without `out`
+    the total is computed first and read back to size the result."""
+    torch = _torch()
+    _check_cuda(x, counts)
+    if total is None:
+        total = torch.zeros((), dtype=torch.int64, device=x.device)
+    xd, cd, td = tensor_descriptor(x), tensor_descriptor(counts), tensor_descriptor(total)
+    lib = L.lib()
+    if out is None:
+        L.check(lib.remora_b200_replicate(_ctx(x).ptr, dtype_of(x), ctypes.addressof(xd), ctypes.addressof(cd),
+                                          None, ctypes.addressof(td), _stream(x)), "replicate")
+        out = torch.empty((int(total.item()),), dtype=x.dtype, device=x.device)
+    od = tensor_descriptor(out)
+    L.check(lib.remora_b200_replicate(_ctx(x).ptr, dtype_of(x), ctypes.addressof(xd), ctypes.addressof(cd),
+                                      ctypes.addressof(od), ctypes.addressof(td), _stream(x)), "replicate")
+    if not sync:
+        return out, total
+    return out[: min(int(total.item()), out.shape[0])]
+
+
+def rotate(x, shift: int, out=None):
+    """out[i] = x[(i + shift) mod N] along axis 0 (remora_rotate_*)."""
+    torch = _torch()
+    _check_cuda(x)
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    xd, od = tensor_descriptor(x), tensor_descriptor(out)
+    L.check(L.lib().remora_b200_rotate(_ctx(out).ptr, dtype_of(x), int(shift), ctypes.addressof(xd),
+                                       ctypes.addressof(od), x.dim(), _stream(out)), "rotate")
+    return out
+
+
+def append(a, b, out=None):
+    """a followed by b along axis 0 (remora_append_*)."""
+    torch = _torch()
+    _check_cuda(a, b)
+    if out is None:
+        out = torch.empty((a.shape[0] + b.shape[0], *a.shape[1:]), dtype=a.dtype, device=a.device)
+    ad, bd, od = tensor_descriptor(a), tensor_descriptor(b), tensor_descriptor(out)
+    L.check(L.lib().remora_b200_append(_ctx(out).ptr, dtype_of(a), ctypes.addressof(ad), ctypes.addressof(bd),
+                                       ctypes.addressof(od), a.dim(), _stream(out)), "append")
+    return out

@@ -222,5 +222,53 @@ def main() -> None:
     save("bce", z=zs, y=ys, loss=np.asarray(losses), dz=np.asarray(grads))
 
 
+def runtime_helpers() -> None:
+    """sort / grade / filter / replicate / rotate / append through the
+    reference interpreter (remora/runtime.py:1135-1189): the reference's own
+    known answers (tests/test_properties.py:450-500) plus seeded cases."""
+    rng = np.random.default_rng(DATA_SEED + 7)
+
+    def ev(src: str, dtype) -> np.ndarray:
+        return np.asarray(evaluate_source(src, include_prelude=False, syntax="lisp").value, dtype=dtype)
+
+    out: dict[str, np.ndarray] = {}
+    # Known answers of the reference's tests.
+    out["ka_sort"] = ev("(sort < [3 1 4 1])", np.int32)
+    out["ka_grade"] = ev("(grade < [3 1 4 1])", np.int32)
+    out["ka_filter"] = ev("(filter (> 0) [1 -2 3 -4])", np.int32)
+    out["ka_filter_none"] = ev("(filter (> 0) [-1 -2 -3])", np.int32)
+    out["ka_replicate"] = ev("(replicate [2 1 3] [10 20 30])", np.int32)
+    out["ka_replicate_zero"] = ev("(replicate [0 1 0] [7 8 9])", np.int32)
+    out["ka_rotate"] = ev("(rotate [1 2 3 4 5] 2)", np.int32)
+    out["ka_rotate2"] = ev("(rotate [[1 2] [3 4] [5 6]] 1)", np.int32)
+    out["ka_append"] = ev("(append [[1 2] [3 4]] [[5 6] [7 8]])", np.int32)
+    # Seeded cases: floats (with repeats), ints with many ties, rank 2 rows.
+    f = rng.standard_normal(300).astype(np.float32)
+    f[::7] = f[3]
+    i = rng.integers(-20, 20, 300).astype(np.int32)
+    m = rng.integers(-9, 9, (6, 50)).astype(np.int32)
+    out["f"], out["i"], out["m"] = f, i, m
+    out["sort_f"] = ev(f"(sort < {lisp_list(f)})", np.float32)
+    out["grade_f"] = ev(f"(grade < {lisp_list(f)})", np.int32)
+    out["sort_i"] = ev(f"(sort < {lisp_list(i)})", np.int32)
+    out["grade_i"] = ev(f"(grade < {lisp_list(i)})", np.int32)
+    rows = "[" + " ".join(lisp_list(r) for r in m) + "]"
+    out["sort_m"] = ev(f"(sort < {rows})", np.int32)
+    out["grade_m"] = ev(f"(grade < {rows})", np.int32)
+    out["filter_f"] = ev(f"(filter (> 0.25) {lisp_list(f)})", np.float32)
+    out["filter_i"] = ev(f"(filter (> 3) {lisp_list(i)})", np.int32)
+    c = rng.integers(0, 4, 300).astype(np.int32)
+    out["c"] = c
+    out["replicate_f"] = ev(f"(replicate {lisp_list(c)} {lisp_list(f)})", np.float32)
+    out["rotate_f"] = ev(f"(rotate {lisp_list(f)} 37)", np.float32)
+    out["rotate_m"] = ev(f"(rotate {rows} 4)", np.int32)
+    out["append_f"] = ev(f"(append {lisp_list(f)} {lisp_list(f[:41])})", np.float32)
+    save("rt_helpers", **out)
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["rt"]:
+        runtime_helpers()
+    else:
+        main()
+        runtime_helpers()
