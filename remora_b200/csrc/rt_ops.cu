@@ -98,7 +98,9 @@ __device__ __forceinline__ U block_excl_sum(U v, U *s_w, U *total = nullptr) {
 // pos[i] is the key's position in the tile stably sorted by that digit.
 // Within a warp the keys are ranked round by round (round i holds positions
 // in lane order), so equal digits keep their input order; warps and digits
-// are then laid out by exclusive sums.
+// are then laid out by exclusive sums.  The lanes sharing a digit are found
+// with eight ballots (one per digit bit), which keeps the work on the
+// integer pipes; the highest such lane updates the warp's counter.
 template <int ITEMS>
 __device__ __forceinline__ void rank_digits(const uint32_t (&k)[ITEMS], int valid_n, int shift,
                                             uint32_t (&pos)[ITEMS], uint32_t (*s_wcnt)[256], uint32_t *s_w) {
@@ -111,16 +113,22 @@ __device__ __forceinline__ void rank_digits(const uint32_t (&k)[ITEMS], int vali
   for (int i = 0; i < ITEMS; ++i) {
     const int q = warp * 32 * ITEMS + i * 32 + lane;
     const bool valid = q < valid_n;
-    const uint32_t d = valid ? (k[i] >> shift) & 255u : 256u;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
-    const int leader = __ffs(peers) - 1;
-    uint32_t old = 0;
-    if (lane == leader && valid) {
-      old = s_wcnt[warp][d];
-      s_wcnt[warp][d] = old + __popc(peers);
+    const uint32_t d = (k[i] >> shift) & 255u;
+    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
+      peers &= ((d >> b) & 1u) ? bal : ~bal;
     }
-    old = __shfl_sync(0xffffffffu, old, leader);
-    r[i] = old + __popc(peers & lt);
+    const uint32_t below = __popc(peers & lt);
+    const int leader = 31 - __clz(peers);  // peers is non-empty for a valid lane
+    uint32_t old = 0;
+    if (valid && lane == leader) {
+      old = s_wcnt[warp][d];
+      s_wcnt[warp][d] = old + below + 1u;
+    }
+    old = __shfl_sync(0xffffffffu, old, leader & 31);
+    r[i] = old + below;
     __syncwarp();
   }
   __syncthreads();
@@ -203,15 +211,34 @@ __global__ void __launch_bounds__(kT) radix_count(const uint32_t *__restrict__ k
                                                   int64_t ntiles, uint32_t *__restrict__ hist) {
   __shared__ uint32_t s_cnt[kWarps][256];
   for (int i = threadIdx.x; i < kWarps * 256; i += kT) (&s_cnt[0][0])[i] = 0u;
-  __syncthreads();
   const int warp = threadIdx.x >> 5;
   const int64_t base = (int64_t)blockIdx.x * kTile;
+  const int valid_n = (int)(n - base < (int64_t)kTile ? n - base : (int64_t)kTile);
+  // All loads are issued before the first shared-memory atomic.
+  uint32_t k[kItems];
+  if (valid_n == kTile && (reinterpret_cast<uintptr_t>(keys) & 15) == 0) {
+    const uint4 *v = reinterpret_cast<const uint4 *>(keys + base);
+#pragma unroll
+    for (int j = 0; j < kItems / 4; ++j) {
+      const uint4 q = v[j * kT + threadIdx.x];
+      k[4 * j] = q.x;
+      k[4 * j + 1] = q.y;
+      k[4 * j + 2] = q.z;
+      k[4 * j + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int q = (i >> 2) * kT * 4 + threadIdx.x * 4 + (i & 3);
+      k[i] = q < valid_n ? keys[base + q] : 0u;
+    }
+  }
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
-    const int64_t idx = base + i * kT + threadIdx.x;
-    if (idx < n) {
-      uint32_t key = keys[idx];
-      if (kFirst) key = to_key<kDtype, kCanon>(key);
+    const int q = (i >> 2) * kT * 4 + threadIdx.x * 4 + (i & 3);
+    if (q < valid_n) {
+      const uint32_t key = kFirst ? to_key<kDtype, kCanon>(k[i]) : k[i];
       atomicAdd(&s_cnt[warp][(key >> shift) & 255u], 1u);
     }
   }
@@ -223,21 +250,41 @@ __global__ void __launch_bounds__(kT) radix_count(const uint32_t *__restrict__ k
   hist[(int64_t)d * ntiles + blockIdx.x] = s;
 }
 
+// Exclusive sum of len values in[0..len) into out (may alias in) by one
+// block, kScanItems consecutive values per thread per round; returns the
+// total to every thread.
+constexpr int kScanItems = 16;
+
+template <typename In, typename Out>
+__device__ __forceinline__ Out block_scan_array(const In *in, Out *out, int64_t len, Out *s_w) {
+  Out run = 0;
+  for (int64_t b = 0; b < len; b += (int64_t)kT * kScanItems) {
+    const int64_t o = b + (int64_t)threadIdx.x * kScanItems;
+    Out v[kScanItems], sum = 0;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+      v[j] = o + j < len ? (Out)in[o + j] : Out(0);
+      sum += v[j];
+    }
+    Out tot;
+    Out r = run + block_excl_sum<Out>(sum, s_w, &tot);
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+      if (o + j < len) out[o + j] = r;
+      r += v[j];
+    }
+    run += tot;
+  }
+  return run;
+}
+
 // Block d: exclusive scan of digit d's per-tile counts in place; the row
 // total goes to totals[d].
 __global__ void __launch_bounds__(kT) radix_scan_rows(uint32_t *__restrict__ hist, int64_t ntiles,
                                                       uint32_t *__restrict__ totals) {
   __shared__ uint32_t s_w[kWarps];
   uint32_t *row = hist + (int64_t)blockIdx.x * ntiles;
-  uint32_t run = 0;
-  for (int64_t b = 0; b < ntiles; b += kT) {
-    const int64_t i = b + threadIdx.x;
-    const uint32_t v = i < ntiles ? row[i] : 0u;
-    uint32_t tot;
-    const uint32_t ex = block_excl_sum<uint32_t>(v, s_w, &tot);
-    if (i < ntiles) row[i] = run + ex;
-    run += tot;
-  }
+  const uint32_t run = block_scan_array<uint32_t, uint32_t>(row, row, ntiles, s_w);
   if (threadIdx.x == 0) totals[blockIdx.x] = run;
 }
 
@@ -462,12 +509,19 @@ __device__ __forceinline__ bool compare(int op, T x, T lit) {
   }
 }
 
+// The word a keep flag is computed from: the mask element, or the value.
 template <typename T, int kMask>
-__device__ __forceinline__ bool keep(const T *__restrict__ src, const void *__restrict__ mask, int64_t i, Pred p) {
-  if (kMask == kMaskI32) return reinterpret_cast<const int32_t *>(mask)[i] != 0;
-  if (kMask == kMaskU8) return reinterpret_cast<const uint8_t *>(mask)[i] != 0;
-  if constexpr (std::is_same<T, float>::value) return compare<float>(p.op, src[i], p.f);
-  else return compare<int>(p.op, src[i], p.i);
+__device__ __forceinline__ uint32_t flag_word(const T *__restrict__ src, const void *__restrict__ mask, int64_t i) {
+  if (kMask == kMaskI32) return (uint32_t)reinterpret_cast<const int32_t *>(mask)[i];
+  if (kMask == kMaskU8) return reinterpret_cast<const uint8_t *>(mask)[i];
+  return *reinterpret_cast<const uint32_t *>(src + i);
+}
+
+template <typename T, int kMask>
+__device__ __forceinline__ bool keep_word(uint32_t w, Pred p) {
+  if (kMask != kMaskPred) return w != 0u;
+  if constexpr (std::is_same<T, float>::value) return compare<float>(p.op, __uint_as_float(w), p.f);
+  else return compare<int>(p.op, (int)w, p.i);
 }
 
 template <typename T, int kMask>
@@ -475,11 +529,17 @@ __global__ void __launch_bounds__(kT) filter_count(const T *__restrict__ src, co
                                                    int64_t n, Pred p, uint32_t *__restrict__ tile_cnt) {
   __shared__ uint32_t s_w[kWarps];
   const int64_t base = (int64_t)blockIdx.x * kTile;
+  uint32_t w[kItems];
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int64_t idx = base + i * kT + threadIdx.x;
+    w[i] = idx < n ? flag_word<T, kMask>(src, mask, idx) : 0u;
+  }
   uint32_t c = 0;
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
     const int64_t idx = base + i * kT + threadIdx.x;
-    if (idx < n && keep<T, kMask>(src, mask, idx, p)) ++c;
+    if (idx < n && keep_word<T, kMask>(w[i], p)) ++c;
   }
   uint32_t total;
   (void)block_excl_sum<uint32_t>(c, s_w, &total);
@@ -493,15 +553,7 @@ __global__ void __launch_bounds__(kT) tile_offsets(const C *__restrict__ cnt, in
                                                    unsigned long long *__restrict__ offs,
                                                    long long *__restrict__ total) {
   __shared__ unsigned long long s_w[kWarps];
-  unsigned long long run = 0;
-  for (int64_t b = 0; b < ntiles; b += kT) {
-    const int64_t i = b + threadIdx.x;
-    const unsigned long long v = i < ntiles ? (unsigned long long)cnt[i] : 0ull;
-    unsigned long long tot;
-    const unsigned long long ex = block_excl_sum<unsigned long long>(v, s_w, &tot);
-    if (i < ntiles) offs[i] = run + ex;
-    run += tot;
-  }
+  const unsigned long long run = block_scan_array<C, unsigned long long>(cnt, offs, ntiles, s_w);
   if (threadIdx.x == 0) *total = (long long)run;
 }
 
@@ -520,12 +572,19 @@ __global__ void __launch_bounds__(kT) filter_compact(const T *__restrict__ src, 
   const int64_t base = (int64_t)blockIdx.x * kTile;
   T v[kItems];
   uint32_t ball[kItems];
+  // All loads first, then the flags.
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
     const int64_t idx = base + i * kT + threadIdx.x;
-    const bool ok = idx < n;
-    v[i] = ok ? src[idx] : T(0);
-    const bool f = ok && keep<T, kMask>(src, mask, idx, p);
+    v[i] = idx < n ? src[idx] : T(0);
+    ball[i] = kMask == kMaskPred ? 0u : (idx < n ? flag_word<T, kMask>(src, mask, idx) : 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int64_t idx = base + i * kT + threadIdx.x;
+    uint32_t word = ball[i];
+    if (kMask == kMaskPred) word = *reinterpret_cast<const uint32_t *>(&v[i]);
+    const bool f = idx < n && keep_word<T, kMask>(word, p);
     ball[i] = __ballot_sync(0xffffffffu, f);
     if (lane == 0) s_cnt[i * kWarps + warp] = __popc(ball[i]);
   }
