@@ -55,6 +55,17 @@ int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h,
                           RemoraMemRef1 *loss, RemoraMemRef1 *dz,
                           float grad_scale, remora_stream_t stream);
 
+/* The same with the hidden layer's bias and ReLU fused in front:
+   h[b,o] = relu(hpre[b,o] + hb[o]) (the select form of
+   examples/crater_train.py:46-48, one rounded add) is written to h and
+   feeds the dense 64 -> 1 layer, the BCE and its gradient as above. */
+int remora_b200_dense_bias_relu_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *hpre,
+                                    const RemoraMemRef1 *hb, RemoraMemRef2 *h,
+                                    const RemoraMemRef1 *w, const RemoraMemRef1 *b,
+                                    const RemoraMemRef1 *y, RemoraMemRef1 *z,
+                                    RemoraMemRef1 *loss, RemoraMemRef1 *dz,
+                                    float grad_scale, remora_stream_t stream);
+
 /* Backward of the dense 64 -> 1 layer on a ReLU'd hidden layer:
    dw[o] = sum_b dz[b] h[b,o], db = sum_b dz[b],
    dh[b,o] = h[b,o] > 0 ? dz[b] * w[o] : 0, and, when dh_colsum is not

@@ -6,9 +6,11 @@ dense 8192->64 + ReLU, dense 64->1, stable BCE on the logit averaged over the
 global batch, SGD p <- p - lr * g.  Every stage is a libremora_b200 call on
 device-resident buffers: forward, backward and the update never leave the
 GPU.  With several ranks each holds the full parameters and 1/world of the
-global batch; the flat gradient buffer (529,217 f32) is summed with one NCCL
-allreduce (the per-sample gradients already carry 1/global_batch), so every
-rank applies the same update and the replicas stay bitwise identical.
+global batch; the flat gradient buffer (529,217 f32) is summed with NCCL
+allreduces in two buckets (the dense layers' gradients are reduced on a side
+stream while the conv layers' backward still runs; the per-sample gradients
+already carry 1/global_batch), so every rank applies the same update and the
+replicas stay bitwise identical.
 
 Gradient views point into one flat buffer in the parameter layout of
 remora_b200.crater, so the kernels write the allreduce buffer directly.
@@ -24,7 +26,7 @@ import numpy as np
 from remora_b200 import _lib as L
 from remora_b200 import crater
 from remora_b200.abi import tensor_descriptor
-from remora_b200.program import BinaryExpr, CmpExpr, SelectExpr, compile_program, const, x
+from remora_b200.program import BinaryExpr, compile_program, const, x
 from remora_b200.runtime import context
 
 _CNN_PROTOS = {
@@ -32,6 +34,7 @@ _CNN_PROTOS = {
     "remora_b200_relu_pool": [ctypes.c_void_p] * 5,
     "remora_b200_unpool": [ctypes.c_void_p] * 5,
     "remora_b200_dense_bce": [ctypes.c_void_p] * 8 + [ctypes.c_float, ctypes.c_void_p],
+    "remora_b200_dense_bias_relu_bce": [ctypes.c_void_p] * 10 + [ctypes.c_float, ctypes.c_void_p],
     "remora_b200_dense_relu_bwd": [ctypes.c_void_p] * 9,
     "remora_b200_conv1_wgrad_pooled": [ctypes.c_void_p] * 7,
     "remora_b200_conv2d_wgrad_bias": [ctypes.c_void_p] * 7,
@@ -106,10 +109,7 @@ class CraterCNN:
         self.dp2 = e(B, 32, 16, 16)
         self.dp1 = e(B, 16, 32, 32)
         self.loss_sum = e(1).reshape(())
-        # fused maps: ReLU(h + b3) with b3 broadcast over the batch, and the
-        # in-place SGD update p - lr * g
-        s = BinaryExpr("+", x(0), x(1))
-        self.prog_bias_relu = compile_program(SelectExpr(CmpExpr(">", s, const(0.0)), s, const(0.0)), 2)
+        # fused map: the in-place SGD update p - lr * g
         self.prog_sgd = compile_program(BinaryExpr("-", x(0), BinaryExpr("*", const(self.lr), x(1))), 2)
         # "3xtf32" (default): split-precision GEMMs and convs, gradients
         # within 1e-4 of the f32 step; "tf32": single-pass TF32 tensor-core
@@ -119,6 +119,15 @@ class CraterCNN:
         self.gemm_spec = L.RemoraGemmSpec(prec, 0)
         self.graph = None
         self._keep: list = []
+        # Two allreduce buckets: w3..b4 (the dense layers, 99 % of the
+        # gradient) is final once the dense1 weight-gradient GEMM is done and
+        # is reduced on a side stream while the conv layers' backward runs;
+        # w1..b2 follows at the end of the backward.
+        o = crater.offsets()
+        split = o["w3"][0]
+        self.bucket_dense = self.grads[split:]
+        self.bucket_conv = self.grads[:split]
+        self.comm = torch.cuda.Stream(self.dev) if allreduce is not None else None
 
     # ------------------------------------------------------------ helpers
     @staticmethod
@@ -164,16 +173,23 @@ class CraterCNN:
                                                          self._d(self.code2), s), "conv2")
         p2flat = self.p2.view(B, 8192)
         self._gemm(p2flat, p["w3"].t(), self.hpre)
-        self._map(self.prog_bias_relu, [self.hpre, p["b3"].unsqueeze(0).expand(B, 64)], self.h)
-        self._check(lib.remora_b200_dense_bce(c, self._d(self.h), self._d(p["w4"]), self._d(p["b4"]),
-                                              self._d(labels), self._d(self.z), self._d(self.loss_b),
-                                              self._d(self.dz), ctypes.c_float(1.0 / self.B_total), s), "dense_bce")
+        # ReLU(hpre + b3), dense 64 -> 1, BCE and dlogit in one kernel
+        self._check(lib.remora_b200_dense_bias_relu_bce(c, self._d(self.hpre), self._d(p["b3"]), self._d(self.h),
+                                                        self._d(p["w4"]), self._d(p["b4"]), self._d(labels),
+                                                        self._d(self.z), self._d(self.loss_b), self._d(self.dz),
+                                                        ctypes.c_float(1.0 / self.B_total), s), "dense_bce")
         # backward
         # dense 64 -> 1 backward; also sums dh over the batch: the hidden bias gradient
         self._check(lib.remora_b200_dense_relu_bwd(c, self._d(self.h), self._d(p["w4"]), self._d(self.dz),
                                                    self._d(self.dh), self._d(g["w4"]), self._d(g["b4"]),
                                                    self._d(g["b3"]), s), "dense2 bwd")
         self._gemm(self.dh.t(), p2flat, g["w3"])
+        if self.allreduce is not None:
+            # the dense bucket is final: reduce it while the convs run
+            cur = self.torch.cuda.current_stream(self.dev)
+            self.comm.wait_stream(cur)
+            with self.torch.cuda.stream(self.comm):
+                self.allreduce(self.bucket_dense)
         self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))
         # conv2 gradients straight from the pooled gradient and the pool codes
         self._check(lib.remora_b200_conv2d_wgrad_bias_unpool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
@@ -187,7 +203,11 @@ class CraterCNN:
 
     def update(self) -> None:
         if self.allreduce is not None:
-            self.allreduce(self.grads)
+            cur = self.torch.cuda.current_stream(self.dev)
+            self.comm.wait_stream(cur)
+            with self.torch.cuda.stream(self.comm):
+                self.allreduce(self.bucket_conv)
+            cur.wait_stream(self.comm)
         self._map(self.prog_sgd, [self.params, self.grads], self.params)
 
     def step(self, images, labels) -> None:

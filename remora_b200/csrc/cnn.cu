@@ -47,20 +47,26 @@ __device__ __forceinline__ void pool4(float v0, float v1, float v2, float v3, fl
 constexpr int kConv1Threads = 256;
 constexpr int kConv1MaxK = 32;
 
-template <int H, int W>
+template <int H, int W, int PARTS>
 __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const float *__restrict__ x,
                                                                         const float *__restrict__ w,
                                                                         const float *__restrict__ bias,
                                                                         float *__restrict__ p,
                                                                         uint8_t *__restrict__ code, int K) {
+  // PARTS blocks share an image, each taking RP consecutive pooled rows (and
+  // the 2 * RP + 2 padded input rows they read), so that small batches
+  // still fill the GPU; every output is computed the same way for any PARTS.
   constexpr int OH = H / 2, OW = W / 2, NP = OH * OW, PWD = W + 2;
-  constexpr int PER = (NP + kConv1Threads - 1) / kConv1Threads;
-  __shared__ float img[(H + 2) * PWD];
+  constexpr int RP = OH / PARTS, NPP = RP * OW, IR = 2 * RP + 2;
+  constexpr int PER = (NPP + kConv1Threads - 1) / kConv1Threads;
+  static_assert(OH % PARTS == 0, "parts split the pooled rows evenly");
+  __shared__ float img[IR * PWD];
   __shared__ float ws[kConv1MaxK * 10];
-  const long long b = blockIdx.x;
+  const long long b = blockIdx.x / PARTS;
+  const int i0 = (blockIdx.x % PARTS) * RP;  // first pooled row of this block
   const float *xb = x + b * (long long)H * W;
-  for (int e = threadIdx.x; e < (H + 2) * PWD; e += kConv1Threads) {
-    const int r = e / PWD - 1, c = e % PWD - 1;
+  for (int e = threadIdx.x; e < IR * PWD; e += kConv1Threads) {
+    const int r = 2 * i0 + e / PWD - 1, c = e % PWD - 1;
     img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
   }
   for (int e = threadIdx.x; e < K * 10; e += kConv1Threads)
@@ -74,10 +80,10 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const fl
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) patch[u][a][c] = pos < NP ? img[(2 * i + a) * PWD + 2 * j + c] : 0.0f;
+      for (int c = 0; c < 4; ++c) patch[u][a][c] = pos < NPP ? img[(2 * i + a) * PWD + 2 * j + c] : 0.0f;
   }
-  float *pb = p + b * (long long)K * NP;
-  uint8_t *cb = code + b * (long long)K * NP;
+  float *pb = p + b * (long long)K * NP + i0 * OW;
+  uint8_t *cb = code + b * (long long)K * NP + i0 * OW;
 #pragma unroll 1
   for (int k = 0; k < K; ++k) {
     float wk[9];
@@ -99,7 +105,7 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const fl
             for (int c = 0; c < 3; ++c) dot = __fadd_rn(dot, __fmul_rn(patch[u][di + a][dj + c], wk[a * 3 + c]));
           v[di * 2 + dj] = __fadd_rn(__fadd_rn(0.0f, dot), bk);
         }
-      if (pos < NP) pool4(v[0], v[1], v[2], v[3], pb + (long long)k * NP + pos, cb + (long long)k * NP + pos);
+      if (pos < NPP) pool4(v[0], v[1], v[2], v[3], pb + (long long)k * NP + pos, cb + (long long)k * NP + pos);
     }
   }
 }
@@ -145,7 +151,10 @@ __global__ void __launch_bounds__(256) unpool_kernel(const float *__restrict__ d
 
 // Dense 64 -> 1 on the ReLU'd hidden layer, the stable BCE and its gradient.
 // One warp per sample.  loss[b] = bce(z, y); dz[b] = (sigmoid(z) - y) * inv.
-__global__ void __launch_bounds__(256) dense_bce_kernel(const float *__restrict__ h, const float *__restrict__ w4,
+// With hb non-null, h is computed first from hpre: h = relu(hpre + hb),
+// stored to h_out, and used in place of a stored hidden layer.
+__global__ void __launch_bounds__(256) dense_bce_kernel(const float *__restrict__ h, const float *__restrict__ hb,
+                                                        float *__restrict__ h_out, const float *__restrict__ w4,
                                                         const float *__restrict__ b4, const float *__restrict__ y,
                                                         float *__restrict__ z_out, float *__restrict__ loss,
                                                         float *__restrict__ dz, int B, int D, float inv) {
@@ -154,7 +163,15 @@ __global__ void __launch_bounds__(256) dense_bce_kernel(const float *__restrict_
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
   for (long long b = warp; b < B; b += nwarps) {
     float acc = 0.0f;
-    for (int o = lane; o < D; o += 32) acc = __fadd_rn(acc, __fmul_rn(__ldg(w4 + o), h[b * D + o]));
+    for (int o = lane; o < D; o += 32) {
+      float hv = h[b * D + o];
+      if (hb) {
+        const float s = __fadd_rn(hv, __ldg(hb + o));
+        hv = s > 0.0f ? s : 0.0f;
+        h_out[b * D + o] = hv;
+      }
+      acc = __fadd_rn(acc, __fmul_rn(__ldg(w4 + o), hv));
+    }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, s));
     if (lane == 0) {
@@ -225,23 +242,27 @@ __global__ void __launch_bounds__(256) dense_bwd_kernel(const float *__restrict_
 
 // conv1 weight and bias gradients straight from the pooled gradient: each
 // pooled output with a recorded element (h, q) contributes
-// dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  One block
-// per image (image in shared memory with a zero border); the 16 lanes of a
-// half-warp share a channel k and stride its pooled positions, keep f32
-// sums, and combine them with a fixed shuffle tree into
-// part[(b * K + k) * 10 + {0..8: taps, 9: bias}].  The finish kernel adds
-// the per-image partials in image order in f64.
-template <int H, int W>
+// dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  PARTS
+// blocks per image, each over RP consecutive pooled rows (its input rows in
+// shared memory with a zero border); the 16 lanes of a half-warp share a
+// channel k and stride its pooled positions, keep f32 sums, and combine them
+// with a fixed shuffle tree into
+// part[((b * PARTS + part) * K + k) * 10 + {0..8: taps, 9: bias}].  The
+// finish kernel adds the partials in (image, part) order in f64.
+template <int H, int W, int PARTS>
 __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const float *__restrict__ x,
                                                                          const float *__restrict__ dp,
                                                                          const uint8_t *__restrict__ code,
                                                                          float *__restrict__ part, int K) {
   constexpr int OW = W / 2, NP = (H / 2) * OW, PWD = W + 2;
-  __shared__ float img[(H + 2) * PWD];
-  const long long b = blockIdx.x;
+  constexpr int RP = (H / 2) / PARTS, NPP = RP * OW, IR = 2 * RP + 2;
+  static_assert((H / 2) % PARTS == 0, "parts split the pooled rows evenly");
+  __shared__ float img[IR * PWD];
+  const long long b = blockIdx.x / PARTS;
+  const int i0 = (blockIdx.x % PARTS) * RP;
   const float *xb = x + b * (long long)H * W;
-  for (int e = threadIdx.x; e < (H + 2) * PWD; e += kConv1Threads) {
-    const int r = e / PWD - 1, c = e % PWD - 1;
+  for (int e = threadIdx.x; e < IR * PWD; e += kConv1Threads) {
+    const int r = 2 * i0 + e / PWD - 1, c = e % PWD - 1;
     img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
   }
   __syncthreads();
@@ -250,9 +271,9 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const f
     float acc[10];
 #pragma unroll
     for (int u = 0; u < 10; ++u) acc[u] = 0.0f;
-    const long long base = (b * K + k) * (long long)NP;
+    const long long base = (b * K + k) * (long long)NP + i0 * OW;
 #pragma unroll 4
-    for (int pos = lane16; pos < NP; pos += 16) {
+    for (int pos = lane16; pos < NPP; pos += 16) {
       const uint8_t c0 = code[base + pos];
       if (c0 == kNoGrad) continue;
       const int c = c0 & 3;  // window index; anything else is not a valid code
@@ -269,13 +290,20 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const f
       float v = acc[u];
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane16 == 0) part[(b * K + k) * 10 + u] = v;
+      if (lane16 == 0) part[((long long)blockIdx.x * K + k) * 10 + u] = v;
     }
   }
 }
 
-// dw1, db1 = sums of the per-image partials, in image order, f64.  One block
-// per output value.
+// Blocks per image for the conv1 kernels: enough blocks for several waves
+// on small batches, one block per image on large ones.
+int conv1_parts(int B, int H) {
+  if (H != 64) return 1;
+  return B <= 1024 ? 4 : (B <= 2048 ? 2 : 1);
+}
+
+// dw1, db1 = sums of the n per-block partials, in block order, f64.  One
+// block per output value.
 __global__ void __launch_bounds__(256) conv1_wgrad_finish_kernel(const float *__restrict__ part,
                                                                  float *__restrict__ dw, float *__restrict__ db,
                                                                  int B, int K) {
@@ -334,9 +362,13 @@ int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, cons
   if (!((H == 64 && W == 64) || (H == 32 && W == 32)) || K > kConv1MaxK)
     return fail(REMORA_ERR_UNSUPPORTED, "conv1_relu_pool: images of 64x64 or 32x32 and at most %d channels",
                 kConv1MaxK);
-  auto kern = H == 64 ? conv1_relu_pool_kernel<64, 64> : conv1_relu_pool_kernel<32, 32>;
+  const int parts = conv1_parts(B, H);
+  auto kern = H != 64      ? conv1_relu_pool_kernel<32, 32, 1>
+              : parts == 4 ? conv1_relu_pool_kernel<64, 64, 4>
+              : parts == 2 ? conv1_relu_pool_kernel<64, 64, 2>
+                           : conv1_relu_pool_kernel<64, 64, 1>;
   note_launch();
-  kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)Wd.data(4),
+  kern<<<B * parts, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)Wd.data(4),
                                                       (const float *)Bd.data(4), (float *)P.data(4),
                                                       (uint8_t *)C.data(1), K);
   REMORA_CUDA_TRY(cudaGetLastError());
@@ -406,8 +438,40 @@ int remora_b200_dense_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *h, const Remo
   if (B == 0) return REMORA_OK;
   note_launch();
   dense_bce_kernel<<<grid_for((long long)B * 32, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
-      (const float *)Hd.data(4), (const float *)Wd.data(4), (const float *)Bd.data(4), (const float *)Y.data(4),
-      (float *)Z.data(4), (float *)Lo.data(4), (float *)Dz.data(4), B, D, grad_scale);
+      (const float *)Hd.data(4), nullptr, nullptr, (const float *)Wd.data(4), (const float *)Bd.data(4),
+      (const float *)Y.data(4), (float *)Z.data(4), (float *)Lo.data(4), (float *)Dz.data(4), B, D, grad_scale);
+  REMORA_CUDA_TRY(cudaGetLastError());
+  return REMORA_OK;
+}
+
+int remora_b200_dense_bias_relu_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *hpre, const RemoraMemRef1 *hb,
+                                    RemoraMemRef2 *h, const RemoraMemRef1 *w, const RemoraMemRef1 *b,
+                                    const RemoraMemRef1 *y, RemoraMemRef1 *z, RemoraMemRef1 *loss, RemoraMemRef1 *dz,
+                                    float grad_scale, remora_stream_t stream) {
+  REMORA_TRY(check_ctx(ctx));
+  DescView Hp, Hb, Hd, Wd, Bd, Y, Z, Lo, Dz;
+  REMORA_TRY(read_desc(hpre, 2, &Hp, "hidden pre-activation"));
+  REMORA_TRY(read_desc(hb, 1, &Hb, "hidden bias"));
+  REMORA_TRY(read_desc(h, 2, &Hd, "hidden"));
+  REMORA_TRY(read_desc(w, 1, &Wd, "dense weights"));
+  REMORA_TRY(read_desc(b, 1, &Bd, "dense bias"));
+  REMORA_TRY(read_desc(y, 1, &Y, "labels"));
+  REMORA_TRY(read_desc(z, 1, &Z, "logits"));
+  REMORA_TRY(read_desc(loss, 1, &Lo, "losses"));
+  REMORA_TRY(read_desc(dz, 1, &Dz, "logit gradients"));
+  for (const DescView *d : {&Hp, &Hb, &Hd, &Wd, &Bd, &Y, &Z, &Lo, &Dz})
+    if (!d->contiguous()) return fail(REMORA_ERR_UNSUPPORTED, "dense_bias_relu_bce: operands must be contiguous");
+  const int B = (int)Hp.sizes[0], D = (int)Hp.sizes[1];
+  if (Hd.sizes[0] != B || Hd.sizes[1] != D || Hb.sizes[0] != D || Wd.sizes[0] != D || Bd.sizes[0] != 1 ||
+      Y.sizes[0] != B || Z.sizes[0] != B || Lo.sizes[0] != B || Dz.sizes[0] != B)
+    return fail(REMORA_ERR_SHAPE,
+                "dense_bias_relu_bce: shapes must be hpre/h [B,D], hb/w [D], b [1], y/z/loss/dz [B]");
+  if (B == 0) return REMORA_OK;
+  note_launch();
+  dense_bce_kernel<<<grid_for((long long)B * 32, ctx->sm_count), 256, 0, (cudaStream_t)stream>>>(
+      (const float *)Hp.data(4), (const float *)Hb.data(4), (float *)Hd.data(4), (const float *)Wd.data(4),
+      (const float *)Bd.data(4), (const float *)Y.data(4), (float *)Z.data(4), (float *)Lo.data(4),
+      (float *)Dz.data(4), B, D, grad_scale);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }
@@ -467,16 +531,20 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, c
     REMORA_CUDA_TRY(cudaMemsetAsync(Db.data(4), 0, (size_t)K * 4, (cudaStream_t)stream));
     return REMORA_OK;
   }
+  const int parts = conv1_parts(B, H);
   Workspace *ws = nullptr;
-  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * K * 10 * sizeof(float) + 256, &ws));
+  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * parts * K * 10 * sizeof(float) + 256, &ws));
   float *part = reinterpret_cast<float *>(ws->buf);
-  auto kern = H == 64 ? conv1_wgrad_pool_kernel<64, 64> : conv1_wgrad_pool_kernel<32, 32>;
+  auto kern = H != 64      ? conv1_wgrad_pool_kernel<32, 32, 1>
+              : parts == 4 ? conv1_wgrad_pool_kernel<64, 64, 4>
+              : parts == 2 ? conv1_wgrad_pool_kernel<64, 64, 2>
+                           : conv1_wgrad_pool_kernel<64, 64, 1>;
   note_launch();
-  kern<<<B, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)P.data(4),
-                                                      (const uint8_t *)C.data(1), part, K);
+  kern<<<B * parts, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)P.data(4),
+                                                              (const uint8_t *)C.data(1), part, K);
   note_launch();
   conv1_wgrad_finish_kernel<<<K * 10, 256, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4),
-                                                                      (float *)Db.data(4), B, K);
+                                                                      (float *)Db.data(4), B * parts, K);
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }

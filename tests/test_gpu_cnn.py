@@ -204,3 +204,85 @@ def test_fused_conv2_pool_matches_unfused(cuda, precision):
                                                     d(dw_fused), d(db_fused), stream) == 0
     np.testing.assert_array_equal(to_host(dw_fused), to_host(dw_ref))
     np.testing.assert_array_equal(to_host(db_fused), to_host(db_ref))
+
+
+def test_conv1_layers_same_for_every_block_split(cuda, oracle_mod):
+    """The first layer splits an image over 1, 2 or 4 blocks depending on the
+    batch (small batches use more blocks per image).  Forward outputs are
+    bit for bit the same for every split; the weight gradient matches the
+    oracle within the f32 tolerance for every split."""
+    import torch
+
+    from remora_b200.abi import tensor_descriptor
+    from remora_b200.cnn import _lib
+    from remora_b200.runtime import context
+
+    lib = _lib()
+    rng = np.random.default_rng(77)
+    K, hw = 16, 64
+    x = rng.standard_normal((2100, 1, hw, hw)).astype(np.float32)
+    w = (rng.standard_normal((K, 1, 3, 3)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal(K) * 0.1).astype(np.float32)
+    ctx = context(cuda.index)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    wd, bd = torch.from_numpy(w).to(cuda), torch.from_numpy(b).to(cuda)
+    outs = {}
+    for B in (5, 1100, 2100):  # 4, 2 and 1 blocks per image
+        xd = torch.from_numpy(x[:B].copy()).to(cuda)
+        p = torch.empty((B, K, 32, 32), dtype=torch.float32, device=cuda)
+        code = torch.empty((B, K, 32, 32), dtype=torch.uint8, device=cuda)
+        keep = [tensor_descriptor(t) for t in (xd, wd, bd, p, code)]
+        assert lib.remora_b200_conv1_relu_pool(ctx.ptr, *[ctypes.addressof(d) for d in keep], stream) == 0
+        outs[B] = (to_host(p), to_host(code))
+        dp = torch.from_numpy(rng.standard_normal((B, K, 32, 32)).astype(np.float32)).to(cuda)
+        dw = torch.empty((K, 1, 3, 3), dtype=torch.float32, device=cuda)
+        db = torch.empty(K, dtype=torch.float32, device=cuda)
+        keep2 = [tensor_descriptor(t) for t in (xd, dp, code, dw, db)]
+        assert lib.remora_b200_conv1_wgrad_pooled(ctx.ptr, *[ctypes.addressof(d) for d in keep2], stream) == 0
+        if B == 1100:
+            a1 = oracle_mod.conv2d_fwd(x[:B], w, b, nthreads=oracle_mod.max_threads())
+            a1 = np.where(a1 > 0, a1, np.float32(0))
+            da = oracle_mod.maxpool2x2_bwd(a1, to_host(dp))
+            da = np.where(a1 > 0, da, np.float32(0))
+            ref_w = oracle_mod.conv2d_wgrad(x[:B], da, (K, 1, 3, 3), nthreads=oracle_mod.max_threads())
+            np.testing.assert_allclose(to_host(dw), ref_w, rtol=1e-5, atol=1e-5 * float(np.abs(ref_w).max()))
+    for B in (5, 1100):
+        np.testing.assert_array_equal(outs[B][0], outs[2100][0][:B])
+        np.testing.assert_array_equal(outs[B][1], outs[2100][1][:B])
+
+
+def test_dense_bias_relu_bce_matches_unfused(cuda):
+    """ReLU(hpre + b3) fused into the dense BCE kernel gives bit for bit the
+    separate map + dense_bce calls."""
+    import torch
+
+    from remora_b200 import ops
+    from remora_b200.abi import tensor_descriptor
+    from remora_b200.cnn import _lib
+    from remora_b200.program import BinaryExpr, CmpExpr, SelectExpr, const, x
+
+    lib = _lib()
+    rng = np.random.default_rng(3)
+    B, D = 300, 64
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    hpre, hb = dev(rng.standard_normal((B, D)).astype(np.float32)), dev(rng.standard_normal(D).astype(np.float32))
+    w4, b4 = dev((rng.standard_normal(D) * 0.2).astype(np.float32)), dev(np.array([0.05], np.float32))
+    y = dev((np.arange(B) % 2).astype(np.float32))
+    s = BinaryExpr("+", x(0), x(1))
+    h_ref = ops.map(SelectExpr(CmpExpr(">", s, const(0.0)), s, const(0.0)), hpre, hb.unsqueeze(0).expand(B, D))
+    e = lambda *sh: torch.empty(sh, dtype=torch.float32, device=cuda)  # noqa: E731
+    z1, l1, g1, z2, l2, g2, h2 = e(B), e(B), e(B), e(B), e(B), e(B), e(B, D)
+    ctx = __import__("remora_b200.runtime", fromlist=["context"]).context(cuda.index)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    keep = []
+
+    def d(t):
+        keep.append(tensor_descriptor(t))
+        return ctypes.addressof(keep[-1])
+
+    assert lib.remora_b200_dense_bce(ctx.ptr, d(h_ref), d(w4), d(b4), d(y), d(z1), d(l1), d(g1),
+                                     ctypes.c_float(1 / B), stream) == 0
+    assert lib.remora_b200_dense_bias_relu_bce(ctx.ptr, d(hpre), d(hb), d(h2), d(w4), d(b4), d(y), d(z2), d(l2),
+                                               d(g2), ctypes.c_float(1 / B), stream) == 0
+    for a, b_ in ((h2, h_ref), (z2, z1), (l2, l1), (g2, g1)):
+        np.testing.assert_array_equal(to_host(a), to_host(b_))
