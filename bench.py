@@ -471,6 +471,7 @@ class CnnWorkload:
     metric, unit, bound = "CNN train samples/s", "samples/s", "tensor"
     scaling = "strong"
     GLOBAL = 4096
+    OVERLAP = None  # the step's own choice
     FLOPS_PER_SAMPLE = 33.8e6  # forward + backward, all layers
 
     def __init__(self, name: str) -> None:
@@ -499,7 +500,8 @@ class CnnWorkload:
         self.x = torch.from_numpy(self.himg).to(dev)
         self.y = torch.from_numpy(self.hlab).to(dev)
         allreduce = process_group_allreduce() if world > 1 else None
-        self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision)
+        self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision,
+                             overlap_allreduce=self.OVERLAP)
         self.net.step(self.x, self.y)  # eager step: compiles map programs, sizes workspaces
         self.net.capture(self.x, self.y)
         # library kernels in one replay of the step's graph, counted at capture
@@ -702,6 +704,7 @@ def run_ours(args) -> None:
     wl.world = world
     if isinstance(wl, CnnWorkload):
         wl.GLOBAL = args.cnn_batch
+        wl.OVERLAP = False if args.cnn_serial_allreduce else None
     wl.setup(dev, rank)
     wl.check()
     stream = torch.cuda.current_stream(dev)
@@ -916,6 +919,9 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cnn-serial-allreduce", action="store_true",
+                    help="CNN: always one gradient allreduce after the backward (by default the dense "
+                         "layers' bucket overlaps the conv backward when a rank holds >= 1024 images)")
     ap.add_argument("--cnn-batch", type=int, default=4096,
                     help="global batch of the cnn configs (4096 is the benchmark; smaller ones show the per-rank "
                          "work of a larger data-parallel job)")
