@@ -99,8 +99,109 @@ class GemmSpec:
 
 
 @dataclass
+class AppendSpec:
+    """out = inputs[left] followed by inputs[1 - left] along axis 0."""
+
+    dtype: int = L.F32
+    left: int = 0
+
+    def launch(self, ctx: Any, ins: list, out: ctypes.Structure, stream: Any = None) -> None:
+        if len(ins) != 2:
+            raise RemoraExecutorError("an append takes two inputs")
+        a, b = ins[self.left], ins[1 - self.left]
+        L.check(
+            L.lib().remora_b200_append(ctx.ptr, self.dtype, ctypes.addressof(a), ctypes.addressof(b),
+                                       ctypes.addressof(out), descriptor_rank(out), stream),
+            "remora_b200_append",
+        )
+
+
+@dataclass
+class RotateSpec:
+    dtype: int = L.F32
+    shift: int = 0
+
+    def launch(self, ctx: Any, ins: list, out: ctypes.Structure, stream: Any = None) -> None:
+        if len(ins) != 1:
+            raise RemoraExecutorError("a rotate takes one input")
+        L.check(
+            L.lib().remora_b200_rotate(ctx.ptr, self.dtype, int(self.shift), ctypes.addressof(ins[0]),
+                                       ctypes.addressof(out), descriptor_rank(out), stream),
+            "remora_b200_rotate",
+        )
+
+
+@dataclass
+class SortSpec:
+    """Ascending sort, or with grade the stable argsort, of rank 1 or rows."""
+
+    dtype: int = L.F32
+    grade: bool = False
+
+    def launch(self, ctx: Any, ins: list, out: ctypes.Structure, stream: Any = None) -> None:
+        if len(ins) != 1:
+            raise RemoraExecutorError("a sort takes one input")
+        fn = L.lib().remora_b200_grade if self.grade else L.lib().remora_b200_sort
+        L.check(fn(ctx.ptr, self.dtype, ctypes.addressof(ins[0]), ctypes.addressof(out), descriptor_rank(out),
+                   stream), "remora_b200_grade" if self.grade else "remora_b200_sort")
+
+
+@dataclass
 class SpecModule:
     kernels: dict[str, Any] = field(default_factory=dict)
+
+
+# ------------------------------------------------- records (plain data)
+def spec_record(spec: Any) -> dict:
+    """A spec as plain data (json-able): the C structs as hex bytes."""
+    if isinstance(spec, MapSpec):
+        return {"kind": "map", "bytes": bytes(spec.program).hex()}
+    if isinstance(spec, FoldSpec):
+        return {"kind": "fold", "bytes": bytes(spec.spec).hex()}
+    if isinstance(spec, ScanSpec):
+        return {"kind": "scan", "bytes": bytes(spec.spec).hex()}
+    if isinstance(spec, GemmSpec):
+        return {"kind": "gemm", "precision": int(spec.precision)}
+    if isinstance(spec, AppendSpec):
+        return {"kind": "append", "dtype": int(spec.dtype), "left": int(spec.left)}
+    if isinstance(spec, RotateSpec):
+        return {"kind": "rotate", "dtype": int(spec.dtype), "shift": int(spec.shift)}
+    if isinstance(spec, SortSpec):
+        return {"kind": "sort", "dtype": int(spec.dtype), "grade": bool(spec.grade)}
+    raise RemoraExecutorError(f"no record form for {type(spec).__name__}")
+
+
+def spec_from_record(rec: dict) -> Any:
+    kind = rec["kind"]
+    if kind in ("map", "fold", "scan"):
+        cls = {"map": L.RemoraMapProgram, "fold": L.RemoraFoldSpec, "scan": L.RemoraScanSpec}[kind]
+        raw = bytes.fromhex(rec["bytes"])
+        if len(raw) != ctypes.sizeof(cls):
+            raise RemoraExecutorError(f"{kind} record holds {len(raw)} bytes, the struct has {ctypes.sizeof(cls)}")
+        st = cls.from_buffer_copy(raw)
+        return {"map": MapSpec, "fold": FoldSpec, "scan": ScanSpec}[kind](st)
+    if kind == "gemm":
+        return GemmSpec(int(rec["precision"]))
+    if kind == "append":
+        return AppendSpec(int(rec["dtype"]), int(rec["left"]))
+    if kind == "rotate":
+        return RotateSpec(int(rec["dtype"]), int(rec["shift"]))
+    if kind == "sort":
+        return SortSpec(int(rec["dtype"]), bool(rec["grade"]))
+    raise RemoraExecutorError(f"unknown spec kind {kind!r}")
+
+
+def meta_record(meta: KernelMeta) -> dict:
+    d = dict(meta.__dict__)
+    d["output_shape"] = None if meta.output_shape is None else list(meta.output_shape)
+    return d
+
+
+def meta_from_record(rec: dict) -> KernelMeta:
+    d = dict(rec)
+    if d.get("output_shape") is not None:
+        d["output_shape"] = tuple(d["output_shape"])
+    return KernelMeta(**d)
 
 
 _DT = {L.F32: "f32", L.I32: "i32", L.BOOL: "i8"}
