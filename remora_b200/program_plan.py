@@ -1,0 +1,674 @@
+"""Whole-program execution on the device.
+
+The reference runs a whole compiled program on the GPU with
+``execute_program_from_ptx`` (remora/executor.py:192-306): every kernel of
+the IREE module in order over two ping-pong buffers, a synchronisation after
+each launch, and, for a scalar result, the last nonzero word of the buffer.
+Here a program becomes a ``Plan``: device buffers (constants, inputs, views
+of other buffers) and an ordered list of library calls over them.
+``plan_from_hir`` builds it from the reference compiler's HIR program
+(nodes matched by class name and field, as in ``reference_codegen``);
+``execute_plan`` uploads the constants and inputs once, enqueues every call on
+one stream, synchronises once and copies the result back.  Intermediates
+stay in device memory for the whole program.
+
+What the planner accepts (anything else raises ``RemoraUnsupportedError``):
+let bindings, array literals and ``iota``; maps over arrays and captured
+scalars with primitive, section, lambda or named-function bodies (fused into
+one program each), including cell maps whose body folds its cell; whole and
+leading-axis (array-accumulator) folds with + or * (and && / || over bools);
+scans; append, rotate, sort, grade; reverse, transpose, static indexing and
+slices as strided views; ``if`` on a scalar condition known at plan time, and
+an elementwise ``if`` over arrays.  Scalar arithmetic on literals is folded
+when the plan is built, as a compiler folds constants.
+
+Plans are plain data (``Plan.to_record`` / ``Plan.from_record``), so a plan
+built where the reference compiler is importable can be run where it is not.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+
+from remora_b200 import _lib as L
+from remora_b200.codegen import fold_spec, scan_spec
+from remora_b200.errors import RemoraUnsupportedError
+from remora_b200.program import (
+    BinaryExpr,
+    CmpExpr,
+    ConstantExpr,
+    Expr,
+    InputExpr,
+    LogicExpr,
+    SelectExpr,
+    UnaryExpr,
+    compile_program,
+)
+
+_NP = {L.F32: np.float32, L.I32: np.int32, L.BOOL: np.bool_}
+_NAME = {L.F32: "float32", L.I32: "int32", L.BOOL: "bool"}
+_CODE = {v: k for k, v in _NAME.items()}
+_ELEM = {"float": L.F32, "int": L.I32, "bool": L.BOOL}
+_ARITH, _CMP, _LOGIC, _UNARY = {"+", "-", "*", "/"}, {"<", "<=", ">", ">=", "==", "!="}, {"&&", "||"}, {"exp", "log"}
+
+
+def _unsupported(msg: str) -> RemoraUnsupportedError:
+    return RemoraUnsupportedError(f"B200 program plan: {msg}")
+
+
+def _kind(node: object) -> str:
+    return type(node).__name__
+
+
+# ------------------------------------------------------------------ plans
+@dataclass
+class Buffer:
+    shape: tuple[int, ...]
+    dtype: int
+    const: np.ndarray | None = None  # uploaded once
+    input: int | None = None  # filled from the caller's k-th input
+    # a strided view of another buffer: (base id, element offset, element strides)
+    view: tuple[int, int, tuple[int, ...]] | None = None
+
+
+@dataclass
+class Plan:
+    buffers: list[Buffer] = field(default_factory=list)
+    steps: list[dict] = field(default_factory=list)
+    result: int = -1
+
+    def to_record(self) -> dict:
+        bufs = []
+        for b in self.buffers:
+            r: dict[str, Any] = {"shape": list(b.shape), "dtype": _NAME[b.dtype]}
+            if b.const is not None:
+                r["const"] = np.ascontiguousarray(b.const, dtype=_NP[b.dtype]).tobytes().hex()
+            if b.input is not None:
+                r["input"] = b.input
+            if b.view is not None:
+                r["view"] = [b.view[0], b.view[1], list(b.view[2])]
+            bufs.append(r)
+        steps = []
+        for s in self.steps:
+            t = dict(s)
+            for key in ("program", "spec"):
+                if key in t:
+                    t[key] = bytes(t[key]).hex()
+            steps.append(t)
+        return {"buffers": bufs, "steps": steps, "result": self.result}
+
+    @classmethod
+    def from_record(cls, rec: dict) -> "Plan":
+        p = cls()
+        for r in rec["buffers"]:
+            code = _CODE[r["dtype"]]
+            shape = tuple(r["shape"])
+            const = None
+            if "const" in r:
+                const = np.frombuffer(bytes.fromhex(r["const"]), dtype=_NP[code]).reshape(shape).copy()
+            view = None
+            if "view" in r:
+                view = (int(r["view"][0]), int(r["view"][1]), tuple(int(v) for v in r["view"][2]))
+            p.buffers.append(Buffer(shape, code, const, r.get("input"), view))
+        for s in rec["steps"]:
+            t = dict(s)
+            if "program" in t:
+                t["program"] = L.RemoraMapProgram.from_buffer_copy(bytes.fromhex(t["program"]))
+            if "spec" in t:
+                cls_ = {"fold": L.RemoraFoldSpec, "array_fold": L.RemoraFoldSpec, "scan": L.RemoraScanSpec}[t["op"]]
+                t["spec"] = cls_.from_buffer_copy(bytes.fromhex(t["spec"]))
+            p.steps.append(t)
+        p.result = int(rec["result"])
+        return p
+
+
+# --------------------------------------------------------------- planner
+# Values while planning: ("buf", id) an array (or a rank-0 device scalar),
+# ("const", value, code) a scalar known at plan time, ("func", params, body)
+# a function value.
+def _scalar_code(t: object) -> int:
+    if _kind(t) != "ScalarType" or t.name not in _ELEM:
+        raise _unsupported(f"element type {t!r}")
+    return _ELEM[t.name]
+
+
+def _shape(t: object) -> tuple[int, ...]:
+    if _kind(t) == "ScalarType":
+        return ()
+    if _kind(t) != "ArrayType":
+        raise _unsupported(f"type {t!r}")
+    out = []
+    for d in t.shape:
+        if _kind(d) != "StaticDim":
+            raise _unsupported("shapes must be static")
+        out.append(int(d.value))
+    return tuple(out)
+
+
+def _elem(t: object) -> int:
+    return _scalar_code(t.element if _kind(t) == "ArrayType" else t)
+
+
+def _base_op(op: str) -> str:
+    for base in sorted(_ARITH | _CMP | _LOGIC | _UNARY, key=len, reverse=True):
+        if op == base or (op.startswith(base) and op[len(base):] in ("f", "i", "b")):
+            return base
+    raise _unsupported(f"primitive {op!r}")
+
+
+def _const_eval(op: str, args: list[tuple[Any, int]], out_code: int) -> tuple[Any, int]:
+    """Plan-time folding of a scalar primitive on literals, in the result's
+    element type (f32 ops rounded once, like the device)."""
+    vals = [np.asarray(v, dtype=_NP[c]) for v, c in args]
+    if op in _ARITH:
+        a, b = (v.astype(_NP[out_code]) for v in vals)
+        if op == "/" and out_code == L.I32:
+            r = np.int32(0) if b == 0 else np.int32(int(a) // int(b) if a * b >= 0 else -(abs(int(a)) // abs(int(b))))
+        else:
+            r = {"+": np.add, "-": np.subtract, "*": np.multiply, "/": np.divide}[op](a, b)
+        return r.astype(_NP[out_code]).item(), out_code
+    if op in _CMP:
+        ct = L.F32 if any(c == L.F32 for _, c in args) else L.I32
+        a, b = (v.astype(_NP[ct]) for v in vals)
+        fn = {"<": np.less, "<=": np.less_equal, ">": np.greater, ">=": np.greater_equal, "==": np.equal,
+              "!=": np.not_equal}[op]
+        return bool(fn(a, b)), L.BOOL
+    if op in _LOGIC:
+        a, b = (bool(v) for v in vals)
+        return (a and b) if op == "&&" else (a or b), L.BOOL
+    if op == "-" and len(vals) == 1:
+        return (-vals[0]).astype(_NP[out_code]).item(), out_code
+    raise _unsupported(f"plan-time folding of {op}")
+
+
+class _Planner:
+    def __init__(self, functions: dict[str, Any]) -> None:
+        self.functions = functions
+        self.plan = Plan()
+
+    # -------------------------------------------------------- buffers
+    def buf(self, shape: tuple[int, ...], code: int, **kw: Any) -> int:
+        self.plan.buffers.append(Buffer(tuple(shape), code, **kw))
+        return len(self.plan.buffers) - 1
+
+    def shape_of(self, b: int) -> tuple[int, ...]:
+        return self.plan.buffers[b].shape
+
+    def code_of(self, b: int) -> int:
+        return self.plan.buffers[b].dtype
+
+    def as_buf(self, v: tuple) -> int:
+        if v[0] == "buf":
+            return v[1]
+        if v[0] == "const":
+            return self.buf((), v[2], const=np.asarray(v[1], dtype=_NP[v[2]]))
+        raise _unsupported("a function where an array is needed")
+
+    def strides_of(self, b: int) -> tuple[int, tuple[int, ...], int]:
+        """(base buffer, element offset, element strides) of b."""
+        bb = self.plan.buffers[b]
+        if bb.view is not None:
+            return bb.view
+        shape, st, acc = bb.shape, [], 1
+        for d in reversed(shape):
+            st.append(acc)
+            acc *= d
+        return b, 0, tuple(reversed(st))
+
+    def view(self, b: int, shape: tuple[int, ...], offset: int, strides: tuple[int, ...]) -> int:
+        base, off0, _ = self.strides_of(b)
+        return self.buf(shape, self.code_of(b), view=(base, off0 + offset, tuple(strides)))
+
+    # ------------------------------------------------------- lowering
+    def lower(self, node: object, env: dict[str, tuple]) -> tuple:
+        k = _kind(node)
+        if k == "HIRLit":
+            return ("const", node.value, _scalar_code(node.type))
+        if k == "HIRVar":
+            if node.name in env:
+                return env[node.name]
+            if node.name in self.functions:
+                f = self.functions[node.name]
+                return ("func", [p.name for p in f.params], f.body)
+            raise _unsupported(f"unbound name {node.name}")
+        if k == "HIRLet":
+            return self.lower(node.body, {**env, node.name: self.lower(node.value, env)})
+        if k == "HIRArrayLit":
+            return ("buf", self.buf(_shape(node.result_type), _elem(node.result_type),
+                                    const=self._literal(node, env)))
+        if k == "HIRIota":
+            n = int(node.size.value) if _kind(node.size) == "StaticDim" else None
+            if n is None:
+                raise _unsupported("iota of a static size")
+            return ("buf", self.buf((n,), L.I32, const=np.arange(n, dtype=np.int32)))
+        if k == "HIRCall":
+            f = self.functions.get(node.func_name)
+            if f is None:
+                raise _unsupported(f"call of unknown function {node.func_name}")
+            args = [self.lower(a, env) for a in node.args]
+            return self.lower(f.body, {**env, **{p.name: a for p, a in zip(f.params, args)}})
+        if k in ("HIRPrimOp", "HIRIf", "HIRCast"):
+            return self.scalar_or_elementwise(node, env)
+        if k == "HIRMap":
+            return self.lower_map(node, env)
+        if k == "HIRFold":
+            return self.lower_fold(node, env)
+        if k == "HIRScan":
+            return self.lower_scan(node, env)
+        if k == "HIRAppend":
+            a, b = self.as_buf(self.lower(node.left, env)), self.as_buf(self.lower(node.right, env))
+            out = self.buf(_shape(node.result_type), _elem(node.result_type))
+            self.plan.steps.append({"op": "append", "a": a, "b": b, "out": out})
+            return ("buf", out)
+        if k == "HIRRotate":
+            a = self.as_buf(self.lower(node.array, env))
+            out = self.buf(self.shape_of(a), self.code_of(a))
+            self.plan.steps.append({"op": "rotate", "in": a, "out": out, "shift": int(node.shift.value)})
+            return ("buf", out)
+        if k in ("HIRSort", "HIRGrade"):
+            a = self.as_buf(self.lower(node.array, env))
+            grade = k == "HIRGrade"
+            out = self.buf(self.shape_of(a), L.I32 if grade else self.code_of(a))
+            self.plan.steps.append({"op": "grade" if grade else "sort", "in": a, "out": out})
+            return ("buf", out)
+        if k == "HIRReverse":
+            a = self.as_buf(self.lower(node.array, env))
+            shape = self.shape_of(a)
+            _, _, st = self.strides_of(a)
+            return ("buf", self.view(a, shape, (shape[0] - 1) * st[0], (-st[0], *st[1:])))
+        if k == "HIRTranspose":
+            a = self.as_buf(self.lower(node.array, env))
+            shape = self.shape_of(a)
+            _, _, st = self.strides_of(a)
+            return ("buf", self.view(a, tuple(reversed(shape)), 0, tuple(reversed(st))))
+        if k == "HIRIndex":
+            return self.lower_index(node, env)
+        if k == "HIRReshape":
+            a = self.as_buf(self.lower(node.array, env))
+            shape = _shape(node.result_type)
+            base, off, st = self.strides_of(a)
+            contiguous = st == self.strides_of(self.buf(self.shape_of(a), self.code_of(a)))[2]
+            if not contiguous:
+                a = self.emit_map(InputExpr(0), [a], self.shape_of(a), self.code_of(a))
+            strides, acc = [], 1
+            for d in reversed(shape):
+                strides.append(acc)
+                acc *= d
+            return ("buf", self.view(a, shape, 0, tuple(reversed(strides))))
+        raise _unsupported(f"{k} nodes")
+
+    def _literal(self, node: object, env: dict) -> np.ndarray:
+        def rec(n: object) -> Any:
+            if _kind(n) == "HIRArrayLit":
+                return [rec(e) for e in n.elements]
+            v = self.lower(n, env)
+            if v[0] != "const":
+                raise _unsupported("array literals of plan-time scalars")
+            return v[1]
+
+        return np.asarray(rec(node), dtype=_NP[_elem(node.result_type)])
+
+    def lower_index(self, node: object, env: dict) -> tuple:
+        a = self.as_buf(self.lower(node.array, env))
+        shape = self.shape_of(a)
+        _, _, st = self.strides_of(a)
+        off, out_shape, out_st = 0, [], []
+        for d, ix in enumerate(node.indices):
+            if _kind(ix) == "HIRSlice":
+                start, end = int(ix.start), int(ix.end)
+                off += start * st[d]
+                out_shape.append(end - start)
+                out_st.append(st[d])
+            else:
+                v = self.lower(ix, env)
+                if v[0] != "const":
+                    raise _unsupported("indices known at plan time")
+                i = int(v[1])
+                if not 0 <= i < shape[d]:
+                    raise _unsupported(f"index {i} outside axis of {shape[d]}")
+                off += i * st[d]
+        for d in range(len(node.indices), len(shape)):
+            out_shape.append(shape[d])
+            out_st.append(st[d])
+        return ("buf", self.view(a, tuple(out_shape), off, tuple(out_st)))
+
+    # ---- elementwise expressions over buffers and constants
+    def expr(self, node: object, env: dict, operands: list[int]) -> tuple[Expr, int]:
+        """(expression, element code) of a scalar-valued HIR node; array or
+        device-scalar operands are appended to `operands` as inputs."""
+        k = _kind(node)
+        if k == "HIRLit":
+            return ConstantExpr(int(node.value) if isinstance(node.value, bool) else node.value), \
+                _scalar_code(node.type)
+        if k == "HIRVar" and node.name in env and env[node.name][0] == "expr":
+            return env[node.name][1], env[node.name][2]
+        if k == "HIRVar" and node.name in env and env[node.name][0] == "const":
+            v = env[node.name]
+            return ConstantExpr(int(v[1]) if isinstance(v[1], bool) else v[1]), v[2]
+        if k == "HIRVar" and node.name in env and env[node.name][0] == "buf":
+            b = env[node.name][1]
+            operands.append(b)
+            return InputExpr(len(operands) - 1), self.code_of(b)
+        if k == "HIRIf":
+            c, _ = self.expr(node.condition, env, operands)
+            t, tc = self.expr(node.then_branch, env, operands)
+            e, _ = self.expr(node.else_branch, env, operands)
+            return SelectExpr(c, t, e), tc
+        if k == "HIRPrimOp":
+            op = _base_op(node.op)
+            args = [self.expr(a, env, operands) for a in node.args]
+            code = _elem(node.result_type)
+            es = [a for a, _ in args]
+            if op in _UNARY:
+                return UnaryExpr(op, es[0]), code
+            if op == "-" and len(es) == 1:
+                return UnaryExpr("neg", es[0]), code
+            if op in _ARITH:
+                return BinaryExpr(op, *es), code
+            if op in _CMP:
+                return CmpExpr(op, *es), code
+            if op in _LOGIC:
+                return LogicExpr(op, *es), code
+            raise _unsupported(f"primitive {op}")
+        # any other array-valued node: computed first, then an operand
+        v = self.lower(node, env)
+        if v[0] == "const":
+            return ConstantExpr(int(v[1]) if isinstance(v[1], bool) else v[1]), v[2]
+        if v[0] == "buf":
+            operands.append(v[1])
+            return InputExpr(len(operands) - 1), self.code_of(v[1])
+        raise _unsupported(f"{k} in an elementwise expression")
+
+    def const_of(self, node: object, env: dict) -> tuple | None:
+        """The value of a scalar node if it is known at plan time."""
+        k = _kind(node)
+        if k == "HIRLit":
+            return ("const", node.value, _scalar_code(node.type))
+        if k == "HIRVar":
+            v = env.get(node.name)
+            return v if v is not None and v[0] == "const" else None
+        if k == "HIRPrimOp":
+            args = [self.const_of(a, env) for a in node.args]
+            if all(a is not None for a in args):
+                return ("const", *_const_eval(_base_op(node.op), [a[1:] for a in args], _elem(node.result_type)))
+            return None
+        if k == "HIRIf":
+            c = self.const_of(node.condition, env)
+            if c is None:
+                return None
+            return self.const_of(node.then_branch if c[1] else node.else_branch, env)
+        if k == "HIRCast":
+            v = self.const_of(node.value, env)
+            if v is None:
+                return None
+            to = _scalar_code(node.to_type)
+            return ("const", np.asarray(v[1], dtype=_NP[v[2]]).astype(_NP[to]).item(), to)
+        return None
+
+    def apply_func(self, func: object, env: dict, arg_exprs: list[tuple[Expr, int]], operands: list[int],
+                   result_code: int) -> Expr:
+        """The expression of a scalar function (primitive, section, lambda or
+        named function) applied to argument expressions."""
+        k = _kind(func)
+        if k == "HIRPrimCallable":
+            op = _base_op(func.op)
+            args = [e for e, _ in arg_exprs]
+            if func.left_arg is not None:
+                args = [self.expr(func.left_arg, env, operands)[0], *args]
+            if func.right_arg is not None:
+                args = [*args, self.expr(func.right_arg, env, operands)[0]]
+            if op in _UNARY:
+                return UnaryExpr(op, args[0])
+            if op == "-" and len(args) == 1:
+                return UnaryExpr("neg", args[0])
+            make = BinaryExpr if op in _ARITH else CmpExpr if op in _CMP else LogicExpr
+            return make(op, *args)
+        if k == "HIRLambda":
+            names, body = [p.name for p in func.params], func.body
+        elif k == "HIRVar":
+            v = self.lower(func, env)
+            if v[0] != "func":
+                raise _unsupported("mapping a non-function")
+            names, body = v[1], v[2]
+        else:
+            raise _unsupported(f"{k} as a scalar function")
+        inner = {**env, **{n: ("expr", e, c) for n, (e, c) in zip(names, arg_exprs)}}
+        return self.expr(body, inner, operands)[0]
+
+    def emit_map(self, expr: Expr, operands: list[int], shape: tuple[int, ...], out_code: int) -> int:
+        in_codes = [self.code_of(b) for b in operands]
+        compute = L.F32 if L.F32 in in_codes + [out_code] else L.I32 if L.I32 in in_codes + [out_code] else L.BOOL
+        if not operands:
+            raise _unsupported("a map with no array operand")
+        prog = compile_program(expr, len(operands), compute=compute, out=out_code, in_dtypes=in_codes)
+        out = self.buf(shape, out_code)
+        self.plan.steps.append({"op": "map", "program": prog, "ins": list(operands), "out": out})
+        return out
+
+    def scalar_or_elementwise(self, node: object, env: dict) -> tuple:
+        c = self.const_of(node, env)
+        if c is not None:
+            return c
+        if _kind(node) == "HIRIf":
+            cond = self.const_of(node.condition, env)
+            if cond is not None:
+                return self.lower(node.then_branch if cond[1] else node.else_branch, env)
+        # elementwise over arrays and device scalars: one fused map
+        operands: list[int] = []
+        e, code = self.expr(node, env, operands)
+        return ("buf", self.emit_map(e, operands, _shape(node.result_type), code))
+
+    def lower_map(self, node: object, env: dict) -> tuple:
+        arrays = [self.as_buf(self.lower(a, env)) for a in node.arrays]
+        shape = _shape(node.result_type)
+        func = node.func
+        if node.cell_shape:
+            return self.lower_cell_map(node, env, arrays, shape)
+        operands = list(arrays)
+        arg_exprs = [(InputExpr(i), self.code_of(b)) for i, b in enumerate(arrays)]
+        # captured scalars and arrays of the body become extra operands
+        expr = self.apply_func(func, env, arg_exprs, operands, _elem(node.result_type))
+        return ("buf", self.emit_map(expr, operands, shape, _elem(node.result_type)))
+
+    def _func_parts(self, func: object, env: dict) -> tuple[list[str], object]:
+        if _kind(func) == "HIRLambda":
+            return [p.name for p in func.params], func.body
+        v = self.lower(func, env)
+        if v[0] != "func":
+            raise _unsupported("a cell map of a non-function")
+        return v[1], v[2]
+
+    def lower_cell_map(self, node: object, env: dict, arrays: list[int], shape: tuple[int, ...]) -> tuple:
+        names, body = self._func_parts(node.func, env)
+        if _kind(body) != "HIRFold" or len(arrays) != 1:
+            raise _unsupported("cell maps other than a fold of the cell")
+        op, init, code = self.fold_op(body, env)
+        if _kind(body.array) != "HIRVar" or body.array.name != names[0]:
+            raise _unsupported("a cell fold folds its cell")
+        if init[0] != "const" or op not in ("+", "*"):
+            raise _unsupported("cell folds with + or * and a literal init")
+        in_code = self.code_of(arrays[0])
+        premap = InputExpr(0) if in_code != code else None
+        sp = fold_spec(op=op, init=init[1], mode="cell", cell_rank=len(node.cell_shape), dtype=code, premap=premap,
+                       premap_in_dtypes=[in_code] if premap is not None else None)
+        out = self.buf(shape, code)
+        self.plan.steps.append({"op": "fold", "spec": sp, "ins": arrays, "out": out})
+        return ("buf", out)
+
+    def fold_op(self, node: object, env: dict) -> tuple[str, Any, int]:
+        """(op, init, accumulator code) of a fold with a + / * / && / || step."""
+        func = node.func
+        code = _elem(node.result_type)
+        if _kind(func) == "HIRPrimCallable" and func.left_arg is None and func.right_arg is None:
+            op = _base_op(func.op)
+        else:
+            names, body = self._func_parts(func, env)
+            if _kind(body) == "HIRPrimOp" and len(body.args) == 2 and \
+                    [getattr(a, "name", None) for a in body.args] == names:
+                op = _base_op(body.op)
+            elif _kind(body) == "HIRMap" and _kind(body.func) == "HIRPrimCallable" and \
+                    [getattr(a, "name", None) for a in body.arrays] == names:
+                op = _base_op(body.func.op)  # an elementwise accumulator step (array fold)
+            else:
+                raise _unsupported("fold steps other than acc op x")
+        init = self.lower(node.init, env)
+        if op not in ("+", "*", "&&", "||"):
+            raise _unsupported(f"fold with {op}")
+        return op, init, code
+
+    def lower_fold(self, node: object, env: dict) -> tuple:
+        op, init, code = self.fold_op(node, env)
+        arr = self.as_buf(self.lower(node.array, env))
+        in_code = self.code_of(arr)
+        if op in ("&&", "||"):
+            # over bools: && is a product and || a sum of 0/1 in i32, then != 0
+            acc_code, op2 = L.I32, ("*" if op == "&&" else "+")
+        else:
+            acc_code, op2 = code, op
+        if in_code == L.BOOL:
+            # the fold kernels read f32 / i32: widen the bools first
+            arr = self.emit_map(InputExpr(0), [arr], self.shape_of(arr), L.I32)
+            in_code = L.I32
+        if init[0] == "const":
+            if len(self.shape_of(arr)) != 1:
+                raise _unsupported("scalar-init folds of rank >= 2 arrays")
+            premap = InputExpr(0) if in_code != acc_code else None
+            sp = fold_spec(op=op2, init=int(init[1]) if acc_code != L.F32 else float(init[1]), mode="all",
+                           dtype=acc_code, premap=premap, premap_in_dtypes=[in_code] if premap is not None else None)
+            out = self.buf((), acc_code)
+            self.plan.steps.append({"op": "fold", "spec": sp, "ins": [arr], "out": out})
+        else:
+            ib = self.as_buf(init)
+            if in_code != acc_code or self.code_of(ib) != acc_code:
+                raise _unsupported("array folds in one element type")
+            sp = fold_spec(op=op2, dtype=acc_code)
+            out = self.buf(self.shape_of(ib), acc_code)
+            self.plan.steps.append({"op": "array_fold", "spec": sp, "in": arr, "init": ib, "out": out})
+        if acc_code != code:
+            out = self.emit_map(CmpExpr("!=", InputExpr(0), ConstantExpr(0)), [out], self.shape_of(out), code)
+        return ("buf", out)
+
+    def lower_scan(self, node: object, env: dict) -> tuple:
+        op, init, code = self.fold_op(node, env)
+        arr = self.as_buf(self.lower(node.array, env))
+        if init[0] != "const" or op not in ("+", "*") or self.code_of(arr) != code:
+            raise _unsupported("scans with + or *, a literal init, one element type")
+        sp = scan_spec(op=op, init=init[1], dtype=code, exclusive=bool(node.exclusive), right=bool(node.right))
+        out = self.buf(self.shape_of(arr), code)
+        self.plan.steps.append({"op": "scan", "spec": sp, "in": arr, "out": out})
+        return ("buf", out)
+
+
+def plan_from_hir(program: object) -> Plan:
+    """A plan for the reference's HIRProgram (its `main` expression, with
+    the program's lifted functions)."""
+    if getattr(program, "main", None) is None:
+        raise _unsupported("a program without a main expression")
+    pl = _Planner({f.name: f for f in program.functions})
+    v = pl.lower(program.main, {})
+    out = pl.as_buf(v)
+    if pl.plan.buffers[out].view is not None or pl.plan.buffers[out].input is not None:
+        # the result is a view: one copy makes it a buffer of its own
+        out = pl.emit_map(InputExpr(0), [out], pl.shape_of(out), pl.code_of(out))
+    pl.plan.result = out
+    return pl.plan
+
+
+# -------------------------------------------------------------- execution
+def execute_plan(plan: Plan, inputs: list[np.ndarray] | None = None, device: int | None = None) -> np.ndarray:
+    """Run a plan on the device and return its result as a numpy array."""
+    import torch
+
+    from remora_b200.abi import make_memref_descriptor
+    from remora_b200.runtime import context
+
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    ctx = context(dev.index)
+    lib = L.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    store: dict[int, Any] = {}
+    for i, b in enumerate(plan.buffers):
+        if b.view is not None:
+            continue
+        if b.const is not None:
+            store[i] = torch.from_numpy(np.ascontiguousarray(b.const)).to(dev)
+        elif b.input is not None:
+            store[i] = torch.from_numpy(np.ascontiguousarray(inputs[b.input], dtype=_NP[b.dtype])).to(dev)
+        else:
+            store[i] = torch.empty(b.shape, dtype=getattr(torch, {L.F32: "float32", L.I32: "int32",
+                                                                  L.BOOL: "bool"}[b.dtype]), device=dev)
+    keep: list = []
+
+    def desc(i: int):
+        b = plan.buffers[i]
+        if b.view is not None:
+            base, off, st = b.view
+            t = store[base]
+            d = make_memref_descriptor(t.data_ptr(), b.shape, st, None, off)
+        else:
+            t = store[i]
+            st, acc = [], 1
+            for s in reversed(b.shape):
+                st.append(acc)
+                acc *= s
+            d = make_memref_descriptor(t.data_ptr(), b.shape, tuple(reversed(st)), None, 0)
+        keep.append(d)
+        return ctypes.addressof(d)
+
+    for s in plan.steps:
+        op = s["op"]
+        if op == "map":
+            ins = s["ins"]
+            ptrs = (ctypes.c_void_p * len(ins))(*[desc(i) for i in ins])
+            ranks = (ctypes.c_int32 * len(ins))(*[len(plan.buffers[i].shape) for i in ins])
+            st = lib.remora_b200_map(ctx.ptr, ctypes.byref(s["program"]), ptrs, ranks, len(ins), desc(s["out"]),
+                                     len(plan.buffers[s["out"]].shape), stream)
+        elif op == "fold":
+            ins = s["ins"]
+            ptrs = (ctypes.c_void_p * len(ins))(*[desc(i) for i in ins])
+            ranks = (ctypes.c_int32 * len(ins))(*[len(plan.buffers[i].shape) for i in ins])
+            st = lib.remora_b200_fold(ctx.ptr, ctypes.byref(s["spec"]), ptrs, ranks, len(ins), desc(s["out"]),
+                                      len(plan.buffers[s["out"]].shape), stream)
+        elif op == "array_fold":
+            st = lib.remora_b200_array_fold(ctx.ptr, ctypes.byref(s["spec"]), desc(s["in"]),
+                                            len(plan.buffers[s["in"]].shape), desc(s["init"]), desc(s["out"]),
+                                            stream)
+        elif op == "scan":
+            st = lib.remora_b200_scan(ctx.ptr, ctypes.byref(s["spec"]), desc(s["in"]), desc(s["out"]),
+                                      len(plan.buffers[s["in"]].shape), stream)
+        elif op == "append":
+            st = lib.remora_b200_append(ctx.ptr, plan.buffers[s["a"]].dtype, desc(s["a"]), desc(s["b"]),
+                                        desc(s["out"]), len(plan.buffers[s["out"]].shape), stream)
+        elif op == "rotate":
+            st = lib.remora_b200_rotate(ctx.ptr, plan.buffers[s["in"]].dtype, int(s["shift"]), desc(s["in"]),
+                                        desc(s["out"]), len(plan.buffers[s["in"]].shape), stream)
+        elif op in ("sort", "grade"):
+            fn = lib.remora_b200_grade if op == "grade" else lib.remora_b200_sort
+            st = fn(ctx.ptr, plan.buffers[s["in"]].dtype, desc(s["in"]), desc(s["out"]),
+                    len(plan.buffers[s["in"]].shape), stream)
+        else:
+            raise _unsupported(f"plan step {op}")
+        L.check(st, f"plan step {op}")
+    L.check(lib.remora_b200_synchronize(ctx.ptr, stream), "plan")
+    res = plan.buffers[plan.result]
+    return store[plan.result].cpu().numpy().astype(_NP[res.dtype]).reshape(res.shape)
+
+
+def compile_source_to_plan(source: str, *, include_prelude: bool = True, syntax: str = "ml") -> Plan:
+    """The reference's front end (parse, type check, elaborate, erase to HIR,
+    defunctionalise, as remora/compiler.py:106-143 does before its MLIR
+    lowering) followed by ``plan_from_hir``.  Needs the reference package."""
+    from remora.compiler import _parse_source  # the reference's front end
+    from remora.defunc import defunctionalize
+    from remora.elaborate import elaborate_program
+    from remora.erase import erase_to_hir
+    from remora.prelude import with_prelude
+    from remora.typechecker import TypeChecker
+
+    text = with_prelude(source) if include_prelude and syntax == "ml" else source
+    typed = TypeChecker().check_program(_parse_source(text, syntax))
+    return plan_from_hir(defunctionalize(erase_to_hir(elaborate_program(typed))))

@@ -1,0 +1,116 @@
+"""Whole-program plans (remora_b200.program_plan) without a GPU.
+
+tests/golden/program_plans.{json,npz} holds the reference's acceptance
+programs (remora/tests/acceptance/pass/*.remora) and a few more, planned from
+the reference front end's HIR, with the reference's result for each.  Here a
+CPU interpreter of plans, built on the oracle, runs every recorded plan and
+must give those results: the plan means what the program says.  Where the
+reference is importable, the planner must reproduce the recorded plans.
+tests/test_gpu_program_plan.py runs the same plans on the device."""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from remora_b200 import _lib as L
+from remora_b200.program_plan import Plan
+
+REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
+have_ref = os.path.isdir(os.path.join(REF, "remora"))
+_NP = {0: np.float32, 1: np.int32, 2: np.bool_}
+
+
+def programs() -> list[dict]:
+    return json.loads((GOLDEN / "program_plans.json").read_text())["programs"]
+
+
+def expected(name: str) -> np.ndarray:
+    with np.load(GOLDEN / "program_plans.npz") as f:
+        return f[f"{name}__out"]
+
+
+def close(got: np.ndarray, want: np.ndarray) -> None:
+    assert got.shape == want.shape and got.dtype == want.dtype, (got.shape, want.shape, got.dtype, want.dtype)
+    if got.dtype == np.float32:
+        np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6 * (float(np.abs(want).max()) if want.size else 0))
+    else:
+        np.testing.assert_array_equal(got, want)
+
+
+def run_plan_on_oracle(orc, plan: Plan) -> np.ndarray:
+    """The plan's steps, each on the oracle, over numpy buffers."""
+    store: dict[int, np.ndarray] = {}
+
+    def get(i: int) -> np.ndarray:
+        b = plan.buffers[i]
+        if b.view is not None:
+            base, off, st = b.view
+            arr = get(base)
+            es = arr.itemsize
+            return np.ndarray(b.shape, dtype=arr.dtype, buffer=arr, offset=off * es, strides=[s * es for s in st])
+        if i not in store:
+            store[i] = (np.array(b.const, dtype=_NP[b.dtype]) if b.const is not None
+                        else np.zeros(b.shape, dtype=_NP[b.dtype]))
+        return store[i]
+
+    for s in plan.steps:
+        op = s["op"]
+        if op == "map":
+            out = plan.buffers[s["out"]]
+            store[s["out"]] = orc.run_map(s["program"], [get(i) for i in s["ins"]], out.shape, _NP[out.dtype])
+        elif op == "fold":
+            sp = s["spec"]
+            ins = [np.ascontiguousarray(get(i)) for i in s["ins"]]
+            store[s["out"]] = (orc.fold_all(sp, ins) if sp.mode == L.FOLD_ALL
+                               else orc.cell_fold(sp, ins, sp.cell_rank))
+        elif op == "array_fold":
+            store[s["out"]] = orc.array_fold(s["spec"], np.ascontiguousarray(get(s["in"])),
+                                             np.ascontiguousarray(get(s["init"])))
+        elif op == "scan":
+            store[s["out"]] = orc.scan(s["spec"], np.ascontiguousarray(get(s["in"])))
+        elif op == "append":
+            store[s["out"]] = orc.append(get(s["a"]), get(s["b"]))
+        elif op == "rotate":
+            store[s["out"]] = orc.rotate(get(s["in"]), int(s["shift"]))
+        elif op == "sort":
+            store[s["out"]] = orc.sort(get(s["in"]))
+        elif op == "grade":
+            store[s["out"]] = orc.grade(get(s["in"]))
+        else:
+            raise AssertionError(op)
+    res = plan.buffers[plan.result]
+    return np.asarray(get(plan.result)).astype(_NP[res.dtype]).reshape(res.shape)
+
+
+def test_fixture_covers_the_acceptance_programs():
+    progs = programs()
+    names = {p["name"] for p in progs}
+    # 43 of the reference's 45 acceptance programs (one uses indexing inside a
+    # cell map; one does not pass the reference's own front end) and 6 more
+    assert len(names) == 49
+    ops = {op for p in progs for op in p["steps"]}
+    assert ops == {"map", "fold", "array_fold", "scan", "append", "rotate", "sort", "grade"}
+    for p in progs:
+        plan = Plan.from_record(p["plan"])
+        assert plan.to_record() == p["plan"]
+
+
+@pytest.mark.parametrize("rec", programs(), ids=lambda r: r["name"])
+def test_plan_on_the_oracle_gives_the_reference_value(oracle_mod, rec):
+    close(run_plan_on_oracle(oracle_mod, Plan.from_record(rec["plan"])), expected(rec["name"]))
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+def test_planner_reproduces_recorded_plans():
+    sys.path.insert(0, REF)
+    from remora_b200.program_plan import compile_source_to_plan
+
+    for rec in programs():
+        plan = compile_source_to_plan(rec["source"], syntax=rec["syntax"])
+        assert plan.to_record() == rec["plan"], rec["name"]
