@@ -67,8 +67,14 @@ constexpr uint32_t align1k(uint32_t v) { return (v + 1023u) & ~1023u; }
 constexpr int kFuseNone = 0, kFusePool = 1, kFuseUnpool = 2;
 constexpr uint8_t kNoGradCode = 255;
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
+// CSPLIT > 1: the input channels of a tile flow through the raw and operand
+// stages in CSPLIT slices of CIN / CSPLIT channels (one TMA load, one
+// transform and the MMAs of those channels each, accumulated into the same
+// TMEM accumulator), so that a tile of many channels still double-buffers.
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
+          int CSPLIT = 1>
 struct ConvCfg {
+  static constexpr int CH = CIN / CSPLIT;              // channels of one stage
   static constexpr bool PAR = FUSE == kFusePool;       // operand split by input row parity
   static constexpr int NPAR = PAR ? 2 : 1;
   static constexpr int PW = PAR ? W + 2 : W + 1;       // padded row pitch (positions)
@@ -79,13 +85,14 @@ struct ConvCfg {
   // planes start one 16-byte bank group apart (NPOS = 1 mod 8)
   static constexpr int NPOS = ((NPOS0 + 7) / 8) * 8 + 1;
   static constexpr uint32_t PLANE = NPOS * 16;  // bytes of one 4-channel plane
-  static constexpr int NPL = CIN / 4;
-  static constexpr uint32_t A_COPY = NPL * NPAR * PLANE;
+  static constexpr int NPL = CIN / 4;            // weight planes (every channel)
+  static constexpr int NPLS = CH / 4;            // operand planes of one stage
+  static constexpr uint32_t A_COPY = NPLS * NPAR * PLANE;
   static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT3 ? 2 : 1));
   // kFuseUnpool: the raw stage holds pooled rows: values, then codes
   static constexpr int PROWS = TH / 2 + 2;
-  static constexpr uint32_t RAW_F32 = FUSE == kFuseUnpool ? CIN * PROWS * (W / 2) * 4 : CIN * ROWS * W * 4;
-  static constexpr uint32_t RAW_CODES = FUSE == kFuseUnpool ? CIN * PROWS * (W / 2) : 0;
+  static constexpr uint32_t RAW_F32 = FUSE == kFuseUnpool ? CH * PROWS * (W / 2) * 4 : CH * ROWS * W * 4;
+  static constexpr uint32_t RAW_CODES = FUSE == kFuseUnpool ? CH * PROWS * (W / 2) : 0;
   static constexpr uint32_t RAW_BYTES = RAW_F32 + RAW_CODES;
   static constexpr uint32_t RAW_CODE_OFF = align1k(RAW_F32);
   static constexpr uint32_t RAW_STAGE = align1k(RAW_CODE_OFF + RAW_CODES);
@@ -96,15 +103,15 @@ struct ConvCfg {
   static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
   static constexpr size_t SMEM = (size_t)OFF_A + A_ST * A_STAGE + 1024;
   static constexpr int ACC_COLS = MB * NPAR * NOUT;  // TMEM columns of one accumulator
-  static constexpr int ITEMS = NPL * ROWS * (W / 4);
-  static constexpr int KSTEPS = CIN / 8;
-  static_assert(CIN % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
+  static constexpr int ITEMS = NPLS * ROWS * (W / 4);
+  static constexpr int KSTEPS = CH / 8;  // K steps of one stage
+  static_assert(CIN % CSPLIT == 0 && CH % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
   static_assert((CG == 8 || CG == 16 || CG == 32) && (NOUT == CG || NOUT == 2 * CG), "channel groups");
   static_assert(FUSE == kFuseNone || (TH % 2 == 0 && W % 32 == 0), "pooled rows are 16-byte TMA boxes");
   static_assert(!PAR || PW % 2 == 0, "pool partners share a lane pair");
   static_assert(2 * ACC_COLS <= 512, "two accumulators fit TMEM");
   static_assert(SMEM <= 232448, "shared memory per block");
-  static_assert(ROWS <= 256 && W <= 256 && CIN <= 256, "TMA box dims");
+  static_assert(ROWS <= 256 && W <= 256 && CH <= 256, "TMA box dims");
   static_assert(NPAR * PLANE / 16 < 16384 && BPLANE / 16 < 16384, "descriptor offsets");
 };
 
@@ -188,13 +195,13 @@ __device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lb
   return tc::smem_desc(saddr, lbo, 128, 0);
 }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE>
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE, int CSPLIT>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmx2,
                       ConvTCParams p) {
   // tmx: input rows (kFuseUnpool: pooled gradient values), tmx2: their pool
   // codes (kFuseUnpool only)
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], afull[A_ST], aempty[A_ST], tfull[2], tempty[2],
@@ -258,22 +265,26 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       tc::prefetch_tmap(&tmx);
       int it = 0;
       int issued = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-        const int st = it % RAW_ST;
-        const uint32_t ph = (it / RAW_ST) & 1;
-        if (!tc::mbar_wait(&rempty[st], ph ^ 1, abort_v, p.err, 201)) break;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * TH;
-        uint8_t *raw = smem + Cf::OFF_RAW + st * Cf::RAW_STAGE;
-        tc::mbar_arrive_expect_tx(&rfull[st], Cf::RAW_BYTES);
-        if (FUSE == kFuseUnpool) {
-          // pooled rows h0/2 - 1 .. h0/2 + TH/2 cover input rows h0 - 1 .. h0 + TH
-          tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 / 2 - 1, n * CIN);
-          tc::tma_load_3d(&tmx2, &rfull[st], raw + Cf::RAW_CODE_OFF, 0, h0 / 2 - 1, n * CIN);
-        } else {
-          tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, n * CIN);
+        for (int cs = 0; cs < CSPLIT; ++cs, ++it) {
+          const int st = it % RAW_ST;
+          const uint32_t ph = (it / RAW_ST) & 1;
+          if (!tc::mbar_wait(&rempty[st], ph ^ 1, abort_v, p.err, 201)) goto producer_done;
+          uint8_t *raw = smem + Cf::OFF_RAW + st * Cf::RAW_STAGE;
+          const int c0 = n * CIN + cs * Cf::CH;
+          tc::mbar_arrive_expect_tx(&rfull[st], Cf::RAW_BYTES);
+          if (FUSE == kFuseUnpool) {
+            // pooled rows h0/2 - 1 .. h0/2 + TH/2 cover input rows h0 - 1 .. h0 + TH
+            tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 / 2 - 1, c0);
+            tc::tma_load_3d(&tmx2, &rfull[st], raw + Cf::RAW_CODE_OFF, 0, h0 / 2 - 1, c0);
+          } else {
+            tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, c0);
+          }
+          ++issued;
         }
-        ++issued;
       }
+    producer_done:
       // Do not leave while a TMA copy may still write this CTA's shared
       // memory: wait (bounded) for the last RAW_ST loads to land.
       for (int j = issued > RAW_ST ? issued - RAW_ST : 0; j < issued; ++j) {
@@ -291,15 +302,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       // shared-memory addresses are below 2^18).
       const uint64_t bd_hi = desc_interleaved(s_base, Cf::BPLANE);
       const uint64_t bd_lo = desc_interleaved(s_base + Cf::W_COPY, Cf::BPLANE);
-      int it = 0;
+      int it = 0, ti = 0;
       bool issued = false;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
+        const int acc = ti & 1;
+        const uint32_t aph = (ti >> 1) & 1;
+        for (int cs = 0; cs < CSPLIT; ++cs, ++it) {
         const int st = it % A_ST;
         const uint32_t ph = (it / A_ST) & 1;
-        const int acc = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (!tc::mbar_wait(&afull[st], ph, abort_v, p.err, 202)) break;
-        if (!tc::mbar_wait(&tempty[acc], aph ^ 1, abort_v, p.err, 203)) break;
+        if (!tc::mbar_wait(&afull[st], ph, abort_v, p.err, 202)) goto mma_done;
+        if (cs == 0 && !tc::mbar_wait(&tempty[acc], aph ^ 1, abort_v, p.err, 203)) goto mma_done;
         tc::fence_after_sync();
         const uint32_t a_hi = s_base + Cf::OFF_A + st * Cf::A_STAGE;
         // the two 4-channel K chunks of one MMA are NPAR planes apart
@@ -322,8 +334,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                 // operand rows start (ro * PW + sc) positions into plane (4-channel group 2kk, parity pp)
                 const uint32_t a_off =
                     (uint32_t)((ro * Cf::PW + sc) * 16 + (2 * kk * Cf::NPAR + pp) * Cf::PLANE) >> 4;
-                const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + 2 * kk) * Cf::BPLANE) >> 4;
-                tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (tap | kk) != 0);
+                const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + cs * Cf::NPLS + 2 * kk) * Cf::BPLANE) >> 4;
+                tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (cs | tap | kk) != 0);
                 if (SPLIT3) {
                   tc::mma_tf32(d, ad_hi + a_off, bd_lo + b_off, idesc, 1);
                   tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc, 1);
@@ -334,8 +346,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
         issued = true;
         tc::mma_commit(&aempty[st]);
-        tc::mma_commit(&tfull[acc]);
+        if (cs == CSPLIT - 1) tc::mma_commit(&tfull[acc]);
+        }
       }
+    mma_done:
       if (issued) {
         tc::mma_commit(&drain);
         const long long t0 = clock64();
@@ -427,8 +441,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     // an order rotated by (qd / 2) % 4 so the 8 lanes of a shared-memory
     // phase hit 8 different 16-byte bank groups.
     const int tt = threadIdx.x - kTransformWarp0 * 32;
-    int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    const int nsub = ((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * CSPLIT;
+    for (int it = 0; it < nsub; ++it) {
       const int rs = it % RAW_ST, as = it % A_ST;
       const uint32_t rph = (it / RAW_ST) & 1, aph = (it / A_ST) & 1;
       if (!tc::mbar_wait(&rfull[rs], rph, abort_v, p.err, 205)) break;
@@ -525,15 +539,16 @@ struct ConvIO {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone>
+template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
+          int CSPLIT = 1>
 int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
+  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
   if (!aligned16(io.x) || (FUSE == kFuseUnpool && !aligned16(io.x_codes)) ||
       (reinterpret_cast<uintptr_t>(io.y) & 3)) {
     *handled = false;  // TMA cannot address the input, or the output is not f32-aligned
     return REMORA_OK;
   }
-  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE>;
+  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
   static bool attr = false;
   if (!attr) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
@@ -541,10 +556,10 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
   }
   CUtensorMap mx, mx2;
   if (FUSE == kFuseUnpool) {
-    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx));
-    REMORA_TRY(encode_activation(io.x_codes, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, CIN, &mx2, true));
+    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, Cf::CH, &mx));
+    REMORA_TRY(encode_activation(io.x_codes, p.N, CIN, p.H / 2, W / 2, Cf::PROWS, Cf::CH, &mx2, true));
   } else {
-    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H, W, Cf::ROWS, CIN, &mx));
+    REMORA_TRY(encode_activation(io.x, p.N, CIN, p.H, W, Cf::ROWS, Cf::CH, &mx));
     mx2 = mx;
   }
   ConvTCParams q = p;
@@ -569,15 +584,16 @@ int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool s
   if (cin == 16 && width == 64 && nout == 32)
     return split ? launch_conv<16, 64, 8, 32, true, 2, 1, 16>(io, p, sm_count, stream, handled)
                  : launch_conv<16, 64, 8, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
+  // 32 input channels: two 16-channel stages per tile, double-buffered
   if (cin == 32 && width == 64 && nout == 16)
-    return split ? launch_conv<32, 64, 4, 16, true, 1, 1, 8>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 64, 8, 16, false, 1, 1, 8>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 64, 4, 16, true, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 64, 8, 16, false, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
   if (cin == 16 && width == 32 && nout == 32)
     return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
                  : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 32 && nout == 16)
-    return split ? launch_conv<32, 32, 8, 16, true, 1, 1, 8>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 1, 1, 8>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 32, 8, 16, true, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
@@ -596,8 +612,8 @@ int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width,
                     cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 32 && width == 32 && p.COUT <= 16 && p.H % 2 == 0)
-    return split ? launch_conv<32, 32, 8, 16, true, 2, 1, 8, kFuseUnpool>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 2, 1, 8, kFuseUnpool>(io, p, sm_count, stream, handled);
+    return split ? launch_conv<32, 32, 8, 16, true, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
+                 : launch_conv<32, 32, 16, 16, false, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
