@@ -853,9 +853,9 @@ TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms"
                                     "matmul": 335_706_368 + 61_118_208, "matmul_3x": None, "bmm": None,
                                     "conv": 67_187_968 + 75_173_120, "conv_dgrad": 134_268_160 + 33_349_888,
                                     "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None,
-                                    # one radix pass's scatter; one compaction
-                                    "sort": 285_516_800 + 223_513_088, "grade": None,
-                                    "filter": 268_590_592 + 103_933_952}
+                                    # a sort or filter call is several kernels; their per-kernel
+                                    # traffic is in profiles/ (radix_sort_*, filter_compact_*)
+                                    "sort": None, "grade": None, "filter": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
