@@ -848,13 +848,12 @@ def run_ours(args) -> None:
 
 
 # Per-call DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel, from the ncu captures summarised under profiles/.
+# dominant kernel, from ncu captures of the same bench commands.
 TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms": None,
                                     "matmul": 335_706_368 + 61_118_208, "matmul_3x": None, "bmm": None,
                                     "conv": 67_187_968 + 75_173_120, "conv_dgrad": 134_268_160 + 33_349_888,
                                     "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None,
-                                    # a sort or filter call is several kernels; their per-kernel
-                                    # traffic is in profiles/ (radix_sort_*, filter_compact_*)
+                                    # a sort or filter call is several kernels: no single figure
                                     "sort": None, "grade": None, "filter": None}
 
 
