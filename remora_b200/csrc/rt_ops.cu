@@ -46,6 +46,12 @@ constexpr int64_t kMaxSortLen = (int64_t)1 << 31;  // grade stores int32 indices
 
 size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 
+// The counting kernels (radix_count, filter_count, rep_tile_sums) walk the
+// tiles from the last to the first: the pass over the same data that
+// follows them starts at the first tile, which is then the part most
+// recently read and still in L2.
+__device__ __forceinline__ int64_t reversed_tile() { return (int64_t)gridDim.x - 1 - blockIdx.x; }
+
 // ------------------------------------------------------------ key order --
 // Order-preserving maps of f32 / i32 bit patterns onto u32: unsigned order of
 // the keys is the numeric order of the values.  For f32, -0.0 sorts before
@@ -212,7 +218,8 @@ __global__ void __launch_bounds__(kT) radix_count(const uint32_t *__restrict__ k
   __shared__ uint32_t s_cnt[kWarps][256];
   for (int i = threadIdx.x; i < kWarps * 256; i += kT) (&s_cnt[0][0])[i] = 0u;
   const int warp = threadIdx.x >> 5;
-  const int64_t base = (int64_t)blockIdx.x * kTile;
+  const int64_t tile = reversed_tile();
+  const int64_t base = tile * kTile;
   const int valid_n = (int)(n - base < (int64_t)kTile ? n - base : (int64_t)kTile);
   // All loads are issued before the first shared-memory atomic.
   uint32_t k[kItems];
@@ -247,7 +254,7 @@ __global__ void __launch_bounds__(kT) radix_count(const uint32_t *__restrict__ k
   uint32_t s = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) s += s_cnt[w][d];
-  hist[(int64_t)d * ntiles + blockIdx.x] = s;
+  hist[(int64_t)d * ntiles + tile] = s;
 }
 
 // Exclusive sum of len values in[0..len) into out (may alias in) by one
@@ -528,7 +535,8 @@ template <typename T, int kMask>
 __global__ void __launch_bounds__(kT) filter_count(const T *__restrict__ src, const void *__restrict__ mask,
                                                    int64_t n, Pred p, uint32_t *__restrict__ tile_cnt) {
   __shared__ uint32_t s_w[kWarps];
-  const int64_t base = (int64_t)blockIdx.x * kTile;
+  const int64_t tile = reversed_tile();
+  const int64_t base = tile * kTile;
   uint32_t w[kItems];
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
@@ -543,7 +551,7 @@ __global__ void __launch_bounds__(kT) filter_count(const T *__restrict__ src, co
   }
   uint32_t total;
   (void)block_excl_sum<uint32_t>(c, s_w, &total);
-  if (threadIdx.x == 0) tile_cnt[blockIdx.x] = total;
+  if (threadIdx.x == 0) tile_cnt[tile] = total;
 }
 
 // One block: exclusive scan of ntiles 32/64-bit counts into 64-bit offsets,
@@ -629,7 +637,8 @@ __device__ __forceinline__ unsigned long long clamp_count(int32_t c) { return c 
 __global__ void __launch_bounds__(kT) rep_tile_sums(const int32_t *__restrict__ cnt, int64_t n,
                                                     unsigned long long *__restrict__ sums) {
   __shared__ unsigned long long s_w[kWarps];
-  const int64_t base = (int64_t)blockIdx.x * kTile;
+  const int64_t tile = reversed_tile();
+  const int64_t base = tile * kTile;
   unsigned long long c = 0;
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
@@ -638,7 +647,7 @@ __global__ void __launch_bounds__(kT) rep_tile_sums(const int32_t *__restrict__ 
   }
   unsigned long long total;
   (void)block_excl_sum<unsigned long long>(c, s_w, &total);
-  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+  if (threadIdx.x == 0) sums[tile] = total;
 }
 
 // offs[i] = sum of clamped counts before i.  The tile's counts are staged in
