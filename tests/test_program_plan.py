@@ -114,3 +114,22 @@ def test_planner_reproduces_recorded_plans():
     for rec in programs():
         plan = compile_source_to_plan(rec["source"], syntax=rec["syntax"])
         assert plan.to_record() == rec["plan"], rec["name"]
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+@pytest.mark.parametrize("source", [
+    "let xs = [[1, 2], [3, 4]] in\nmap (\\row -> row[0] + row[1]) xs",  # an index inside a cell map
+    "fold (\\acc x -> acc * x + 1) 1 (iota 5)",                            # a fold step other than acc op x
+])
+def test_unsupported_programs_raise(source):
+    sys.path.insert(0, REF)
+    from remora_b200.errors import RemoraUnsupportedError
+    from remora_b200.program_plan import compile_source_to_plan
+
+    try:
+        compile_source_to_plan(source)
+    except RemoraUnsupportedError:
+        return
+    except Exception as exc:  # the reference's own front end rejected it first
+        pytest.skip(f"front end: {type(exc).__name__}")
+    raise AssertionError("expected RemoraUnsupportedError")
