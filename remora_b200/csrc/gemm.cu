@@ -14,9 +14,14 @@
 //                  row segments straight to global memory
 // Operands may be K-major (SWIZZLE_128B tiles) or M/N-major
 // (SWIZZLE_128B_BASE32B tiles); both are native UMMA layouts.
-// 3xTF32: A and B are split into hi = tf32(x) (low 13 mantissa bits
-// cleared) and lo = x - hi (exact) by a prep pass; the MMA issues
-// hi*hi + hi*lo + lo*hi per K step into the same f32 accumulator.
+// 3xTF32: each operand is split into hi = tf32(x) (low 13 mantissa bits
+// cleared) and lo = x - hi (exact), and the MMA issues hi*hi + hi*lo +
+// lo*hi per K step into the same f32 accumulator.  Small GEMMs (at most
+// one tile per SM, or a short K) split in the kernel: TMA loads A and B as
+// they are and warps 2-3 split each stage in shared memory (hi in place, lo
+// beside it).  Large ones take operands split by a prep pass, whose cost is
+// small against their MMAs and which keeps the transform off their
+// critical path.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -115,7 +120,26 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, 
   nb = r - mb * p.nt;
 }
 
-template <bool SPLIT3, int BN_>
+// x -> (hi, lo) for the `bytes` of one operand tile at shared address t
+// (hi in place, lo at t + bytes); 64 threads, 16 bytes each per step.
+__device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid) {
+  for (uint32_t off = (uint32_t)tid * 16; off < bytes; off += 64 * 16) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(t + off) : "memory");
+    const float h0 = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    const float h1 = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    const float h2 = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    const float h3 = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + off), "f"(h0), "f"(h1), "f"(h2), "f"(h3)
+                 : "memory");
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + bytes + off), "f"(__fsub_rn(v.x, h0)),
+                 "f"(__fsub_rn(v.y, h1)), "f"(__fsub_rn(v.z, h2)), "f"(__fsub_rn(v.w, h3))
+                 : "memory");
+  }
+}
+
+template <bool SPLIT3, int BN_, bool INK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
@@ -126,7 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t B_BYTES = C::B_BYTES;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
+  // xfull: a 3xTF32 stage has been split into hi / lo (2 transform warps)
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], xfull[STAGES], tfull[2], tempty[2], drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -135,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
+      tc::mbar_init(&xfull[s], 2);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
@@ -147,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
-    if (SPLIT3) {
+    if (SPLIT3 && !INK) {
       tc::prefetch_tmap(&tmAl);
       tc::prefetch_tmap(&tmBl);
     }
@@ -175,15 +201,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&empty[s], ph ^ 1, abort_v, p.err, 101)) goto producer_done;
         uint8_t *sa = smem + (size_t)s * C::STAGE_BYTES;
-        tc::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        tc::mbar_arrive_expect_tx(&full[s], SPLIT3 && !INK ? C::STAGE_BYTES : A_BYTES + B_BYTES);
         load_operand(&tmA, &full[s], sa, p.a_mn, mb * BM, BM, kb * BK, b);
-        if (SPLIT3) {
+        if (SPLIT3 && !INK) {
           load_operand(&tmAl, &full[s], sa + A_BYTES, p.a_mn, mb * BM, BM, kb * BK, b);
-          load_operand(&tmB, &full[s], sa + 2 * A_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
           load_operand(&tmBl, &full[s], sa + 2 * A_BYTES + B_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
-        } else {
-          load_operand(&tmB, &full[s], sa + A_BYTES, p.b_mn, nb * BN, BN, kb * BK, b);
         }
+        // 3xTF32: B goes to its hi slot (split in the kernel: raw, split there)
+        load_operand(&tmB, &full[s], sa + (SPLIT3 ? 2 * A_BYTES : A_BYTES), p.b_mn, nb * BN, BN, kb * BK, b);
         issued_ph[s] = ph;
         pending[s] = true;
         if (++s == STAGES) s = 0, ph ^= 1;
@@ -213,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       const uint32_t d = tbase + buf * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 103)) goto mma_done;
+        if (!tc::mbar_wait(INK ? &xfull[s] : &full[s], ph, abort_v, p.err, 103)) goto mma_done;
         tc::fence_after_sync();
         const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
         const uint32_t sb = SPLIT3 ? sa + 2 * A_BYTES : sa + A_BYTES;
@@ -241,6 +266,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (!tc::mbar_test(&drain, 0) && clock64() - t0 < tc::kWaitCycles) {
       }
     }
+  } else if (INK && (warp == 2 || warp == 3)) {
+    // ------------------------------------------------ 3xTF32 hi/lo split
+    // Elementwise and in place: hi keeps the raw tile's position (and so its
+    // swizzle), lo goes to the same position of the lo slot.
+    const int tid = threadIdx.x - 64;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < nunits && !*abort_v; u += gridDim.x) {
+      int t, kb0, kb1, slot;
+      decode_unit(u, p, t, kb0, kb1, slot);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 105)) goto split_done;
+        const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
+        split_hi_lo(sa, A_BYTES, tid);
+        split_hi_lo(sa + 2 * A_BYTES, B_BYTES, tid);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&xfull[s]);
+        if (++s == STAGES) s = 0, ph ^= 1;
+      }
+    }
+  split_done:;
   } else if (warp >= 4) {
     // --------------------------------------------------------- epilogue
     const int e = warp - 4;
@@ -401,7 +448,7 @@ bool tma_ok(const Operand &o, int batch) {
   return (a & 15) == 0 && o.ld > 0 && (o.ld & 3) == 0 && (batch == 1 || ((o.bs & 3) == 0 && o.bs > 0));
 }
 
-template <bool SPLIT3, int BN>
+template <bool SPLIT3, int BN, bool INK>
 int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Operand &Bl, GemmParams p,
                 int sm_count, cudaStream_t stream) {
   using C = Cfg<SPLIT3, BN>;
@@ -409,17 +456,17 @@ int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Ope
   CUtensorMap ma, mb, mal, mbl;
   REMORA_TRY(encode_operand(A, BM, p.batch, &ma));
   REMORA_TRY(encode_operand(B, BN, p.batch, &mb));
-  if (SPLIT3) {
+  if (SPLIT3 && !INK) {
     REMORA_TRY(encode_operand(Al, BM, p.batch, &mal));
     REMORA_TRY(encode_operand(Bl, BN, p.batch, &mbl));
   } else {
-    mal = ma;
+    mal = ma;  // TF32, or 3xTF32 split in shared memory: no lo operands
     mbl = mb;
   }
   static bool attr_set = false;
   if (!attr_set) {
-    REMORA_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<SPLIT3, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM));
+    REMORA_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<SPLIT3, BN, INK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
     attr_set = true;
   }
   const int ntiles = p.batch * p.mt * p.nt;
@@ -435,7 +482,7 @@ int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Ope
   const int nunits = ntiles * p.split;
   const int grid = std::min(nunits, sm_count);
   note_launch();
-  gemm_tf32_kernel<SPLIT3, BN><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
+  gemm_tf32_kernel<SPLIT3, BN, INK><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
   REMORA_CUDA_TRY(cudaGetLastError());
   if (p.split > 1) {
     const long long n = (long long)ntiles * BM * BN;
@@ -508,6 +555,12 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   Operand a, b;
   make(A, M, true, &a);
   make(B, N, false, &b);
+  // 3xTF32 split in the kernel for at most one tile per SM or a short K;
+  // otherwise by the prep pass (a plain staging copy is still made for views
+  // TMA cannot address)
+  const long long tiles_est = (long long)batch * ((M + BM - 1) / BM) * ((N + (N <= 64 ? 63 : 255)) / (N <= 64 ? 64 : 256));
+  const bool ink = split && (tiles_est <= ctx->sm_count || K <= 256);
+  const bool prep_split = split && !ink;
   char *ws = scratch;
   size_t used = 0;
   auto take = [&](size_t bytes) -> float * {
@@ -526,8 +579,8 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
     const long long si = op.mn ? s_rows : s_k, so = op.mn ? s_k : s_rows;
     const long long inner_pad = (inner + 3) & ~3LL;
     float *hi = take((size_t)batch * outer * inner_pad * 4);
-    float *lp = split ? take((size_t)batch * outer * inner_pad * 4) : nullptr;
-    if (!hi || (split && !lp)) return fail(REMORA_ERR_LIMIT, "gemm: workspace too small");
+    float *lp = prep_split ? take((size_t)batch * outer * inner_pad * 4) : nullptr;
+    if (!hi || (prep_split && !lp)) return fail(REMORA_ERR_LIMIT, "gemm: workspace too small");
     note_launch();
     prep_operand_kernel<<<grid_for((long long)batch * outer * inner_pad, ctx->sm_count), 256, 0, stream>>>(
         reinterpret_cast<const float *>(d.data(4)), rank == 3 ? d.strides[0] : 0, so, si, batch, outer, inner,
@@ -537,18 +590,16 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
     op.ld = inner_pad;
     op.bs = outer * inner_pad;
     if (op.mn) op.rows = inner; else op.K = K;
-    if (split) {
-      lo = op;
-      lo.base = lp;
-    }
+    lo = op;
+    if (prep_split) lo.base = lp;
     return REMORA_OK;
   };
   Operand al{}, bl{};
-  if (split || a.ld < 0 || !tma_ok(a, batch)) {
+  if (prep_split || a.ld < 0 || !tma_ok(a, batch)) {
     if (a.ld < 0) a.mn = 0;
     REMORA_TRY(stage(A, true, a, al));
   }
-  if (split || b.ld < 0 || !tma_ok(b, batch)) {
+  if (prep_split || b.ld < 0 || !tma_ok(b, batch)) {
     if (b.ld < 0) b.mn = 0;
     REMORA_TRY(stage(B, false, b, bl));
   }
@@ -568,11 +619,14 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   p.err = err;
   p.part = take(kSplitPartBytes);  // null when the workspace has no room: no split
   const bool narrow = N <= 64;
+  if (prep_split)
+    return narrow ? launch_gemm<true, 64, false>(a, b, al, bl, p, ctx->sm_count, stream)
+                  : launch_gemm<true, 256, false>(a, b, al, bl, p, ctx->sm_count, stream);
   if (split)
-    return narrow ? launch_gemm<true, 64>(a, b, al, bl, p, ctx->sm_count, stream)
-                  : launch_gemm<true, 256>(a, b, al, bl, p, ctx->sm_count, stream);
-  return narrow ? launch_gemm<false, 64>(a, b, a, b, p, ctx->sm_count, stream)
-                : launch_gemm<false, 256>(a, b, a, b, p, ctx->sm_count, stream);
+    return narrow ? launch_gemm<true, 64, true>(a, b, a, b, p, ctx->sm_count, stream)
+                  : launch_gemm<true, 256, true>(a, b, a, b, p, ctx->sm_count, stream);
+  return narrow ? launch_gemm<false, 64, false>(a, b, a, b, p, ctx->sm_count, stream)
+                : launch_gemm<false, 256, false>(a, b, a, b, p, ctx->sm_count, stream);
 }
 
 }  // namespace remora
