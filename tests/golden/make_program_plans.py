@@ -4,7 +4,8 @@ the reference's own acceptance programs (remora/tests/acceptance/pass/
 planned by remora_b200.program_plan, with the result the reference
 interpreter gives (remora/runtime.py:evaluate_source).  Where the acceptance
 manifest holds the expected stdout of the reference's compiled CPU path, the
-interpreter's value is checked against it here.  The tests replay the
+interpreter's value is checked against it here, and the text is recorded
+for the command-line tests.  The tests replay the
 recorded plans, so neither the reference nor its front end is needed to run
 them.  Regenerate with:
 
@@ -87,8 +88,11 @@ def main() -> None:
             if not np.array_equal(stated, want):
                 raise SystemExit(f"{name}: the reference value {want.tolist()} differs from the manifest's {text}")
         arrays[f"{name}__out"] = want
-        records.append({"name": name, "source": src.strip(), "syntax": syntax, "plan": plan.to_record(),
-                        "steps": [s["op"] for s in plan.steps]})
+        rec = {"name": name, "source": src.strip(), "syntax": syntax, "plan": plan.to_record(),
+               "steps": [s["op"] for s in plan.steps]}
+        if name in expected_stdout:
+            rec["stdout"] = expected_stdout[name]  # what the reference CLI prints for it
+        records.append(rec)
         print(f"{name:28s} {len(plan.steps)} steps {[s['op'] for s in plan.steps]}")
     for name, why in skipped:
         print(f"{name:28s} skipped ({why})")
