@@ -353,6 +353,10 @@ class _Planner:
             b = env[node.name][1]
             operands.append(b)
             return InputExpr(len(operands) - 1), self.code_of(b)
+        cell = self._cell_operand(node, env)
+        if cell is not None:
+            operands.append(cell)
+            return InputExpr(len(operands) - 1), self.code_of(cell)
         if k == "HIRIf":
             c, _ = self.expr(node.condition, env, operands)
             t, tc = self.expr(node.then_branch, env, operands)
@@ -483,21 +487,71 @@ class _Planner:
         return v[1], v[2]
 
     def lower_cell_map(self, node: object, env: dict, arrays: list[int], shape: tuple[int, ...]) -> tuple:
+        """``map f xs`` over cells of rank >= 1 whose result per cell is a
+        scalar: f's body is a fold of the cell, or an elementwise expression
+        of folds of the cell and of its elements at indices known at plan
+        time (``\\row -> row[0] + row[1]``).  The cell parameter stands for
+        the whole array; each use of it becomes a frame-shaped operand (a
+        cell-fold step, or a strided view), and the body one fused map."""
         names, body = self._func_parts(node.func, env)
-        if _kind(body) != "HIRFold" or len(arrays) != 1:
-            raise _unsupported("cell maps other than a fold of the cell")
+        if len(arrays) != 1:
+            raise _unsupported("cell maps of one array")
+        cell_rank = len(node.cell_shape)
+        frame = self.shape_of(arrays[0])[:len(self.shape_of(arrays[0])) - cell_rank]
+        if tuple(shape) != tuple(frame):
+            raise _unsupported("cell maps other than one scalar per cell")
+        inner = {**env, names[0]: ("cell", arrays[0], cell_rank)}
+        if _kind(body) == "HIRFold":
+            return ("buf", self.cell_fold(body, inner))
+        operands: list[int] = []
+        e, code = self.expr(body, inner, operands)
+        if not operands:
+            raise _unsupported("a cell map whose body does not use its cell")
+        return ("buf", self.emit_map(e, operands, tuple(frame), code))
+
+    def _cell_operand(self, node: object, env: dict) -> int | None:
+        """A frame-shaped buffer for a use of a cell parameter inside a cell
+        map's body (an index at plan-time positions, or a fold), else None."""
+        k = _kind(node)
+        arr = getattr(node, "array", None)
+        if k not in ("HIRIndex", "HIRFold") or _kind(arr) != "HIRVar" or env.get(arr.name, ("",))[0] != "cell":
+            return None
+        if k == "HIRFold":
+            return self.cell_fold(node, env)
+        _, b, cell_rank = env[arr.name]
+        shape = self.shape_of(b)
+        fr = len(shape) - cell_rank
+        if len(node.indices) != cell_rank or any(_kind(ix) == "HIRSlice" for ix in node.indices):
+            raise _unsupported("cell indices that pick one element of the cell")
+        _, _, st = self.strides_of(b)
+        off = 0
+        for d, ix in enumerate(node.indices):
+            v = self.const_of(ix, env)
+            if v is None:
+                raise _unsupported("cell indices known at plan time")
+            i = int(v[1])
+            if not 0 <= i < shape[fr + d]:
+                raise _unsupported(f"index {i} outside axis of {shape[fr + d]}")
+            off += i * st[fr + d]
+        return self.view(b, shape[:fr], off, st[:fr])
+
+    def cell_fold(self, body: object, env: dict) -> int:
+        """A fold of a cell parameter: one cell-fold step over the whole array."""
         op, init, code = self.fold_op(body, env)
-        if _kind(body.array) != "HIRVar" or body.array.name != names[0]:
+        cell = env.get(getattr(body.array, "name", None)) if _kind(body.array) == "HIRVar" else None
+        if cell is None or cell[0] != "cell":
             raise _unsupported("a cell fold folds its cell")
         if init[0] != "const" or op not in ("+", "*"):
             raise _unsupported("cell folds with + or * and a literal init")
-        in_code = self.code_of(arrays[0])
+        _, b, cell_rank = cell
+        in_code = self.code_of(b)
         premap = InputExpr(0) if in_code != code else None
-        sp = fold_spec(op=op, init=init[1], mode="cell", cell_rank=len(node.cell_shape), dtype=code, premap=premap,
+        sp = fold_spec(op=op, init=init[1], mode="cell", cell_rank=cell_rank, dtype=code, premap=premap,
                        premap_in_dtypes=[in_code] if premap is not None else None)
-        out = self.buf(shape, code)
-        self.plan.steps.append({"op": "fold", "spec": sp, "ins": arrays, "out": out})
-        return ("buf", out)
+        shape = self.shape_of(b)
+        out = self.buf(shape[:len(shape) - cell_rank], code)
+        self.plan.steps.append({"op": "fold", "spec": sp, "ins": [b], "out": out})
+        return out
 
     def fold_op(self, node: object, env: dict) -> tuple[str, Any, int]:
         """(op, init, accumulator code) of a fold with a + / * / && / || step."""

@@ -41,6 +41,12 @@ EXTRA = {
     "extra_grade": ("(grade < [3 1 4 1 5 9 2 6])", "lisp"),
     "extra_append": ("(append (iota 4) (map (lambda (x) (* x 10)) (iota 3)))", "lisp"),
     "extra_rotate": ("(rotate (map (lambda (x) (* x 2)) (iota 10)) 3)", "lisp"),
+    "extra_row_mean": ("let xs = reshape [6, 5] (map (* 0.5) (iota 30)) in map (\\row -> fold (+) 0.0 row / 5.0) xs",
+                       "ml"),
+    "extra_row_span": ("let xs = reshape [4, 6] (map (\\v -> v * v - 3 * v) (iota 24)) in\n"
+                       "map (\\row -> row[5] - row[0] + fold (+) 0 row) xs", "ml"),
+    "extra_cell_index2": ("let m = reshape [3, 2, 2] (map (* 1.5) (iota 12)) in map (\\c -> c[1, 0] * 2.0 - c[0, 1]) m",
+                          "ml"),
 }
 
 

@@ -91,9 +91,9 @@ def run_plan_on_oracle(orc, plan: Plan) -> np.ndarray:
 def test_fixture_covers_the_acceptance_programs():
     progs = programs()
     names = {p["name"] for p in progs}
-    # 43 of the reference's 45 acceptance programs (one uses indexing inside a
-    # cell map; one does not pass the reference's own front end) and 6 more
-    assert len(names) == 49
+    # 44 of the reference's 45 acceptance programs (one does not pass the
+    # reference's own front end) and 9 more
+    assert len(names) == 53
     ops = {op for p in progs for op in p["steps"]}
     assert ops == {"map", "fold", "array_fold", "scan", "append", "rotate", "sort", "grade"}
     for p in progs:
@@ -118,7 +118,8 @@ def test_planner_reproduces_recorded_plans():
 
 @pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
 @pytest.mark.parametrize("source", [
-    "let xs = [[1, 2], [3, 4]] in\nmap (\\row -> row[0] + row[1]) xs",  # an index inside a cell map
+    "let xs = [[1, 2], [3, 4]] in\nmap (\\row -> row[0 + 1 * 0] * row) xs",  # a whole cell in a scalar body
+    "let xs = [[1, 2], [3, 4]] in\nmap (\\row -> row[0:1]) xs",             # a cell slice
     "fold (\\acc x -> acc * x + 1) 1 (iota 5)",                            # a fold step other than acc op x
 ])
 def test_unsupported_programs_raise(source):
