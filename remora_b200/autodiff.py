@@ -22,6 +22,8 @@ from __future__ import annotations
 
 from typing import Any
 
+import numpy as np
+
 from remora_b200 import _lib as L
 from remora_b200.codegen import FoldSpec, KernelMeta, MapSpec, SpecModule, fold_spec
 from remora_b200.errors import RemoraUnsupportedError
@@ -139,9 +141,12 @@ def _apply(op: str, args: list[Expr]) -> Expr:
     return LogicExpr(op, *args)
 
 
-def _elementwise(node: object, env: dict[str, Expr]) -> Expr:
-    """An elementwise HIR expression over the parameters as an Expr."""
+def _elementwise(node: object, env: dict[str, Expr], on_fold=None) -> Expr:
+    """An elementwise HIR expression over the parameters as an Expr
+    (``on_fold`` turns a fold met on the way into an Expr, where allowed)."""
     k = _kind(node)
+    if k == "HIRFold" and on_fold is not None:
+        return on_fold(node, env)
     if k == "HIRVar":
         if node.name not in env:
             raise RemoraUnsupportedError(f"autodiff: free variable {node.name}")
@@ -151,22 +156,22 @@ def _elementwise(node: object, env: dict[str, Expr]) -> Expr:
     if k in ("HIRApply", "HIRMap"):
         if node.cell_shape:
             raise RemoraUnsupportedError("autodiff: maps over cells of rank >= 1")
-        args = [_elementwise(a, env) for a in node.arrays]
+        args = [_elementwise(a, env, on_fold) for a in node.arrays]
         f = node.func
         if _kind(f) == "HIRPrimCallable":
             if f.left_arg is not None:
-                args = [_elementwise(f.left_arg, env), *args]
+                args = [_elementwise(f.left_arg, env, on_fold), *args]
             if f.right_arg is not None:
-                args = [*args, _elementwise(f.right_arg, env)]
+                args = [*args, _elementwise(f.right_arg, env, on_fold)]
             return _apply(_base_op(f.op), args)
         if _kind(f) == "HIRLambda":
-            return _elementwise(f.body, {**env, **{p.name: a for p, a in zip(f.params, args)}})
+            return _elementwise(f.body, {**env, **{p.name: a for p, a in zip(f.params, args)}}, on_fold)
         raise RemoraUnsupportedError(f"autodiff: {_kind(f)} as a mapped function")
     if k == "HIRPrimOp":
-        return _apply(_base_op(node.op), [_elementwise(a, env) for a in node.args])
+        return _apply(_base_op(node.op), [_elementwise(a, env, on_fold) for a in node.args])
     if k == "HIRIf":
-        return SelectExpr(_elementwise(node.condition, env), _elementwise(node.then_branch, env),
-                          _elementwise(node.else_branch, env))
+        return SelectExpr(_elementwise(node.condition, env, on_fold), _elementwise(node.then_branch, env, on_fold),
+                          _elementwise(node.else_branch, env, on_fold))
     raise RemoraUnsupportedError(f"autodiff: {k} in a loss expression")
 
 
@@ -223,3 +228,227 @@ def compile_value_and_grad_source(source: str, function_name: str, param_types: 
     artifact = compile_function_source(source, function_name, param_types, verify=False,
                                        include_prelude=include_prelude, syntax=syntax)
     return value_and_grad_from_hir(artifact.hir_function, name or f"remora_{function_name}")
+
+
+# ------------------------------------------------- losses as device plans
+def _walk_inputs(e: Expr) -> set[int]:
+    return {x.index for x in _walk(e) if isinstance(x, InputExpr)}
+
+
+def _substitute(e: Expr, slot: dict[int, int]) -> Expr:
+    """``e`` with every ``InputExpr(i)`` renumbered to ``InputExpr(slot[i])``."""
+    if isinstance(e, InputExpr):
+        return InputExpr(slot[e.index])
+    if isinstance(e, ConstantExpr):
+        return e
+    if isinstance(e, UnaryExpr):
+        return UnaryExpr(e.op, _substitute(e.operand, slot))
+    if isinstance(e, SelectExpr):
+        return SelectExpr(_substitute(e.condition, slot), _substitute(e.then_expr, slot),
+                          _substitute(e.else_expr, slot))
+    return type(e)(e.op, _substitute(e.left, slot), _substitute(e.right, slot))
+
+
+def _type_of(node: object) -> object:
+    return getattr(node, "result_type", None) or getattr(node, "type", None)
+
+
+def _dims(t: object) -> tuple[int, ...]:
+    if _kind(t) == "ScalarType":
+        return ()
+    if _kind(t) != "ArrayType" or any(_kind(d) != "StaticDim" for d in t.shape):
+        raise RemoraUnsupportedError("autodiff: arrays of static shape")
+    return tuple(int(d.value) for d in t.shape)
+
+
+class _LossPlanner:
+    """Builds the plan of ``value_and_grad_plan_from_hir``.
+
+    Slots number the scalar values and arrays an expression may read:
+    0..P-1 are the parameters, then one slot per fold of the loss (its
+    value, a rank-0 buffer), then one per partial sum the scalar
+    parameters' gradients need.  Every Expr here is over slots; each map
+    or fold step renumbers the slots it reads to its own inputs."""
+
+    def __init__(self, params: list) -> None:
+        from remora_b200.program_plan import _Planner
+
+        self.pl = _Planner({})
+        self.shapes: dict[int, tuple[int, ...]] = {}  # slot -> shape
+        self.buf: dict[int, int] = {}  # slot -> plan buffer
+        for k, p in enumerate(params):
+            t = p.type
+            elem = t if _kind(t) == "ScalarType" else getattr(t, "element", None)
+            if _kind(elem) != "ScalarType" or elem.name != "float":
+                raise RemoraUnsupportedError("autodiff: parameters must be f32 scalars or arrays")
+            self.shapes[k] = _dims(t)
+            self.buf[k] = self.pl.buf(self.shapes[k], L.F32, input=k)
+        self.n_params = len(params)
+        self.env = {p.name: InputExpr(k) for k, p in enumerate(params)}
+        self.folds: list[tuple[float, Expr, tuple[int, ...]]] = []  # (init, summand, shape)
+
+    def new_slot(self, shape: tuple[int, ...], b: int) -> int:
+        k = max(self.buf) + 1
+        self.buf[k], self.shapes[k] = b, shape
+        return k
+
+    # ---- the loss: h(folds, scalar parameters)
+    def on_fold(self, node: object, env: dict) -> Expr:
+        f = node.func
+        if _kind(f) != "HIRPrimCallable" or _base_op(f.op) != "+" or f.left_arg is not None or \
+                f.right_arg is not None or _kind(node.init) != "HIRLit":
+            raise RemoraUnsupportedError("autodiff: folds of the loss are fold (+) <literal> <expression>")
+        e, shape, extra = self.summand(node.array, env)
+        self.folds.append((float(node.init.value) + extra, e, shape))
+        return InputExpr(-len(self.folds))  # renumbered once the folds are known
+
+    def summand(self, node: object, env: dict) -> tuple[Expr, tuple[int, ...], float]:
+        """(E, shape, c): the fold adds c and every element of E, an
+        elementwise expression over arrays of ``shape``.  A map over cells
+        whose body is itself ``fold (+) lit cell-expression`` (a sum over a
+        rank >= 2 array) flattens into its elements, each cell adding lit."""
+        if _kind(node) in ("HIRMap", "HIRApply") and node.cell_shape:
+            f = node.func
+            if _kind(f) != "HIRLambda" or _kind(f.body) != "HIRFold":
+                raise RemoraUnsupportedError("autodiff: cell maps in a loss fold their cells")
+            inner = f.body
+            g = inner.func
+            if _kind(g) != "HIRPrimCallable" or _base_op(g.op) != "+" or g.left_arg is not None or \
+                    g.right_arg is not None or _kind(inner.init) != "HIRLit":
+                raise RemoraUnsupportedError("autodiff: cell folds are fold (+) <literal> <expression>")
+            shapes = {_dims(_type_of(a)) for a in node.arrays}
+            if len(shapes) != 1:
+                raise RemoraUnsupportedError("autodiff: cell maps over arrays of one shape")
+            shape = next(iter(shapes))
+            args = [_elementwise(a, env) for a in node.arrays]
+            e, _, extra = self.summand(inner.array, {**env, **{p.name: a for p, a in zip(f.params, args)}})
+            cells = int(np.prod(shape[:len(shape) - len(node.cell_shape)], dtype=np.int64))
+            return e, shape, cells * (float(inner.init.value) + extra)
+        return _elementwise(node, env), _dims(_type_of(node)), 0.0
+
+    # ---- steps
+    def emit(self, e: Expr, shape: tuple[int, ...]) -> int:
+        """A map step computing ``e`` over ``shape`` (rank-0 operands splat)."""
+        used = sorted(_walk_inputs(e))
+        for i in used:
+            if self.shapes[i] not in ((), shape):
+                raise RemoraUnsupportedError("autodiff: an expression over arrays of different shapes")
+        operands = [self.buf[i] for i in used]
+        expr = _substitute(e, {i: j for j, i in enumerate(used)})
+        if not operands:
+            # a constant (a parameter the loss ignores has gradient 0): a
+            # rank-0 constant, or a map over a parameter of the shape that
+            # reads none of it
+            if shape == ():
+                return self.pl.buf((), L.F32, const=np.asarray(_constant(expr), dtype=np.float32))
+            operands = [next(self.buf[i] for i in range(self.n_params) if self.shapes[i] == shape)]
+        return self.pl.emit_map(expr, operands, shape, L.F32)
+
+    def fold_sum(self, e: Expr, shape: tuple[int, ...], init: float) -> int:
+        """A rank-0 buffer holding init + the sum of every element of e."""
+        used = sorted(_walk_inputs(e))
+        if not used:
+            raise RemoraUnsupportedError("autodiff: a fold of an expression of no parameter")
+        arrays = [i for i in used if self.shapes[i] == shape and shape != ()]
+        n = int(np.prod(shape, dtype=np.int64))
+        flat = lambda b: self.pl.view(b, (n,), 0, (1,))  # noqa: E731  (every operand here is contiguous)
+        if len(arrays) == len(used) and len(used) <= 2:
+            ins = [flat(self.buf[i]) for i in used]
+            premap = None if isinstance(e, InputExpr) else _substitute(e, {i: j for j, i in enumerate(used)})
+        else:
+            ins, premap = [flat(self.emit(e, shape))], None
+        sp = fold_spec(op="+", init=init, mode="all", dtype=L.F32, premap=premap, n_inputs=len(ins))
+        out = self.pl.buf((), L.F32)
+        self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": ins, "out": out})
+        return out
+
+
+def _constant(e: Expr) -> np.float32:
+    """The f32 value of an expression without inputs."""
+    f = np.float32
+    if isinstance(e, ConstantExpr):
+        return f(e.value)
+    if isinstance(e, UnaryExpr):
+        v = _constant(e.operand)
+        return {"neg": lambda: -v, "exp": lambda: f(np.exp(v)), "log": lambda: f(np.log(v))}[e.op]()
+    if isinstance(e, BinaryExpr):
+        a, b = _constant(e.left), _constant(e.right)
+        return {"+": lambda: f(a + b), "-": lambda: f(a - b), "*": lambda: f(a * b), "/": lambda: f(a / b)}[e.op]()
+    raise RemoraUnsupportedError(f"autodiff: a constant expression {e!r} as a result")
+
+
+def value_and_grad_plan_from_hir(function: object):
+    """One device plan for a loss and its gradient with respect to every
+    parameter, from the reference's HIR function.
+
+    The loss is any scalar expression h of f32 scalar parameters and of
+    sums ``S_i = fold (+) lit_i E_i``, where E_i is elementwise over
+    parameters (arrays of one shape, scalars broadcast); a sum over a rank
+    >= 2 array written as a map of cell folds counts as one sum.  The plan's
+    forward computes every S_i (one fold, fused with E_i where it reads at
+    most two arrays) and the loss h; its backward applies the VJP rules of
+    remora/ad.py:85-179 through the chain rule:
+
+        dL/dx = sum_i dh/dS_i * dE_i/dx                      (x an array: one map)
+        dL/dw = dh/dw + sum_i dh/dS_i * sum(dE_i/dw)         (w a scalar: folds, then a map)
+
+    The folds' adjoint broadcasts along the folded axis (remora/ad.py:
+    fold VJP) and a scalar's adjoint is the sum over the elements it was
+    broadcast to (the unbroadcast rule).  ``plan.results`` lists the loss,
+    then one gradient per parameter; run it with
+    ``program_plan.execute_plan_results``."""
+    lp = _LossPlanner(list(function.params))
+    if _dims(function.return_type) != ():
+        raise RemoraUnsupportedError("autodiff: the loss is a scalar")
+    h = _elementwise(function.body, lp.env, lp.on_fold)
+    if not lp.folds:
+        raise RemoraUnsupportedError("autodiff: the loss sums an array with fold (+)")
+    for i in _walk_inputs(h):
+        if i >= 0 and lp.shapes[i] != ():
+            raise RemoraUnsupportedError("autodiff: an array parameter outside the loss's folds")
+    # folds became InputExpr(-1), InputExpr(-2), ...: give them slots
+    fold_slot = {}
+    for i, (init, e, shape) in enumerate(lp.folds):
+        for j in _walk_inputs(e):
+            if lp.shapes[j] not in ((), shape):
+                raise RemoraUnsupportedError("autodiff: a fold over arrays of different shapes")
+        fold_slot[-(i + 1)] = lp.new_slot((), lp.fold_sum(e, shape, init))
+    h = _substitute(h, {**fold_slot, **{k: k for k in range(lp.n_params)}})
+    results = [lp.buf[next(iter(_walk_inputs(h)))] if isinstance(h, InputExpr) else lp.emit(h, ())]
+    adj = [derivative(h, fold_slot[-(i + 1)]) for i in range(len(lp.folds))]
+    for k in range(lp.n_params):
+        shape = lp.shapes[k]
+        if shape != ():
+            g: Expr = _ZERO
+            for i, (_, e, fshape) in enumerate(lp.folds):
+                if fshape == shape:
+                    g = _add(g, _mul(adj[i], derivative(e, k)))
+            results.append(lp.emit(g, shape))
+        else:
+            g = derivative(h, k)
+            for i, (_, e, fshape) in enumerate(lp.folds):
+                de = derivative(e, k)
+                if not _is(de, 0.0):
+                    g = _add(g, _mul(adj[i], InputExpr(lp.new_slot((), lp.fold_sum(de, fshape, 0.0)))))
+            results.append(lp.emit(g, ()))
+    lp.pl.plan.result = results[0]
+    lp.pl.plan.results = results
+    return lp.pl.plan
+
+
+def compile_value_and_grad_plan_source(source: str, function_name: str, param_types: tuple[Any, ...], *,
+                                       include_prelude: bool = False, syntax: str = "lisp"):
+    """The reference's front end followed by ``value_and_grad_plan_from_hir``."""
+    from remora.compiler import compile_function_source  # the reference's front end
+
+    artifact = compile_function_source(source, function_name, param_types, verify=False,
+                                       include_prelude=include_prelude, syntax=syntax)
+    return value_and_grad_plan_from_hir(artifact.hir_function)
+
+
+def execute_value_and_grad(plan, inputs: list[Any], device: int | None = None):
+    """(loss, [gradient per parameter]) of a value-and-grad plan on the device."""
+    from remora_b200.program_plan import execute_plan_results
+
+    out = execute_plan_results(plan, [np.asarray(a, dtype=np.float32) for a in inputs], device)
+    return float(out[0]), out[1:]

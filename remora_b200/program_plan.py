@@ -36,7 +36,7 @@ import numpy as np
 
 from remora_b200 import _lib as L
 from remora_b200.codegen import fold_spec, scan_spec
-from remora_b200.errors import RemoraUnsupportedError
+from remora_b200.errors import RemoraShapeError, RemoraUnsupportedError
 from remora_b200.program import (
     BinaryExpr,
     CmpExpr,
@@ -80,6 +80,8 @@ class Plan:
     buffers: list[Buffer] = field(default_factory=list)
     steps: list[dict] = field(default_factory=list)
     result: int = -1
+    # a plan with several results (a loss and its gradients) lists them all
+    results: list[int] = field(default_factory=list)
 
     def to_record(self) -> dict:
         bufs = []
@@ -99,7 +101,10 @@ class Plan:
                 if key in t:
                     t[key] = bytes(t[key]).hex()
             steps.append(t)
-        return {"buffers": bufs, "steps": steps, "result": self.result}
+        rec = {"buffers": bufs, "steps": steps, "result": self.result}
+        if self.results:
+            rec["results"] = list(self.results)
+        return rec
 
     @classmethod
     def from_record(cls, rec: dict) -> "Plan":
@@ -123,6 +128,7 @@ class Plan:
                 t["spec"] = cls_.from_buffer_copy(bytes.fromhex(t["spec"]))
             p.steps.append(t)
         p.result = int(rec["result"])
+        p.results = [int(r) for r in rec.get("results", [])]
         return p
 
 
@@ -635,12 +641,41 @@ def plan_from_hir(program: object) -> Plan:
 # -------------------------------------------------------------- execution
 def execute_plan(plan: Plan, inputs: list[np.ndarray] | None = None, device: int | None = None) -> np.ndarray:
     """Run a plan on the device and return its result as a numpy array."""
+    return _execute(plan, inputs, device, [plan.result])[0]
+
+
+def execute_plan_results(plan: Plan, inputs: list[np.ndarray] | None = None,
+                         device: int | None = None) -> list[np.ndarray]:
+    """Run a plan on the device and return every one of its results."""
+    return _execute(plan, inputs, device, plan.results or [plan.result])
+
+
+def _check_inputs(plan: Plan, inputs: list[np.ndarray] | None) -> list[np.ndarray]:
+    """The caller's inputs, converted to the plan's element types; their
+    count and shapes must be the plan's, since the device reads exactly the
+    planned extents."""
+    want = sorted({b.input for b in plan.buffers if b.input is not None})
+    inputs = list(inputs or [])
+    if want != list(range(len(inputs))):
+        raise RemoraShapeError(f"the plan takes {len(want)} inputs, got {len(inputs)}")
+    out = []
+    for k, a in enumerate(inputs):
+        b = next(b for b in plan.buffers if b.input == k)
+        arr = np.array(a, dtype=_NP[b.dtype], order="C")  # rank 0 stays rank 0
+        if arr.shape != tuple(b.shape):
+            raise RemoraShapeError(f"plan input {k} has shape {arr.shape}, the plan wants {tuple(b.shape)}")
+        out.append(arr)
+    return out
+
+
+def _execute(plan: Plan, inputs: list[np.ndarray] | None, device: int | None, results: list[int]) -> list[np.ndarray]:
     import torch
 
     from remora_b200.abi import make_memref_descriptor
     from remora_b200.runtime import context
 
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    inputs = _check_inputs(plan, inputs)
     ctx = context(dev.index)
     lib = L.lib()
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
@@ -651,7 +686,7 @@ def execute_plan(plan: Plan, inputs: list[np.ndarray] | None = None, device: int
         if b.const is not None:
             store[i] = torch.from_numpy(np.ascontiguousarray(b.const)).to(dev)
         elif b.input is not None:
-            store[i] = torch.from_numpy(np.ascontiguousarray(inputs[b.input], dtype=_NP[b.dtype])).to(dev)
+            store[i] = torch.from_numpy(inputs[b.input]).to(dev)
         else:
             store[i] = torch.empty(b.shape, dtype=getattr(torch, {L.F32: "float32", L.I32: "int32",
                                                                   L.BOOL: "bool"}[b.dtype]), device=dev)
@@ -708,8 +743,13 @@ def execute_plan(plan: Plan, inputs: list[np.ndarray] | None = None, device: int
             raise _unsupported(f"plan step {op}")
         L.check(st, f"plan step {op}")
     L.check(lib.remora_b200_synchronize(ctx.ptr, stream), "plan")
-    res = plan.buffers[plan.result]
-    return store[plan.result].cpu().numpy().astype(_NP[res.dtype]).reshape(res.shape)
+    out = []
+    for r in results:
+        res = plan.buffers[r]
+        if res.view is not None:
+            raise _unsupported("a plan result that is a view")
+        out.append(store[r].cpu().numpy().astype(_NP[res.dtype]).reshape(res.shape))
+    return out
 
 
 def compile_source_to_plan(source: str, *, include_prelude: bool = True, syntax: str = "ml") -> Plan:

@@ -2,7 +2,10 @@
 ``fold + lit (elementwise expression)`` compiled by the reference's front
 end and lowered by remora_b200.autodiff to a value fold and one gradient map
 per parameter; expected values and gradients from the reference's tape AD
-(remora/ad.py:trace_via_tape_multi).  The first three losses and their
+(remora/ad.py:trace_via_tape_multi).  Also tests/golden/
+value_and_grad_plans.{json,npz}: wider losses (scalar parameters, several
+folds, rank-2 and rank-3 arrays) as value-and-grad plans, with the
+interpreter's value and the tape's gradients.  The first three losses and their
 closed-form gradients are the reference's own GPU gradient tests
 (remora/tests/test_ad_source.py:569-605).  Regenerate with:
 
@@ -46,6 +49,74 @@ LOSSES = [
 ]
 
 
+# Losses for the value-and-grad plans (autodiff.value_and_grad_plan_from_hir):
+# scalar parameters, several folds, arrays of rank 2 and 3 summed by maps of
+# cell folds, scalars outside the folds.  (name, source, parameter shapes;
+# None = a Float scalar)
+def A(*dims: int) -> ArrayType:
+    return ArrayType(FLOAT, tuple(StaticDim(d) for d in dims))
+
+
+PLAN_LOSSES = [
+    ("linreg", "(define/pi () (loss [w Float b Float x (Array Float 256) y (Array Float 256)] Float) "
+               "(/ (fold + 0.0 (* (- (+ (* w x) b) y) (- (+ (* w x) b) y))) 256.0))", [None, None, (256,), (256,)]),
+    ("logistic", "(define/pi () (loss [w Float b Float x (Array Float 300) t (Array Float 300)] Float) "
+                 "(fold + 0.0 (log (+ 1.0 (exp (- 0.0 (* t (+ (* w x) b))))))))", [None, None, (300,), (300,)]),
+    ("frobenius", "(define/pi () (loss [m (Array Float 16 24)] Float) "
+                  "(fold + 0.0 (map (lambda (row) (fold + 0.0 (map (lambda (v) (* v v)) row))) m)))", [(16, 24)]),
+    ("rank3_cells", "(define/pi () (loss [m (Array Float 2 3 40)] Float) (fold + 0.0 (map (lambda (p) "
+                    "(fold + 0.0 (map (lambda (row) (fold + 0.0 (* row (exp row)))) p))) m)))", [(2, 3, 40)]),
+    ("scaled", "(define/pi () (loss [s Float x (Array Float 200)] Float) (* s (fold + 0.0 (* x x))))",
+     [None, (200,)]),
+    ("cell_inits", "(define/pi () (loss [m (Array Float 12 20)] Float) "
+                   "(fold + 1.5 (map (lambda (row) (fold + 0.25 (exp row))) m)))", [(12, 20)]),
+    ("two_shapes", "(define/pi () (loss [x (Array Float 64) y (Array Float 48)] Float) "
+                   "(+ (* 0.5 (fold + 0.0 (* x x))) (log (fold + 0.0 (exp y)))))", [(64,), (48,)]),
+    ("large", "(define/pi () (loss [m (Array Float 64 1024) c Float] Float) (/ (fold + 0.0 (map (lambda (row) "
+              "(fold + 0.0 (map (lambda (v) (* (- v c) (- v c))) row))) m)) 65536.0))", [(64, 1024), None]),
+    # log (1 + sum exp y): the fold's init enters the loss non-linearly
+    ("log_init", "(define/pi () (loss [y (Array Float 40)] Float) (log (fold + 1.0 (exp y))))", [(40,)]),
+]
+
+
+def closed_log_init(y: np.ndarray) -> np.ndarray:
+    """d/dy log(1 + sum exp y) = exp y / (1 + sum exp y)."""
+    e = np.exp(y.astype(np.float64))
+    return e / (1.0 + e.sum())
+
+
+def plan_losses(rng) -> None:
+    from remora_b200.autodiff import compile_value_and_grad_plan_source
+
+    records, arrays = [], {}
+    for name, src, shapes in PLAN_LOSSES:
+        ptypes = tuple(FLOAT if s is None else A(*s) for s in shapes)
+        plan = compile_value_and_grad_plan_source(src, "loss", ptypes)
+        args = [np.float32(rng.uniform(0.5, 1.0)) if s is None else rng.uniform(-1.0, 1.0, s).astype(np.float32)
+                for s in shapes]
+        if name == "logistic":
+            args[3] = np.where(rng.random(300) < 0.5, -1.0, 1.0).astype(np.float32)
+        sp = specialise(src, "loss", list(ptypes), FLOAT)
+        tape, idx = trace_via_tape_multi(sp.body, [np.asarray(a, np.float64) for a in args], [p[0] for p in sp.params])
+        adj = tape.reverse()
+        grads = [np.asarray(adj[i], dtype=np.float64).reshape(np.shape(a)) for i, a in zip(idx, args)]
+        if name == "log_init":
+            # remora/ad.py:_trace_fold records a fold's value without its
+            # init, so the tape's gradient here is exp y / sum exp y; the
+            # mathematics (and the interpreter's value) say 1 + sum exp y
+            arrays[f"{name}__tape_grad0"] = grads[0]
+            grads = [closed_log_init(args[0])]
+        arrays[f"{name}__value"] = np.asarray(_lambda_callable(sp, {})(*args), dtype=np.float64)
+        for k, a in enumerate(args):
+            arrays[f"{name}__in{k}"] = np.asarray(a, np.float32)
+            arrays[f"{name}__grad{k}"] = grads[k]
+        records.append({"name": name, "source": src, "shapes": [None if s is None else list(s) for s in shapes],
+                        "plan": plan.to_record(), "steps": [s["op"] for s in plan.steps]})
+        print(name, [s["op"] for s in plan.steps])
+    (HERE / "value_and_grad_plans.json").write_text(json.dumps(records, indent=1) + "\n")
+    np.savez(HERE / "value_and_grad_plans.npz", **arrays)
+
+
 def main() -> None:
     x = np.linspace(0.25, 2.0, N, dtype=np.float32)
     y = np.linspace(-1.0, 1.5, N, dtype=np.float32)
@@ -76,6 +147,7 @@ def main() -> None:
         arrays[f"{name}__closed"] = g.astype(np.float32)
     (HERE / "reference_gradients.json").write_text(json.dumps(records, indent=1) + "\n")
     np.savez(HERE / "reference_gradients.npz", **arrays)
+    plan_losses(np.random.default_rng(2718))
 
 
 if __name__ == "__main__":

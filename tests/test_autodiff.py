@@ -101,3 +101,128 @@ def test_recorded_specs_on_the_oracle(oracle_mod):
                     np.testing.assert_allclose(got, a[f"{rec['name']}__closed"], rtol=1e-5, atol=1e-6)
     assert {r["name"] for r in records()} >= {"polynomial", "cubic", "division"}
     assert L.F32 == 0
+
+
+# ------------------------------------------------- value-and-grad plans
+# tests/golden/value_and_grad_plans.{json,npz}: wider losses (scalar
+# parameters, several folds, rank-2 and rank-3 arrays summed by maps of cell
+# folds, scalars outside the folds) planned from the reference's front end,
+# with the reference interpreter's value and the tape's gradients.
+# Tolerances: elementwise gradients rtol 1e-5 + atol 1e-6·max|ref|; sums
+# (the value and the gradients of scalar parameters) rtol 1e-4, since an f32
+# fold of up to 65,536 terms, added in sequence as the reference's compiled
+# path adds them, is 1.5e-5 from the f64 tape.
+def plan_records():
+    return json.loads((GOLDEN / "value_and_grad_plans.json").read_text())
+
+
+def plan_arrays():
+    with np.load(GOLDEN / "value_and_grad_plans.npz") as f:
+        return {k: f[k] for k in f.files}
+
+
+def check_value_and_grads(rec, got: list[np.ndarray]) -> None:
+    a = plan_arrays()
+    n = rec["name"]
+    assert float(got[0]) == pytest.approx(float(a[f"{n}__value"]), rel=1e-4)
+    for k, shape in enumerate(rec["shapes"]):
+        g, want = np.asarray(got[k + 1], np.float64), a[f"{n}__grad{k}"]
+        assert g.shape == want.shape
+        if shape is None:
+            assert float(g) == pytest.approx(float(want), rel=1e-4, abs=1e-6)
+        else:
+            np.testing.assert_allclose(g, want, rtol=1e-5, atol=1e-6 * float(np.abs(want).max()))
+
+
+@pytest.mark.parametrize("rec", plan_records(), ids=lambda r: r["name"])
+def test_value_and_grad_plan_on_the_oracle(oracle_mod, rec):
+    from remora_b200.program_plan import Plan
+    from test_program_plan import run_plan_on_oracle
+
+    a = plan_arrays()
+    ins = [a[f"{rec['name']}__in{k}"] for k in range(len(rec["shapes"]))]
+    plan = Plan.from_record(rec["plan"])
+    assert plan.to_record() == rec["plan"]
+    check_value_and_grads(rec, run_plan_on_oracle(oracle_mod, plan, ins, all_results=True))
+
+
+def test_the_fixture_covers_scalars_ranks_and_several_folds():
+    recs = {r["name"]: r for r in plan_records()}
+    assert any(None in r["shapes"] for r in recs.values())
+    assert {len(s) for r in recs.values() for s in r["shapes"] if s} == {1, 2, 3}
+    assert recs["two_shapes"]["steps"].count("fold") == 2
+
+
+def test_the_reference_tape_drops_a_fold_init():
+    """remora/ad.py:_trace_fold records sum(arr) as a fold's value, without
+    its init: for log (fold + 1.0 (exp y)) its gradient is exp y / sum exp y
+    where the mathematics give exp y / (1 + sum exp y).  The plan follows the
+    mathematics (the fixture's expected gradient is the closed form)."""
+    a = plan_arrays()
+    y = a["log_init__in0"].astype(np.float64)
+    e = np.exp(y)
+    np.testing.assert_allclose(a["log_init__tape_grad0"], e / e.sum(), rtol=1e-12)
+    np.testing.assert_allclose(a["log_init__grad0"], e / (1.0 + e.sum()), rtol=1e-12)
+
+
+@pytest.mark.skipif(not __import__("os").path.isdir(__import__("os").environ.get(
+    "REMORA_REFERENCE", "/root/reference") + "/remora"), reason="the reference front end is not importable here")
+def test_planner_reproduces_recorded_value_and_grad_plans():
+    import os
+    import sys
+
+    sys.path.insert(0, os.environ.get("REMORA_REFERENCE", "/root/reference"))
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.autodiff import compile_value_and_grad_plan_source
+
+    for rec in plan_records():
+        ptypes = tuple(FLOAT if s is None else ArrayType(FLOAT, tuple(StaticDim(d) for d in s))
+                       for s in rec["shapes"])
+        assert compile_value_and_grad_plan_source(rec["source"], "loss", ptypes).to_record() == rec["plan"]
+
+
+@pytest.mark.skipif(not __import__("os").path.isdir(__import__("os").environ.get(
+    "REMORA_REFERENCE", "/root/reference") + "/remora"), reason="the reference front end is not importable here")
+@pytest.mark.parametrize("src, shapes", [
+    # an array parameter outside the folds
+    ("(define/pi () (loss [x (Array Float 4)] Float) (+ (fold + 0.0 x) (index x 0)))", [(4,)]),
+    # a product fold
+    ("(define/pi () (loss [x (Array Float 4)] Float) (fold * 1.0 x))", [(4,)]),
+    # int parameters
+    ("(define/pi () (loss [x (Array Int 4)] Int) (fold + 0 x))", ["int"]),
+    # no fold at all
+    ("(define/pi () (loss [w Float] Float) (* w w))", [None]),
+])
+def test_unsupported_losses_raise(src, shapes):
+    import os
+    import sys
+
+    sys.path.insert(0, os.environ.get("REMORA_REFERENCE", "/root/reference"))
+    from remora.types import FLOAT, INT, ArrayType, StaticDim
+
+    from remora_b200.autodiff import compile_value_and_grad_plan_source
+
+    ptypes = tuple(FLOAT if s is None else ArrayType(INT, (StaticDim(4),)) if s == "int"
+                   else ArrayType(FLOAT, tuple(StaticDim(d) for d in s)) for s in shapes)
+    try:
+        compile_value_and_grad_plan_source(src, "loss", ptypes)
+    except RemoraUnsupportedError:
+        return
+    except Exception as exc:  # the reference's own front end rejected it first
+        pytest.skip(f"front end: {type(exc).__name__}")
+    raise AssertionError("expected RemoraUnsupportedError")
+
+
+def test_plan_inputs_are_checked_against_the_plan():
+    from remora_b200.errors import RemoraShapeError
+    from remora_b200.program_plan import Plan, _check_inputs
+
+    rec = next(r for r in plan_records() if r["name"] == "linreg")
+    plan = Plan.from_record(rec["plan"])
+    good = [np.float32(1.0), np.float32(0.0), np.zeros(256, np.float32), np.zeros(256, np.float32)]
+    assert [a.shape for a in _check_inputs(plan, good)] == [(), (), (256,), (256,)]
+    with pytest.raises(RemoraShapeError):
+        _check_inputs(plan, good[:3])
+    with pytest.raises(RemoraShapeError):
+        _check_inputs(plan, [*good[:3], np.zeros(255, np.float32)])

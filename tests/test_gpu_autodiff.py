@@ -37,3 +37,18 @@ def test_value_and_grad_on_device(cuda, rec):
             np.testing.assert_allclose(got, a[f"{rec['name']}__grad{k}"], rtol=1e-5, atol=1e-6)
             if k == 0 and f"{rec['name']}__closed" in a:
                 np.testing.assert_allclose(got, a[f"{rec['name']}__closed"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("rec", __import__("test_autodiff").plan_records(), ids=lambda r: r["name"])
+def test_value_and_grad_plan_on_device(cuda, rec):
+    """The wider losses as one device plan each (forward folds, backward maps
+    and folds, one stream, one synchronisation), at the tolerances the CPU
+    test of the same plans states."""
+    from remora_b200.autodiff import execute_value_and_grad
+    from remora_b200.program_plan import Plan
+    from test_autodiff import check_value_and_grads, plan_arrays
+
+    a = plan_arrays()
+    ins = [a[f"{rec['name']}__in{k}"] for k in range(len(rec["shapes"]))]
+    loss, grads = execute_value_and_grad(Plan.from_record(rec["plan"]), ins)
+    check_value_and_grads(rec, [np.float32(loss), *grads])

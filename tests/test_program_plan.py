@@ -43,9 +43,13 @@ def close(got: np.ndarray, want: np.ndarray) -> None:
         np.testing.assert_array_equal(got, want)
 
 
-def run_plan_on_oracle(orc, plan: Plan) -> np.ndarray:
-    """The plan's steps, each on the oracle, over numpy buffers."""
+def run_plan_on_oracle(orc, plan: Plan, inputs: list[np.ndarray] | None = None, *, all_results: bool = False):
+    """The plan's steps, each on the oracle, over numpy buffers: its result,
+    or with ``all_results`` the list of ``plan.results``."""
     store: dict[int, np.ndarray] = {}
+    for i, b in enumerate(plan.buffers):
+        if b.input is not None:
+            store[i] = np.ascontiguousarray(inputs[b.input], dtype=_NP[b.dtype]).reshape(b.shape)
 
     def get(i: int) -> np.ndarray:
         b = plan.buffers[i]
@@ -84,8 +88,13 @@ def run_plan_on_oracle(orc, plan: Plan) -> np.ndarray:
             store[s["out"]] = orc.grade(get(s["in"]))
         else:
             raise AssertionError(op)
-    res = plan.buffers[plan.result]
-    return np.asarray(get(plan.result)).astype(_NP[res.dtype]).reshape(res.shape)
+    def result(r: int) -> np.ndarray:
+        res = plan.buffers[r]
+        return np.asarray(get(r)).astype(_NP[res.dtype]).reshape(res.shape)
+
+    if all_results:
+        return [result(r) for r in (plan.results or [plan.result])]
+    return result(plan.result)
 
 
 def test_fixture_covers_the_acceptance_programs():
