@@ -639,15 +639,18 @@ def plan_from_hir(program: object) -> Plan:
 
 
 # -------------------------------------------------------------- execution
+_TORCH = {L.F32: "float32", L.I32: "int32", L.BOOL: "bool"}
+
+
 def execute_plan(plan: Plan, inputs: list[np.ndarray] | None = None, device: int | None = None) -> np.ndarray:
     """Run a plan on the device and return its result as a numpy array."""
-    return _execute(plan, inputs, device, [plan.result])[0]
+    return PlanRunner(plan, device, results=[plan.result]).run(inputs)[0]
 
 
 def execute_plan_results(plan: Plan, inputs: list[np.ndarray] | None = None,
                          device: int | None = None) -> list[np.ndarray]:
     """Run a plan on the device and return every one of its results."""
-    return _execute(plan, inputs, device, plan.results or [plan.result])
+    return PlanRunner(plan, device).run(inputs)
 
 
 def _check_inputs(plan: Plan, inputs: list[np.ndarray] | None) -> list[np.ndarray]:
@@ -668,88 +671,149 @@ def _check_inputs(plan: Plan, inputs: list[np.ndarray] | None) -> list[np.ndarra
     return out
 
 
-def _execute(plan: Plan, inputs: list[np.ndarray] | None, device: int | None, results: list[int]) -> list[np.ndarray]:
-    import torch
+class PlanRunner:
+    """A plan bound to device memory, for one run or many.
 
-    from remora_b200.abi import make_memref_descriptor
-    from remora_b200.runtime import context
+    Construction allocates every buffer of the plan on the device, uploads
+    its constants, builds each step's descriptors and arguments once, and
+    makes a stream of its own.  ``run(inputs)`` copies the inputs into the
+    plan's input buffers through pinned host memory, enqueues every step on
+    that stream, copies the results back, and synchronises once, reading the
+    library's device error flags (remora_b200_synchronize).  With
+    ``graph=True`` the first run, eager, also sizes the stream's workspace
+    and compiles the kernels; the steps are then recorded as one CUDA graph,
+    and later runs replay it: one launch instead of one library call per
+    step, for plans run many times (a training loop's value and gradient)."""
 
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
-    inputs = _check_inputs(plan, inputs)
-    ctx = context(dev.index)
-    lib = L.lib()
-    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    store: dict[int, Any] = {}
-    for i, b in enumerate(plan.buffers):
-        if b.view is not None:
-            continue
-        if b.const is not None:
-            store[i] = torch.from_numpy(np.ascontiguousarray(b.const)).to(dev)
-        elif b.input is not None:
-            store[i] = torch.from_numpy(inputs[b.input]).to(dev)
-        else:
-            store[i] = torch.empty(b.shape, dtype=getattr(torch, {L.F32: "float32", L.I32: "int32",
-                                                                  L.BOOL: "bool"}[b.dtype]), device=dev)
-    keep: list = []
+    def __init__(self, plan: Plan, device: int | None = None, *, graph: bool = False,
+                 results: list[int] | None = None) -> None:
+        import torch
 
-    def desc(i: int):
-        b = plan.buffers[i]
-        if b.view is not None:
-            base, off, st = b.view
-            t = store[base]
-            d = make_memref_descriptor(t.data_ptr(), b.shape, st, None, off)
-        else:
-            t = store[i]
-            st, acc = [], 1
-            for s in reversed(b.shape):
-                st.append(acc)
-                acc *= s
-            d = make_memref_descriptor(t.data_ptr(), b.shape, tuple(reversed(st)), None, 0)
-        keep.append(d)
-        return ctypes.addressof(d)
+        from remora_b200.abi import make_memref_descriptor
+        from remora_b200.runtime import context
 
-    for s in plan.steps:
-        op = s["op"]
-        if op == "map":
-            ins = s["ins"]
-            ptrs = (ctypes.c_void_p * len(ins))(*[desc(i) for i in ins])
-            ranks = (ctypes.c_int32 * len(ins))(*[len(plan.buffers[i].shape) for i in ins])
-            st = lib.remora_b200_map(ctx.ptr, ctypes.byref(s["program"]), ptrs, ranks, len(ins), desc(s["out"]),
-                                     len(plan.buffers[s["out"]].shape), stream)
-        elif op == "fold":
-            ins = s["ins"]
-            ptrs = (ctypes.c_void_p * len(ins))(*[desc(i) for i in ins])
-            ranks = (ctypes.c_int32 * len(ins))(*[len(plan.buffers[i].shape) for i in ins])
-            st = lib.remora_b200_fold(ctx.ptr, ctypes.byref(s["spec"]), ptrs, ranks, len(ins), desc(s["out"]),
-                                      len(plan.buffers[s["out"]].shape), stream)
-        elif op == "array_fold":
-            st = lib.remora_b200_array_fold(ctx.ptr, ctypes.byref(s["spec"]), desc(s["in"]),
-                                            len(plan.buffers[s["in"]].shape), desc(s["init"]), desc(s["out"]),
-                                            stream)
-        elif op == "scan":
-            st = lib.remora_b200_scan(ctx.ptr, ctypes.byref(s["spec"]), desc(s["in"]), desc(s["out"]),
-                                      len(plan.buffers[s["in"]].shape), stream)
-        elif op == "append":
-            st = lib.remora_b200_append(ctx.ptr, plan.buffers[s["a"]].dtype, desc(s["a"]), desc(s["b"]),
-                                        desc(s["out"]), len(plan.buffers[s["out"]].shape), stream)
-        elif op == "rotate":
-            st = lib.remora_b200_rotate(ctx.ptr, plan.buffers[s["in"]].dtype, int(s["shift"]), desc(s["in"]),
-                                        desc(s["out"]), len(plan.buffers[s["in"]].shape), stream)
-        elif op in ("sort", "grade"):
-            fn = lib.remora_b200_grade if op == "grade" else lib.remora_b200_sort
-            st = fn(ctx.ptr, plan.buffers[s["in"]].dtype, desc(s["in"]), desc(s["out"]),
-                    len(plan.buffers[s["in"]].shape), stream)
-        else:
-            raise _unsupported(f"plan step {op}")
-        L.check(st, f"plan step {op}")
-    L.check(lib.remora_b200_synchronize(ctx.ptr, stream), "plan")
-    out = []
-    for r in results:
-        res = plan.buffers[r]
-        if res.view is not None:
-            raise _unsupported("a plan result that is a view")
-        out.append(store[r].cpu().numpy().astype(_NP[res.dtype]).reshape(res.shape))
-    return out
+        self.torch, self.plan, self.graph_wanted, self.graph = torch, plan, graph, None
+        self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.ctx = context(self.dev.index)
+        self.lib = L.lib()
+        self.stream = torch.cuda.Stream(self.dev)
+        self._s = ctypes.c_void_p(self.stream.cuda_stream)
+        self.results = list(results or plan.results or [plan.result])
+        for r in self.results:
+            if plan.buffers[r].view is not None:
+                raise _unsupported("a plan result that is a view")
+        self.launches_per_run: int | None = None
+        self.store: dict[int, Any] = {}
+        self.host_in: dict[int, Any] = {}
+        self.host_out: dict[int, Any] = {}
+        with torch.cuda.stream(self.stream):
+            for i, b in enumerate(plan.buffers):
+                if b.view is not None:
+                    continue
+                dt = getattr(torch, _TORCH[b.dtype])
+                if b.const is not None:
+                    host = torch.from_numpy(np.array(b.const, dtype=_NP[b.dtype], order="C").reshape(b.shape))
+                    self.store[i] = host.to(self.dev)
+                else:
+                    self.store[i] = torch.empty(b.shape, dtype=dt, device=self.dev)
+                if b.input is not None:
+                    self.host_in[i] = torch.empty(b.shape, dtype=dt, pin_memory=True)
+        for r in self.results:
+            b = plan.buffers[r]
+            self.host_out.setdefault(r, torch.empty(b.shape, dtype=getattr(torch, _TORCH[b.dtype]), pin_memory=True))
+        self._keep: list = []
+
+        def desc(i: int) -> int:
+            b = plan.buffers[i]
+            if b.view is not None:
+                base, off, st = b.view
+                d = make_memref_descriptor(self.store[base].data_ptr(), b.shape, st, None, off)
+            else:
+                st, acc = [], 1
+                for n in reversed(b.shape):
+                    st.append(acc)
+                    acc *= n
+                d = make_memref_descriptor(self.store[i].data_ptr(), b.shape, tuple(reversed(st)), None, 0)
+            self._keep.append(d)
+            return ctypes.addressof(d)
+
+        def rank(i: int) -> int:
+            return len(plan.buffers[i].shape)
+
+        def descs(ids: list[int]) -> tuple:
+            ptrs = (ctypes.c_void_p * len(ids))(*[desc(i) for i in ids])
+            ranks = (ctypes.c_int32 * len(ids))(*[rank(i) for i in ids])
+            self._keep += [ptrs, ranks]
+            return ptrs, ranks
+
+        lib, ctx, s = self.lib, self.ctx.ptr, self._s
+        self.calls: list[tuple[str, Any, tuple]] = []
+        for st in plan.steps:
+            op = st["op"]
+            if op == "map":
+                ptrs, ranks = descs(st["ins"])
+                self._keep.append(st["program"])
+                call = (lib.remora_b200_map, (ctx, ctypes.byref(st["program"]), ptrs, ranks, len(st["ins"]),
+                                              desc(st["out"]), rank(st["out"]), s))
+            elif op == "fold":
+                ptrs, ranks = descs(st["ins"])
+                call = (lib.remora_b200_fold, (ctx, ctypes.byref(st["spec"]), ptrs, ranks, len(st["ins"]),
+                                               desc(st["out"]), rank(st["out"]), s))
+            elif op == "array_fold":
+                call = (lib.remora_b200_array_fold, (ctx, ctypes.byref(st["spec"]), desc(st["in"]), rank(st["in"]),
+                                                     desc(st["init"]), desc(st["out"]), s))
+            elif op == "scan":
+                call = (lib.remora_b200_scan, (ctx, ctypes.byref(st["spec"]), desc(st["in"]), desc(st["out"]),
+                                               rank(st["in"]), s))
+            elif op == "append":
+                call = (lib.remora_b200_append, (ctx, plan.buffers[st["a"]].dtype, desc(st["a"]), desc(st["b"]),
+                                                 desc(st["out"]), rank(st["out"]), s))
+            elif op == "rotate":
+                call = (lib.remora_b200_rotate, (ctx, plan.buffers[st["in"]].dtype, int(st["shift"]), desc(st["in"]),
+                                                 desc(st["out"]), rank(st["in"]), s))
+            elif op in ("sort", "grade"):
+                fn = lib.remora_b200_grade if op == "grade" else lib.remora_b200_sort
+                call = (fn, (ctx, plan.buffers[st["in"]].dtype, desc(st["in"]), desc(st["out"]), rank(st["in"]), s))
+            else:
+                raise _unsupported(f"plan step {op}")
+            self.calls.append((op, *call))
+
+    def _enqueue(self) -> None:
+        for op, fn, args in self.calls:
+            L.check(fn(*args), f"plan step {op}")
+
+    def run(self, inputs: list[np.ndarray] | None = None) -> list[np.ndarray]:
+        """Copy the inputs in, run every step, and return the results."""
+        torch = self.torch
+        inputs = _check_inputs(self.plan, inputs)
+        with torch.cuda.stream(self.stream):
+            for i, host in self.host_in.items():
+                host.numpy()[...] = inputs[self.plan.buffers[i].input]
+                self.store[i].copy_(host, non_blocking=True)
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                n0 = L.launch_count()
+                self._enqueue()
+                self.launches_per_run = L.launch_count() - n0
+            for r, host in self.host_out.items():
+                host.copy_(self.store[r], non_blocking=True)
+        L.check(self.lib.remora_b200_synchronize(self.ctx.ptr, self._s), "plan")
+        out = [self.host_out[r].numpy().copy() for r in self.results]
+        if self.graph_wanted and self.graph is None:
+            self._capture()
+        return out
+
+    def _capture(self) -> None:
+        """Record the steps as a CUDA graph on the runner's stream (after an
+        eager run: kernels compiled, the stream's workspace sized)."""
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        n0 = L.launch_count()
+        with torch.cuda.graph(g, stream=self.stream):
+            self._enqueue()
+        self.launches_per_run = L.launch_count() - n0
+        self.graph = g
 
 
 def compile_source_to_plan(source: str, *, include_prelude: bool = True, syntax: str = "ml") -> Plan:

@@ -52,3 +52,34 @@ def test_value_and_grad_plan_on_device(cuda, rec):
     ins = [a[f"{rec['name']}__in{k}"] for k in range(len(rec["shapes"]))]
     loss, grads = execute_value_and_grad(Plan.from_record(rec["plan"]), ins)
     check_value_and_grads(rec, [np.float32(loss), *grads])
+
+
+@pytest.mark.parametrize("rec", __import__("test_autodiff").plan_records(), ids=lambda r: r["name"])
+def test_value_and_grad_plan_replayed_on_new_inputs(cuda, oracle_mod, rec):
+    """A training loop's use: one PlanRunner with a CUDA graph, run on the
+    fixture's inputs and then on new ones; each replay equals a fresh eager
+    run bit for bit, and the oracle run of the same plan on the new inputs
+    within the tolerances above."""
+    from remora_b200.program_plan import Plan, PlanRunner, execute_plan_results
+    from test_autodiff import plan_arrays
+    from test_program_plan import run_plan_on_oracle
+
+    a = plan_arrays()
+    plan = Plan.from_record(rec["plan"])
+    ins = [a[f"{rec['name']}__in{k}"] for k in range(len(rec["shapes"]))]
+    runner = PlanRunner(plan, graph=True)
+    runner.run(ins)
+    rng = np.random.default_rng(11)
+    for step in range(3):
+        new = [np.asarray(x * np.float32(1.0 + 0.1 * (step + 1)) + np.float32(0.01) * rng.standard_normal(
+            np.shape(x)).astype(np.float32), dtype=np.float32) for x in ins]
+        got = runner.run(new)
+        for g, e in zip(got, execute_plan_results(plan, new)):
+            np.testing.assert_array_equal(g, e)
+        want = run_plan_on_oracle(oracle_mod, plan, new, all_results=True)
+        assert float(got[0]) == pytest.approx(float(want[0]), rel=1e-4)
+        for g, w in zip(got[1:], want[1:]):
+            if g.ndim == 0:
+                assert float(g) == pytest.approx(float(w), rel=1e-4, abs=1e-6)
+            else:
+                np.testing.assert_allclose(g, w, rtol=1e-5, atol=1e-6 * float(np.abs(w).max()))

@@ -6,6 +6,7 @@ per program, and must give the reference's result."""
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 
 from remora_b200.program_plan import Plan, execute_plan
@@ -17,3 +18,22 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("rec", programs(), ids=lambda r: r["name"])
 def test_program_on_device(cuda, rec):
     close(execute_plan(Plan.from_record(rec["plan"])), expected(rec["name"]))
+
+
+@pytest.mark.parametrize("rec", programs()[::4], ids=lambda r: r["name"])
+def test_plan_runner_graph_replays_match_the_eager_run(cuda, rec):
+    """A PlanRunner with graph=True runs eagerly once, records the steps as a
+    CUDA graph, and replays it: every replay gives the eager result bit for
+    bit (the kernels are deterministic) and the reference's value."""
+    from remora_b200.program_plan import PlanRunner
+
+    plan = Plan.from_record(rec["plan"])
+    eager = execute_plan(plan)
+    runner = PlanRunner(plan, graph=True)
+    first = runner.run()[0]
+    assert runner.graph is not None and runner.launches_per_run >= len(plan.steps)
+    for _ in range(3):
+        again = runner.run()[0]
+        np.testing.assert_array_equal(again, eager)
+    np.testing.assert_array_equal(first, eager)
+    close(again, expected(rec["name"]))
