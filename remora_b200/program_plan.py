@@ -676,13 +676,15 @@ class PlanRunner:
 
     Construction allocates every buffer of the plan on the device, uploads
     its constants, builds each step's descriptors and arguments once, and
-    makes a stream of its own.  ``run(inputs)`` copies the inputs into the
-    plan's input buffers through pinned host memory, enqueues every step on
-    that stream, copies the results back, and synchronises once, reading the
-    library's device error flags (remora_b200_synchronize).  With
-    ``graph=True`` the first run, eager, also sizes the stream's workspace
-    and compiles the kernels; the steps are then recorded as one CUDA graph,
-    and later runs replay it: one launch instead of one library call per
+    makes a stream of its own.  The plan's inputs share one device arena
+    and its results another, each staged through one pinned host buffer.
+    ``run(inputs)`` writes the inputs into the staging buffer, then on that
+    stream copies them in (one copy), enqueues every step, copies the
+    results out (one copy), and synchronises once, reading the library's
+    device error flags (remora_b200_synchronize).  With ``graph=True`` the
+    first run, eager, also sizes the stream's workspace and compiles the
+    kernels; the copies and steps are then recorded as one CUDA graph, and
+    later runs replay it: one launch per run instead of one library call per
     step, for plans run many times (a training loop's value and gradient)."""
 
     def __init__(self, plan: Plan, device: int | None = None, *, graph: bool = False,
@@ -704,23 +706,22 @@ class PlanRunner:
                 raise _unsupported("a plan result that is a view")
         self.launches_per_run: int | None = None
         self.store: dict[int, Any] = {}
-        self.host_in: dict[int, Any] = {}
-        self.host_out: dict[int, Any] = {}
+        # Inputs and results live in one device arena each, staged through
+        # one pinned host buffer each: a run copies once in and once out.
+        ins = [i for i, b in enumerate(plan.buffers) if b.input is not None and b.view is None]
+        outs = list(dict.fromkeys(r for r in self.results if plan.buffers[r].input is None
+                                  and plan.buffers[r].const is None))
+        self._in_arena, self._in_host, self._in_np = self._arena(ins)
+        self._out_arena, self._out_host, self._out_np = self._arena(outs)
         with torch.cuda.stream(self.stream):
             for i, b in enumerate(plan.buffers):
-                if b.view is not None:
+                if b.view is not None or i in self.store:
                     continue
-                dt = getattr(torch, _TORCH[b.dtype])
                 if b.const is not None:
                     host = torch.from_numpy(np.array(b.const, dtype=_NP[b.dtype], order="C").reshape(b.shape))
                     self.store[i] = host.to(self.dev)
                 else:
-                    self.store[i] = torch.empty(b.shape, dtype=dt, device=self.dev)
-                if b.input is not None:
-                    self.host_in[i] = torch.empty(b.shape, dtype=dt, pin_memory=True)
-        for r in self.results:
-            b = plan.buffers[r]
-            self.host_out.setdefault(r, torch.empty(b.shape, dtype=getattr(torch, _TORCH[b.dtype]), pin_memory=True))
+                    self.store[i] = torch.empty(b.shape, dtype=getattr(torch, _TORCH[b.dtype]), device=self.dev)
         self._keep: list = []
 
         def desc(i: int) -> int:
@@ -778,35 +779,69 @@ class PlanRunner:
                 raise _unsupported(f"plan step {op}")
             self.calls.append((op, *call))
 
+    def _arena(self, ids: list[int]) -> tuple[Any, Any, dict[int, np.ndarray]]:
+        """One device arena and one pinned host buffer holding the buffers
+        ``ids`` at 256-byte aligned offsets; the device slices become the
+        buffers' storage, the host slices their numpy staging views."""
+        torch = self.torch
+        offs, total = {}, 0
+        for i in ids:
+            b = self.plan.buffers[i]
+            offs[i] = total
+            total += (int(np.prod(b.shape, dtype=np.int64)) * np.dtype(_NP[b.dtype]).itemsize + 255) & ~255
+        dev = torch.empty(max(total, 256), dtype=torch.uint8, device=self.dev)
+        host = torch.empty(max(total, 256), dtype=torch.uint8, pin_memory=True)
+        views = {}
+        for i in ids:
+            b = self.plan.buffers[i]
+            n = int(np.prod(b.shape, dtype=np.int64)) * np.dtype(_NP[b.dtype]).itemsize
+            dt = getattr(torch, _TORCH[b.dtype])
+            self.store[i] = dev[offs[i]:offs[i] + n].view(dt).view(b.shape)
+            views[i] = host[offs[i]:offs[i] + n].numpy().view(_NP[b.dtype]).reshape(b.shape)
+        return dev, host, views
+
     def _enqueue(self) -> None:
+        """The input copy, every step and the result copy, on the runner's
+        stream (the copies are plain cudaMemcpyAsync between the arenas and
+        their pinned staging buffers, which a graph records as copy nodes)."""
+        ctx, s, lib = self.ctx.ptr, self._s, self.lib
+        L.check(lib.remora_b200_memcpy_h2d(ctx, ctypes.c_void_p(self._in_arena.data_ptr()),
+                                           ctypes.c_void_p(self._in_host.data_ptr()), self._in_arena.numel(), s),
+                "plan inputs")
         for op, fn, args in self.calls:
             L.check(fn(*args), f"plan step {op}")
+        L.check(lib.remora_b200_memcpy_d2h(ctx, ctypes.c_void_p(self._out_host.data_ptr()),
+                                           ctypes.c_void_p(self._out_arena.data_ptr()), self._out_arena.numel(), s),
+                "plan results")
 
     def run(self, inputs: list[np.ndarray] | None = None) -> list[np.ndarray]:
         """Copy the inputs in, run every step, and return the results."""
         torch = self.torch
         inputs = _check_inputs(self.plan, inputs)
+        for i, view in self._in_np.items():
+            view[...] = inputs[self.plan.buffers[i].input]
         with torch.cuda.stream(self.stream):
-            for i, host in self.host_in.items():
-                host.numpy()[...] = inputs[self.plan.buffers[i].input]
-                self.store[i].copy_(host, non_blocking=True)
             if self.graph is not None:
                 self.graph.replay()
             else:
                 n0 = L.launch_count()
                 self._enqueue()
                 self.launches_per_run = L.launch_count() - n0
-            for r, host in self.host_out.items():
-                host.copy_(self.store[r], non_blocking=True)
         L.check(self.lib.remora_b200_synchronize(self.ctx.ptr, self._s), "plan")
-        out = [self.host_out[r].numpy().copy() for r in self.results]
-        if self.graph_wanted and self.graph is None:
+        out = []
+        for r in self.results:
+            if r in self._out_np:
+                out.append(self._out_np[r].copy())
+            else:  # a result that is an input or a constant of the plan
+                out.append(self.store[r].cpu().numpy().reshape(self.plan.buffers[r].shape))
+        if self.graph_wanted and self.graph is None and self.calls:
             self._capture()
         return out
 
     def _capture(self) -> None:
-        """Record the steps as a CUDA graph on the runner's stream (after an
-        eager run: kernels compiled, the stream's workspace sized)."""
+        """Record the input copy, the steps and the result copy as one CUDA
+        graph on the runner's stream (after an eager run: kernels compiled,
+        the stream's workspace sized)."""
         torch = self.torch
         g = torch.cuda.CUDAGraph()
         n0 = L.launch_count()
