@@ -2,9 +2,11 @@
 
 ``python -m remora_b200.cli FILE --call NAME --input a.npy [--input b.npy]``
 is the reference's ``remorac FILE --call NAME --input ...``
-(remora/cli.py:141-187): the named function is typed from the .npy inputs,
-compiled by the reference front end, lowered to this backend's specs
-(``reference_codegen``) and run through ``B200Executor``.
+(remora/cli.py:141-187): the named function is typed from the .npy inputs
+(a 0-d input is a scalar parameter), compiled by the reference front end,
+lowered to this backend's specs (``reference_codegen``) and run through
+``B200Executor``; a function no single kernel computes runs as a device plan
+(``program_plan.plan_from_function``).
 
 ``python -m remora_b200.cli FILE`` runs a whole program, as
 ``remorac FILE --target gpu-nvidia`` does (remora/cli.py:190-212,
@@ -74,20 +76,32 @@ def _param_type(arr: np.ndarray):
         elem = INT
     else:
         raise RemoraB200Error(f"input of dtype {arr.dtype}: save --input arrays as float32, int32 or bool")
+    if arr.ndim == 0:
+        return elem  # a 0-d input is a scalar parameter
     return ArrayType(elem, tuple(StaticDim(int(d)) for d in arr.shape))
 
 
 def call_function(source: str, name: str, arrays: list[np.ndarray], *, syntax: str = "ml") -> np.ndarray:
     """Compile function ``name`` of ``source`` for the argument shapes and
-    dtypes of ``arrays`` and run it on the device."""
+    dtypes of ``arrays`` and run it on the device: as one kernel where the
+    codegen takes the function whole (``reference_codegen``), else as a
+    device plan of several steps (``program_plan.plan_from_function``)."""
+    from remora_b200.errors import RemoraUnsupportedError
+    from remora_b200.program_plan import compile_function_source_to_plan
     from remora_b200.reference_codegen import compile_function_source_to_b200_artifacts
 
     arrays = [a.astype(np.int32) if np.issubdtype(a.dtype, np.integer) else a for a in arrays]
+    plan = None
     try:
-        module, kernels, _hir = compile_function_source_to_b200_artifacts(
-            source, name, tuple(_param_type(a) for a in arrays), syntax=syntax)
+        types = tuple(_param_type(a) for a in arrays)
+        try:
+            module, kernels, _hir = compile_function_source_to_b200_artifacts(source, name, types, syntax=syntax)
+        except RemoraUnsupportedError:
+            plan = compile_function_source_to_plan(source, name, types, syntax=syntax)
     except Exception as exc:
         raise _CliError(f"GPU function compilation failed: {exc}") from exc
+    if plan is not None:
+        return run_plan(plan, arrays)
     try:
         from remora_b200.executor import B200Executor
 

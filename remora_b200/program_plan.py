@@ -593,7 +593,19 @@ class _Planner:
             # the fold kernels read f32 / i32: widen the bools first
             arr = self.emit_map(InputExpr(0), [arr], self.shape_of(arr), L.I32)
             in_code = L.I32
-        if init[0] == "const":
+        if init[0] == "buf" and self.shape_of(init[1]) == () and len(self.shape_of(arr)) == 1:
+            # a scalar init known only at run time (a parameter, an earlier
+            # result): fold from the identity, then combine with the init
+            ib = init[1]
+            if self.code_of(ib) != acc_code:
+                raise _unsupported("a fold init of another element type")
+            sp = fold_spec(op=op2, init=(0 if op2 == "+" else 1), mode="all", dtype=acc_code,
+                           premap=InputExpr(0) if in_code != acc_code else None,
+                           premap_in_dtypes=[in_code] if in_code != acc_code else None)
+            total = self.buf((), acc_code)
+            self.plan.steps.append({"op": "fold", "spec": sp, "ins": [arr], "out": total})
+            out = self.emit_map(BinaryExpr(op2, InputExpr(0), InputExpr(1)), [ib, total], (), acc_code)
+        elif init[0] == "const":
             if len(self.shape_of(arr)) != 1:
                 raise _unsupported("scalar-init folds of rank >= 2 arrays")
             premap = InputExpr(0) if in_code != acc_code else None
@@ -636,6 +648,34 @@ def plan_from_hir(program: object) -> Plan:
         out = pl.emit_map(InputExpr(0), [out], pl.shape_of(out), pl.code_of(out))
     pl.plan.result = out
     return pl.plan
+
+
+def plan_from_function(function: object, functions: dict[str, Any] | None = None) -> Plan:
+    """A plan for one of the reference's HIR functions (``HIRFunction``, as
+    remora/compiler.py:compile_function_source builds it): parameter k is
+    the plan's input k (arrays, and scalars as rank-0 buffers), the body its
+    steps.  ``functions`` holds other functions the body calls, by name."""
+    pl = _Planner(dict(functions or {}))
+    env = {}
+    for k, p in enumerate(function.params):
+        env[p.name] = ("buf", pl.buf(_shape(p.type), _elem(p.type), input=k))
+    out = pl.as_buf(pl.lower(function.body, env))
+    if pl.plan.buffers[out].view is not None or pl.plan.buffers[out].input is not None:
+        out = pl.emit_map(InputExpr(0), [out], pl.shape_of(out), pl.code_of(out))
+    pl.plan.result = out
+    return pl.plan
+
+
+def compile_function_source_to_plan(source: str, function_name: str, param_types: tuple[Any, ...], *,
+                                    include_prelude: bool = True, syntax: str = "ml") -> Plan:
+    """The reference's function front end (remora/compiler.py:
+    compile_function_source: parse, type check, specialise to
+    ``param_types``, lower to HIR) followed by ``plan_from_function``."""
+    from remora.compiler import compile_function_source  # the reference's front end
+
+    artifact = compile_function_source(source, function_name, param_types, verify=False,
+                                       include_prelude=include_prelude, syntax=syntax)
+    return plan_from_function(artifact.hir_function)
 
 
 # -------------------------------------------------------------- execution

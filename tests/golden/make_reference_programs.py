@@ -10,7 +10,10 @@ reference nor its front end.  The reference is only needed to regenerate:
 
 The first programs are the ones the reference's GPU executor tests compile
 (remora/tests/test_executor.py: scale, add, sum, dot, inc); the rest cover
-the other shapes the codegen accepts.
+the other shapes the codegen accepts.  tests/golden/function_plans.{json,npz}
+hold functions no single kernel computes, planned by
+remora_b200.program_plan.plan_from_function, with seeded inputs and the
+interpreter's outputs.
 """
 
 from __future__ import annotations
@@ -114,6 +117,53 @@ PROGRAMS = [
 ELEMENTWISE = {"bool_and": lambda x, y: np.logical_and(x, y)}
 
 
+# Functions no single kernel computes, run as device plans
+# (program_plan.plan_from_function): several steps, views, scalar parameters
+# (dims None), a fold whose init is a parameter.
+FUNCTION_PLANS = [
+    ("scan_of_map", "ml", "def f xs = scan (+) 0.0 (map (* 0.5) xs)", "f", [("f", (100,))], "normal"),
+    ("reverse_map", "ml", "def f xs = map (+ 1) (reverse xs)", "f", [("i", (9,))], "ints"),
+    ("scalar_param", "ml", "def f s xs = map (\\x -> x * s + 1.0) xs", "f", [("f", None), ("f", (7,))], "normal"),
+    ("fold_init_param", "ml", "def f s xs = fold (+) s xs", "f", [("f", None), ("f", (50,))], "normal"),
+    ("int_fold_init", "ml", "def f k xs = fold (+) k (map (* 3) xs)", "f", [("i", None), ("i", (40,))], "ints"),
+    ("rows_then_sort", "lisp", """
+(define/pi () (f [x (Array Float 6 30)] (Array Float 6)) (sort < (map (lambda (row) (fold + 0.0 row)) x)))
+""", "f", [("f", (6, 30))], "normal"),
+    ("transpose_rows", "lisp", """
+(define/pi () (f [x (Array Float 5 8)] (Array Float 8)) (map (lambda (row) (fold + 0.0 row)) (transpose x)))
+""", "f", [("f", (5, 8))], "normal"),
+    ("mask_count", "lisp", """
+(define/pi () (f [t Float x (Array Float 64)] Int) (fold + 0 (map (lambda (v) (select (> v t) 1 0)) x)))
+""", "f", [("f", None), ("f", (64,))], "normal"),
+]
+
+
+def function_plans(rng) -> None:
+    from remora.compiler import compile_function_source
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    records, arrays = [], {}
+    for name, syntax, source, fn, params, kind in FUNCTION_PLANS:
+        ptypes = tuple(ELEM[e] if d is None else A(e, *d) for e, d in params)
+        plan = compile_function_source_to_plan(source, fn, ptypes, syntax=syntax)
+        rtype = compile_function_source(source, fn, ptypes, verify=False, include_prelude=False,
+                                        syntax=syntax).function_type.result
+        inputs = [make_input(kind, k, e, d or (), rng) for k, (e, d) in enumerate(params)]
+        out = np.asarray(interpret(source, syntax, fn, ptypes, rtype, [np.array(a) for a in inputs]))
+        res = plan.buffers[plan.result]
+        out = out.astype({0: np.float32, 1: np.int32, 2: np.bool_}[res.dtype]).reshape(res.shape)
+        for k, a in enumerate(inputs):
+            arrays[f"{name}__in{k}"] = a
+        arrays[f"{name}__out"] = out
+        records.append({"name": name, "source": source.strip(), "syntax": syntax, "function": fn,
+                        "params": [[e, None if d is None else list(d)] for e, d in params],
+                        "plan": plan.to_record(), "steps": [st["op"] for st in plan.steps]})
+        print(name, [st["op"] for st in plan.steps], out.shape, out.dtype)
+    (HERE / "function_plans.json").write_text(json.dumps(records, indent=1) + "\n")
+    np.savez(HERE / "function_plans.npz", **arrays)
+
+
 def make_input(kind: str, k: int, e: str, dims: tuple[int, ...], rng) -> np.ndarray:
     if kind.startswith("known:"):
         vals = kind[6:].split("|")[k]
@@ -165,6 +215,7 @@ def main() -> None:
         print(name, type(spec).__name__, out.shape, out.dtype)
     (HERE / "reference_programs.json").write_text(json.dumps(records, indent=1) + "\n")
     np.savez(HERE / "reference_programs.npz", **arrays)
+    function_plans(np.random.default_rng(SEED + 1))
 
 
 if __name__ == "__main__":

@@ -28,6 +28,8 @@ from test_reference_codegen import oracle_run
 REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
 have_ref = os.path.isdir(os.path.join(REF, "remora"))
 needs_ref = pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+if have_ref and REF not in sys.path:
+    sys.path.insert(0, REF)  # the CLI compiles through the reference's front end
 
 
 def plans() -> list[dict]:
@@ -44,7 +46,7 @@ def run(argv: list[str], capsys) -> tuple[int, str, str]:
 def on_oracle(monkeypatch, oracle_mod):
     """Device execution replaced by the oracle."""
     monkeypatch.setattr("remora_b200.program_plan.execute_plan",
-                        lambda plan, inputs=None, device=None: run_plan_on_oracle(oracle_mod, plan))
+                        lambda plan, inputs=None, device=None: run_plan_on_oracle(oracle_mod, plan, inputs))
 
     class OracleExecutor:
         def __init__(self, module, kernels):
@@ -158,9 +160,29 @@ def test_call_without_inputs_fails(tmp_path, capsys):
 
 
 @needs_ref
+@pytest.mark.parametrize("rec", __import__("test_program_plan").function_records(), ids=lambda r: r["name"])
+def test_call_runs_a_multi_step_function_as_a_plan(rec, tmp_path, capsys, on_oracle):
+    """Functions no single kernel computes (several steps, scalar parameters
+    given as 0-d .npy inputs) run through --call as device plans."""
+    from test_program_plan import close, function_io
+
+    ins, want = function_io(rec)
+    src = tmp_path / "f.remora"
+    src.write_text(rec["source"] + "\n")
+    argv = [str(src), "--syntax", rec["syntax"], "--call", rec["function"]]
+    for k, a in enumerate(ins):
+        np.save(tmp_path / f"in{k}.npy", a)
+        argv += ["--input", str(tmp_path / f"in{k}.npy")]
+    code, out, err = run(argv, capsys)
+    assert code == 0, err
+    got = np.asarray(eval(out.replace("true", "True").replace("false", "False")), dtype=want.dtype)
+    close(got.reshape(want.shape), want)
+
+
+@needs_ref
 def test_call_of_an_unsupported_function_fails_at_compilation(tmp_path, capsys):
     src = tmp_path / "f.remora"
-    src.write_text("def f xs = reverse (map (* 2.0) xs)\n")
+    src.write_text("def f xs = fold (\\acc x -> acc * x + 1.0) 1.0 xs\n")
     np.save(tmp_path / "a.npy", np.arange(4, dtype=np.float32))
     code, _, err = run([str(src), "--call", "f", "--input", str(tmp_path / "a.npy")], capsys)
     assert code == 1 and err.startswith("remorac: GPU function compilation failed:")

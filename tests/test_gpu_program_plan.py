@@ -37,3 +37,13 @@ def test_plan_runner_graph_replays_match_the_eager_run(cuda, rec):
         np.testing.assert_array_equal(again, eager)
     np.testing.assert_array_equal(first, eager)
     close(again, expected(rec["name"]))
+
+
+@pytest.mark.parametrize("rec", __import__("test_program_plan").function_records(), ids=lambda r: r["name"])
+def test_function_plan_on_device(cuda, rec):
+    """Functions with array and scalar parameters as device plans, against
+    the reference interpreter's outputs on the recorded inputs."""
+    from test_program_plan import function_io
+
+    ins, want = function_io(rec)
+    close(execute_plan(Plan.from_record(rec["plan"]), ins), want)

@@ -143,3 +143,49 @@ def test_unsupported_programs_raise(source):
     except Exception as exc:  # the reference's own front end rejected it first
         pytest.skip(f"front end: {type(exc).__name__}")
     raise AssertionError("expected RemoraUnsupportedError")
+
+
+# ------------------------------------------------------- function plans
+# tests/golden/function_plans.{json,npz}: functions with parameters (arrays
+# and scalars) that no single kernel computes, planned by plan_from_function
+# from the reference's function front end; seeded inputs and the
+# interpreter's outputs.
+def function_records() -> list[dict]:
+    return json.loads((GOLDEN / "function_plans.json").read_text())
+
+
+def function_io(rec: dict) -> tuple[list[np.ndarray], np.ndarray]:
+    with np.load(GOLDEN / "function_plans.npz") as f:
+        return [f[f"{rec['name']}__in{k}"] for k in range(len(rec["params"]))], f[f"{rec['name']}__out"]
+
+
+@pytest.mark.parametrize("rec", function_records(), ids=lambda r: r["name"])
+def test_function_plan_on_the_oracle_gives_the_interpreter_value(oracle_mod, rec):
+    ins, want = function_io(rec)
+    plan = Plan.from_record(rec["plan"])
+    assert plan.to_record() == rec["plan"]
+    assert [b.input for b in plan.buffers if b.input is not None] == list(range(len(rec["params"])))
+    close(run_plan_on_oracle(oracle_mod, plan, ins), want)
+
+
+def test_a_fold_with_a_runtime_init_folds_from_the_identity():
+    rec = next(r for r in function_records() if r["name"] == "fold_init_param")
+    plan = Plan.from_record(rec["plan"])
+    fold, combine = plan.steps
+    assert fold["op"] == "fold" and fold["spec"].init_f == 0.0 and combine["op"] == "map"
+    assert plan.buffers[combine["ins"][0]].input == 0  # the init parameter, then the sum
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+def test_planner_reproduces_recorded_function_plans():
+    sys.path.insert(0, REF)
+    from remora.types import BOOL, FLOAT, INT, ArrayType, StaticDim
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    elem = {"f": FLOAT, "i": INT, "b": BOOL}
+    for rec in function_records():
+        ptypes = tuple(elem[e] if d is None else ArrayType(elem[e], tuple(StaticDim(x) for x in d))
+                       for e, d in rec["params"])
+        plan = compile_function_source_to_plan(rec["source"], rec["function"], ptypes, syntax=rec["syntax"])
+        assert plan.to_record() == rec["plan"], rec["name"]
