@@ -715,8 +715,9 @@ class PlanRunner:
     """A plan bound to device memory, for one run or many.
 
     Construction allocates every buffer of the plan on the device, uploads
-    its constants, builds each step's descriptors and arguments once, and
-    makes a stream of its own.  The plan's inputs share one device arena
+    its constants and builds each step's descriptors and arguments once.
+    It runs on the caller's current stream, or with ``graph=True`` on a
+    stream of its own.  The plan's inputs share one device arena
     and its results another, each staged through one pinned host buffer.
     ``run(inputs)`` writes the inputs into the staging buffer, then on that
     stream copies them in (one copy), enqueues every step, copies the
@@ -738,7 +739,10 @@ class PlanRunner:
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
         self.ctx = context(self.dev.index)
         self.lib = L.lib()
-        self.stream = torch.cuda.Stream(self.dev)
+        # One-shot runs use the caller's stream (the library keeps a
+        # workspace per stream until shutdown); a graph is captured on a
+        # stream of the runner's own.
+        self.stream = torch.cuda.Stream(self.dev) if graph else torch.cuda.current_stream(self.dev)
         self._s = ctypes.c_void_p(self.stream.cuda_stream)
         self.results = list(results or plan.results or [plan.result])
         for r in self.results:
