@@ -112,6 +112,7 @@ __device__ __forceinline__ void rank_digits(const uint32_t (&k)[ITEMS], int vali
                                             uint32_t (&pos)[ITEMS], uint32_t (*s_wcnt)[256], uint32_t *s_w) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t lt = (1u << lane) - 1u;
+  const bool full = valid_n >= kT * ITEMS;
   for (int i = threadIdx.x; i < kWarps * 256; i += kT) (&s_wcnt[0][0])[i] = 0u;
   __syncthreads();
   uint32_t r[ITEMS];
@@ -120,11 +121,13 @@ __device__ __forceinline__ void rank_digits(const uint32_t (&k)[ITEMS], int vali
     const int q = warp * 32 * ITEMS + i * 32 + lane;
     const bool valid = q < valid_n;
     const uint32_t d = (k[i] >> shift) & 255u;
-    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+    // a full tile (the same for the whole block) needs no validity ballot
+    uint32_t peers = full ? 0xffffffffu : __ballot_sync(0xffffffffu, valid);
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
-      const uint32_t bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
-      peers &= ((d >> b) & 1u) ? bal : ~bal;
+      const uint32_t bit = (d >> b) & 1u;
+      // the ballot where this lane's bit is set, its complement where clear
+      peers &= __ballot_sync(0xffffffffu, bit) ^ (bit - 1u);
     }
     const uint32_t below = __popc(peers & lt);
     const int leader = 31 - __clz(peers);  // peers is non-empty for a valid lane
@@ -297,9 +300,12 @@ __global__ void __launch_bounds__(kT) radix_scan_rows(uint32_t *__restrict__ his
 
 // Stable scatter of one tile.  kFirst: keys come raw from the input and the
 // values are generated (source indices).  kLast: keys leave in their original
-// bit pattern.  kKeys / kVals: which streams are written.
+// bit pattern.  kKeys / kVals: which streams are written.  Three blocks per
+// SM (80 registers, a few spilled): the first pass waits on its loads, and
+// 24 warps hide that latency better than 16 (2^26 f32 keys: 2.25 -> 1.84 ms
+// per sort together with the leaner ranking above).
 template <int kDtype, bool kFirst, bool kLast, bool kCanon, bool kKeys, bool kVals>
-__global__ void __launch_bounds__(kT) radix_scatter(const uint32_t *__restrict__ kin, const uint32_t *__restrict__ vin,
+__global__ void __launch_bounds__(kT, 3) radix_scatter(const uint32_t *__restrict__ kin, const uint32_t *__restrict__ vin,
                                                     uint32_t *__restrict__ kout, uint32_t *__restrict__ vout,
                                                     int64_t n, int shift, int64_t ntiles,
                                                     const uint32_t *__restrict__ hist,
