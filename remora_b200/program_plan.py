@@ -504,6 +504,9 @@ class _Planner:
             raise _unsupported("cell maps of one array")
         cell_rank = len(node.cell_shape)
         frame = self.shape_of(arrays[0])[:len(self.shape_of(arrays[0])) - cell_rank]
+        dot = self.lifted_dot(names[0], body, env, arrays[0], cell_rank)
+        if dot is not None:
+            return ("buf", dot)
         if tuple(shape) != tuple(frame):
             raise _unsupported("cell maps other than one scalar per cell")
         inner = {**env, names[0]: ("cell", arrays[0], cell_rank)}
@@ -514,6 +517,112 @@ class _Planner:
         if not operands:
             raise _unsupported("a cell map whose body does not use its cell")
         return ("buf", self.emit_map(e, operands, tuple(frame), code))
+
+    # ---- lifted dot products: rows times a vector, rows times rows
+    def _resolve(self, node: object, subst: dict) -> tuple[object, dict]:
+        """What ``node`` stands for once let-bound and argument names are
+        followed (the front end inlines ``dot``/``sum`` as a chain of lets):
+        (node, its names) or (("free", name), ...) for a name bound outside."""
+        while True:
+            k = _kind(node)
+            if k == "HIRVar":
+                if node.name not in subst:
+                    return ("free", node.name), subst
+                node, subst = subst[node.name]
+            elif k == "HIRLet":
+                subst = {**subst, node.name: (node.value, subst)}
+                node = node.body
+            elif k == "HIRCall" and node.func_name in self.functions:
+                f = self.functions[node.func_name]
+                subst = {p.name: (a, subst) for p, a in zip(f.params, node.args)}
+                node = f.body
+            else:
+                return node, subst
+
+    def _match_dot(self, body: object) -> tuple[set[str], float] | None:
+        """({a, b}, init) when ``body`` is ``fold (+) init (map (*) a b)`` of
+        two names bound outside it (the prelude's ``dot a b``), else None."""
+        node, s = self._resolve(body, {})
+        if not _kind(node) == "HIRFold":
+            return None
+        f = node.func
+        if _kind(f) != "HIRPrimCallable" or _base_op(f.op) != "+" or f.left_arg is not None or \
+                f.right_arg is not None:
+            return None
+        init, _ = self._resolve(node.init, s)
+        if _kind(init) != "HIRLit" or isinstance(init.value, bool):
+            return None
+        m, s2 = self._resolve(node.array, s)
+        if _kind(m) not in ("HIRMap", "HIRApply") or m.cell_shape or len(m.arrays) != 2:
+            return None
+        g = m.func
+        if _kind(g) == "HIRPrimCallable":
+            if _base_op(g.op) != "*" or g.left_arg is not None or g.right_arg is not None:
+                return None
+        elif _kind(g) == "HIRLambda":
+            b = g.body
+            if _kind(b) != "HIRPrimOp" or _base_op(b.op) != "*" or \
+                    sorted(getattr(a, "name", "") for a in b.args) != sorted(p.name for p in g.params):
+                return None
+        else:
+            return None
+        leaves = [self._resolve(a, s2)[0] for a in m.arrays]
+        if not all(isinstance(x, tuple) and x[0] == "free" for x in leaves):
+            return None
+        return {leaves[0][1], leaves[1][1]}, float(init.value)
+
+    def lifted_dot(self, cell: str, body: object, env: dict, arr: int, cell_rank: int) -> int | None:
+        """``map (\\row -> dot row v) A`` (a vector per row of A: a cell fold
+        whose premap multiplies the row by a stride-0 view of v) or
+        ``map (\\r -> map (\\c -> dot r c) B) A`` (A times B's rows: one
+        3xTF32 GEMM step, the f32-accurate form of the tensor-core GEMM),
+        as remora/lowering/tensor_ops.py lowers the lifted dot of the prelude
+        (stdlib/prelude.rem:14); None for any other body."""
+        if cell_rank != 1 or self.code_of(arr) != L.F32 or len(self.shape_of(arr)) != 2:
+            return None
+        m_rows, k = self.shape_of(arr)
+        inner, s = self._resolve(body, {})
+        if _kind(inner) in ("HIRMap", "HIRApply") and len(inner.cell_shape) == 1 and len(inner.arrays) == 1 \
+                and _kind(inner.func) == "HIRLambda" and len(inner.func.params) == 1:
+            match = self._match_dot(inner.func.body)
+            if match is None or match[0] != {cell, inner.func.params[0].name}:
+                return None
+            src, s2 = self._resolve(inner.arrays[0], s)
+            if isinstance(src, tuple):
+                v = env.get(src[1])
+                if v is None or v[0] != "buf":
+                    return None
+                b = v[1]
+            elif not s2:
+                b = self.as_buf(self.lower(src, env))
+            else:
+                return None
+            if self.code_of(b) != L.F32 or len(self.shape_of(b)) != 2 or self.shape_of(b)[1] != k:
+                return None
+            n = self.shape_of(b)[0]
+            _, _, st = self.strides_of(b)
+            bt = self.view(b, (k, n), 0, (st[1], st[0]))  # the GEMM's B: columns are the rows of b
+            out = self.buf((m_rows, n), L.F32)
+            self.plan.steps.append({"op": "gemm", "a": arr, "b": bt, "out": out, "precision": L.PREC_3XTF32})
+            init = match[1]
+        else:
+            match = self._match_dot(body)
+            if match is None or cell not in match[0] or len(match[0]) != 2:
+                return None
+            (other,) = match[0] - {cell}
+            v = env.get(other)
+            if v is None or v[0] != "buf" or self.code_of(v[1]) != L.F32 or self.shape_of(v[1]) != (k,):
+                return None
+            _, _, st = self.strides_of(v[1])
+            vb = self.view(v[1], (m_rows, k), 0, (0, st[0]))  # v repeated for every row
+            sp = fold_spec(op="+", init=match[1], mode="cell", cell_rank=1, dtype=L.F32,
+                           premap=BinaryExpr("*", InputExpr(0), InputExpr(1)), n_inputs=2)
+            out = self.buf((m_rows,), L.F32)
+            self.plan.steps.append({"op": "fold", "spec": sp, "ins": [arr, vb], "out": out})
+            return out
+        if init != 0.0:
+            out = self.emit_map(BinaryExpr("+", InputExpr(0), ConstantExpr(init)), [out], self.shape_of(out), L.F32)
+        return out
 
     def _cell_operand(self, node: object, env: dict) -> int | None:
         """A frame-shaped buffer for a use of a cell parameter inside a cell
@@ -819,6 +928,12 @@ class PlanRunner:
             elif op in ("sort", "grade"):
                 fn = lib.remora_b200_grade if op == "grade" else lib.remora_b200_sort
                 call = (fn, (ctx, plan.buffers[st["in"]].dtype, desc(st["in"]), desc(st["out"]), rank(st["in"]), s))
+            elif op == "gemm":
+                spec = L.RemoraGemmSpec()
+                spec.precision = int(st["precision"])
+                self._keep.append(spec)
+                call = (lib.remora_b200_gemm, (ctx, ctypes.byref(spec), desc(st["a"]), desc(st["b"]), desc(st["out"]),
+                                               2, s))
             else:
                 raise _unsupported(f"plan step {op}")
             self.calls.append((op, *call))

@@ -135,6 +135,19 @@ FUNCTION_PLANS = [
     ("mask_count", "lisp", """
 (define/pi () (f [t Float x (Array Float 64)] Int) (fold + 0 (map (lambda (v) (select (> v t) 1 0)) x)))
 """, "f", [("f", None), ("f", (64,))], "normal"),
+    # lifted dot products, written as the prelude's dot a b = sum (map (*) a b)
+    # inlined (stdlib/prelude.rem:11,14): rows times a vector, rows times rows
+    ("matvec", "ml", "def mv m v = map (\\row -> fold (+) 0.0 (map (*) row v)) m", "mv",
+     [("f", (64, 48)), ("f", (48,))], "normal"),
+    ("matvec_init", "lisp", """
+(define/pi () (f [m (Array Float 7 9) v (Array Float 9)] (Array Float 7)) (map (lambda (row) (fold + 1.5 (map * row v))) m))
+""", "f", [("f", (7, 9)), ("f", (9,))], "normal"),
+    ("linear", "ml", "def lin w x b = map (+) (map (\\row -> fold (+) 0.0 (map (*) row x)) w) b", "lin",
+     [("f", (32, 64)), ("f", (64,)), ("f", (32,))], "normal"),
+    ("matmul_rows", "ml", "def mm a bt = map (\\r -> map (\\c -> fold (+) 0.0 (map (*) r c)) bt) a", "mm",
+     [("f", (96, 40)), ("f", (80, 40))], "normal"),
+    ("matmul_transpose", "ml", "def mm a b = map (\\r -> map (\\c -> fold (+) 0.0 (map (*) r c)) (transpose b)) a",
+     "mm", [("f", (33, 20)), ("f", (20, 17))], "normal"),
 ]
 
 

@@ -43,7 +43,7 @@ def test_plan_runner_graph_replays_match_the_eager_run(cuda, rec):
 def test_function_plan_on_device(cuda, rec):
     """Functions with array and scalar parameters as device plans, against
     the reference interpreter's outputs on the recorded inputs."""
-    from test_program_plan import function_io
+    from test_program_plan import close_for, function_io
 
     ins, want = function_io(rec)
-    close(execute_plan(Plan.from_record(rec["plan"]), ins), want)
+    close_for(rec, execute_plan(Plan.from_record(rec["plan"]), ins), want)

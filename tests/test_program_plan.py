@@ -86,6 +86,8 @@ def run_plan_on_oracle(orc, plan: Plan, inputs: list[np.ndarray] | None = None, 
             store[s["out"]] = orc.sort(get(s["in"]))
         elif op == "grade":
             store[s["out"]] = orc.grade(get(s["in"]))
+        elif op == "gemm":
+            store[s["out"]] = orc.matmul(get(s["a"]), get(s["b"]))
         else:
             raise AssertionError(op)
     def result(r: int) -> np.ndarray:
@@ -159,6 +161,16 @@ def function_io(rec: dict) -> tuple[list[np.ndarray], np.ndarray]:
         return [f[f"{rec['name']}__in{k}"] for k in range(len(rec["params"]))], f[f"{rec['name']}__out"]
 
 
+def close_for(rec: dict, got: np.ndarray, want: np.ndarray) -> None:
+    """A plan with a GEMM step runs it in 3xTF32 on the device, checked at the
+    3xTF32 GEMM tolerance (rtol 1e-4 + atol 1e-4·max|ref|); every other plan
+    at the f32 one."""
+    if "gemm" in rec["steps"]:
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * float(np.abs(want).max()))
+    else:
+        close(got, want)
+
+
 @pytest.mark.parametrize("rec", function_records(), ids=lambda r: r["name"])
 def test_function_plan_on_the_oracle_gives_the_interpreter_value(oracle_mod, rec):
     ins, want = function_io(rec)
@@ -166,6 +178,37 @@ def test_function_plan_on_the_oracle_gives_the_interpreter_value(oracle_mod, rec
     assert plan.to_record() == rec["plan"]
     assert [b.input for b in plan.buffers if b.input is not None] == list(range(len(rec["params"])))
     close(run_plan_on_oracle(oracle_mod, plan, ins), want)
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+@pytest.mark.parametrize("name, with_dot", [
+    ("matvec", "def mv m v = map (\\row -> dot row v) m"),
+    ("matmul_rows", "def mm a bt = map (\\r -> map (\\c -> dot r c) bt) a"),
+])
+def test_the_preludes_dot_plans_like_its_inlined_form(name, with_dot):
+    """``dot`` reaches the planner as the front end's chain of lets over
+    ``sum (map (*) a b)``; it must give the same plan as the inlined fold."""
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    rec = next(r for r in function_records() if r["name"] == name)
+    ptypes = tuple(ArrayType(FLOAT, tuple(StaticDim(x) for x in d)) for _, d in rec["params"])
+    plan = compile_function_source_to_plan(with_dot, rec["function"], ptypes)
+    assert plan.to_record() == rec["plan"]
+
+
+def test_lifted_dots_become_one_fold_or_one_gemm():
+    recs = {r["name"]: r for r in function_records()}
+    assert recs["matvec"]["steps"] == ["fold"] and recs["matmul_rows"]["steps"] == ["gemm"]
+    plan = Plan.from_record(recs["matvec"]["plan"])
+    (step,) = plan.steps
+    vec = plan.buffers[step["ins"][1]]
+    assert vec.view is not None and vec.view[2][0] == 0  # the vector, repeated for every row
+    plan = Plan.from_record(recs["matmul_transpose"]["plan"])
+    (step,) = plan.steps
+    assert plan.buffers[step["b"]].shape == (20, 17)
 
 
 def test_a_fold_with_a_runtime_init_folds_from_the_identity():
