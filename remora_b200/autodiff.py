@@ -141,9 +141,10 @@ def _apply(op: str, args: list[Expr]) -> Expr:
     return LogicExpr(op, *args)
 
 
-def _elementwise(node: object, env: dict[str, Expr], on_fold=None) -> Expr:
+def _elementwise(node: object, env: dict[str, Expr], on_fold=None, on_cellmap=None) -> Expr:
     """An elementwise HIR expression over the parameters as an Expr
-    (``on_fold`` turns a fold met on the way into an Expr, where allowed)."""
+    (``on_fold`` / ``on_cellmap`` turn a fold / a map over cells met on the
+    way into an Expr, where allowed)."""
     k = _kind(node)
     if k == "HIRFold" and on_fold is not None:
         return on_fold(node, env)
@@ -155,23 +156,27 @@ def _elementwise(node: object, env: dict[str, Expr], on_fold=None) -> Expr:
         return ConstantExpr(float(node.value))
     if k in ("HIRApply", "HIRMap"):
         if node.cell_shape:
+            if on_cellmap is not None:
+                return on_cellmap(node, env)
             raise RemoraUnsupportedError("autodiff: maps over cells of rank >= 1")
-        args = [_elementwise(a, env, on_fold) for a in node.arrays]
+        args = [_elementwise(a, env, on_fold, on_cellmap) for a in node.arrays]
         f = node.func
         if _kind(f) == "HIRPrimCallable":
             if f.left_arg is not None:
-                args = [_elementwise(f.left_arg, env, on_fold), *args]
+                args = [_elementwise(f.left_arg, env, on_fold, on_cellmap), *args]
             if f.right_arg is not None:
-                args = [*args, _elementwise(f.right_arg, env, on_fold)]
+                args = [*args, _elementwise(f.right_arg, env, on_fold, on_cellmap)]
             return _apply(_base_op(f.op), args)
         if _kind(f) == "HIRLambda":
-            return _elementwise(f.body, {**env, **{p.name: a for p, a in zip(f.params, args)}}, on_fold)
+            inner = {**env, **{p.name: a for p, a in zip(f.params, args)}}
+            return _elementwise(f.body, inner, on_fold, on_cellmap)
         raise RemoraUnsupportedError(f"autodiff: {_kind(f)} as a mapped function")
     if k == "HIRPrimOp":
-        return _apply(_base_op(node.op), [_elementwise(a, env, on_fold) for a in node.args])
+        return _apply(_base_op(node.op), [_elementwise(a, env, on_fold, on_cellmap) for a in node.args])
     if k == "HIRIf":
-        return SelectExpr(_elementwise(node.condition, env, on_fold), _elementwise(node.then_branch, env, on_fold),
-                          _elementwise(node.else_branch, env, on_fold))
+        return SelectExpr(_elementwise(node.condition, env, on_fold, on_cellmap),
+                          _elementwise(node.then_branch, env, on_fold, on_cellmap),
+                          _elementwise(node.else_branch, env, on_fold, on_cellmap))
     raise RemoraUnsupportedError(f"autodiff: {k} in a loss expression")
 
 
@@ -286,6 +291,7 @@ class _LossPlanner:
         self.n_params = len(params)
         self.env = {p.name: InputExpr(k) for k, p in enumerate(params)}
         self.folds: list[tuple[float, Expr, tuple[int, ...]]] = []  # (init, summand, shape)
+        self.matvec_slot: dict[tuple[int, int, float], int] = {}  # (W, x, init) -> slot of W x + init
 
     def new_slot(self, shape: tuple[int, ...], b: int) -> int:
         k = max(self.buf) + 1
@@ -324,7 +330,35 @@ class _LossPlanner:
             e, _, extra = self.summand(inner.array, {**env, **{p.name: a for p, a in zip(f.params, args)}})
             cells = int(np.prod(shape[:len(shape) - len(node.cell_shape)], dtype=np.int64))
             return e, shape, cells * (float(inner.init.value) + extra)
-        return _elementwise(node, env), _dims(_type_of(node)), 0.0
+        return _elementwise(node, env, on_cellmap=self.on_cellmap), _dims(_type_of(node)), 0.0
+
+    def on_cellmap(self, node: object, env: dict) -> Expr:
+        """``map (\\row -> fold (+) lit (map (*) row x)) W`` (the lifted dot
+        of stdlib/prelude.rem:14, W and x parameters) inside a summand: a
+        matrix-vector product, computed in the forward as one cell fold and
+        remembered for the backward; the Expr reads its result."""
+        f = node.func
+        if len(node.arrays) != 1 or _kind(f) != "HIRLambda" or len(f.params) != 1:
+            raise RemoraUnsupportedError("autodiff: maps over cells other than rows times a vector")
+        w = _elementwise(node.arrays[0], env)
+        match = self.pl._match_dot(f.body)
+        if not isinstance(w, InputExpr) or w.index >= self.n_params or len(self.shapes[w.index]) != 2 or \
+                match is None or f.params[0].name not in match[0] or len(match[0]) != 2:
+            raise RemoraUnsupportedError("autodiff: maps over cells other than rows times a vector")
+        (other,) = match[0] - {f.params[0].name}
+        x = env.get(other)
+        n, c = self.shapes[w.index]
+        if not isinstance(x, InputExpr) or x.index >= self.n_params or self.shapes[x.index] != (c,):
+            raise RemoraUnsupportedError("autodiff: rows times a parameter vector of the row length")
+        key = (w.index, x.index, match[1])
+        if key not in self.matvec_slot:
+            xv = self.pl.view(self.buf[x.index], (n, c), 0, (0, 1))  # x repeated for every row
+            sp = fold_spec(op="+", init=match[1], mode="cell", cell_rank=1, dtype=L.F32,
+                           premap=BinaryExpr("*", InputExpr(0), InputExpr(1)), n_inputs=2)
+            out = self.pl.buf((n,), L.F32)
+            self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [self.buf[w.index], xv], "out": out})
+            self.matvec_slot[key] = self.new_slot((n,), out)
+        return InputExpr(self.matvec_slot[key])
 
     # ---- steps
     def emit(self, e: Expr, shape: tuple[int, ...]) -> int:
@@ -394,7 +428,11 @@ def value_and_grad_plan_from_hir(function: object):
 
     The folds' adjoint broadcasts along the folded axis (remora/ad.py:
     fold VJP) and a scalar's adjoint is the sum over the elements it was
-    broadcast to (the unbroadcast rule).  ``plan.results`` lists the loss,
+    broadcast to (the unbroadcast rule).  E_i may also read a matrix-vector
+    product of parameters, ``map (\\row -> dot row x) W`` (a linear layer,
+    examples/crater_train.py:38-44): the forward computes it once, and its
+    adjoint g reaches W as the outer product g x^T (one map over two
+    stride-0 views) and x as W^T g (one cell fold over W's transposed view).  ``plan.results`` lists the loss,
     then one gradient per parameter; run it with
     ``program_plan.execute_plan_results``."""
     lp = _LossPlanner(list(function.params))
@@ -416,6 +454,27 @@ def value_and_grad_plan_from_hir(function: object):
     h = _substitute(h, {**fold_slot, **{k: k for k in range(lp.n_params)}})
     results = [lp.buf[next(iter(_walk_inputs(h)))] if isinstance(h, InputExpr) else lp.emit(h, ())]
     adj = [derivative(h, fold_slot[-(i + 1)]) for i in range(len(lp.folds))]
+    # matrix-vector products z = W x: their adjoint g_z flows on to W as the
+    # outer product g_z x^T and to x as W^T g_z
+    contrib: dict[int, list[int]] = {}
+    for (wk, xk, _), z in lp.matvec_slot.items():
+        gz: Expr = _ZERO
+        for i, (_, e, fshape) in enumerate(lp.folds):
+            if fshape == lp.shapes[z]:
+                gz = _add(gz, _mul(adj[i], derivative(e, z)))
+        if _is(gz, 0.0):
+            continue
+        gzb = lp.emit(gz, lp.shapes[z])
+        n, c = lp.shapes[wk]
+        prod = BinaryExpr("*", InputExpr(0), InputExpr(1))
+        dw = lp.pl.emit_map(prod, [lp.pl.view(gzb, (n, c), 0, (1, 0)), lp.pl.view(lp.buf[xk], (n, c), 0, (0, 1))],
+                            (n, c), L.F32)
+        dx = lp.pl.buf((c,), L.F32)
+        sp = fold_spec(op="+", init=0.0, mode="cell", cell_rank=1, dtype=L.F32, premap=prod, n_inputs=2)
+        lp.pl.plan.steps.append({"op": "fold", "spec": sp, "out": dx, "ins": [
+            lp.pl.view(lp.buf[wk], (c, n), 0, (1, c)), lp.pl.view(gzb, (c, n), 0, (0, 1))]})  # W^T, g_z per row
+        contrib.setdefault(wk, []).append(dw)
+        contrib.setdefault(xk, []).append(dx)
     for k in range(lp.n_params):
         shape = lp.shapes[k]
         if shape != ():
@@ -423,6 +482,12 @@ def value_and_grad_plan_from_hir(function: object):
             for i, (_, e, fshape) in enumerate(lp.folds):
                 if fshape == shape:
                     g = _add(g, _mul(adj[i], derivative(e, k)))
+            parts = contrib.get(k, [])
+            if _is(g, 0.0) and len(parts) == 1:
+                results.append(parts[0])
+                continue
+            for b in parts:
+                g = _add(g, InputExpr(lp.new_slot(shape, b)))
             results.append(lp.emit(g, shape))
         else:
             g = derivative(h, k)

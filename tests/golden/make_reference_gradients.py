@@ -76,7 +76,25 @@ PLAN_LOSSES = [
               "(fold + 0.0 (map (lambda (v) (* (- v c) (- v c))) row))) m)) 65536.0))", [(64, 1024), None]),
     # log (1 + sum exp y): the fold's init enters the loss non-linearly
     ("log_init", "(define/pi () (loss [y (Array Float 40)] Float) (log (fold + 1.0 (exp y))))", [(40,)]),
+    # a linear layer (examples/crater_train.py:38-44): rows of w times x
+    ("linear_mse", "def loss w x y = fold (+) 0.0 (map (\\r -> r * r) (map (-) "
+                   "(map (\\row -> fold (+) 0.0 (map (*) row x)) w) y))", [(48, 32), (32,), (48,)], "ml"),
+    ("linear_bias_mean", "def loss w x b y = (fold (+) 0.0 (map (\\r -> r * r) (map (-) (map (+) "
+                         "(map (\\row -> fold (+) 0.0 (map (*) row x)) w) b) y))) / 64.0",
+     [(64, 40), (40,), (64,), (64,)], "ml"),
+    ("linear_logistic", "def loss w x t = fold (+) 0.0 (map (\\z -> log (1.0 + exp (0.0 - z))) (map (*) t "
+                        "(map (\\row -> fold (+) 0.0 (map (*) row x)) w)))", [(30, 20), (20,), (30,)], "ml"),
 ]
+
+
+def specialise_ml(src: str, name: str, ptypes, rtype):
+    from remora.parser import parse_program
+    from remora.typechecker import TypeChecker
+    from remora.types import FuncType
+
+    ch = TypeChecker()
+    ch.check_program(parse_program(src))
+    return ch._typed_top_level_function(ch._functions[name], FuncType(tuple(ptypes), rtype), ch._build_prelude_env())
 
 
 def closed_log_init(y: np.ndarray) -> np.ndarray:
@@ -89,14 +107,15 @@ def plan_losses(rng) -> None:
     from remora_b200.autodiff import compile_value_and_grad_plan_source
 
     records, arrays = [], {}
-    for name, src, shapes in PLAN_LOSSES:
+    for name, src, shapes, *rest in PLAN_LOSSES:
+        syntax = rest[0] if rest else "lisp"
         ptypes = tuple(FLOAT if s is None else A(*s) for s in shapes)
-        plan = compile_value_and_grad_plan_source(src, "loss", ptypes)
+        plan = compile_value_and_grad_plan_source(src, "loss", ptypes, syntax=syntax)
         args = [np.float32(rng.uniform(0.5, 1.0)) if s is None else rng.uniform(-1.0, 1.0, s).astype(np.float32)
                 for s in shapes]
         if name == "logistic":
             args[3] = np.where(rng.random(300) < 0.5, -1.0, 1.0).astype(np.float32)
-        sp = specialise(src, "loss", list(ptypes), FLOAT)
+        sp = (specialise_ml if syntax == "ml" else specialise)(src, "loss", list(ptypes), FLOAT)
         tape, idx = trace_via_tape_multi(sp.body, [np.asarray(a, np.float64) for a in args], [p[0] for p in sp.params])
         adj = tape.reverse()
         grads = [np.asarray(adj[i], dtype=np.float64).reshape(np.shape(a)) for i, a in zip(idx, args)]
@@ -110,7 +129,8 @@ def plan_losses(rng) -> None:
         for k, a in enumerate(args):
             arrays[f"{name}__in{k}"] = np.asarray(a, np.float32)
             arrays[f"{name}__grad{k}"] = grads[k]
-        records.append({"name": name, "source": src, "shapes": [None if s is None else list(s) for s in shapes],
+        records.append({"name": name, "source": src, "syntax": syntax,
+                        "shapes": [None if s is None else list(s) for s in shapes],
                         "plan": plan.to_record(), "steps": [s["op"] for s in plan.steps]})
         print(name, [s["op"] for s in plan.steps])
     (HERE / "value_and_grad_plans.json").write_text(json.dumps(records, indent=1) + "\n")

@@ -153,6 +153,22 @@ def test_the_fixture_covers_scalars_ranks_and_several_folds():
     assert recs["two_shapes"]["steps"].count("fold") == 2
 
 
+def test_a_linear_layer_backward_is_an_outer_product_and_a_transposed_product():
+    """For loss = sum((W x - y)^2): the forward folds rows of W times x once;
+    dL/dW is one map over stride-0 views of the adjoint and of x, dL/dx one
+    cell fold over W's transposed view."""
+    from remora_b200.program_plan import Plan
+
+    rec = next(r for r in plan_records() if r["name"] == "linear_mse")
+    plan = Plan.from_record(rec["plan"])
+    w_grad, x_grad = plan.buffers[plan.results[1]], plan.buffers[plan.results[2]]
+    assert w_grad.shape == (48, 32) and x_grad.shape == (32,)
+    outer = next(s for s in plan.steps if s.get("out") == plan.results[1])
+    assert outer["op"] == "map" and [plan.buffers[i].view[2] for i in outer["ins"]] == [(1, 0), (0, 1)]
+    wt = next(s for s in plan.steps if s.get("out") == plan.results[2])
+    assert wt["op"] == "fold" and plan.buffers[wt["ins"][0]].view[2] == (1, 32)
+
+
 def test_the_reference_tape_drops_a_fold_init():
     """remora/ad.py:_trace_fold records sum(arr) as a fold's value, without
     its init: for log (fold + 1.0 (exp y)) its gradient is exp y / sum exp y
@@ -179,7 +195,8 @@ def test_planner_reproduces_recorded_value_and_grad_plans():
     for rec in plan_records():
         ptypes = tuple(FLOAT if s is None else ArrayType(FLOAT, tuple(StaticDim(d) for d in s))
                        for s in rec["shapes"])
-        assert compile_value_and_grad_plan_source(rec["source"], "loss", ptypes).to_record() == rec["plan"]
+        plan = compile_value_and_grad_plan_source(rec["source"], "loss", ptypes, syntax=rec.get("syntax", "lisp"))
+        assert plan.to_record() == rec["plan"], rec["name"]
 
 
 @pytest.mark.skipif(not __import__("os").path.isdir(__import__("os").environ.get(
