@@ -148,6 +148,9 @@ def _elementwise(node: object, env: dict[str, Expr], on_fold=None, on_cellmap=No
     k = _kind(node)
     if k == "HIRFold" and on_fold is not None:
         return on_fold(node, env)
+    if k == "HIRLet":
+        value = _elementwise(node.value, env, on_fold, on_cellmap)
+        return _elementwise(node.body, {**env, node.name: value}, on_fold, on_cellmap)
     if k == "HIRVar":
         if node.name not in env:
             raise RemoraUnsupportedError(f"autodiff: free variable {node.name}")
@@ -291,7 +294,9 @@ class _LossPlanner:
         self.n_params = len(params)
         self.env = {p.name: InputExpr(k) for k, p in enumerate(params)}
         self.folds: list[tuple[float, Expr, tuple[int, ...]]] = []  # (init, summand, shape)
-        self.matvec_slot: dict[tuple[int, int, float], int] = {}  # (W, x, init) -> slot of W x + init
+        # (W, x, init) -> (slot of W x + init, W's slot, x's slot), in forward order
+        self.matvec_slot: dict[tuple[int, str, float], tuple[int, int, int]] = {}
+        self.computed: dict[int, Expr] = {}  # slots of computed layer inputs -> their expression
 
     def new_slot(self, shape: tuple[int, ...], b: int) -> int:
         k = max(self.buf) + 1
@@ -348,17 +353,23 @@ class _LossPlanner:
         (other,) = match[0] - {f.params[0].name}
         x = env.get(other)
         n, c = self.shapes[w.index]
-        if not isinstance(x, InputExpr) or x.index >= self.n_params or self.shapes[x.index] != (c,):
-            raise RemoraUnsupportedError("autodiff: rows times a parameter vector of the row length")
-        key = (w.index, x.index, match[1])
+        if x is None or any(i < 0 or self.shapes[i] not in ((), (c,)) for i in _walk_inputs(x)):
+            raise RemoraUnsupportedError("autodiff: rows times a vector of the row length")
+        key = (w.index, repr(x), match[1])
         if key not in self.matvec_slot:
-            xv = self.pl.view(self.buf[x.index], (n, c), 0, (0, 1))  # x repeated for every row
+            if isinstance(x, InputExpr) and self.shapes[x.index] == (c,):
+                xs = x.index  # a parameter vector, or an earlier layer's output
+            else:
+                # a vector computed from parameters and earlier layers (h = relu(W1 x + b1))
+                xs = self.new_slot((c,), self.emit(x, (c,)))
+                self.computed[xs] = x
+            xv = self.pl.view(self.buf[xs], (n, c), 0, (0, 1))  # x repeated for every row
             sp = fold_spec(op="+", init=match[1], mode="cell", cell_rank=1, dtype=L.F32,
                            premap=BinaryExpr("*", InputExpr(0), InputExpr(1)), n_inputs=2)
             out = self.pl.buf((n,), L.F32)
             self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [self.buf[w.index], xv], "out": out})
-            self.matvec_slot[key] = self.new_slot((n,), out)
-        return InputExpr(self.matvec_slot[key])
+            self.matvec_slot[key] = (self.new_slot((n,), out), w.index, xs)
+        return InputExpr(self.matvec_slot[key][0])
 
     # ---- steps
     def emit(self, e: Expr, shape: tuple[int, ...]) -> int:
@@ -432,13 +443,17 @@ def value_and_grad_plan_from_hir(function: object):
     product of parameters, ``map (\\row -> dot row x) W`` (a linear layer,
     examples/crater_train.py:38-44): the forward computes it once, and its
     adjoint g reaches W as the outer product g x^T (one map over two
-    stride-0 views) and x as W^T g (one cell fold over W's transposed view).  ``plan.results`` lists the loss,
+    stride-0 views) and x as W^T g (one cell fold over W's transposed view).
+    x may itself be computed from parameters and earlier layers (a ``let``
+    of ``relu (W1 x + b1)``): the forward computes it once, and the backward
+    runs the layers last to first, passing W^T g through dx/d(inputs) to the
+    earlier layers and parameters (a two-layer perceptron).  ``plan.results`` lists the loss,
     then one gradient per parameter; run it with
     ``program_plan.execute_plan_results``."""
     lp = _LossPlanner(list(function.params))
     if _dims(function.return_type) != ():
         raise RemoraUnsupportedError("autodiff: the loss is a scalar")
-    h = _elementwise(function.body, lp.env, lp.on_fold)
+    h = _elementwise(function.body, lp.env, lp.on_fold, lp.on_cellmap)
     if not lp.folds:
         raise RemoraUnsupportedError("autodiff: the loss sums an array with fold (+)")
     for i in _walk_inputs(h):
@@ -456,12 +471,18 @@ def value_and_grad_plan_from_hir(function: object):
     adj = [derivative(h, fold_slot[-(i + 1)]) for i in range(len(lp.folds))]
     # matrix-vector products z = W x: their adjoint g_z flows on to W as the
     # outer product g_z x^T and to x as W^T g_z
-    contrib: dict[int, list[int]] = {}
-    for (wk, xk, _), z in lp.matvec_slot.items():
+    # Layers go last to first: a layer's adjoint is complete once every later
+    # layer that reads its output (through a computed input) has added to it.
+    contrib: dict[int, list[int]] = {}  # parameter slot -> gradient parts
+    later: dict[int, list[int]] = {}  # layer output slot -> adjoint parts from later layers
+    outputs = {z for z, _, _ in lp.matvec_slot.values()}
+    for z, wk, xk in reversed(list(lp.matvec_slot.values())):
         gz: Expr = _ZERO
         for i, (_, e, fshape) in enumerate(lp.folds):
             if fshape == lp.shapes[z]:
                 gz = _add(gz, _mul(adj[i], derivative(e, z)))
+        for b in later.get(z, []):
+            gz = _add(gz, InputExpr(lp.new_slot(lp.shapes[z], b)))
         if _is(gz, 0.0):
             continue
         gzb = lp.emit(gz, lp.shapes[z])
@@ -474,7 +495,21 @@ def value_and_grad_plan_from_hir(function: object):
         lp.pl.plan.steps.append({"op": "fold", "spec": sp, "out": dx, "ins": [
             lp.pl.view(lp.buf[wk], (c, n), 0, (1, c)), lp.pl.view(gzb, (c, n), 0, (0, 1))]})  # W^T, g_z per row
         contrib.setdefault(wk, []).append(dw)
-        contrib.setdefault(xk, []).append(dx)
+        if xk not in lp.computed:
+            contrib.setdefault(xk, []).append(dx)
+            continue
+        # a computed input x = X(...): its adjoint dx flows on through dX/dq
+        X, ds = lp.computed[xk], lp.new_slot((c,), dx)
+        for q in sorted(_walk_inputs(X)):
+            dq = _mul(InputExpr(ds), derivative(X, q))
+            if _is(dq, 0.0):
+                continue
+            if q in outputs:
+                later.setdefault(q, []).append(lp.emit(dq, (c,)))
+            elif lp.shapes[q] == ():
+                contrib.setdefault(q, []).append(lp.fold_sum(dq, (c,), 0.0))
+            else:
+                contrib.setdefault(q, []).append(lp.emit(dq, (c,)))
     for k in range(lp.n_params):
         shape = lp.shapes[k]
         if shape != ():
@@ -495,6 +530,8 @@ def value_and_grad_plan_from_hir(function: object):
                 de = derivative(e, k)
                 if not _is(de, 0.0):
                     g = _add(g, _mul(adj[i], InputExpr(lp.new_slot((), lp.fold_sum(de, fshape, 0.0)))))
+            for b in contrib.get(k, []):
+                g = _add(g, InputExpr(lp.new_slot((), b)))
             results.append(lp.emit(g, ()))
     lp.pl.plan.result = results[0]
     lp.pl.plan.results = results

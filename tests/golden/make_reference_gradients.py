@@ -84,6 +84,16 @@ PLAN_LOSSES = [
      [(64, 40), (40,), (64,), (64,)], "ml"),
     ("linear_logistic", "def loss w x t = fold (+) 0.0 (map (\\z -> log (1.0 + exp (0.0 - z))) (map (*) t "
                         "(map (\\row -> fold (+) 0.0 (map (*) row x)) w)))", [(30, 20), (20,), (30,)], "ml"),
+    # two layers: h = relu(W1 x + b1), loss = sum((W2 h - y)^2)
+    ("mlp_relu", "def loss w1 b1 w2 x y = let h = map (\\v -> if v < 0.0 then 0.0 else v) (map (+) "
+                 "(map (\\row -> fold (+) 0.0 (map (*) row x)) w1) b1) in fold (+) 0.0 (map (\\r -> r * r) "
+                 "(map (-) (map (\\row -> fold (+) 0.0 (map (*) row h)) w2) y))",
+     [(64, 32), (64,), (16, 64), (32,), (16,)], "ml"),
+    # two layers with a smooth activation scaled by a scalar parameter
+    ("mlp_scaled", "def loss w1 s w2 x = let h = map (\\v -> s * exp (0.0 - v * v)) "
+                   "(map (\\row -> fold (+) 0.0 (map (*) row x)) w1) in "
+                   "fold (+) 0.0 (map (\\r -> r * r) (map (\\row -> fold (+) 0.0 (map (*) row h)) w2))",
+     [(24, 16), None, (8, 24), (16,)], "ml"),
 ]
 
 
