@@ -297,6 +297,7 @@ class _LossPlanner:
         # (W, x, init) -> (slot of W x + init, W's slot, x's slot), in forward order
         self.matvec_slot: dict[tuple[int, str, float], tuple[int, int, int]] = {}
         self.computed: dict[int, Expr] = {}  # slots of computed layer inputs -> their expression
+        self.gemm_slot: dict[tuple[int, str, float], tuple[int, int, int]] = {}  # batched layers: (Z, W, X)
 
     def new_slot(self, shape: tuple[int, ...], b: int) -> int:
         k = max(self.buf) + 1
@@ -331,7 +332,7 @@ class _LossPlanner:
             if len(shapes) != 1:
                 raise RemoraUnsupportedError("autodiff: cell maps over arrays of one shape")
             shape = next(iter(shapes))
-            args = [_elementwise(a, env) for a in node.arrays]
+            args = [_elementwise(a, env, on_cellmap=self.on_cellmap) for a in node.arrays]
             e, _, extra = self.summand(inner.array, {**env, **{p.name: a for p, a in zip(f.params, args)}})
             cells = int(np.prod(shape[:len(shape) - len(node.cell_shape)], dtype=np.int64))
             return e, shape, cells * (float(inner.init.value) + extra)
@@ -345,6 +346,9 @@ class _LossPlanner:
         f = node.func
         if len(node.arrays) != 1 or _kind(f) != "HIRLambda" or len(f.params) != 1:
             raise RemoraUnsupportedError("autodiff: maps over cells other than rows times a vector")
+        batched = self._batched_layer(node, env)
+        if batched is not None:
+            return batched
         w = _elementwise(node.arrays[0], env)
         match = self.pl._match_dot(f.body)
         if not isinstance(w, InputExpr) or w.index >= self.n_params or len(self.shapes[w.index]) != 2 or \
@@ -370,6 +374,36 @@ class _LossPlanner:
             self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [self.buf[w.index], xv], "out": out})
             self.matvec_slot[key] = (self.new_slot((n,), out), w.index, xs)
         return InputExpr(self.matvec_slot[key][0])
+
+    def _batched_layer(self, node: object, env: dict) -> Expr | None:
+        """``map (\\xi -> map (\\row -> dot row xi) W) X``: every row of the
+        batch X [B, c] times W [n, c]'s rows, Z = X W^T [B, n], as one 3xTF32
+        GEMM step; None for any other cell map."""
+        f = node.func
+        inner, s = self.pl._resolve(f.body, {})
+        if isinstance(inner, tuple) or _kind(inner) not in ("HIRMap", "HIRApply") or len(inner.cell_shape) != 1 \
+                or len(inner.arrays) != 1 or _kind(inner.func) != "HIRLambda" or len(inner.func.params) != 1:
+            return None
+        match = self.pl._match_dot(inner.func.body)
+        if match is None or match[0] != {inner.func.params[0].name, f.params[0].name}:
+            return None
+        src, _ = self.pl._resolve(inner.arrays[0], s)
+        x, w = _elementwise(node.arrays[0], env), env.get(src[1]) if isinstance(src, tuple) else None
+        if not isinstance(x, InputExpr) or not isinstance(w, InputExpr) or max(x.index, w.index) >= self.n_params:
+            raise RemoraUnsupportedError("autodiff: a batch of parameter rows times a parameter matrix")
+        (b, c), (n, c2) = self.shapes[x.index], self.shapes[w.index]
+        if c != c2:
+            raise RemoraUnsupportedError("autodiff: rows of different lengths")
+        key = (w.index, f"batch {x.index}", match[1])
+        if key not in self.gemm_slot:
+            out = self.pl.buf((b, n), L.F32)
+            wt = self.pl.view(self.buf[w.index], (c, n), 0, (1, c))  # W^T
+            self.pl.plan.steps.append({"op": "gemm", "a": self.buf[x.index], "b": wt, "out": out,
+                                       "precision": L.PREC_3XTF32})
+            if match[1] != 0.0:
+                out = self.pl.emit_map(BinaryExpr("+", InputExpr(0), ConstantExpr(match[1])), [out], (b, n), L.F32)
+            self.gemm_slot[key] = (self.new_slot((b, n), out), w.index, x.index)
+        return InputExpr(self.gemm_slot[key][0])
 
     # ---- steps
     def emit(self, e: Expr, shape: tuple[int, ...]) -> int:
@@ -447,7 +481,10 @@ def value_and_grad_plan_from_hir(function: object):
     x may itself be computed from parameters and earlier layers (a ``let``
     of ``relu (W1 x + b1)``): the forward computes it once, and the backward
     runs the layers last to first, passing W^T g through dx/d(inputs) to the
-    earlier layers and parameters (a two-layer perceptron).  ``plan.results`` lists the loss,
+    earlier layers and parameters (a two-layer perceptron).  A batch of rows
+    through a layer, ``map (\\xi -> map (\\row -> dot row xi) W) X``, is
+    one 3xTF32 GEMM Z = X W^T forward and two backward, dW = G^T X and
+    dX = G W, on the tensor cores.  ``plan.results`` lists the loss,
     then one gradient per parameter; run it with
     ``program_plan.execute_plan_results``."""
     lp = _LossPlanner(list(function.params))
@@ -510,6 +547,22 @@ def value_and_grad_plan_from_hir(function: object):
                 contrib.setdefault(q, []).append(lp.fold_sum(dq, (c,), 0.0))
             else:
                 contrib.setdefault(q, []).append(lp.emit(dq, (c,)))
+    # batched layers Z = X W^T: dW = G^T X and dX = G W, two 3xTF32 GEMMs
+    for z, wk, xk in lp.gemm_slot.values():
+        gz = _ZERO
+        for i, (_, e, fshape) in enumerate(lp.folds):
+            if fshape == lp.shapes[z]:
+                gz = _add(gz, _mul(adj[i], derivative(e, z)))
+        if _is(gz, 0.0):
+            continue
+        gzb = lp.emit(gz, lp.shapes[z])
+        (b, n), c = lp.shapes[z], lp.shapes[wk][1]
+        dw, dx = lp.pl.buf((n, c), L.F32), lp.pl.buf((b, c), L.F32)
+        lp.pl.plan.steps.append({"op": "gemm", "a": lp.pl.view(gzb, (n, b), 0, (1, n)), "b": lp.buf[xk], "out": dw,
+                                 "precision": L.PREC_3XTF32})
+        lp.pl.plan.steps.append({"op": "gemm", "a": gzb, "b": lp.buf[wk], "out": dx, "precision": L.PREC_3XTF32})
+        contrib.setdefault(wk, []).append(dw)
+        contrib.setdefault(xk, []).append(dx)
     for k in range(lp.n_params):
         shape = lp.shapes[k]
         if shape != ():

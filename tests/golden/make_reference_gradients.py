@@ -94,7 +94,34 @@ PLAN_LOSSES = [
                    "(map (\\row -> fold (+) 0.0 (map (*) row x)) w1) in "
                    "fold (+) 0.0 (map (\\r -> r * r) (map (\\row -> fold (+) 0.0 (map (*) row h)) w2))",
      [(24, 16), None, (8, 24), (16,)], "ml"),
+    # a batch of rows through a layer: Z = X W^T, summed over both axes
+    ("batched_linear", "def loss w x y = fold (+) 0.0 (map (\\r -> fold (+) 0.0 (map (\\v -> v * v) r)) "
+                       "(map (-) (map (\\xi -> map (\\row -> fold (+) 0.0 (map (*) row xi)) w) x) y))",
+     [(48, 32), (64, 32), (64, 48)], "ml"),
+    ("batched_relu", "def loss w x y = fold (+) 0.0 (map (\\r -> fold (+) 0.0 (map (\\v -> v * v) r)) "
+                     "(map (-) (map (\\v -> if v < 0.0 then 0.0 else v) "
+                     "(map (\\xi -> map (\\row -> fold (+) 0.0 (map (*) row xi)) w) x)) y))",
+     [(40, 24), (72, 24), (72, 40)], "ml"),
 ]
+
+
+def closed_batched(name: str, args: list[np.ndarray]) -> list[np.ndarray]:
+    """Gradients of the batched-layer losses.  The reference's tape cannot
+    trace a map nested in a map over another array (remora/ad.py broadcasts
+    the two operands of the inner product against each other), so these
+    come from the derivative: Z = X W^T, G = dL/dZ, dW = G^T X, dX = G W."""
+    w, x, y = (np.asarray(a, np.float64) for a in args)
+    z = x @ w.T
+    if name == "batched_relu":
+        r = np.maximum(z, 0.0) - y
+        g = 2.0 * r * (z > 0.0)
+    else:
+        r = z - y
+        g = 2.0 * r
+    return [g.T @ x, g @ w, -2.0 * r]
+
+
+CLOSED = {"batched_linear": closed_batched, "batched_relu": closed_batched}
 
 
 def specialise_ml(src: str, name: str, ptypes, rtype):
@@ -126,9 +153,13 @@ def plan_losses(rng) -> None:
         if name == "logistic":
             args[3] = np.where(rng.random(300) < 0.5, -1.0, 1.0).astype(np.float32)
         sp = (specialise_ml if syntax == "ml" else specialise)(src, "loss", list(ptypes), FLOAT)
-        tape, idx = trace_via_tape_multi(sp.body, [np.asarray(a, np.float64) for a in args], [p[0] for p in sp.params])
-        adj = tape.reverse()
-        grads = [np.asarray(adj[i], dtype=np.float64).reshape(np.shape(a)) for i, a in zip(idx, args)]
+        if name in CLOSED:
+            grads = CLOSED[name](name, args)
+        else:
+            tape, idx = trace_via_tape_multi(sp.body, [np.asarray(a, np.float64) for a in args],
+                                             [p[0] for p in sp.params])
+            adj = tape.reverse()
+            grads = [np.asarray(adj[i], dtype=np.float64).reshape(np.shape(a)) for i, a in zip(idx, args)]
         if name == "log_init":
             # remora/ad.py:_trace_fold records a fold's value without its
             # init, so the tape's gradient here is exp y / sum exp y; the
@@ -139,6 +170,8 @@ def plan_losses(rng) -> None:
         for k, a in enumerate(args):
             arrays[f"{name}__in{k}"] = np.asarray(a, np.float32)
             arrays[f"{name}__grad{k}"] = grads[k]
+        if name in CLOSED:
+            arrays[f"{name}__closed_form"] = np.asarray(1)  # gradients from the derivative, not the tape
         records.append({"name": name, "source": src, "syntax": syntax,
                         "shapes": [None if s is None else list(s) for s in shapes],
                         "plan": plan.to_record(), "steps": [s["op"] for s in plan.steps]})

@@ -130,6 +130,10 @@ def check_value_and_grads(rec, got: list[np.ndarray]) -> None:
         assert g.shape == want.shape
         if shape is None:
             assert float(g) == pytest.approx(float(want), rel=1e-4, abs=1e-6)
+        elif "gemm" in rec["steps"]:
+            # a batched layer's products run as 3xTF32 GEMMs on the device:
+            # the 3xTF32 GEMM tolerance
+            np.testing.assert_allclose(g, want, rtol=1e-4, atol=1e-4 * float(np.abs(want).max()))
         else:
             np.testing.assert_allclose(g, want, rtol=1e-5, atol=1e-6 * float(np.abs(want).max()))
 
@@ -151,6 +155,17 @@ def test_the_fixture_covers_scalars_ranks_and_several_folds():
     assert any(None in r["shapes"] for r in recs.values())
     assert {len(s) for r in recs.values() for s in r["shapes"] if s} == {1, 2, 3}
     assert recs["two_shapes"]["steps"].count("fold") == 2
+
+
+def test_a_batched_layer_is_one_gemm_forward_and_two_backward():
+    """Z = X W^T forward; dW = G^T X and dX = G W backward.  The reference's
+    tape cannot trace these nested maps, so the fixture's gradients are the
+    derivative's closed form (marked in the fixture); the value is the
+    reference interpreter's."""
+    recs = {r["name"]: r for r in plan_records()}
+    a = plan_arrays()
+    for name in ("batched_linear", "batched_relu"):
+        assert recs[name]["steps"].count("gemm") == 3 and f"{name}__closed_form" in a
 
 
 def test_a_linear_layer_backward_is_an_outer_product_and_a_transposed_product():
