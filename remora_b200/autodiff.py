@@ -273,10 +273,12 @@ class _LossPlanner:
     """Builds the plan of ``value_and_grad_plan_from_hir``.
 
     Slots number the scalar values and arrays an expression may read:
-    0..P-1 are the parameters, then one slot per fold of the loss (its
-    value, a rank-0 buffer), then one per partial sum the scalar
-    parameters' gradients need.  Every Expr here is over slots; each map
-    or fold step renumbers the slots it reads to its own inputs."""
+    0..P-1 are the parameters; the rest are added as the plan grows: the
+    value of each fold of the loss (a rank-0 buffer), each layer's output
+    (W x, or X W^T for a batch) and computed layer input, and each adjoint
+    part or partial sum the backward needs.  Every Expr here is over
+    slots; each map or fold step renumbers the slots it reads to its own
+    inputs."""
 
     def __init__(self, params: list) -> None:
         from remora_b200.program_plan import _Planner
