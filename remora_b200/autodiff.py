@@ -296,10 +296,10 @@ class _LossPlanner:
         self.n_params = len(params)
         self.env = {p.name: InputExpr(k) for k, p in enumerate(params)}
         self.folds: list[tuple[float, Expr, tuple[int, ...]]] = []  # (init, summand, shape)
-        # (W, x, init) -> (slot of W x + init, W's slot, x's slot), in forward order
-        self.matvec_slot: dict[tuple[int, str, float], tuple[int, int, int]] = {}
+        # dense layers in forward order: (W, x, init) -> (kind, output slot,
+        # W's slot, input's slot); kind "vec" for W x, "batch" for X W^T
+        self.layers: dict[tuple, tuple[str, int, int, int]] = {}
         self.computed: dict[int, Expr] = {}  # slots of computed layer inputs -> their expression
-        self.gemm_slot: dict[tuple[int, str, float], tuple[int, int, int]] = {}  # batched layers: (Z, W, X)
 
     def new_slot(self, shape: tuple[int, ...], b: int) -> int:
         k = max(self.buf) + 1
@@ -361,8 +361,8 @@ class _LossPlanner:
         n, c = self.shapes[w.index]
         if x is None or any(i < 0 or self.shapes[i] not in ((), (c,)) for i in _walk_inputs(x)):
             raise RemoraUnsupportedError("autodiff: rows times a vector of the row length")
-        key = (w.index, repr(x), match[1])
-        if key not in self.matvec_slot:
+        key = ("vec", w.index, repr(x), match[1])
+        if key not in self.layers:
             if isinstance(x, InputExpr) and self.shapes[x.index] == (c,):
                 xs = x.index  # a parameter vector, or an earlier layer's output
             else:
@@ -374,8 +374,8 @@ class _LossPlanner:
                            premap=BinaryExpr("*", InputExpr(0), InputExpr(1)), n_inputs=2)
             out = self.pl.buf((n,), L.F32)
             self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [self.buf[w.index], xv], "out": out})
-            self.matvec_slot[key] = (self.new_slot((n,), out), w.index, xs)
-        return InputExpr(self.matvec_slot[key][0])
+            self.layers[key] = ("vec", self.new_slot((n,), out), w.index, xs)
+        return InputExpr(self.layers[key][1])
 
     def _batched_layer(self, node: object, env: dict) -> Expr | None:
         """``map (\\xi -> map (\\row -> dot row xi) W) X``: every row of the
@@ -391,21 +391,29 @@ class _LossPlanner:
             return None
         src, _ = self.pl._resolve(inner.arrays[0], s)
         x, w = _elementwise(node.arrays[0], env), env.get(src[1]) if isinstance(src, tuple) else None
-        if not isinstance(x, InputExpr) or not isinstance(w, InputExpr) or max(x.index, w.index) >= self.n_params:
-            raise RemoraUnsupportedError("autodiff: a batch of parameter rows times a parameter matrix")
-        (b, c), (n, c2) = self.shapes[x.index], self.shapes[w.index]
-        if c != c2:
-            raise RemoraUnsupportedError("autodiff: rows of different lengths")
-        key = (w.index, f"batch {x.index}", match[1])
-        if key not in self.gemm_slot:
+        if not isinstance(w, InputExpr) or w.index >= self.n_params or len(self.shapes[w.index]) != 2:
+            raise RemoraUnsupportedError("autodiff: a batch of rows times a parameter matrix")
+        xshape = _dims(_type_of(node.arrays[0]))
+        (n, c) = self.shapes[w.index]
+        if len(xshape) != 2 or xshape[1] != c or \
+                any(i < 0 or self.shapes[i] not in ((), xshape) for i in _walk_inputs(x)):
+            raise RemoraUnsupportedError("autodiff: a batch of rows of the layer's row length")
+        b = xshape[0]
+        key = ("batch", w.index, repr(x), match[1])
+        if key not in self.layers:
+            if isinstance(x, InputExpr) and self.shapes[x.index] == xshape:
+                xs = x.index  # a parameter batch, or an earlier layer's output
+            else:
+                xs = self.new_slot(xshape, self.emit(x, xshape))  # computed (H = relu(X W1^T))
+                self.computed[xs] = x
             out = self.pl.buf((b, n), L.F32)
             wt = self.pl.view(self.buf[w.index], (c, n), 0, (1, c))  # W^T
-            self.pl.plan.steps.append({"op": "gemm", "a": self.buf[x.index], "b": wt, "out": out,
+            self.pl.plan.steps.append({"op": "gemm", "a": self.buf[xs], "b": wt, "out": out,
                                        "precision": L.PREC_3XTF32})
             if match[1] != 0.0:
                 out = self.pl.emit_map(BinaryExpr("+", InputExpr(0), ConstantExpr(match[1])), [out], (b, n), L.F32)
-            self.gemm_slot[key] = (self.new_slot((b, n), out), w.index, x.index)
-        return InputExpr(self.gemm_slot[key][0])
+            self.layers[key] = ("batch", self.new_slot((b, n), out), w.index, xs)
+        return InputExpr(self.layers[key][1])
 
     # ---- steps
     def emit(self, e: Expr, shape: tuple[int, ...]) -> int:
@@ -508,63 +516,58 @@ def value_and_grad_plan_from_hir(function: object):
     h = _substitute(h, {**fold_slot, **{k: k for k in range(lp.n_params)}})
     results = [lp.buf[next(iter(_walk_inputs(h)))] if isinstance(h, InputExpr) else lp.emit(h, ())]
     adj = [derivative(h, fold_slot[-(i + 1)]) for i in range(len(lp.folds))]
-    # matrix-vector products z = W x: their adjoint g_z flows on to W as the
-    # outer product g_z x^T and to x as W^T g_z
-    # Layers go last to first: a layer's adjoint is complete once every later
-    # layer that reads its output (through a computed input) has added to it.
+    # Dense layers go last to first: a layer's adjoint g is complete once
+    # every later layer that reads its output (through a computed input) has
+    # added to it.  W x: g reaches W as the outer product g x^T and x as
+    # W^T g; X W^T: dW = g^T X and dX = g W, two 3xTF32 GEMMs.
     contrib: dict[int, list[int]] = {}  # parameter slot -> gradient parts
     later: dict[int, list[int]] = {}  # layer output slot -> adjoint parts from later layers
-    outputs = {z for z, _, _ in lp.matvec_slot.values()}
-    for z, wk, xk in reversed(list(lp.matvec_slot.values())):
+    outputs = {z for _, z, _, _ in lp.layers.values()}
+    prod = BinaryExpr("*", InputExpr(0), InputExpr(1))
+    for kind, z, wk, xk in reversed(list(lp.layers.values())):
         gz: Expr = _ZERO
         for i, (_, e, fshape) in enumerate(lp.folds):
             if fshape == lp.shapes[z]:
                 gz = _add(gz, _mul(adj[i], derivative(e, z)))
-        for b in later.get(z, []):
-            gz = _add(gz, InputExpr(lp.new_slot(lp.shapes[z], b)))
+        for part in later.get(z, []):
+            gz = _add(gz, InputExpr(lp.new_slot(lp.shapes[z], part)))
         if _is(gz, 0.0):
             continue
-        gzb = lp.emit(gz, lp.shapes[z])
+        # a single part handed on by a later layer is already a buffer
+        single = isinstance(gz, InputExpr) and lp.shapes[gz.index] == lp.shapes[z]
+        gzb = lp.buf[gz.index] if single else lp.emit(gz, lp.shapes[z])
         n, c = lp.shapes[wk]
-        prod = BinaryExpr("*", InputExpr(0), InputExpr(1))
-        dw = lp.pl.emit_map(prod, [lp.pl.view(gzb, (n, c), 0, (1, 0)), lp.pl.view(lp.buf[xk], (n, c), 0, (0, 1))],
-                            (n, c), L.F32)
-        dx = lp.pl.buf((c,), L.F32)
-        sp = fold_spec(op="+", init=0.0, mode="cell", cell_rank=1, dtype=L.F32, premap=prod, n_inputs=2)
-        lp.pl.plan.steps.append({"op": "fold", "spec": sp, "out": dx, "ins": [
-            lp.pl.view(lp.buf[wk], (c, n), 0, (1, c)), lp.pl.view(gzb, (c, n), 0, (0, 1))]})  # W^T, g_z per row
+        xshape = lp.shapes[xk]
+        dx = lp.pl.buf(xshape, L.F32)
+        if kind == "vec":
+            dw = lp.pl.emit_map(prod, [lp.pl.view(gzb, (n, c), 0, (1, 0)), lp.pl.view(lp.buf[xk], (n, c), 0, (0, 1))],
+                                (n, c), L.F32)
+            sp = fold_spec(op="+", init=0.0, mode="cell", cell_rank=1, dtype=L.F32, premap=prod, n_inputs=2)
+            lp.pl.plan.steps.append({"op": "fold", "spec": sp, "out": dx, "ins": [
+                lp.pl.view(lp.buf[wk], (c, n), 0, (1, c)), lp.pl.view(gzb, (c, n), 0, (0, 1))]})  # W^T, g per row
+        else:
+            b = xshape[0]
+            dw = lp.pl.buf((n, c), L.F32)
+            lp.pl.plan.steps.append({"op": "gemm", "a": lp.pl.view(gzb, (n, b), 0, (1, n)), "b": lp.buf[xk],
+                                     "out": dw, "precision": L.PREC_3XTF32})
+            lp.pl.plan.steps.append({"op": "gemm", "a": gzb, "b": lp.buf[wk], "out": dx,
+                                     "precision": L.PREC_3XTF32})
         contrib.setdefault(wk, []).append(dw)
         if xk not in lp.computed:
             contrib.setdefault(xk, []).append(dx)
             continue
         # a computed input x = X(...): its adjoint dx flows on through dX/dq
-        X, ds = lp.computed[xk], lp.new_slot((c,), dx)
+        X, ds = lp.computed[xk], lp.new_slot(xshape, dx)
         for q in sorted(_walk_inputs(X)):
             dq = _mul(InputExpr(ds), derivative(X, q))
             if _is(dq, 0.0):
                 continue
             if q in outputs:
-                later.setdefault(q, []).append(lp.emit(dq, (c,)))
+                later.setdefault(q, []).append(lp.emit(dq, xshape))
             elif lp.shapes[q] == ():
-                contrib.setdefault(q, []).append(lp.fold_sum(dq, (c,), 0.0))
+                contrib.setdefault(q, []).append(lp.fold_sum(dq, xshape, 0.0))
             else:
-                contrib.setdefault(q, []).append(lp.emit(dq, (c,)))
-    # batched layers Z = X W^T: dW = G^T X and dX = G W, two 3xTF32 GEMMs
-    for z, wk, xk in lp.gemm_slot.values():
-        gz = _ZERO
-        for i, (_, e, fshape) in enumerate(lp.folds):
-            if fshape == lp.shapes[z]:
-                gz = _add(gz, _mul(adj[i], derivative(e, z)))
-        if _is(gz, 0.0):
-            continue
-        gzb = lp.emit(gz, lp.shapes[z])
-        (b, n), c = lp.shapes[z], lp.shapes[wk][1]
-        dw, dx = lp.pl.buf((n, c), L.F32), lp.pl.buf((b, c), L.F32)
-        lp.pl.plan.steps.append({"op": "gemm", "a": lp.pl.view(gzb, (n, b), 0, (1, n)), "b": lp.buf[xk], "out": dw,
-                                 "precision": L.PREC_3XTF32})
-        lp.pl.plan.steps.append({"op": "gemm", "a": gzb, "b": lp.buf[wk], "out": dx, "precision": L.PREC_3XTF32})
-        contrib.setdefault(wk, []).append(dw)
-        contrib.setdefault(xk, []).append(dx)
+                contrib.setdefault(q, []).append(lp.emit(dq, xshape))
     for k in range(lp.n_params):
         shape = lp.shapes[k]
         if shape != ():

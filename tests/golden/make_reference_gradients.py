@@ -102,6 +102,12 @@ PLAN_LOSSES = [
                      "(map (-) (map (\\v -> if v < 0.0 then 0.0 else v) "
                      "(map (\\xi -> map (\\row -> fold (+) 0.0 (map (*) row xi)) w) x)) y))",
      [(40, 24), (72, 24), (72, 40)], "ml"),
+    # a batch through two layers: H = relu(X W1^T), Z = H W2^T
+    ("batched_mlp", "def loss w1 w2 x y = let h = map (\\v -> if v < 0.0 then 0.0 else v) "
+                    "(map (\\xi -> map (\\row -> fold (+) 0.0 (map (*) row xi)) w1) x) in "
+                    "fold (+) 0.0 (map (\\r -> fold (+) 0.0 (map (\\v -> v * v) r)) "
+                    "(map (-) (map (\\hi -> map (\\row -> fold (+) 0.0 (map (*) row hi)) w2) h) y))",
+     [(32, 16), (8, 32), (48, 16), (48, 8)], "ml"),
 ]
 
 
@@ -121,7 +127,18 @@ def closed_batched(name: str, args: list[np.ndarray]) -> list[np.ndarray]:
     return [g.T @ x, g @ w, -2.0 * r]
 
 
-CLOSED = {"batched_linear": closed_batched, "batched_relu": closed_batched}
+def closed_batched_mlp(name: str, args: list[np.ndarray]) -> list[np.ndarray]:
+    """H = relu(X W1^T), Z = H W2^T, loss = sum((Z - Y)^2)."""
+    w1, w2, x, y = (np.asarray(a, np.float64) for a in args)
+    a1 = x @ w1.T
+    h = np.maximum(a1, 0.0)
+    r = h @ w2.T - y
+    g2 = 2.0 * r
+    g1 = (g2 @ w2) * (a1 > 0.0)
+    return [g1.T @ x, g2.T @ h, g1 @ w1, -2.0 * r]
+
+
+CLOSED = {"batched_linear": closed_batched, "batched_relu": closed_batched, "batched_mlp": closed_batched_mlp}
 
 
 def specialise_ml(src: str, name: str, ptypes, rtype):

@@ -166,6 +166,8 @@ def test_a_batched_layer_is_one_gemm_forward_and_two_backward():
     a = plan_arrays()
     for name in ("batched_linear", "batched_relu"):
         assert recs[name]["steps"].count("gemm") == 3 and f"{name}__closed_form" in a
+    # two layers: two GEMMs forward, four backward (dW2, dH, dW1, dX)
+    assert recs["batched_mlp"]["steps"].count("gemm") == 6 and "batched_mlp__closed_form" in a
 
 
 def test_a_linear_layer_backward_is_an_outer_product_and_a_transposed_product():
