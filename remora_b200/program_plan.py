@@ -629,10 +629,10 @@ class _Planner:
         map's body (an index at plan-time positions, or a fold), else None."""
         k = _kind(node)
         arr = getattr(node, "array", None)
-        if k not in ("HIRIndex", "HIRFold") or _kind(arr) != "HIRVar" or env.get(arr.name, ("",))[0] != "cell":
-            return None
         if k == "HIRFold":
-            return self.cell_fold(node, env)
+            return self.cell_fold(node, env) if self._cell_of(arr, env)[0] is not None else None
+        if k != "HIRIndex" or _kind(arr) != "HIRVar" or env.get(arr.name, ("",))[0] != "cell":
+            return None
         _, b, cell_rank = env[arr.name]
         shape = self.shape_of(b)
         fr = len(shape) - cell_rank
@@ -650,17 +650,43 @@ class _Planner:
             off += i * st[fr + d]
         return self.view(b, shape[:fr], off, st[:fr])
 
+    def _cell_of(self, node: object, env: dict) -> tuple[tuple | None, Expr | None]:
+        """(cell, premap) for the array a cell fold folds: the cell parameter
+        itself (premap None), or an elementwise map over it alone
+        (``map (\\v -> v * v) row``), whose function becomes the fold's
+        premap; (None, None) for anything else."""
+        k = _kind(node)
+        if k == "HIRVar":
+            cell = env.get(node.name)
+            return (cell, None) if cell is not None and cell[0] == "cell" else (None, None)
+        if k not in ("HIRMap", "HIRApply") or node.cell_shape or not node.arrays or \
+                any(_kind(a) != "HIRVar" or env.get(a.name, ("",))[0] != "cell" for a in node.arrays) or \
+                len({env[a.name][1] for a in node.arrays}) != 1:
+            return None, None
+        cell = env[node.arrays[0].name]
+        code = self.code_of(cell[1])
+        if code == L.BOOL:
+            raise _unsupported("a fold of a map over a bool cell")
+        operands: list[int] = []
+        e = self.apply_func(node.func, env, [(InputExpr(0), code)] * len(node.arrays), operands,
+                            _elem(node.result_type))
+        if operands:
+            raise _unsupported("a map inside a cell fold that reads more than its cell")
+        return cell, e
+
     def cell_fold(self, body: object, env: dict) -> int:
-        """A fold of a cell parameter: one cell-fold step over the whole array."""
+        """A fold of a cell parameter, or of an elementwise map over it: one
+        cell-fold step over the whole array (the map fused as its premap)."""
         op, init, code = self.fold_op(body, env)
-        cell = env.get(getattr(body.array, "name", None)) if _kind(body.array) == "HIRVar" else None
-        if cell is None or cell[0] != "cell":
+        cell, premap = self._cell_of(body.array, env)
+        if cell is None:
             raise _unsupported("a cell fold folds its cell")
         if init[0] != "const" or op not in ("+", "*"):
             raise _unsupported("cell folds with + or * and a literal init")
         _, b, cell_rank = cell
         in_code = self.code_of(b)
-        premap = InputExpr(0) if in_code != code else None
+        if premap is None and in_code != code:
+            premap = InputExpr(0)
         sp = fold_spec(op=op, init=init[1], mode="cell", cell_rank=cell_rank, dtype=code, premap=premap,
                        premap_in_dtypes=[in_code] if premap is not None else None)
         shape = self.shape_of(b)

@@ -45,6 +45,10 @@ EXTRA = {
                        "ml"),
     "extra_row_span": ("let xs = reshape [4, 6] (map (\\v -> v * v - 3 * v) (iota 24)) in\n"
                        "map (\\row -> row[5] - row[0] + fold (+) 0 row) xs", "ml"),
+    "extra_row_sumsq": ("let xs = reshape [8, 16] (map (* 0.25) (iota 128)) in map (\\row -> fold (+) 0.0 (map (*) row row)) xs",
+                        "ml"),
+    "extra_row_meansq": ("let xs = reshape [8, 16] (map (* 0.25) (iota 128)) in\n"
+                         "map (\\row -> fold (+) 0.0 (map (*) row row) / 16.0) xs", "ml"),
     "extra_cell_index2": ("let m = reshape [3, 2, 2] (map (* 1.5) (iota 12)) in map (\\c -> c[1, 0] * 2.0 - c[0, 1]) m",
                           "ml"),
 }

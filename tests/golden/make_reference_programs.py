@@ -135,6 +135,12 @@ FUNCTION_PLANS = [
     ("mask_count", "lisp", """
 (define/pi () (f [t Float x (Array Float 64)] Int) (fold + 0 (map (lambda (v) (select (> v t) 1 0)) x)))
 """, "f", [("f", None), ("f", (64,))], "normal"),
+    # folds of a map over each row, the map fused into the fold: row sums of
+    # squares, and the thresholded chain of the chained-map benchmark
+    ("row_sumsq", "ml", "def rn x = map (\\row -> fold (+) 0.0 (map (\\v -> v * v) row)) x", "rn",
+     [("f", (64, 256))], "normal"),
+    ("chained_rows", "ml", "def ch x = map (\\row -> fold (+) 0.0 (map (\\v -> if 0.5 < v * 2.5 + 1.0 "
+                           "then v * 2.5 + 1.0 else 0.0) row)) x", "ch", [("f", (16, 32, 64))], "normal"),
     # lifted dot products, written as the prelude's dot a b = sum (map (*) a b)
     # inlined (stdlib/prelude.rem:11,14): rows times a vector, rows times rows
     ("matvec", "ml", "def mv m v = map (\\row -> fold (+) 0.0 (map (*) row v)) m", "mv",

@@ -103,8 +103,8 @@ def test_fixture_covers_the_acceptance_programs():
     progs = programs()
     names = {p["name"] for p in progs}
     # 44 of the reference's 45 acceptance programs (one does not pass the
-    # reference's own front end) and 9 more
-    assert len(names) == 53
+    # reference's own front end) and 11 more
+    assert len(names) == 55
     ops = {op for p in progs for op in p["steps"]}
     assert ops == {"map", "fold", "array_fold", "scan", "append", "rotate", "sort", "grade"}
     for p in progs:
@@ -197,6 +197,14 @@ def test_the_preludes_dot_plans_like_its_inlined_form(name, with_dot):
     ptypes = tuple(ArrayType(FLOAT, tuple(StaticDim(x) for x in d)) for _, d in rec["params"])
     plan = compile_function_source_to_plan(with_dot, rec["function"], ptypes)
     assert plan.to_record() == rec["plan"]
+
+
+def test_a_fold_of_a_mapped_row_is_one_fused_fold():
+    recs = {r["name"]: r for r in function_records()}
+    for name in ("row_sumsq", "chained_rows"):
+        plan = Plan.from_record(recs[name]["plan"])
+        (step,) = plan.steps
+        assert step["op"] == "fold" and step["spec"].has_premap and step["spec"].cell_rank == 1
 
 
 def test_lifted_dots_become_one_fold_or_one_gemm():
