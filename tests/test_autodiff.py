@@ -9,6 +9,8 @@ from __future__ import annotations
 
 import json
 import math
+import os
+import sys
 
 import numpy as np
 import pytest
@@ -19,6 +21,11 @@ from remora_b200.autodiff import derivative
 from remora_b200.codegen import spec_from_record
 from remora_b200.errors import RemoraUnsupportedError
 from remora_b200.program import BinaryExpr, CmpExpr, ConstantExpr, InputExpr, SelectExpr, UnaryExpr
+
+
+REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
+needs_ref = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "remora")),
+                               reason="the reference front end is not importable here")
 
 
 def records():
@@ -198,13 +205,9 @@ def test_the_reference_tape_drops_a_fold_init():
     np.testing.assert_allclose(a["log_init__grad0"], e / (1.0 + e.sum()), rtol=1e-12)
 
 
-@pytest.mark.skipif(not __import__("os").path.isdir(__import__("os").environ.get(
-    "REMORA_REFERENCE", "/root/reference") + "/remora"), reason="the reference front end is not importable here")
+@needs_ref
 def test_planner_reproduces_recorded_value_and_grad_plans():
-    import os
-    import sys
-
-    sys.path.insert(0, os.environ.get("REMORA_REFERENCE", "/root/reference"))
+    sys.path.insert(0, REF)
     from remora.types import FLOAT, ArrayType, StaticDim
 
     from remora_b200.autodiff import compile_value_and_grad_plan_source
@@ -216,8 +219,7 @@ def test_planner_reproduces_recorded_value_and_grad_plans():
         assert plan.to_record() == rec["plan"], rec["name"]
 
 
-@pytest.mark.skipif(not __import__("os").path.isdir(__import__("os").environ.get(
-    "REMORA_REFERENCE", "/root/reference") + "/remora"), reason="the reference front end is not importable here")
+@needs_ref
 @pytest.mark.parametrize("src, shapes", [
     # an array parameter outside the folds
     ("(define/pi () (loss [x (Array Float 4)] Float) (+ (fold + 0.0 x) (index x 0)))", [(4,)]),
@@ -229,10 +231,7 @@ def test_planner_reproduces_recorded_value_and_grad_plans():
     ("(define/pi () (loss [w Float] Float) (* w w))", [None]),
 ])
 def test_unsupported_losses_raise(src, shapes):
-    import os
-    import sys
-
-    sys.path.insert(0, os.environ.get("REMORA_REFERENCE", "/root/reference"))
+    sys.path.insert(0, REF)
     from remora.types import FLOAT, INT, ArrayType, StaticDim
 
     from remora_b200.autodiff import compile_value_and_grad_plan_source

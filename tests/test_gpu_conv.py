@@ -1,7 +1,7 @@
 """GPU parity of the NCHW convolution and its reverse mode.
 
 TF32 tensor-core results (3x3 / pad 1 / stride 1 shapes) are held to the
-north_star tolerance for TF32 conv and gradients, rtol 1e-3 + atol
+TF32 tolerance for convolutions and their gradients, rtol 1e-3 + atol
 1e-3 * max|ref|, against the oracle; 3xTF32 (the same tensor-core kernels
 with hi/lo split operands) and the direct path (other shapes, computing in
 the oracle's order) are held to rtol 1e-5 + atol 1e-5 * max|ref|."""

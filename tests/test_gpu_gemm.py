@@ -1,7 +1,7 @@
 """GPU parity of the tcgen05 dense core (matmul as the lifted dot).
 
 Every result is checked against the oracle's sequential-k f32 lifted dot at
-the north_star tolerance for TF32 GEMMs (rtol 1e-3 + atol 1e-3 * max|ref|).
+the TF32 GEMM tolerance (rtol 1e-3 + atol 1e-3 * max|ref|).
 3xTF32 is also held to the exact (f64) product at rtol 1e-5 + atol
 1e-4 * max|ref| (measured worst case 3.1e-5 * max|ref| at K = 4096, from the
 tensor core's f32 accumulation): ten times inside the TF32 bound."""
