@@ -29,6 +29,7 @@ built where the reference compiler is importable can be run where it is not.
 from __future__ import annotations
 
 import ctypes
+import dataclasses
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -785,6 +786,102 @@ def plan_from_hir(program: object) -> Plan:
     return pl.plan
 
 
+# ------------------------------------------------- let inlining (functions)
+def _is_node(v: object) -> bool:
+    return dataclasses.is_dataclass(v) and not isinstance(v, type) and type(v).__name__.startswith("HIR")
+
+
+def _fields(node: object):
+    """(field name, value) of the fields of a HIR node that hold nodes or lists of nodes."""
+    for f in dataclasses.fields(node):
+        v = getattr(node, f.name)
+        if _is_node(v) or (isinstance(v, list) and any(_is_node(x) for x in v)):
+            yield f.name, v
+
+
+def _free(node: object) -> set[str]:
+    """Names read by ``node`` that it does not bind itself."""
+    k = _kind(node)
+    if k == "HIRVar":
+        return {node.name}
+    if k == "HIRLet":
+        return _free(node.value) | (_free(node.body) - {node.name})
+    if k == "HIRLambda":
+        return _free(node.body) - {p.name for p in node.params}
+    out: set[str] = set()
+    for _, v in _fields(node):
+        for x in (v if isinstance(v, list) else [v]):
+            if _is_node(x):
+                out |= _free(x)
+    return out
+
+
+def _uses(node: object, name: str) -> int:
+    k = _kind(node)
+    if k == "HIRVar":
+        return int(node.name == name)
+    if k == "HIRLet":
+        return _uses(node.value, name) + (0 if node.name == name else _uses(node.body, name))
+    if k == "HIRLambda" and name in {p.name for p in node.params}:
+        return 0
+    return sum(_uses(x, name) for _, v in _fields(node) for x in (v if isinstance(v, list) else [v]) if _is_node(x))
+
+
+def _substitute_name(node: object, name: str, value: object, value_free: set[str]) -> object | None:
+    """``node`` with the free uses of ``name`` replaced by ``value``; None
+    where a binder on the way would capture a name ``value`` reads."""
+    k = _kind(node)
+    if k == "HIRVar":
+        return value if node.name == name else node
+    if k in ("HIRLet", "HIRLambda"):
+        bound = {node.name} if k == "HIRLet" else {p.name for p in node.params}
+        changes = {}
+        if k == "HIRLet":
+            v = _substitute_name(node.value, name, value, value_free)
+            if v is None:
+                return None
+            changes["value"] = v
+        if name not in bound and _uses(node.body, name):
+            if bound & value_free:
+                return None
+            b = _substitute_name(node.body, name, value, value_free)
+            if b is None:
+                return None
+            changes["body"] = b
+        return dataclasses.replace(node, **changes) if changes else node
+    changes = {}
+    for fname, v in _fields(node):
+        if isinstance(v, list):
+            new = [(_substitute_name(x, name, value, value_free) if _is_node(x) else x) for x in v]
+            if any(x is None for x in new):
+                return None
+            changes[fname] = new
+        else:
+            new = _substitute_name(v, name, value, value_free)
+            if new is None:
+                return None
+            changes[fname] = new
+    return dataclasses.replace(node, **changes) if changes else node
+
+
+def _inline_lets(node: object) -> object:
+    """The front end inlines called functions (the prelude's ``sum``,
+    ``dot``) as chains of lets binding their parameters.  A let whose value
+    is a plain name, or whose name is read once, is substituted into its
+    body (unless a lambda on the way rebinds a name the value reads), so
+    ``let xs = row in fold (+) 0.0 xs`` plans like ``fold (+) 0.0 row``."""
+    changes = {}
+    for fname, v in _fields(node):
+        changes[fname] = [(_inline_lets(x) if _is_node(x) else x) for x in v] if isinstance(v, list) \
+            else _inline_lets(v)
+    node = dataclasses.replace(node, **changes) if changes else node
+    if _kind(node) == "HIRLet" and (_kind(node.value) == "HIRVar" or _uses(node.body, node.name) <= 1):
+        inlined = _substitute_name(node.body, node.name, node.value, _free(node.value))
+        if inlined is not None:
+            return inlined
+    return node
+
+
 def plan_from_function(function: object, functions: dict[str, Any] | None = None) -> Plan:
     """A plan for one of the reference's HIR functions (``HIRFunction``, as
     remora/compiler.py:compile_function_source builds it): parameter k is
@@ -794,7 +891,7 @@ def plan_from_function(function: object, functions: dict[str, Any] | None = None
     env = {}
     for k, p in enumerate(function.params):
         env[p.name] = ("buf", pl.buf(_shape(p.type), _elem(p.type), input=k))
-    out = pl.as_buf(pl.lower(function.body, env))
+    out = pl.as_buf(pl.lower(_inline_lets(function.body), env))
     if pl.plan.buffers[out].view is not None or pl.plan.buffers[out].input is not None:
         out = pl.emit_map(InputExpr(0), [out], pl.shape_of(out), pl.code_of(out))
     pl.plan.result = out

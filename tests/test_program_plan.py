@@ -240,3 +240,38 @@ def test_planner_reproduces_recorded_function_plans():
                        for e, d in rec["params"])
         plan = compile_function_source_to_plan(rec["source"], rec["function"], ptypes, syntax=rec["syntax"])
         assert plan.to_record() == rec["plan"], rec["name"]
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+def test_prelude_functions_inside_cell_maps_plan_like_written_out_folds(oracle_mod):
+    """The front end inlines ``sum`` and ``dot`` as chains of lets; after
+    let inlining they plan exactly like the folds written out."""
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    rec = next(r for r in function_records() if r["name"] == "row_sumsq")
+    ptypes = (ArrayType(FLOAT, tuple(StaticDim(d) for d in rec["params"][0][1])),)
+    assert compile_function_source_to_plan("def rn x = map (\\row -> dot row row) x", "rn",
+                                           ptypes).to_record() == rec["plan"]
+    summed = compile_function_source_to_plan("def rs x = map (\\row -> sum row) x", "rs", ptypes)
+    written = compile_function_source_to_plan("def rs x = map (\\row -> fold (+) 0.0 row) x", "rs", ptypes)
+    assert summed.to_record() == written.to_record()
+    x = np.random.default_rng(3).standard_normal(rec["params"][0][1]).astype(np.float32)
+    close(run_plan_on_oracle(oracle_mod, summed, [x]), x.astype(np.float64).sum(axis=1).astype(np.float32))
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+def test_let_inlining_keeps_a_let_that_a_lambda_would_capture(oracle_mod):
+    """In ``let t = s in map (\\s -> s * t) v`` substituting t := s would
+    make the lambda's own s the factor; the let stays and t is the outer s."""
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    plan = compile_function_source_to_plan("def f s v = let t = s in map (\\s -> s * t) v", "f",
+                                           (FLOAT, ArrayType(FLOAT, (StaticDim(3),))))
+    got = run_plan_on_oracle(oracle_mod, plan, [np.float32(2.0), np.array([1.0, 2.0, 3.0], np.float32)])
+    np.testing.assert_array_equal(got, np.array([2.0, 4.0, 6.0], np.float32))
