@@ -597,8 +597,10 @@ def value_and_grad_plan_from_hir(function: object):
 
 
 def compile_value_and_grad_plan_source(source: str, function_name: str, param_types: tuple[Any, ...], *,
-                                       include_prelude: bool = False, syntax: str = "lisp"):
-    """The reference's front end followed by ``value_and_grad_plan_from_hir``."""
+                                       include_prelude: bool = True, syntax: str = "lisp"):
+    """The reference's front end followed by ``value_and_grad_plan_from_hir``
+    (ML sources see the prelude's ``sum``, ``dot``, ``scale`` ... unless
+    ``include_prelude`` is False)."""
     from remora.compiler import compile_function_source  # the reference's front end
 
     artifact = compile_function_source(source, function_name, param_types, verify=False,

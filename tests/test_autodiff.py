@@ -259,3 +259,27 @@ def test_plan_inputs_are_checked_against_the_plan():
         _check_inputs(plan, good[:3])
     with pytest.raises(RemoraShapeError):
         _check_inputs(plan, [*good[:3], np.zeros(255, np.float32)])
+
+
+@needs_ref
+def test_losses_written_with_the_preludes_sum_and_dot(oracle_mod):
+    """``sum`` and ``dot`` reach the loss as the front end's lets; the plan
+    reads through them: loss = sum (x * y) + dot x x / 2, so dL/dx = y + x
+    and dL/dy = x."""
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.autodiff import compile_value_and_grad_plan_source
+    from remora_b200.program_plan import Plan
+    from test_program_plan import run_plan_on_oracle
+
+    vec = ArrayType(FLOAT, (StaticDim(50),))
+    plan = compile_value_and_grad_plan_source("def loss x y = sum (map (*) x y) + dot x x / 2.0", "loss",
+                                              (vec, vec), syntax="ml")
+    rng = np.random.default_rng(9)
+    x, y = (rng.standard_normal(50).astype(np.float32) for _ in range(2))
+    value, gx, gy = run_plan_on_oracle(oracle_mod, Plan.from_record(plan.to_record()), [x, y], all_results=True)
+    xd, yd = x.astype(np.float64), y.astype(np.float64)
+    assert float(value) == pytest.approx(float((xd * yd).sum() + (xd * xd).sum() / 2), rel=1e-5)
+    np.testing.assert_allclose(gx, yd + xd, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gy, xd, rtol=1e-5, atol=1e-6)
