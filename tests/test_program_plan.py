@@ -275,3 +275,32 @@ def test_let_inlining_keeps_a_let_that_a_lambda_would_capture(oracle_mod):
                                            (FLOAT, ArrayType(FLOAT, (StaticDim(3),))))
     got = run_plan_on_oracle(oracle_mod, plan, [np.float32(2.0), np.array([1.0, 2.0, 3.0], np.float32)])
     np.testing.assert_array_equal(got, np.array([2.0, 4.0, 6.0], np.float32))
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+@pytest.mark.parametrize("source, fn, shapes", [
+    # an integer lifted dot: not the f32 dense core, and not a fold of the cell alone
+    ("def f m v = map (\\row -> fold (+) 0 (map (*) row v)) m", "f", [("i", (4, 3)), ("i", (3,))]),
+    # a product of row times vector: not a dot
+    ("def f m v = map (\\row -> fold (*) 1.0 (map (*) row v)) m", "f", [("f", (4, 3)), ("f", (3,))]),
+    # a map over the cell that reads a scalar parameter
+    ("def f s m = map (\\row -> fold (+) 0.0 (map (\\x -> x * s) row)) m", "f", [("f", None), ("f", (4, 3))]),
+    # a fold step other than acc op x inside a cell map
+    ("def f m = map (\\row -> fold (\\acc x -> acc * x + 1.0) 1.0 row) m", "f", [("f", (4, 3))]),
+])
+def test_near_miss_function_forms_raise(source, fn, shapes):
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, INT, ArrayType, StaticDim
+
+    from remora_b200.errors import RemoraUnsupportedError
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    elem = {"f": FLOAT, "i": INT}
+    ptypes = tuple(elem[e] if d is None else ArrayType(elem[e], tuple(StaticDim(x) for x in d)) for e, d in shapes)
+    try:
+        compile_function_source_to_plan(source, fn, ptypes)
+    except RemoraUnsupportedError:
+        return
+    except Exception as exc:  # the reference's own front end rejected it first
+        pytest.skip(f"front end: {type(exc).__name__}")
+    raise AssertionError("expected RemoraUnsupportedError")
