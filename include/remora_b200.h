@@ -301,7 +301,11 @@ int remora_b200_scan(RemoraB200Ctx *ctx, const RemoraScanSpec *spec,
    memory that every GPU loading the library holds until the process exits.
    Limits: a rank-1 scan may have at most 268,304,384 elements (larger scans
    return REMORA_ERR_LIMIT before any work is queued); input and output must
-   be contiguous (strided views return REMORA_ERR_UNSUPPORTED).  The first
+   be contiguous (strided views return REMORA_ERR_UNSUPPORTED).  A rank >= 2
+   scan runs on fewer row segments here (at most 63 SMs' worth of blocks, so
+   that their carries fit the array), so its f32 sums may round differently
+   from remora_b200_scan's by reassociation; integer results are identical.
+   The first
    call on a device looks up the array's device address (cudaGetSymbolAddress)
    and caches it; make that first call before any stream capture.  Every call
    on a device shares the array: calls that overlap on the GPU (different

@@ -799,68 +799,86 @@ def _fields(node: object):
             yield f.name, v
 
 
-def _free(node: object) -> set[str]:
-    """Names read by ``node`` that it does not bind itself."""
+def _binds(node: object) -> set[str] | None:
+    """Names a binding node binds over its ``body`` (a let its name, a
+    lambda its parameters, an unbox its value and hidden index names); None
+    for a node that binds nothing.  The bound names scope over ``body``
+    only, never over the let's value or the unbox's boxed operand."""
     k = _kind(node)
-    if k == "HIRVar":
-        return {node.name}
     if k == "HIRLet":
-        return _free(node.value) | (_free(node.body) - {node.name})
+        return {node.name}
     if k == "HIRLambda":
-        return _free(node.body) - {p.name for p in node.params}
-    out: set[str] = set()
+        return {p.name for p in node.params}
+    if k == "HIRUnbox":
+        return {node.value_name, *node.hidden_names}
+    return None
+
+
+def _children(node: object):
     for _, v in _fields(node):
         for x in (v if isinstance(v, list) else [v]):
             if _is_node(x):
-                out |= _free(x)
+                yield x
+
+
+def _free(node: object) -> set[str]:
+    """Names read by ``node`` that it does not bind itself."""
+    if _kind(node) == "HIRVar":
+        return {node.name}
+    bound = _binds(node)
+    out: set[str] = set()
+    for fname, v in _fields(node):
+        for x in (v if isinstance(v, list) else [v]):
+            if _is_node(x):
+                out |= (_free(x) - bound) if bound is not None and fname == "body" else _free(x)
     return out
 
 
 def _uses(node: object, name: str) -> int:
-    k = _kind(node)
-    if k == "HIRVar":
+    if _kind(node) == "HIRVar":
         return int(node.name == name)
-    if k == "HIRLet":
-        return _uses(node.value, name) + (0 if node.name == name else _uses(node.body, name))
-    if k == "HIRLambda" and name in {p.name for p in node.params}:
-        return 0
-    return sum(_uses(x, name) for _, v in _fields(node) for x in (v if isinstance(v, list) else [v]) if _is_node(x))
+    bound = _binds(node)
+    n = 0
+    for fname, v in _fields(node):
+        if bound is not None and fname == "body" and name in bound:
+            continue
+        for x in (v if isinstance(v, list) else [v]):
+            if _is_node(x):
+                n += _uses(x, name)
+    return n
 
 
 def _substitute_name(node: object, name: str, value: object, value_free: set[str]) -> object | None:
     """``node`` with the free uses of ``name`` replaced by ``value``; None
-    where a binder on the way would capture a name ``value`` reads."""
+    where a binder on the way would capture a name ``value`` reads, or
+    where a use sits inside a lambda and ``value`` is more than a name or a
+    literal (substituting it there would move array work into the
+    per-cell body)."""
     k = _kind(node)
     if k == "HIRVar":
         return value if node.name == name else node
-    if k in ("HIRLet", "HIRLambda"):
-        bound = {node.name} if k == "HIRLet" else {p.name for p in node.params}
-        changes = {}
-        if k == "HIRLet":
-            v = _substitute_name(node.value, name, value, value_free)
-            if v is None:
-                return None
-            changes["value"] = v
-        if name not in bound and _uses(node.body, name):
-            if bound & value_free:
-                return None
-            b = _substitute_name(node.body, name, value, value_free)
-            if b is None:
-                return None
-            changes["body"] = b
-        return dataclasses.replace(node, **changes) if changes else node
+    bound = _binds(node)
+    if k == "HIRLambda" and _uses(node, name) and _kind(value) not in ("HIRVar", "HIRLit"):
+        return None
     changes = {}
     for fname, v in _fields(node):
+        if bound is not None and fname == "body":
+            if name in bound or not _uses(v, name):
+                continue
+            if bound & value_free:
+                return None
         if isinstance(v, list):
             new = [(_substitute_name(x, name, value, value_free) if _is_node(x) else x) for x in v]
             if any(x is None for x in new):
                 return None
-            changes[fname] = new
+            if any(a is not b for a, b in zip(new, v)):
+                changes[fname] = new
         else:
             new = _substitute_name(v, name, value, value_free)
             if new is None:
                 return None
-            changes[fname] = new
+            if new is not v:
+                changes[fname] = new
     return dataclasses.replace(node, **changes) if changes else node
 
 
@@ -868,8 +886,11 @@ def _inline_lets(node: object) -> object:
     """The front end inlines called functions (the prelude's ``sum``,
     ``dot``) as chains of lets binding their parameters.  A let whose value
     is a plain name, or whose name is read once, is substituted into its
-    body (unless a lambda on the way rebinds a name the value reads), so
-    ``let xs = row in fold (+) 0.0 xs`` plans like ``fold (+) 0.0 row``."""
+    body (unless a binder on the way rebinds a name the value reads, or the
+    one use sits inside a lambda and the value is more than a name or a
+    literal), so ``let xs = row in fold (+) 0.0 xs`` plans like
+    ``fold (+) 0.0 row``, while ``let r = map (*) v v in map (\\row -> ... r ...) m``
+    keeps ``r`` as one array computed once."""
     changes = {}
     for fname, v in _fields(node):
         changes[fname] = [(_inline_lets(x) if _is_node(x) else x) for x in v] if isinstance(v, list) \

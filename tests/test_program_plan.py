@@ -295,12 +295,36 @@ def test_near_miss_function_forms_raise(source, fn, shapes):
     from remora_b200.errors import RemoraUnsupportedError
     from remora_b200.program_plan import compile_function_source_to_plan
 
+    from remora.compiler import compile_function_source
+    from remora_b200.program_plan import plan_from_function
+
     elem = {"f": FLOAT, "i": INT}
     ptypes = tuple(elem[e] if d is None else ArrayType(elem[e], tuple(StaticDim(x) for x in d)) for e, d in shapes)
+    # the reference's front end alone first: only its own rejection skips
     try:
-        compile_function_source_to_plan(source, fn, ptypes)
-    except RemoraUnsupportedError:
-        return
-    except Exception as exc:  # the reference's own front end rejected it first
+        artifact = compile_function_source(source, fn, ptypes, verify=False, include_prelude=True, syntax="ml")
+    except Exception as exc:
         pytest.skip(f"front end: {type(exc).__name__}")
-    raise AssertionError("expected RemoraUnsupportedError")
+    # the planner on the HIR it returned must refuse with exactly this error
+    with pytest.raises(RemoraUnsupportedError):
+        plan_from_function(artifact.hir_function)
+
+
+@pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
+def test_a_let_read_once_inside_a_lambda_stays_one_array(oracle_mod):
+    """``let r = map (*) v v`` read once inside a cell map's lambda is not
+    substituted into the lambda (that would make the vector product part of
+    the per-row body): the plan computes r once, then one fused fold."""
+    sys.path.insert(0, REF)
+    from remora.types import FLOAT, ArrayType, StaticDim
+
+    from remora_b200.program_plan import compile_function_source_to_plan
+
+    src = "def f v m = let r = map (*) v v in map (\\row -> fold (+) 0.0 (map (*) row r)) m"
+    plan = compile_function_source_to_plan(src, "f", (ArrayType(FLOAT, (StaticDim(3),)),
+                                                      ArrayType(FLOAT, (StaticDim(4), StaticDim(3)))))
+    assert [st["op"] for st in plan.steps] == ["map", "fold"]
+    v = np.array([1.0, 2.0, 3.0], np.float32)
+    m = np.arange(12, dtype=np.float32).reshape(4, 3)
+    got = run_plan_on_oracle(oracle_mod, plan, [v, m])
+    np.testing.assert_allclose(got, (m * (v * v)).sum(axis=1), rtol=1e-6)
