@@ -10,8 +10,23 @@
 // are two-level and deterministic: fixed per-block ranges, fixed-order
 // combine of the block partials by the last block to finish.
 #include <algorithm>
+#include <unordered_map>
 
 #include "jit.cuh"
+
+// Cell-fold launch choices (compile-time; the defaults are the measured best).
+#ifndef REMORA_FOLD_MINB
+#define REMORA_FOLD_MINB 0
+#endif
+#ifndef REMORA_FOLD_PF
+#define REMORA_FOLD_PF 1
+#endif
+#ifndef REMORA_FOLD_GRID
+#define REMORA_FOLD_GRID 1
+#endif
+#ifndef REMORA_FOLD_U
+#define REMORA_FOLD_U 0
+#endif
 
 namespace remora {
 
@@ -212,7 +227,12 @@ struct FoldAllArgs {
   int32_t init_i;
 };
 
-std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U) {
+// Cell-fold module for cells of G lanes x U rows per lane group.  minb > 0
+// asks for at least that many resident 256-thread blocks per SM (register
+// budget); one = 1 when every lane of a group reads exactly one 16-byte
+// vector per row (L / 4 == G), in which case the vector kernel issues the
+// next pass's loads before this pass's butterfly.
+std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U, int minb = 0, int one = 0) {
   const bool f = sp.dtype == REMORA_F32;
   std::string s = kPrelude;
   RemoraMapProgram ident{};
@@ -268,34 +288,26 @@ std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U)
     s += "#define HS " + std::to_string(std::min(lu, lg)) + "\n";  // halving steps of the butterfly
   }
   // ---- cell fold, 128-bit loads (L % 4 == 0, 16-byte aligned rows)
-  s += R"(
-extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_vec(FoldCellArgs a) {
-  PDL_PROLOGUE();
-  const int lane = threadIdx.x & 31, sub = lane & (G - 1), grp = lane / G;
-  const i64 warp = (i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const i64 nwarps = (i64)gridDim.x * (blockDim.x >> 5);
-  const i64 rows_per_warp = (32 / G) * U;
-  const i64 nv = a.L >> 2;
-  for (i64 base = warp * rows_per_warp; base < a.rows; base += nwarps * rows_per_warp) {
-    const i64 r0 = base + (i64)grp * U;
-    ACC acc[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) acc[u] = IDENT;
-#pragma unroll 4
-    for (i64 c = sub; c < nv; c += G) {
-)";
-  s += "      " + inV + " va[U]; " + inV1 + " vb[U];\n";
-  s += "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        const i64 r = r0 + u;\n"
-       "        if (r < a.rows) {\n";
-  s += "          va[u] = __ldcs((const " + inV + "*)a.in[0] + r * nv + c);\n";
-  if (n_in == 2) s += "          vb[u] = __ldcs((const " + inV1 + "*)a.in[1] + r * nv + c);\n";
-  else s += "          vb[u] = va[u];\n";
-  s += "        }\n      }\n";
-  s += "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        if (r0 + u < a.rows) {\n";
-  for (const char *c : {"x", "y", "z", "w"})
-    s += std::string("          acc[u] = acc_op(acc[u], ELEM(") + cvt + "(va[u]." + c + "), " + cvt + "(vb[u]." + c + ")));\n";
-  s += "        }\n      }\n    }\n";
-  s += R"(
+  const std::string lb = minb > 0 ? "__launch_bounds__(256, " + std::to_string(minb) + ")" : "__launch_bounds__(256)";
+  // loads of the U rows starting at row R into (VA, VB), vector column C
+  auto loads = [&](const std::string &VA, const std::string &VB, const std::string &R, const std::string &C) {
+    std::string t = "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        const i64 r = " + R +
+                    " + u;\n        if (r < a.rows) {\n";
+    t += "          " + VA + "[u] = __ldcs((const " + inV + "*)a.in[0] + r * nv + " + C + ");\n";
+    if (n_in == 2) t += "          " + VB + "[u] = __ldcs((const " + inV1 + "*)a.in[1] + r * nv + " + C + ");\n";
+    else t += "          " + VB + "[u] = " + VA + "[u];\n";
+    t += "        }\n      }\n";
+    return t;
+  };
+  auto accum = [&](const std::string &VA, const std::string &VB) {
+    std::string t = "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        if (r0 + u < a.rows) {\n";
+    for (const char *c : {"x", "y", "z", "w"})
+      t += std::string("          acc[u] = acc_op(acc[u], ELEM(") + cvt + "(" + VA + "[u]." + c + "), " + cvt +
+           "(" + VB + "[u]." + c + ")));\n";
+    t += "        }\n      }\n";
+    return t;
+  };
+  const std::string butterfly = R"(
     // Butterfly over the G lanes of a group for its U rows at once: the
     // first HS steps halve the rows a lane holds (it keeps one half and
     // sends the other), the rest are plain xor steps.  Each partial sum
@@ -327,9 +339,44 @@ extern "C" __global__ void __launch_bounds__(256) remora_fold_cell_vec(FoldCellA
       for (int j = 0; j < (U >> HS); ++j)
         if (r0 + u0 + j < a.rows) put(a.out, r0 + u0 + j, acc[j], )" + init_arg + R"();
     }
-  }
-}
 )";
+  s += "\nextern \"C\" __global__ void " + lb + " remora_fold_cell_vec(FoldCellArgs a) {\n";
+  s += R"(  PDL_PROLOGUE();
+  const int lane = threadIdx.x & 31, sub = lane & (G - 1), grp = lane / G;
+  const i64 warp = (i64)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const i64 nwarps = (i64)gridDim.x * (blockDim.x >> 5);
+  const i64 rows_per_warp = (32 / G) * U;
+  const i64 nv = a.L >> 2;
+)";
+  if (one) {
+    // One vector per lane per row: pass k+1's loads are in flight while
+    // pass k's butterfly and stores run.
+    s += "  const i64 stride = nwarps * rows_per_warp;\n  i64 base = warp * rows_per_warp;\n";
+    s += "  " + inV + " va[U]; " + inV1 + " vb[U];\n  {\n    const i64 r0 = base + (i64)grp * U;\n";
+    s += loads("va", "vb", "r0", "sub");
+    s += "  }\n  for (; base < a.rows; base += stride) {\n    const i64 r0 = base + (i64)grp * U;\n";
+    s += "    " + inV + " na[U]; " + inV1 + " nb[U];\n    {\n      const i64 rn = r0 + stride;\n";
+    s += loads("na", "nb", "rn", "sub");
+    s += "    }\n    ACC acc[U];\n#pragma unroll\n    for (int u = 0; u < U; ++u) acc[u] = IDENT;\n";
+    s += accum("va", "vb");
+    s += butterfly;
+    s += "#pragma unroll\n    for (int u = 0; u < U; ++u) { va[u] = na[u]; vb[u] = nb[u]; }\n  }\n}\n";
+  } else {
+    s += R"(  for (i64 base = warp * rows_per_warp; base < a.rows; base += nwarps * rows_per_warp) {
+    const i64 r0 = base + (i64)grp * U;
+    ACC acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = IDENT;
+#pragma unroll 4
+    for (i64 c = sub; c < nv; c += G) {
+)";
+    s += "      " + inV + " va[U]; " + inV1 + " vb[U];\n";
+    s += loads("va", "vb", "r0", "c");
+    s += accum("va", "vb");
+    s += "    }\n";
+    s += butterfly;
+    s += "  }\n}\n";
+  }
 
   // ---- cell fold, scalar loads (any L, any 4-byte alignment)
   s += R"(
@@ -462,6 +509,23 @@ int pow2_floor(int64_t v) {
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Blocks of `block` threads of kernel k that one SM holds at once (cached
+// per kernel; at least 1).
+int resident_blocks(cudaKernel_t k, int block) {
+  static std::mutex mu;
+  static std::unordered_map<const void *, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find((const void *)k);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, (const void *)k, block, 0) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache.emplace((const void *)k, n);
+  return n;
+}
 
 // Every JIT kernel starts with PDL_PROLOGUE, so it may be launched as a
 // programmatic dependent of the previous kernel in the stream: its blocks
@@ -667,14 +731,19 @@ int run_fold(RemoraB200Ctx *ctx, const RemoraFoldSpec &sp, const DescView *ins_i
     const int64_t per_lane = (units + G - 1) / G;
     int U = 1;
     if (per_lane < 4) U = (int)std::max<int64_t>(1, 4 / std::max<int64_t>(per_lane, 1));
+    if (REMORA_FOLD_U > 0 && per_lane < 4) U = REMORA_FOLD_U;
+    const int one = (vec && REMORA_FOLD_PF && units == G) ? 1 : 0;
+    const int minb = REMORA_FOLD_MINB;
     std::string key("fold");
     key_append(key, sp);
     key_append(key, n_in);
     key_append(key, G);
     key_append(key, U);
+    key_append(key, one);
+    key_append(key, minb);
     cudaKernel_t kern;
     REMORA_TRY(jit_kernel_keyed(key, vec ? "remora_fold_cell_vec" : "remora_fold_cell_scalar",
-                                [&]() { return fold_module_source(sp, n_in, G, U); }, &kern));
+                                [&]() { return fold_module_source(sp, n_in, G, U, minb, one); }, &kern));
     FoldCellArgs a{};
     a.out = dst;
     a.rows = rows;
@@ -684,8 +753,13 @@ int run_fold(RemoraB200Ctx *ctx, const RemoraFoldSpec &sp, const DescView *ins_i
     a.init_f = sp.init_f;
     a.init_i = sp.init_i;
     const int64_t rows_per_block = (int64_t)(block / 32) * (32 / G) * U;
-    int64_t grid = std::max<int64_t>(1, std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
-                                                          (int64_t)ctx->sm_count * 8));
+    // Every block resident at once: a grid of at most the blocks the SMs
+    // hold together, each striding over the row blocks, so no block waits
+    // for a second wave and every block makes the same number of passes
+    // (to within one).
+    int64_t cap = (int64_t)ctx->sm_count * 8;
+    if (REMORA_FOLD_GRID) cap = (int64_t)ctx->sm_count * resident_blocks(kern, block);
+    int64_t grid = std::max<int64_t>(1, std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block, cap));
     if (rows > 0) REMORA_TRY(launch(kern, (int)grid, block, &a, stream));
   }
   if (!out_contig) REMORA_TRY(copy_from_contiguous(dst, out_in, out_es, stream, ctx->sm_count));
@@ -780,6 +854,8 @@ int remora_b200_jit_check(const RemoraMapProgram *prog, int32_t fold_op, char *s
     std::string fsrc = fold_module_source(sp, prog->n_inputs, 16, 4);
     REMORA_TRY(nvrtc_compile(fsrc, nullptr));
     src += fsrc;
+    // the form with the next pass's loads in flight (one vector per lane)
+    REMORA_TRY(nvrtc_compile(fold_module_source(sp, prog->n_inputs, 16, 4, 4, 1), nullptr));
   }
   if (src_out && n) std::snprintf(src_out, n, "%s", src.c_str());
   return REMORA_OK;
