@@ -62,6 +62,11 @@ struct Cfg {
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory per block");
 };
+// Tile columns per group of the tile order (decode_tile).
+#ifndef REMORA_GEMM_GROUP_COLS
+#define REMORA_GEMM_GROUP_COLS 8
+#endif
+constexpr int kGroupCols = REMORA_GEMM_GROUP_COLS;
 // Scratch for K-split partials: at most one 128 x 256 f32 tile per SM.
 constexpr size_t kSplitPartBytes = (size_t)148 * BM * 256 * 4 + 256;
 
@@ -73,27 +78,34 @@ struct GemmParams {
   long long ldc;
   long long c_bstride;
   int *err;
-  // A launch of few tiles splits each along K into `split` ranges; their
-  // BM x BN partials go to `part` ([tile][split][BM][BN]) and
+  // Tiles from `split_from` on are split along K into `split` ranges; their
+  // BM x BN partials go to `part` ([tile - split_from][split][BM][BN]) and
   // gemm_split_fixup adds them in split order.  split == 1: no split.
+  // split_from == 0 splits every tile (a launch of few tiles); a larger
+  // split_from splits only the tiles past the last full wave, so that the
+  // persistent CTAs end together instead of a part-filled last wave.
   int split;
+  int split_from;
   float *part;
+  // tile order: groups of `gn` tile columns, row-major inside a group
+  int gn;
 };
 
 // Work unit u -> tile, K-block range, and partial slot (-1: the whole tile).
 __device__ __forceinline__ void decode_unit(int u, const GemmParams &p, int &tile, int &kb0, int &kb1,
                                             int &slot) {
-  if (p.split == 1) {
+  if (p.split == 1 || u < p.split_from) {
     tile = u;
     kb0 = 0;
     kb1 = p.kt;
     slot = -1;
   } else {
-    const int part = u % p.split;
-    tile = u / p.split;
+    const int v = u - p.split_from;
+    const int part = v % p.split;
+    tile = p.split_from + v / p.split;
     kb0 = (int)((long long)p.kt * part / p.split);
     kb1 = (int)((long long)p.kt * (part + 1) / p.split);
-    slot = u;
+    slot = v;
   }
 }
 
@@ -112,12 +124,19 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t saddr, int mn, int kk)
   return mn ? tc::desc_mnmajor(saddr, 4096, kk) : tc::desc_kmajor(saddr, kk);
 }
 
+// Tile t -> (batch, row block, column block).  Tiles run in groups of gn
+// column blocks, row-major inside a group: the CTAs of one wave share few
+// B column blocks and reuse each A row block across gn tiles, which keeps a
+// wave's operands in L2.
 __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, int &mb, int &nb) {
   const int per = p.mt * p.nt;
   b = t / per;
   const int r = t - b * per;
-  mb = r / p.nt;
-  nb = r - mb * p.nt;
+  const int g = r / (p.mt * p.gn);
+  const int gw = min(p.gn, p.nt - g * p.gn);
+  const int i = r - g * p.mt * p.gn;
+  mb = i / gw;
+  nb = g * p.gn + (i - mb * gw);
 }
 
 // x -> (hi, lo) for the `bytes` of one operand tile at shared address t
@@ -183,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
   const int ntiles = p.batch * p.mt * p.nt;
-  const int nunits = ntiles * p.split;
+  const int nunits = p.split == 1 ? ntiles : p.split_from + (ntiles - p.split_from) * p.split;
   volatile int *abort_v = &abort_flag;
 
   if (warp == 0 && lane == 0) {
@@ -374,16 +393,16 @@ __global__ void __launch_bounds__(256) prep_operand_kernel(const float *__restri
 template <int BN>
 __global__ void __launch_bounds__(256) gemm_split_fixup(const float *__restrict__ part, GemmParams p) {
   const long long per = (long long)BM * BN;
-  const long long n = (long long)p.batch * p.mt * p.nt * per;
+  const long long n = ((long long)p.batch * p.mt * p.nt - p.split_from) * per;
   const long long step = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
-    const int t = (int)(i / per);
+    const int st = (int)(i / per);  // index among the split tiles
     const int r = (int)((i % per) / BN), c = (int)(i % BN);
     int b, mb, nb;
-    decode_tile(t, p, b, mb, nb);
+    decode_tile(p.split_from + st, p, b, mb, nb);
     const int row = mb * BM + r, col = nb * BN + c;
     if (row >= p.M || col >= p.N) continue;
-    const float *src = part + ((long long)t * p.split) * per + (long long)r * BN + c;
+    const float *src = part + ((long long)st * p.split) * per + (long long)r * BN + c;
     float v = src[0];
     for (int s = 1; s < p.split; ++s) v = __fadd_rn(v, src[(long long)s * per]);
     p.C[(long long)b * p.c_bstride + (long long)row * p.ldc + col] = v;
@@ -470,22 +489,37 @@ int launch_gemm(const Operand &A, const Operand &B, const Operand &Al, const Ope
     attr_set = true;
   }
   const int ntiles = p.batch * p.mt * p.nt;
+  p.gn = std::max(1, std::min(p.nt, kGroupCols));
   // Few tiles and a long K (a dense layer's forward or weight gradient):
   // split K so that the launch fills the SMs.
   p.split = 1;
+  p.split_from = 0;
+  const long long cap = (long long)(kSplitPartBytes - 256) / ((long long)BM * BN * 4);
   if (p.part != nullptr && 2 * ntiles <= sm_count && p.kt >= 8) {
-    const long long cap = (long long)(kSplitPartBytes - 256) / ((long long)BM * BN * 4);
     int s = std::min(sm_count / ntiles, p.kt / 4);
     s = (int)std::min<long long>(s, cap / ntiles);
     if (s >= 2) p.split = s;
+  } else if (p.part != nullptr && ntiles > sm_count && p.kt >= 16) {
+    // Several waves with a part-filled last one: the tiles past the last
+    // full wave are split along K over all the SMs instead (when at most
+    // half a wave is left, so that each splits at least in two).
+    const int rem = ntiles % sm_count;
+    if (rem > 0 && 2 * rem <= sm_count) {
+      int s = std::min(sm_count / rem, p.kt / 8);
+      s = (int)std::min<long long>(s, cap / rem);
+      if (s >= 2) {
+        p.split = s;
+        p.split_from = ntiles - rem;
+      }
+    }
   }
-  const int nunits = ntiles * p.split;
+  const int nunits = p.split == 1 ? ntiles : p.split_from + (ntiles - p.split_from) * p.split;
   const int grid = std::min(nunits, sm_count);
   note_launch();
   gemm_tf32_kernel<SPLIT3, BN, INK><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, mal, mbl, p);
   REMORA_CUDA_TRY(cudaGetLastError());
   if (p.split > 1) {
-    const long long n = (long long)ntiles * BM * BN;
+    const long long n = (long long)(ntiles - p.split_from) * BM * BN;
     note_launch();
     gemm_split_fixup<BN><<<(int)std::min<long long>((n + 255) / 256, (long long)sm_count * 16), 256, 0, stream>>>(
         p.part, p);

@@ -119,3 +119,27 @@ def test_gemm_batched_full_sampled(cuda, oracle_mod):
         rows = np.arange(bi * 13 % 1000, bi * 13 % 1000 + 24)
         check(got[bi, rows], oracle_mod.matmul(a[bi, rows], b[bi], nthreads=oracle_mod.max_threads()), "3xtf32",
               exact(a[bi, rows], b[bi]))
+
+
+@pytest.mark.parametrize("shape", [(1, 2600, 2000, 520), (5, 1100, 900, 600), (1, 4096, 4096, 4096)])
+@pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
+def test_gemm_split_last_wave_whole_output(cuda, shape, prec):
+    """Launches of more tiles than SMs whose last wave is at most half full
+    split those last tiles along K (partials added in split order by the
+    fix-up kernel).  Every element, edge tiles and the split tiles included,
+    is checked against the exact f64 product."""
+    import torch
+
+    batch, M, N, K = shape
+    g = torch.Generator(device=cuda)
+    g.manual_seed(M + N + K)
+    a = torch.rand((batch, M, K), generator=g, device=cuda) * 2 - 1
+    b = torch.rand((batch, K, N), generator=g, device=cuda) * 2 - 1
+    if batch == 1:
+        a, b = a[0], b[0]
+    got = ops.gemm(a, b, precision=prec)
+    ref = torch.matmul(a.double(), b.double())
+    scale = max(1.0, float(ref.abs().max()))
+    err = float((got.double() - ref).abs().max()) / scale
+    assert err <= (1e-3 if prec == "tf32" else 1e-4), err
+    ops.synchronize(cuda.index)
