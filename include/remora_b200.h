@@ -173,7 +173,15 @@ typedef struct {
 /* ------------------------------------------------------------------------ */
 /* Dense core and convolution specs                                         */
 /* ------------------------------------------------------------------------ */
-enum { REMORA_PREC_TF32 = 0, REMORA_PREC_3XTF32 = 1 };
+/* Tensor-core precision.  TF32: operands as TF32 (10-bit mantissa), f32
+   accumulation.  3XTF32: each operand split into hi = TF32(x) and
+   lo = x - hi, products hi*hi + hi*lo + lo*hi (close to f32).  2XTF32
+   (convolutions only): one operand split, the other TF32 -- the weights in
+   the forward and input gradient, the output gradient in the weight
+   gradient; for backward passes whose gradients must stay within 1e-3
+   (an error study of the crater CNN gives 3.9e-4 for its second layer's
+   backward in this mode, 2e-2 for plain TF32). */
+enum { REMORA_PREC_TF32 = 0, REMORA_PREC_3XTF32 = 1, REMORA_PREC_2XTF32 = 2 };
 
 typedef struct {
   int32_t precision; /* REMORA_PREC_TF32 or REMORA_PREC_3XTF32             */
@@ -183,7 +191,7 @@ typedef struct {
 typedef struct {
   int32_t stride; /* square stride (1 in the benchmark shape)              */
   int32_t pad;    /* zero padding on every side                            */
-  int32_t precision;
+  int32_t precision; /* REMORA_PREC_TF32, _3XTF32 or _2XTF32             */
   int32_t reserved_;
 } RemoraConvSpec;
 
@@ -237,6 +245,17 @@ int remora_b200_memset_d32(RemoraB200Ctx *ctx, void *dst, uint32_t value,
    reports REMORA_ERR_TIMEOUT if a bounded device wait ran out since the
    previous check on this stream's workspace. */
 int remora_b200_synchronize(RemoraB200Ctx *ctx, remora_stream_t stream);
+/* Failure-detection check of the bounded device waits (no counterpart in
+   the reference, whose generated kernels have no device-side waits).
+   Launches one block that waits, with the same bounded mbarrier wait every
+   tcgen05 kernel of this library uses, for a phase that completes only when
+   `signal` is 1.  With signal = 0 the wait gives up after `limit_cycles` SM
+   clock cycles (0 .. 2^40), records code 900 in the stream's error word and
+   returns: the next remora_b200_synchronize on that stream returns
+   REMORA_ERR_TIMEOUT, and the context and the device stay usable.  Nothing
+   is in flight during the wait (no copies, no MMAs, no tensor memory). */
+int remora_b200_wait_check(RemoraB200Ctx *ctx, int64_t limit_cycles,
+                           int32_t signal, remora_stream_t stream);
 /* Pins a host buffer for asynchronous copies (cudaHostRegister). */
 int remora_b200_host_register(void *ptr, size_t nbytes);
 int remora_b200_host_unregister(void *ptr);

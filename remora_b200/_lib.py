@@ -43,7 +43,7 @@ MAP_MAX_REGS = 64
 FOLD_ADD, FOLD_MUL = 0, 1
 FOLD_CELL, FOLD_ALL = 0, 1
 EPI_NONE, EPI_SQRT = 0, 1
-PREC_TF32, PREC_3XTF32 = 0, 1
+PREC_TF32, PREC_3XTF32, PREC_2XTF32 = 0, 1, 2
 
 
 # ----------------------------------------------------------------- structs
@@ -144,6 +144,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "remora_b200_memcpy_d2h": (_I32, [_VP, _VP, _VP, _SZ, _VP]),
     "remora_b200_memset_d32": (_I32, [_VP, _VP, ctypes.c_uint32, _SZ, _VP]),
     "remora_b200_synchronize": (_I32, [_VP, _VP]),
+    "remora_b200_wait_check": (_I32, [_VP, ctypes.c_int64, _I32, _VP]),
     "remora_b200_host_register": (_I32, [_VP, _SZ]),
     "remora_b200_host_unregister": (_I32, [_VP]),
     "remora_b200_jit_check": (_I32, [ctypes.POINTER(RemoraMapProgram), _I32, ctypes.c_char_p, _SZ]),

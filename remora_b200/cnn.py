@@ -68,6 +68,48 @@ def process_group_allreduce(group=None):
     return allreduce
 
 
+CHECKPOINT_FORMAT = 1
+
+
+def save_checkpoint(path, params: np.ndarray, step: int, *, lr: float, batch_total: int,
+                    precision: str = "mixed", data_seed: int = crater.DATA_SEED,
+                    parameter_seed: int = crater.PARAMETER_SEED) -> None:
+    """Write the training state of the crater CNN to `path` (.npz): the flat
+    parameter vector in the layout of remora_b200.crater, the number of SGD
+    steps taken, and what the run needs to continue identically (learning
+    rate, global batch, precision, seeds).  The reference keeps parameter
+    snapshots every K epochs in memory (examples/crater_train.py:236,263-264);
+    this is their on-disk form.  The file is written under a temporary name
+    and renamed, so a reader never sees a partial checkpoint."""
+    import os
+
+    flat = np.ascontiguousarray(params, dtype=np.float32).reshape(-1)
+    if flat.size != crater.NPARAMS:
+        raise ValueError(f"a checkpoint holds {crater.NPARAMS} parameters, got {flat.size}")
+    path = os.fspath(path)
+    tmp = path + ".tmp.npz"
+    np.savez(tmp, params=flat, step=np.int64(step), lr=np.float64(lr), batch_total=np.int64(batch_total),
+             precision=np.array(precision), data_seed=np.int64(data_seed), parameter_seed=np.int64(parameter_seed),
+             layout=np.array([f"{k}:{'x'.join(map(str, sh))}" for k, sh in crater.LAYOUT]),
+             format=np.int64(CHECKPOINT_FORMAT))
+    os.replace(tmp, path)
+
+
+def load_checkpoint(path) -> dict:
+    """The state save_checkpoint wrote; raises ValueError when the file's
+    parameter layout is not this model's."""
+    with np.load(path) as f:
+        if int(f["format"]) != CHECKPOINT_FORMAT:
+            raise ValueError(f"checkpoint format {int(f['format'])}, expected {CHECKPOINT_FORMAT}")
+        layout = [str(v) for v in f["layout"]]
+        want = [f"{k}:{'x'.join(map(str, sh))}" for k, sh in crater.LAYOUT]
+        if layout != want:
+            raise ValueError(f"checkpoint layout {layout} is not the crater CNN's {want}")
+        return {"params": f["params"].copy(), "step": int(f["step"]), "lr": float(f["lr"]),
+                "batch_total": int(f["batch_total"]), "precision": str(f["precision"]),
+                "data_seed": int(f["data_seed"]), "parameter_seed": int(f["parameter_seed"])}
+
+
 def _lib():
     lib = L.lib()
     for name, args in _CNN_PROTOS.items():
@@ -83,7 +125,7 @@ class CraterCNN:
     [batch,1,64,64] and [batch]."""
 
     def __init__(self, device: Any, batch: int, batch_total: int | None = None, lr: float = 0.01,
-                 params: np.ndarray | None = None, allreduce=None, precision: str = "3xtf32",
+                 params: np.ndarray | None = None, allreduce=None, precision: str = "mixed",
                  overlap_allreduce: bool | None = None) -> None:
         import torch
 
@@ -112,13 +154,23 @@ class CraterCNN:
         self.loss_sum = e(1).reshape(())
         # fused map: the in-place SGD update p - lr * g
         self.prog_sgd = compile_program(BinaryExpr("-", x(0), BinaryExpr("*", const(self.lr), x(1))), 2)
-        # "3xtf32" (default): split-precision GEMMs and convs, gradients
-        # within 1e-4 of the f32 step; "tf32": single-pass TF32 tensor-core
-        # convs and GEMMs, faster, first-layer gradient off by ~3e-2 of max
-        prec = {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32}[precision]
-        self.conv_spec = L.RemoraConvSpec(1, 1, prec, 0)
-        self.gemm_spec = L.RemoraGemmSpec(prec, 0)
+        # "mixed" (default): 3xTF32 for the conv forward and every GEMM,
+        # 2xTF32 (one operand split) for the conv layer's two gradients; an
+        # f64 error study of the step puts every gradient within 4e-4 of
+        # the f32 step (a forward in TF32 shifts ReLU masks and pool choices:
+        # 1e-2).  "3xtf32": split precision everywhere, gradients within
+        # 1e-4.  "tf32": single-pass TF32 everywhere, outside the 1e-3
+        # gradient tolerance (first layer ~3e-2 of max): a speed reference.
+        if precision not in ("mixed", "3xtf32", "tf32"):
+            raise ValueError(f"unknown precision {precision!r}")
+        self.precision = precision
+        fwd = L.PREC_TF32 if precision == "tf32" else L.PREC_3XTF32
+        bwd = {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32, "mixed": L.PREC_2XTF32}[precision]
+        self.conv_spec = L.RemoraConvSpec(1, 1, fwd, 0)
+        self.conv_bwd_spec = L.RemoraConvSpec(1, 1, bwd, 0)
+        self.gemm_spec = L.RemoraGemmSpec(fwd, 0)
         self.graph = None
+        self.graphs: list = []
         self._keep: list = []
         # Two allreduce buckets: w3..b4 (the dense layers, 99 % of the
         # gradient) is final once the dense1 weight-gradient GEMM is done and
@@ -164,49 +216,72 @@ class CraterCNN:
                                              out.dim(), self._stream()), "map")
 
     # ---------------------------------------------------------- the step
+    def stages(self, images, labels) -> list[tuple[str, Any]]:
+        """The step's library calls up to the gradient, in order, as (name,
+        callable) pairs; each callable enqueues its call on the current
+        stream.  ``forward_backward`` runs them all; a benchmark may time one
+        alone (it reads and writes this rank's own buffers)."""
+        lib, c = self.lib, self.ctx.ptr
+        p, g = self.p, self.g
+        B = self.B
+        d, chk, spec, bspec = self._d, self._check, self.conv_spec, self.conv_bwd_spec
+        p2flat = self.p2.view(B, 8192)
+
+        def conv1():
+            chk(lib.remora_b200_conv1_relu_pool(c, d(images), d(p["w1"]), d(p["b1"]), d(self.p1), d(self.code1),
+                                                self._stream()), "conv1")
+
+        def conv2():  # conv2 + bias + ReLU + pool: the [B,32,32,32] activation never exists
+            chk(lib.remora_b200_conv2d_fwd_relu_pool(c, ctypes.byref(spec), d(self.p1), d(p["w2"]), d(p["b2"]),
+                                                     d(self.p2), d(self.code2), self._stream()), "conv2")
+
+        def dense1():
+            self._gemm(p2flat, p["w3"].t(), self.hpre)
+
+        def head():  # ReLU(hpre + b3), dense 64 -> 1, BCE and dlogit
+            chk(lib.remora_b200_dense_bias_relu_bce(c, d(self.hpre), d(p["b3"]), d(self.h), d(p["w4"]), d(p["b4"]),
+                                                    d(labels), d(self.z), d(self.loss_b), d(self.dz),
+                                                    ctypes.c_float(1.0 / self.B_total), self._stream()), "dense_bce")
+
+        def head_bwd():  # dense 64 -> 1 backward; sums dh over the batch: the hidden bias gradient
+            chk(lib.remora_b200_dense_relu_bwd(c, d(self.h), d(p["w4"]), d(self.dz), d(self.dh), d(g["w4"]),
+                                               d(g["b4"]), d(g["b3"]), self._stream()), "dense2 bwd")
+
+        def dense1_wgrad():
+            self._gemm(self.dh.t(), p2flat, g["w3"])
+
+        def dense1_dgrad():
+            self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))
+
+        def conv2_wgrad():  # straight from the pooled gradient and the pool codes
+            chk(lib.remora_b200_conv2d_wgrad_bias_unpool(c, ctypes.byref(bspec), d(self.p1), d(self.dp2),
+                                                         d(self.code2), d(g["w2"]), d(g["b2"]), self._stream()),
+                "conv2 wgrad")
+
+        def conv2_dgrad():
+            chk(lib.remora_b200_conv2d_dgrad_unpool(c, ctypes.byref(bspec), d(self.dp2), d(self.code2), d(p["w2"]),
+                                                    d(self.dp1), self._stream()), "conv2 dgrad")
+
+        def conv1_wgrad():
+            chk(lib.remora_b200_conv1_wgrad_pooled(c, d(images), d(self.dp1), d(self.code1), d(g["w1"]),
+                                                   d(g["b1"]), self._stream()), "conv1 wgrad")
+
+        return [("conv1_fwd", conv1), ("conv2_fwd", conv2), ("dense1_fwd", dense1), ("head", head),
+                ("head_bwd", head_bwd), ("dense1_wgrad", dense1_wgrad), ("dense1_dgrad", dense1_dgrad),
+                ("conv2_wgrad", conv2_wgrad), ("conv2_dgrad", conv2_dgrad), ("conv1_wgrad", conv1_wgrad)]
+
     def forward_backward(self, images, labels) -> None:
         """Loss and gradients of this rank's shard into self.grads (not yet
         reduced over ranks)."""
-        lib, c, s = self.lib, self.ctx.ptr, self._stream()
-        p, g = self.p, self.g
         self._keep = []
-        B = self.B
-        # forward
-        self._check(lib.remora_b200_conv1_relu_pool(c, self._d(images), self._d(p["w1"]), self._d(p["b1"]),
-                                                    self._d(self.p1), self._d(self.code1), s), "conv1")
-        # conv2 + bias + ReLU + pool in one kernel: the [B,32,32,32] activation never exists
-        self._check(lib.remora_b200_conv2d_fwd_relu_pool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
-                                                         self._d(p["w2"]), self._d(p["b2"]), self._d(self.p2),
-                                                         self._d(self.code2), s), "conv2")
-        p2flat = self.p2.view(B, 8192)
-        self._gemm(p2flat, p["w3"].t(), self.hpre)
-        # ReLU(hpre + b3), dense 64 -> 1, BCE and dlogit in one kernel
-        self._check(lib.remora_b200_dense_bias_relu_bce(c, self._d(self.hpre), self._d(p["b3"]), self._d(self.h),
-                                                        self._d(p["w4"]), self._d(p["b4"]), self._d(labels),
-                                                        self._d(self.z), self._d(self.loss_b), self._d(self.dz),
-                                                        ctypes.c_float(1.0 / self.B_total), s), "dense_bce")
-        # backward
-        # dense 64 -> 1 backward; also sums dh over the batch: the hidden bias gradient
-        self._check(lib.remora_b200_dense_relu_bwd(c, self._d(self.h), self._d(p["w4"]), self._d(self.dz),
-                                                   self._d(self.dh), self._d(g["w4"]), self._d(g["b4"]),
-                                                   self._d(g["b3"]), s), "dense2 bwd")
-        self._gemm(self.dh.t(), p2flat, g["w3"])
-        if self.allreduce is not None and self.overlap:
-            # the dense bucket is final: reduce it while the convs run
-            cur = self.torch.cuda.current_stream(self.dev)
-            self.comm.wait_stream(cur)
-            with self.torch.cuda.stream(self.comm):
-                self.allreduce(self.bucket_dense)
-        self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))
-        # conv2 gradients straight from the pooled gradient and the pool codes
-        self._check(lib.remora_b200_conv2d_wgrad_bias_unpool(c, ctypes.byref(self.conv_spec), self._d(self.p1),
-                                                             self._d(self.dp2), self._d(self.code2),
-                                                             self._d(g["w2"]), self._d(g["b2"]), s), "conv2 wgrad")
-        self._check(lib.remora_b200_conv2d_dgrad_unpool(c, ctypes.byref(self.conv_spec), self._d(self.dp2),
-                                                        self._d(self.code2), self._d(p["w2"]), self._d(self.dp1),
-                                                        s), "conv2 dgrad")
-        self._check(lib.remora_b200_conv1_wgrad_pooled(c, self._d(images), self._d(self.dp1), self._d(self.code1),
-                                                       self._d(g["w1"]), self._d(g["b1"]), s), "conv1 wgrad")
+        for name, run in self.stages(images, labels):
+            run()
+            if name == "dense1_wgrad" and self.allreduce is not None and self.overlap:
+                # the dense bucket is final: reduce it while the convs run
+                cur = self.torch.cuda.current_stream(self.dev)
+                self.comm.wait_stream(cur)
+                with self.torch.cuda.stream(self.comm):
+                    self.allreduce(self.bucket_dense)
 
     def update(self) -> None:
         if self.allreduce is not None:
@@ -221,6 +296,26 @@ class CraterCNN:
         self.forward_backward(images, labels)
         self.update()
 
+    # -------------------------------------------------- checkpoint/resume
+    def save(self, path, step: int) -> None:
+        """Checkpoint this replica's parameters after `step` SGD steps (the
+        replicas of a data-parallel run are identical; rank 0 writes)."""
+        self.torch.cuda.synchronize(self.dev)
+        save_checkpoint(path, self.params.cpu().numpy(), step, lr=self.lr, batch_total=self.B_total,
+                        precision=self.precision)
+
+    def restore(self, path) -> int:
+        """Load a checkpoint's parameters into this model, in place (captured
+        graphs keep reading the same buffer); returns the step it was taken
+        at.  The learning rate, global batch and precision must match."""
+        st = load_checkpoint(path)
+        if st["batch_total"] != self.B_total or abs(st["lr"] - self.lr) > 0.0 or st["precision"] != self.precision:
+            raise ValueError(f"checkpoint of lr {st['lr']}, global batch {st['batch_total']}, {st['precision']}; "
+                             f"this model has lr {self.lr}, global batch {self.B_total}, {self.precision}")
+        self.params.copy_(self.torch.from_numpy(st["params"]))
+        self.torch.cuda.synchronize(self.dev)
+        return st["step"]
+
     def loss(self) -> float:
         """This rank's share of the batch-mean loss of the last step (sum of
         its per-sample losses / global batch)."""
@@ -230,10 +325,12 @@ class CraterCNN:
         return float(self.loss_sum.item()) / self.B_total
 
     # ------------------------------------------------------ graph capture
-    def capture(self, images, labels) -> None:
-        """Record one step (forward, backward, allreduce, update) as a CUDA
-        graph on a side stream; replay() then launches it whole.  Call after
-        at least one eager step (kernels compiled, workspace sized)."""
+    def capture(self, images, labels) -> int:
+        """Record one step (forward, backward, allreduce, update) on
+        ``images``/``labels`` as a CUDA graph on a side stream; replay() then
+        launches it whole.  Runs one eager step first (kernels compiled,
+        workspace sized).  Several graphs, one per input buffer, may be
+        captured (double-buffered inputs); returns this graph's index."""
         torch = self.torch
         side = torch.cuda.Stream(self.dev)
         side.wait_stream(torch.cuda.current_stream(self.dev))
@@ -241,12 +338,36 @@ class CraterCNN:
             self.step(images, labels)  # sizes the side stream's workspace outside capture
         torch.cuda.current_stream(self.dev).wait_stream(side)
         torch.cuda.synchronize(self.dev)
-        self.graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph()
         n0 = L.launch_count()
-        with torch.cuda.graph(self.graph, stream=side):
+        with torch.cuda.graph(graph, stream=side):
             self.step(images, labels)
         self.graph_launches = L.launch_count() - n0  # library kernels per replay
-        self._graph_keep = list(self._keep)
+        self.graphs.append((graph, list(self._keep)))
+        self.graph = graph
+        return len(self.graphs) - 1
 
-    def replay(self) -> None:
-        self.graph.replay()
+    def replay(self, which: int | None = None) -> None:
+        (self.graph if which is None else self.graphs[which][0]).replay()
+
+    def release_graphs(self) -> None:
+        """Drop every captured graph (those holding NCCL calls must go
+        before the process group is destroyed)."""
+        self.graph = None
+        self.graphs = []
+
+    def stage_graph(self, name: str, images, labels, reps: int):
+        """One stage of the step (a name of ``stages``) repeated ``reps``
+        times as a CUDA graph, for timing that stage alone."""
+        torch = self.torch
+        run = dict(self.stages(images, labels))[name]
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            run()  # compiles and sizes this stream's workspace outside capture
+        torch.cuda.synchronize(self.dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(reps):
+                run()
+        return graph, list(self._keep)

@@ -253,7 +253,7 @@ template <int H, int W, int PARTS>
 __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const float *__restrict__ x,
                                                                          const float *__restrict__ dp,
                                                                          const uint8_t *__restrict__ code,
-                                                                         float *__restrict__ part, int K) {
+                                                                         double *__restrict__ part, int K) {
   constexpr int OW = W / 2, NP = (H / 2) * OW, PWD = W + 2;
   constexpr int RP = (H / 2) / PARTS, NPP = RP * OW, IR = 2 * RP + 2;
   static_assert((H / 2) % PARTS == 0, "parts split the pooled rows evenly");
@@ -268,9 +268,11 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const f
   __syncthreads();
   const int lane16 = threadIdx.x & 15;
   for (int k = threadIdx.x >> 4; k < K; k += kConv1Threads / 16) {
-    float acc[10];
+    // f64 sums: the weight gradient adds every pixel of the batch with
+    // heavy cancellation, where f32 partials lose about 1e-4 of the result
+    double acc[10];
 #pragma unroll
-    for (int u = 0; u < 10; ++u) acc[u] = 0.0f;
+    for (int u = 0; u < 10; ++u) acc[u] = 0.0;
     const long long base = (b * K + k) * (long long)NP + i0 * OW;
 #pragma unroll 4
     for (int pos = lane16; pos < NPP; pos += 16) {
@@ -282,12 +284,13 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const f
 #pragma unroll
       for (int a = 0; a < 3; ++a)
 #pragma unroll
-        for (int bb = 0; bb < 3; ++bb) acc[a * 3 + bb] = fmaf(g, img[(h + a) * PWD + q + bb], acc[a * 3 + bb]);
-      acc[9] += g;
+        for (int bb = 0; bb < 3; ++bb)
+          acc[a * 3 + bb] = fma((double)g, (double)img[(h + a) * PWD + q + bb], acc[a * 3 + bb]);
+      acc[9] += (double)g;
     }
 #pragma unroll
     for (int u = 0; u < 10; ++u) {
-      float v = acc[u];
+      double v = acc[u];
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane16 == 0) part[((long long)blockIdx.x * K + k) * 10 + u] = v;
@@ -304,13 +307,13 @@ int conv1_parts(int B, int H) {
 
 // dw1, db1 = sums of the n per-block partials, in block order, f64.  One
 // block per output value.
-__global__ void __launch_bounds__(256) conv1_wgrad_finish_kernel(const float *__restrict__ part,
+__global__ void __launch_bounds__(256) conv1_wgrad_finish_kernel(const double *__restrict__ part,
                                                                  float *__restrict__ dw, float *__restrict__ db,
                                                                  int B, int K) {
   __shared__ double sh[256];
   const int k = blockIdx.x / 10, u = blockIdx.x % 10;
   double s = 0.0;
-  for (int b = threadIdx.x; b < B; b += 256) s += (double)part[((long long)b * K + k) * 10 + u];
+  for (int b = threadIdx.x; b < B; b += 256) s += part[((long long)b * K + k) * 10 + u];
   sh[threadIdx.x] = s;
   __syncthreads();
   for (int o = 128; o > 0; o >>= 1) {
@@ -533,8 +536,8 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, c
   }
   const int parts = conv1_parts(B, H);
   Workspace *ws = nullptr;
-  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * parts * K * 10 * sizeof(float) + 256, &ws));
-  float *part = reinterpret_cast<float *>(ws->buf);
+  REMORA_TRY(get_workspace(ctx, (cudaStream_t)stream, (size_t)B * parts * K * 10 * sizeof(double) + 256, &ws));
+  double *part = reinterpret_cast<double *>(ws->buf);
   auto kern = H != 64      ? conv1_wgrad_pool_kernel<32, 32, 1>
               : parts == 4 ? conv1_wgrad_pool_kernel<64, 64, 4>
               : parts == 2 ? conv1_wgrad_pool_kernel<64, 64, 2>

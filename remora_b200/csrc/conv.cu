@@ -270,7 +270,8 @@ int read_conv(const RemoraConvSpec *spec, const RemoraMemRef4 *xin, const Remora
               bool x_is_input, DescView *X, DescView *Wd, DescView *Y, ConvGeom *g) {
   if (spec == nullptr) return fail(REMORA_ERR_ARG, "conv: null spec");
   if (spec->stride < 1 || spec->pad < 0) return fail(REMORA_ERR_ARG, "conv: stride %d pad %d", spec->stride, spec->pad);
-  if (spec->precision != REMORA_PREC_TF32 && spec->precision != REMORA_PREC_3XTF32)
+  if (spec->precision != REMORA_PREC_TF32 && spec->precision != REMORA_PREC_3XTF32 &&
+      spec->precision != REMORA_PREC_2XTF32)
     return fail(REMORA_ERR_ARG, "conv: unknown precision %d", spec->precision);
   REMORA_TRY(read_desc(xin, 4, X, x_is_input ? "conv input" : "conv output gradient"));
   REMORA_TRY(read_desc(w, 4, Wd, "conv weights"));

@@ -40,9 +40,14 @@
 // Raw stages, operand stages and two accumulators let TMA, transform, MMA
 // and epilogue of consecutive tiles overlap.  Input gradient: the same
 // kernel on dY with w'[c][k][r][s] = w[k][c][2-r][2-s].
-// 3xTF32: hi = x with the low 13 mantissa bits cleared, lo = x - hi, for
-// activations and weights; the MMA adds hi*hi + hi*lo + lo*hi into one
-// f32 accumulator.
+// Precision PREC: 0 TF32 (both operands as given, the tensor core reads
+// their TF32 part); 1 3xTF32: hi = x with the low 13 mantissa bits
+// cleared, lo = x - hi, for activations and weights, and the MMA adds
+// hi*hi + hi*lo + lo*hi into one f32 accumulator; 2 2xTF32: the weights
+// alone are split, their hi and lo halves stacked as the N = 2 * NOUT
+// columns of one MMA against the TF32 activations, and the epilogue adds
+// column c and column NOUT + c (one MMA of twice the width in place of
+// three: the activation operand is read once, not three times).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -71,9 +76,11 @@ constexpr uint8_t kNoGradCode = 255;
 // stages in CSPLIT slices of CIN / CSPLIT channels (one TMA load, one
 // transform and the MMAs of those channels each, accumulated into the same
 // TMEM accumulator), so that a tile of many channels still double-buffers.
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
+template <int CIN, int W, int TH, int NOUT, int PREC, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
           int CSPLIT = 1>
 struct ConvCfg {
+  static constexpr bool SPLIT3 = PREC == 1;            // hi / lo copies of both operands
+  static constexpr int NB = PREC == 2 ? 2 * NOUT : NOUT;  // MMA N: weight hi rows, then lo rows
   static constexpr int CH = CIN / CSPLIT;              // channels of one stage
   static constexpr bool PAR = FUSE == kFusePool;       // operand split by input row parity
   static constexpr int NPAR = PAR ? 2 : 1;
@@ -96,13 +103,13 @@ struct ConvCfg {
   static constexpr uint32_t RAW_BYTES = RAW_F32 + RAW_CODES;
   static constexpr uint32_t RAW_CODE_OFF = align1k(RAW_F32);
   static constexpr uint32_t RAW_STAGE = align1k(RAW_CODE_OFF + RAW_CODES);
-  static constexpr uint32_t BPLANE = NOUT * 16;
+  static constexpr uint32_t BPLANE = NB * 16;
   static constexpr uint32_t W_COPY = 9 * NPL * BPLANE;
   static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT3 ? 2 : 1));
   static constexpr uint32_t OFF_RAW = W_REGION;
   static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
   static constexpr size_t SMEM = (size_t)OFF_A + A_ST * A_STAGE + 1024;
-  static constexpr int ACC_COLS = MB * NPAR * NOUT;  // TMEM columns of one accumulator
+  static constexpr int ACC_COLS = MB * NPAR * NB;  // TMEM columns of one accumulator
   static constexpr int ITEMS = NPLS * ROWS * (W / 4);
   static constexpr int KSTEPS = CH / 8;  // K steps of one stage
   static_assert(CIN % CSPLIT == 0 && CH % 8 == 0 && W % 16 == 0 && (NOUT == 16 || NOUT == 32), "shape");
@@ -195,13 +202,15 @@ __device__ __forceinline__ uint64_t desc_interleaved(uint32_t saddr, uint32_t lb
   return tc::smem_desc(saddr, lbo, 128, 0);
 }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE, int CSPLIT>
+template <int CIN, int W, int TH, int NOUT, int PREC, int RAW_ST, int A_ST, int CG, int FUSE, int CSPLIT>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv3x3_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmx2,
                       ConvTCParams p) {
   // tmx: input rows (kFuseUnpool: pooled gradient values), tmx2: their pool
   // codes (kFuseUnpool only)
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
+  using Cf = ConvCfg<CIN, W, TH, NOUT, PREC, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
+  constexpr bool SPLIT3 = Cf::SPLIT3;
+  constexpr int NB = Cf::NB;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], afull[A_ST], aempty[A_ST], tfull[2], tempty[2],
@@ -247,6 +256,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       const float h = tf32_hi(v);
       *reinterpret_cast<float *>(smem + off) = h;
       *reinterpret_cast<float *>(smem + Cf::W_COPY + off) = __fsub_rn(v, h);
+    } else if (PREC == 2) {
+      // hi in row co, lo in row NOUT + co of the same plane
+      const float h = tf32_hi(v);
+      *reinterpret_cast<float *>(smem + off) = h;
+      *reinterpret_cast<float *>(smem + off + NOUT * 16) = __fsub_rn(v, h);
     } else {
       *reinterpret_cast<float *>(smem + off) = v;
     }
@@ -296,7 +310,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------ MMA issue
-      const uint32_t idesc = tc::idesc_tf32(128, NOUT, 0, 0);
+      const uint32_t idesc = tc::idesc_tf32(128, NB, 0, 0);
       // Descriptors are built once; an operand at byte offset o from a base
       // is the base descriptor plus o >> 4 (start-address field, no carry:
       // shared-memory addresses are below 2^18).
@@ -322,8 +336,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           const uint64_t ad_hi = ad_hi0 + (uint64_t)(mb * 128), ad_lo = ad_lo0 + (uint64_t)(mb * 128);
 #pragma unroll
           for (int a = 0; a < Cf::NPAR; ++a) {
-            // accumulator of conv rows with parity a (one block of NOUT columns each)
-            const uint32_t d = tbase + acc * Cf::ACC_COLS + (mb * Cf::NPAR + a) * NOUT;
+            // accumulator of conv rows with parity a (one block of NB columns each)
+            const uint32_t d = tbase + acc * Cf::ACC_COLS + (mb * Cf::NPAR + a) * NB;
 #pragma unroll
             for (int tap = 0; tap < 9; ++tap) {
               const int r = tap / 3, sc = tap % 3;
@@ -398,8 +412,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 / 2 + i) * (W / 2) +
                               col / 2;
           uint32_t top[CG], bot[CG];
-          tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NOUT, top);
-          tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NOUT, bot);
+          tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NB, top);
+          tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NB, bot);
+          if constexpr (PREC == 2) {
+            uint32_t tl[CG], bl[CG];
+            tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NB + NOUT, tl);
+            tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NB + NOUT, bl);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < CG; ++c) {
+              top[c] = __float_as_uint(__fadd_rn(__uint_as_float(top[c]), __uint_as_float(tl[c])));
+              bot[c] = __float_as_uint(__fadd_rn(__uint_as_float(bot[c]), __uint_as_float(bl[c])));
+            }
+          }
           tc::tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < CG; ++c) {
@@ -421,7 +446,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           const bool store = col < W && i < TH && h0 + i < p.H;
           const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 + i) * W + col;
           uint32_t r[CG];
-          tmem_ld_cols<CG>(tacc + mb * NOUT, r);
+          tmem_ld_cols<CG>(tacc + mb * NB, r);
+          if constexpr (PREC == 2) {
+            uint32_t rl[CG];
+            tmem_ld_cols<CG>(tacc + mb * NB + NOUT, rl);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < CG; ++c) r[c] = __float_as_uint(__fadd_rn(__uint_as_float(r[c]), __uint_as_float(rl[c])));
+          }
           tc::tmem_ld_wait();
 #pragma unroll
           for (int c = 0; c < CG; ++c)
@@ -539,16 +571,16 @@ struct ConvIO {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int CIN, int W, int TH, int NOUT, bool SPLIT3, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
+template <int CIN, int W, int TH, int NOUT, int PREC, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
           int CSPLIT = 1>
 int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStream_t stream, bool *handled) {
-  using Cf = ConvCfg<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
+  using Cf = ConvCfg<CIN, W, TH, NOUT, PREC, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
   if (!aligned16(io.x) || (FUSE == kFuseUnpool && !aligned16(io.x_codes)) ||
       (reinterpret_cast<uintptr_t>(io.y) & 3)) {
     *handled = false;  // TMA cannot address the input, or the output is not f32-aligned
     return REMORA_OK;
   }
-  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, SPLIT3, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
+  auto kern = conv3x3_tc_kernel<CIN, W, TH, NOUT, PREC, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
   static bool attr = false;
   if (!attr) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
@@ -576,49 +608,61 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
 }
 
 // Picks the instantiation for (input channels, width, output channels,
-// precision); *handled = false if there is none.
-int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+// precision); *handled = false if there is none.  prec: 0 TF32, 1 3xTF32,
+// 2 2xTF32 (weights split).
+int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, int prec, int sm_count,
              cudaStream_t stream, bool *handled) {
   *handled = false;
   const int nout = p.COUT <= 16 ? 16 : 32;
   if (cin == 16 && width == 64 && nout == 32)
-    return split ? launch_conv<16, 64, 8, 32, true, 2, 1, 16>(io, p, sm_count, stream, handled)
-                 : launch_conv<16, 64, 8, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<16, 64, 8, 32, 1, 2, 1, 16>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<16, 64, 4, 32, 2, 2, 2, 16>(io, p, sm_count, stream, handled)
+                     : launch_conv<16, 64, 8, 32, 0, 2, 2, 16>(io, p, sm_count, stream, handled);
   // 32 input channels: two 16-channel stages per tile, double-buffered
   if (cin == 32 && width == 64 && nout == 16)
-    return split ? launch_conv<32, 64, 4, 16, true, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 64, 8, 16, false, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<32, 64, 4, 16, 1, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<32, 64, 8, 16, 2, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+                     : launch_conv<32, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
   if (cin == 16 && width == 32 && nout == 32)
-    return split ? launch_conv<16, 32, 16, 32, true, 1, 1, 16>(io, p, sm_count, stream, handled)
-                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<16, 32, 16, 32, 1, 1, 1, 16>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16>(io, p, sm_count, stream, handled)
+                     : launch_conv<16, 32, 16, 32, 0, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 32 && nout == 16)
-    return split ? launch_conv<32, 32, 8, 16, true, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<32, 32, 8, 16, 1, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<32, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
+                     : launch_conv<32, 32, 16, 16, 0, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
 // The fused forms of the crater CNN's second layer (16 -> 32 channels on
 // 32 x 32 images and its input gradient).
-int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, int prec, int sm_count,
                   cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 16 && width == 32 && p.COUT > 16 && p.COUT <= 32 && p.H % 2 == 0)
-    return split ? launch_conv<16, 32, 16, 32, true, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
-                 : launch_conv<16, 32, 16, 32, false, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<16, 32, 16, 32, 1, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled)
+                     : launch_conv<16, 32, 16, 32, 0, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
-int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width, bool split, int sm_count,
+int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width, int prec, int sm_count,
                     cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 32 && width == 32 && p.COUT <= 16 && p.H % 2 == 0)
-    return split ? launch_conv<32, 32, 8, 16, true, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
-                 : launch_conv<32, 32, 16, 16, false, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled);
+    return prec == 1 ? launch_conv<32, 32, 8, 16, 1, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
+         : prec == 2 ? launch_conv<32, 32, 16, 16, 2, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
+                     : launch_conv<32, 32, 16, 16, 0, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled);
   return REMORA_OK;
 }
 
+int prec_code(int precision) {
+  return precision == REMORA_PREC_3XTF32 ? 1 : precision == REMORA_PREC_2XTF32 ? 2 : 0;
+}
+
 bool shape_ok(const ConvGeom &g, const void *x, int precision) {
-  return (precision == REMORA_PREC_TF32 || precision == REMORA_PREC_3XTF32) && g.R == 3 && g.S == 3 &&
+  return (precision == REMORA_PREC_TF32 || precision == REMORA_PREC_3XTF32 || precision == REMORA_PREC_2XTF32) &&
+         g.R == 3 && g.S == 3 &&
          g.pad == 1 && g.stride == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && g.N > 0 && g.H > 0;
 }
 
@@ -631,7 +675,7 @@ int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const flo
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, y, nullptr, g.N, g.H, g.K, 0, 0, ws->err};
-  return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
+  return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, prec_code(precision), ctx->sm_count,
                   stream, handled);
 }
 
@@ -642,7 +686,7 @@ int conv_tc_fwd_relu_pool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x,
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, pooled, codes, g.N, g.H, g.K, 0, 0, ws->err};
-  return dispatch_pool(ConvIO{x, nullptr, pooled, codes}, p, g.C, g.W, precision == REMORA_PREC_3XTF32,
+  return dispatch_pool(ConvIO{x, nullptr, pooled, codes}, p, g.C, g.W, prec_code(precision),
                        ctx->sm_count, stream, handled);
 }
 
@@ -653,7 +697,7 @@ int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpo
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
-  return dispatch_unpool(ConvIO{dpooled, codes, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32,
+  return dispatch_unpool(ConvIO{dpooled, codes, dx, nullptr}, p, g.K, g.W, prec_code(precision),
                          ctx->sm_count, stream, handled);
 }
 
@@ -665,7 +709,7 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights
   ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
-  return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, precision == REMORA_PREC_3XTF32, ctx->sm_count,
+  return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, prec_code(precision), ctx->sm_count,
                   stream, handled);
 }
 

@@ -22,7 +22,9 @@
 //                   3xTF32 adds a second one against the low halves of x:
 //                   [dy_hi; dy_lo] x x_hi + [dy_hi; dy_lo] x x_lo covers
 //                   hi*hi, lo*hi, hi*lo (and lo*lo) in one accumulator whose
-//                   two 32-row halves the epilogue adds.
+//                   two 32-row halves the epilogue adds.  2xTF32 keeps the
+//                   split rows of dy and the first MMA only:
+//                   [dy_hi; dy_lo] x x (x as TF32).
 //   warps 2-5       epilogue, once at the end: TMEM -> shared -> partials.
 // Chunks of the operands are 16 bytes longer than their rows so that the
 // lanes of the transform, which walk consecutive chunks, hit different
@@ -52,15 +54,18 @@ constexpr int kWgTransformThreads = kWgTransformWarps * 32;
 // UNPOOL: dy is given as a pooled gradient and its 2x2 max-pool codes
 // ([COUT][H/2][W/2] each); the transform expands it (the pooled value goes
 // to the recorded window element, the others are 0).
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL = false>
+// PREC: 0 TF32, 1 3xTF32 (dy and x split), 2 2xTF32 (dy split, x TF32).
+template <int W, int R, int PREC, int RAW_ST, int OP_ST, bool UNPOOL = false>
 struct WgCfg {
+  static constexpr bool SPLIT_A = PREC >= 1;  // dy as [hi; lo] rows
+  static constexpr bool SPLIT_B = PREC == 1;  // x hi and lo copies
   static constexpr int CPR = W / 4;     // 4-pixel chunks per image row
   static constexpr int NCH = R * CPR;   // chunks per tile
   static constexpr uint32_t A_CH = kWgRowsA * 16 + 16;
   static constexpr uint32_t B_CH = kWgRowsB * 16 + 16;
   static constexpr uint32_t A_BYTES = NCH * A_CH;
   static constexpr uint32_t B_BYTES = NCH * B_CH;
-  static constexpr uint32_t OP_STAGE = wg_align1k(A_BYTES + B_BYTES * (SPLIT3 ? 2 : 1));
+  static constexpr uint32_t OP_STAGE = wg_align1k(A_BYTES + B_BYTES * (SPLIT_B ? 2 : 1));
   static constexpr uint32_t RAWX = kWgCin * (R + 2) * W * 4;
   static constexpr uint32_t RAWD = UNPOOL ? 32 * (R / 2) * (W / 2) * 4 : 32 * R * W * 4;
   static constexpr uint32_t RAWC = UNPOOL ? 32 * (R / 2) * (W / 2) : 0;  // codes
@@ -116,12 +121,12 @@ __device__ __forceinline__ void wg_put(uint32_t hi, uint32_t lo, float4 v) {
   }
 }
 
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL>
+template <int W, int R, int PREC, int RAW_ST, int OP_ST, bool UNPOOL>
 __global__ void __launch_bounds__(kWgThreads, 1)
     conv_wgrad_tc_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmd,
                          const __grid_constant__ CUtensorMap tmc, WgParams p) {
   // tmd: dy rows, or with UNPOOL the pooled gradient; tmc: its codes
-  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
+  using Cf = WgCfg<W, R, PREC, RAW_ST, OP_ST, UNPOOL>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t rfull[RAW_ST], rempty[RAW_ST], ofull[OP_ST], oempty[OP_ST], drain, efull;
@@ -209,7 +214,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
           const uint64_t ao = (uint64_t)((2 * j * Cf::A_CH) >> 4), bo = (uint64_t)((2 * j * Cf::B_CH) >> 4);
           tc::mma_tf32(tbase, ad + ao, bd + bo, idesc, accum);
           accum = 1;
-          if (SPLIT3) tc::mma_tf32(tbase, ad + ao, bld + bo, idesc, 1);
+          if (Cf::SPLIT_B) tc::mma_tf32(tbase, ad + ao, bld + bo, idesc, 1);
         }
         issued = true;
         tc::mma_commit(&oempty[st]);
@@ -285,7 +290,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
           v = wg_ld4(rawd + (uint32_t)((co * R + hr) * W + w0) * 4);
         }
         const uint32_t dst = a0 + kc * Cf::A_CH + co * 16;
-        wg_put<SPLIT3>(dst, dst + 32 * 16, v);
+        wg_put<Cf::SPLIT_A>(dst, dst + 32 * 16, v);
       }
       // B: x rows shifted by the tap, three column shifts from one read
       for (int item = tt; item < Cf::ITEMS_B; item += kWgTransformThreads) {
@@ -296,9 +301,10 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         const float prev = w0 > 0 ? wg_ld1(row + (w0 - 1) * 4) : 0.0f;
         const float next = w0 + 4 < W ? wg_ld1(row + (w0 + 4) * 4) : 0.0f;
         const uint32_t dst = b0 + kc * Cf::B_CH + ((r * 3) * kWgCin + ci) * 16;
-        wg_put<SPLIT3>(dst, dst + Cf::B_BYTES, make_float4(prev, L.x, L.y, L.z));
-        wg_put<SPLIT3>(dst + kWgCin * 16, dst + kWgCin * 16 + Cf::B_BYTES, L);
-        wg_put<SPLIT3>(dst + 2 * kWgCin * 16, dst + 2 * kWgCin * 16 + Cf::B_BYTES, make_float4(L.y, L.z, L.w, next));
+        wg_put<Cf::SPLIT_B>(dst, dst + Cf::B_BYTES, make_float4(prev, L.x, L.y, L.z));
+        wg_put<Cf::SPLIT_B>(dst + kWgCin * 16, dst + kWgCin * 16 + Cf::B_BYTES, L);
+        wg_put<Cf::SPLIT_B>(dst + 2 * kWgCin * 16, dst + 2 * kWgCin * 16 + Cf::B_BYTES,
+                            make_float4(L.y, L.z, L.w, next));
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -353,11 +359,11 @@ int wg_encode(const void *x, int N, int C, int H, int W, int box_rows, int box_c
   return REMORA_OK;
 }
 
-template <int W, int R, bool SPLIT3, int RAW_ST, int OP_ST, bool UNPOOL = false>
+template <int W, int R, int PREC, int RAW_ST, int OP_ST, bool UNPOOL = false>
 int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, const uint8_t *codes,
                  float *dw, float *db, cudaStream_t stream) {
-  using Cf = WgCfg<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
-  auto kern = conv_wgrad_tc_kernel<W, R, SPLIT3, RAW_ST, OP_ST, UNPOOL>;
+  using Cf = WgCfg<W, R, PREC, RAW_ST, OP_ST, UNPOOL>;
+  auto kern = conv_wgrad_tc_kernel<W, R, PREC, RAW_ST, OP_ST, UNPOOL>;
   static bool attr = false;
   if (!attr) {
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
@@ -387,23 +393,30 @@ int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const fl
   return REMORA_OK;
 }
 
+// 0 TF32, 1 3xTF32, 2 2xTF32; -1 for an unknown precision
+int wg_prec(int precision) {
+  return precision == REMORA_PREC_TF32 ? 0 : precision == REMORA_PREC_3XTF32 ? 1 : precision == REMORA_PREC_2XTF32 ? 2 : -1;
+}
+
 }  // namespace
 
 int conv_tc_wgrad_bias(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, float *dw, float *db,
                        int precision, cudaStream_t stream, bool *handled) {
   *handled = false;
-  const bool split = precision == REMORA_PREC_3XTF32;
-  if (!(precision == REMORA_PREC_TF32 || split) || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
+  const int prec = wg_prec(precision);
+  if (prec < 0 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
       g.C != kWgCin || g.K < 1 || g.K > 32 || g.N < 1 || g.H < 1 || g.OH != g.H || g.OW != g.W)
     return REMORA_OK;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(dy) & 15)) return REMORA_OK;
   *handled = true;
   if (g.W == 32)
-    return split ? launch_wgrad<32, 2, true, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
-                 : launch_wgrad<32, 2, false, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
+    return prec == 1 ? launch_wgrad<32, 2, 1, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+         : prec == 2 ? launch_wgrad<32, 2, 2, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+                     : launch_wgrad<32, 2, 0, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
   if (g.W == 64)
-    return split ? launch_wgrad<64, 1, true, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
-                 : launch_wgrad<64, 1, false, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
+    return prec == 1 ? launch_wgrad<64, 1, 1, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+         : prec == 2 ? launch_wgrad<64, 1, 2, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+                     : launch_wgrad<64, 1, 0, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
   *handled = false;
   return REMORA_OK;
 }
@@ -412,16 +425,17 @@ int conv_tc_wgrad_bias_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float
                               const uint8_t *codes, float *dw, float *db, int precision, cudaStream_t stream,
                               bool *handled) {
   *handled = false;
-  const bool split = precision == REMORA_PREC_3XTF32;
-  if (!(precision == REMORA_PREC_TF32 || split) || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
+  const int prec = wg_prec(precision);
+  if (prec < 0 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
       g.C != kWgCin || g.K < 1 || g.K > 32 || g.N < 1 || g.H < 2 || g.H % 2 || g.OH != g.H || g.OW != g.W ||
       g.W != 32)
     return REMORA_OK;
   const auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!a16(x) || !a16(dpooled) || !a16(codes)) return REMORA_OK;
   *handled = true;
-  return split ? launch_wgrad<32, 2, true, 1, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream)
-               : launch_wgrad<32, 2, false, 2, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream);
+  return prec == 1 ? launch_wgrad<32, 2, 1, 1, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream)
+       : prec == 2 ? launch_wgrad<32, 2, 2, 2, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream)
+                   : launch_wgrad<32, 2, 0, 2, 2, true>(ctx, g, x, dpooled, codes, dw, db, stream);
 }
 
 }  // namespace remora

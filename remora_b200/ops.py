@@ -169,7 +169,8 @@ def gemm(a, b, *, precision: str = "3xtf32", out=None):
 
 # ---------------------------------------------------------- convolution
 def _conv_spec(stride: int, pad: int, precision: str) -> L.RemoraConvSpec:
-    return L.RemoraConvSpec(int(stride), int(pad), {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32}[precision], 0)
+    return L.RemoraConvSpec(int(stride), int(pad), {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32,
+                                                    "2xtf32": L.PREC_2XTF32}[precision], 0)
 
 
 def conv2d_fwd(x, w, bias=None, *, stride: int = 1, pad: int = 1, precision: str = "3xtf32", out=None):
@@ -259,6 +260,17 @@ def synchronize(device: int | None = None) -> None:
     dev = torch.cuda.current_device() if device is None else device
     s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     L.check(L.lib().remora_b200_synchronize(context(dev).ptr, s), "synchronize")
+
+
+def wait_check(limit_cycles: int, signal: bool = False, device: int | None = None) -> None:
+    """Enqueue the bounded-wait check (remora_b200_wait_check) on the current
+    stream: a wait on a barrier that only `signal` completes, given up after
+    `limit_cycles`.  The next synchronize() raises RemoraTimeoutError when it
+    ran out."""
+    torch = _torch()
+    dev = torch.cuda.current_device() if device is None else device
+    s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    L.check(L.lib().remora_b200_wait_check(context(dev).ptr, int(limit_cycles), int(bool(signal)), s), "wait_check")
 
 
 # ------------------------------------------- the C runtime helpers on GPU

@@ -42,6 +42,17 @@ def _run(cuda, oracle_mod, batch, precision, steps=1):
     return loss, grads, to_host(net.params), ref_loss, ref_grads, ref_params
 
 
+def _compare_from(grads, ref, tol, start):
+    """_compare over the tensors that start at or after flat index `start`."""
+    for name, (a, b, _) in crater.offsets().items():
+        if a < start:
+            continue
+        r = ref[a:b].astype(np.float64)
+        scale = max(float(np.abs(r).max()), 1e-12)
+        err = float(np.abs(grads[a:b] - r).max()) / scale
+        assert err <= tol, f"{name}: scaled error {err:.3g} > {tol}"
+
+
 def _compare(grads, ref, tol):
     for name, (a, b, _) in crater.offsets().items():
         r = ref[a:b].astype(np.float64)
@@ -56,6 +67,55 @@ def test_cnn_step_3xtf32_matches_oracle(cuda, oracle_mod, batch):
     assert abs(loss - ref_loss) <= 1e-4 * max(1.0, abs(ref_loss))
     _compare(grads, ref_grads, 1e-4)
     np.testing.assert_allclose(params, ref_params, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("batch, batch_total, precision", [(512, 4096, "mixed"), (4096, 4096, "mixed"),
+                                                        (512, 4096, "3xtf32")])
+def test_cnn_graph_step_matches_oracle_at_bench_sizes(cuda, oracle_mod, batch, batch_total, precision):
+    """The step the benchmark times, at the sizes it times: 4096 images on
+    one GPU, and the 512-image shard of one rank of an 8-GPU run (conv1
+    split over several blocks per image, one allreduce of the whole
+    gradient after the backward; on one GPU the sum over ranks is the
+    tensor itself).  capture() runs one eager step and records the next;
+    replay() runs it from the CUDA graph.  Loss, every gradient tensor and
+    the parameters after both steps are compared with two oracle steps.
+
+    The loss and the dense layers' gradients are held to 1e-4 * max|ref|;
+    the two conv layers' gradients to the 1e-3 gradient tolerance of the
+    tensor-core path.  Each of those sums every pixel of the batch with
+    heavy cancellation, against an oracle that accumulates in f64, while the
+    tensor core accumulates a CTA's share of the batch in f32: measured on a
+    B200 at 512 of 4096 in 3xTF32, 4.3e-4 * max|ref| for conv2's weight
+    gradient.  The default mixed precision (2xTF32 for the conv layer's two
+    gradients) adds about 4e-4 more by an f64 error study of the step."""
+    import torch
+
+    from remora_b200.cnn import CraterCNN
+
+    params = crater.init_params()
+    imgs, labels = crater.make_batch(batch)
+    reduced = []
+
+    def allreduce(t) -> None:  # one rank: the sum over ranks is the tensor itself
+        reduced.append(t.numel())
+
+    net = CraterCNN(cuda, batch, batch_total, lr=0.01, params=params, precision=precision,
+                    allreduce=allreduce if batch < batch_total else None)
+    xi, yi = torch.from_numpy(imgs).to(cuda), torch.from_numpy(labels).to(cuda)
+    net.capture(xi, yi)
+    net.replay()
+    grads, got = to_host(net.grads).copy(), to_host(net.params)
+    loss = net.loss()
+    ref = params.copy()
+    nt = oracle_mod.max_threads()
+    oracle_mod.cnn_step(ref, imgs, labels, batch_total=batch_total, lr=0.01, nthreads=nt)
+    ref_loss, ref_grads = oracle_mod.cnn_step(ref, imgs, labels, batch_total=batch_total, lr=0.01, nthreads=nt)
+    assert abs(loss - ref_loss) <= 1e-4 * max(1.0, abs(ref_loss))
+    _compare(grads, ref_grads, 1e-3)
+    _compare_from(grads, ref_grads, 1e-4, crater.offsets()["w3"][0])
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+    if batch < batch_total:
+        assert not net.overlap and reduced and reduced[-1] == crater.NPARAMS
 
 
 def test_cnn_step_tf32_matches_oracle(cuda, oracle_mod):
@@ -148,7 +208,7 @@ def test_conv1_relu_pool_and_wgrad_layers(cuda, oracle_mod, hw):
     np.testing.assert_allclose(to_host(db), ref_b, rtol=1e-5, atol=1e-5 * float(np.abs(ref_b).max()))
 
 
-@pytest.mark.parametrize("precision", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("precision", ["tf32", "3xtf32", "2xtf32"])
 def test_fused_conv2_pool_matches_unfused(cuda, precision):
     """conv2 + ReLU + max-pool in one kernel, and the conv2 gradients taken
     straight from the pooled gradient, give bit for bit what the separate
@@ -167,7 +227,8 @@ def test_fused_conv2_pool_matches_unfused(cuda, precision):
     x = dev(rng.standard_normal((B, 16, 32, 32)).astype(np.float32))
     w = dev((rng.standard_normal((32, 16, 3, 3)) * 0.1).astype(np.float32))
     b = dev((rng.standard_normal(32) * 0.1).astype(np.float32))
-    spec = L.RemoraConvSpec(1, 1, {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32}[precision], 0)
+    spec = L.RemoraConvSpec(1, 1, {"tf32": L.PREC_TF32, "3xtf32": L.PREC_3XTF32, "2xtf32": L.PREC_2XTF32}[precision],
+                            0)
     ctx = context(cuda.index)
     stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
     keep = []
@@ -286,3 +347,28 @@ def test_dense_bias_relu_bce_matches_unfused(cuda):
                                                d(g2), ctypes.c_float(1 / B), stream) == 0
     for a, b_ in ((h2, h_ref), (z2, z1), (l2, l1), (g2, g1)):
         np.testing.assert_array_equal(to_host(a), to_host(b_))
+
+
+def test_cnn_resume_from_checkpoint_matches_unbroken_run(cuda, tmp_path):
+    """Three SGD steps on the device, against two steps, a checkpoint, a new
+    model restored from it (its step captured as a CUDA graph) and one more
+    step: the same parameters bit for bit (the step is deterministic)."""
+    import torch
+
+    from remora_b200.cnn import CraterCNN
+
+    imgs, labels = crater.make_batch(64)
+    xi, yi = torch.from_numpy(imgs).to(cuda), torch.from_numpy(labels).to(cuda)
+    a = CraterCNN(cuda, 64, lr=0.05)
+    for _ in range(3):
+        a.step(xi, yi)
+    b = CraterCNN(cuda, 64, lr=0.05)
+    for _ in range(2):
+        b.step(xi, yi)
+    b.save(tmp_path / "cnn.npz", step=2)
+    c = CraterCNN(cuda, 64, lr=0.05, params=np.zeros(crater.NPARAMS, np.float32))
+    c.step(xi, yi)               # compile and size workspaces on throwaway parameters
+    c.capture(xi, yi)            # then record the step's graph
+    assert c.restore(tmp_path / "cnn.npz") == 2
+    c.replay()                   # step 3 from the graph, on the restored parameters
+    np.testing.assert_array_equal(to_host(c.params), to_host(a.params))
