@@ -2,25 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
 
-Default workload (``--config chained``): the fused chained-map fold
-f32[64,64,64,64] ~ N(0,1): y = x*2.5 + 1.0, mask y > 0.5 ? y : 0, fold (+)
-over the last axis -> f32[64,64,64]; metric HBM GB/s of algorithmic bytes
-(67,108,864 read + 1,048,576 written per call).  One step = one pass over a
-rotation of 8 distinct inputs (545 MB, more than 4x the 126 MB L2, so every
-call streams from HBM).
+Default workload (``--config cnn``): one SGD step of the crater CNN on a
+global batch of 4096 synthetic 64x64 images (conv3x3 1->16 + ReLU, pool,
+conv3x3 16->32 + ReLU, pool, dense 8192->64 + ReLU, dense 64->1, sigmoid BCE,
+SGD lr 0.01), in samples/s of the whole job.  Tensor-core math is mixed:
+3xTF32 for the forward convolution and the dense layers, 2xTF32 for the
+convolution's two gradients, every gradient within 1e-3 of the f32 step.  With
+N GPUs (torchrun, one process per GPU) the batch is split 4096/N per rank and
+the gradient (529,217 f32) is summed by an NCCL allreduce inside the step's
+CUDA graph: strong scaling, the only workload here with a collective.  The
+roofline is that of the step's dominant stage, each stage timed alone.
 
-Other configs: ``row_norms`` (f32[8192,1024] -> sqrt(sum x*x)), ``matmul``
-(A,B f32[4096,4096], TF32; ``matmul_3x`` the 3xTF32 form), ``bmm``
+Other configs: ``chained`` (the fused chained-map fold f32[64,64,64,64] ~
+N(0,1): y = x*2.5 + 1.0, mask y > 0.5 ? y : 0, fold (+) over the last axis,
+in HBM GB/s over a rotation of 8 distinct inputs, 545 MB > 126 MB L2),
+``row_norms`` (f32[8192,1024] -> sqrt(sum x*x)), ``matmul`` (A,B
+f32[4096,4096], TF32; ``matmul_3x`` the 3xTF32 form), ``bmm``
 ([32,1024,1024] x [32,1024,1024], TF32), ``conv`` / ``conv_dgrad`` /
-``conv_wgrad`` (x [256,16,64,64] * w [32,16,3,3], pad 1), ``cnn`` (crater-CNN
-SGD step, global batch 4096, data parallel over N ranks with an NCCL
-gradient allreduce: strong scaling; 3xTF32, ``cnn_tf32`` the TF32 form),
-``sort`` / ``grade`` / ``filter`` (the reference's C runtime helpers on
-2^26 f32 keys ~ N(0,1); filter keeps x > 0).
+``conv_wgrad`` (x [256,16,64,64] * w [32,16,3,3], pad 1), ``cnn_3x`` (the
+CNN step with 3xTF32 everywhere), ``cnn_tf32`` (the
+CNN step in plain TF32, outside the 1e-3 gradient tolerance: a speed
+reference only), ``scan`` (inclusive + scan of 2^28 f32), ``sort`` /
+``grade`` / ``filter`` (the reference's C runtime helpers on 2^26 f32 keys ~
+N(0,1); filter keeps x > 0).  Those run as independent replicas when N > 1
+(weak scaling: folds shard frames, matmuls shard rows; no collective).
 
-With N GPUs (torchrun, one process per GPU) every rank runs its own copy of
-the workload (weak scaling: folds shard frames, matmuls shard rows; no
-data-path collective); rank 0 prints the aggregate over max-over-ranks time.
 ``--impl reference`` times the CPU restatement of the reference's CPU path
 (the oracle, OpenMP over all host threads) on a bounded sample of the same
 workload and prints the same JSON line with ``"impl": "reference"``.
@@ -474,10 +480,28 @@ class CnnWorkload:
     OVERLAP = None  # the step's own choice
     FLOPS_PER_SAMPLE = 33.8e6  # forward + backward, all layers
 
+    # Algorithmic work per image of each stage of the step (CraterCNN.stages):
+    # (flops, bytes, runs on the tensor cores).  Bytes count each operand and
+    # result once: conv2 reads p1 [16,32,32] (65,536 B) and writes the pooled
+    # [32,16,16] f32 (32,768 B) plus its pool codes (8,192 B); its two
+    # gradients read the pooled gradient and codes and write or read p1.
+    STAGE_WORK = {
+        "conv1_fwd": (2 * 4096 * 16 * 9, 16384 + 65536 + 16384, False),
+        "conv2_fwd": (2 * 1024 * 32 * 144, 65536 + 32768 + 8192, True),
+        "dense1_fwd": (2 * 8192 * 64, 32768 + 256, True),
+        "head": (4 * 64 + 16, 256 * 2 + 16, False),
+        "head_bwd": (6 * 64, 256 * 2 + 8, False),
+        "dense1_wgrad": (2 * 8192 * 64, 32768 + 256, True),
+        "dense1_dgrad": (2 * 8192 * 64, 32768 + 256, True),
+        "conv2_wgrad": (2 * 1024 * 32 * 144, 65536 + 32768 + 8192, True),
+        "conv2_dgrad": (2 * 1024 * 16 * 288, 32768 + 8192 + 65536, True),
+        "conv1_wgrad": (2 * 4096 * 16 * 9, 16384 + 65536 + 16384, False),
+    }
+
     def __init__(self, name: str) -> None:
         self.name = name
         self.rotate = 1
-        self.precision = "tf32" if name == "cnn_tf32" else "3xtf32"
+        self.precision = {"cnn": "mixed", "cnn_3x": "3xtf32", "cnn_tf32": "tf32"}[name]
         self.desc = (f"crater CNN train step ({self.precision}), global batch 4096 of 64x64 synthetic images (noise 0.1, 1-3 rims r 4-16 "
                      "on positives, 50/50): conv3x3 1->16+ReLU, pool, conv3x3 16->32+ReLU, pool, dense 8192->64+ReLU, "
                      "dense 64->1, sigmoid BCE, SGD lr 0.01")
@@ -486,9 +510,7 @@ class CnnWorkload:
         import torch
 
         from remora_b200 import crater
-        from remora_b200.cnn import CraterCNN
-
-        from remora_b200.cnn import process_group_allreduce, shard
+        from remora_b200.cnn import CraterCNN, process_group_allreduce, shard
 
         world = getattr(self, "world", 1)
         self.torch, self.dev = torch, dev
@@ -497,21 +519,23 @@ class CnnWorkload:
         self.B = hi - lo
         self.work_per_call = float(self.B)  # samples per rank per step; x world in the harness
         self.himg, self.hlab = crater.make_batch(self.B, start=lo)
-        self.x = torch.from_numpy(self.himg).to(dev)
-        self.y = torch.from_numpy(self.hlab).to(dev)
+        # two input buffers: the end-to-end run copies step k+1's batch into
+        # one while step k reads the other (one captured graph per buffer)
+        self.xs = [torch.from_numpy(self.himg).to(dev) for _ in range(2)]
+        self.ys = [torch.from_numpy(self.hlab).to(dev) for _ in range(2)]
         allreduce = process_group_allreduce() if world > 1 else None
         self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision,
                              overlap_allreduce=self.OVERLAP)
-        self.net.step(self.x, self.y)  # eager step: compiles map programs, sizes workspaces
-        self.net.capture(self.x, self.y)
+        self.net.step(self.xs[0], self.ys[0])  # eager step: compiles map programs, sizes workspaces
+        self.gid = [self.net.capture(self.xs[k], self.ys[k]) for k in range(2)]
         # library kernels in one replay of the step's graph, counted at capture
         self.graph_launches_per_call = self.net.graph_launches
 
     def call(self, k: int) -> None:
-        self.net.replay()
+        self.net.replay(self.gid[0])
 
     def close(self) -> None:
-        self.net.graph = None
+        self.net.release_graphs()
         self.torch.cuda.synchronize()
 
     def check(self) -> None:
@@ -519,18 +543,92 @@ class CnnWorkload:
         if not bool(self.torch.isfinite(self.net.params).all()):
             raise SystemExit("non-finite parameters after the warm-up steps")
 
+    def stage_times(self, peaks: dict, reps: int = 10) -> dict:
+        """Each stage of the step timed alone on this rank (a CUDA graph of
+        `reps` calls, CUDA events on the launching stream, after one warm-up
+        replay) with its roofline: the larger of the HBM time of its bytes and
+        the tensor time of its flops.  3xTF32 issues three TF32 products per
+        product and 2xTF32 two, so their tensor peaks are a third and a half
+        of the TF32 rate; the mixed step runs its forward and GEMMs in 3xTF32
+        and the conv layer's gradients in 2xTF32."""
+        torch = self.torch
+        stream = torch.cuda.current_stream(self.dev)
+        tf32 = tf32_peak(peaks) * 1e12
+        out = {}
+        for name, (fl, by, tensor) in self.STAGE_WORK.items():
+            mult = self.tf32_products(name)
+            graph, keep = self.net.stage_graph(name, self.xs[0], self.ys[0], reps)
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            flops, nbytes = fl * self.B, by * self.B
+            t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+            t_tc = mult * flops / tf32 if tensor else 0.0
+            bound = "tensor" if t_tc > t_hbm else "hbm"
+            if bound == "tensor":
+                achieved, peak, unit = flops / (ms * 1e-3) / 1e12, tf32 / mult / 1e12, "TFLOP/s"
+            else:
+                achieved, peak, unit = nbytes / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+            out[name] = {"ms": round(ms, 5), "bound": bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
+                         "unit": unit, "frac": round(achieved / peak, 4), "flops": flops, "bytes": nbytes}
+            del graph, keep
+        return out
+
+    def tf32_products(self, stage: str) -> float:
+        """TF32 tensor-core products per product of a stage's arithmetic."""
+        if self.precision == "tf32":
+            return 1.0
+        if self.precision == "mixed" and stage in ("conv2_wgrad", "conv2_dgrad"):
+            return 2.0
+        return 3.0
+
     def e2e_setup(self) -> tuple[int, int]:
         torch = self.torch
         self.pin_x = torch.from_numpy(self.himg).pin_memory()
         self.pin_y = torch.from_numpy(self.hlab).pin_memory()
-        self.pin_loss = torch.empty(self.B, dtype=torch.float32).pin_memory()
+        self.pin_loss = torch.empty(2, dtype=torch.float32).pin_memory()
+        self.copy_stream = torch.cuda.Stream(self.dev)
+        self.e2e_k = 0
+        self.step_done = [None, None]
         return (self.pin_x.numel() + self.pin_y.numel()) * 4, 4
 
+    def _h2d(self, buf: int):
+        """Host->device copy of a step's batch into input buffer `buf` on the
+        copy stream, after the step that last read that buffer."""
+        torch = self.torch
+        with torch.cuda.stream(self.copy_stream):
+            if self.step_done[buf] is not None:
+                self.copy_stream.wait_event(self.step_done[buf])
+            self.xs[buf].copy_(self.pin_x, non_blocking=True)
+            self.ys[buf].copy_(self.pin_y, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
+        return ev
+
+    def e2e_begin(self) -> None:
+        """Start of a timed end-to-end run: the first step's batch is copied
+        inside the timed region like every other."""
+        self.e2e_k = 0
+        self.ready = self._h2d(0)
+
     def e2e_step(self) -> None:
-        self.x.copy_(self.pin_x, non_blocking=True)
-        self.y.copy_(self.pin_y, non_blocking=True)
-        self.net.replay()
+        """Step k on input buffer k % 2, with step k+1's batch copied into the
+        other buffer meanwhile; the step's loss is read back to host."""
+        torch = self.torch
+        cur = torch.cuda.current_stream(self.dev)
+        buf = self.e2e_k % 2
+        cur.wait_event(self.ready)
+        self.net.replay(self.gid[buf])
+        done = torch.cuda.Event()
+        done.record(cur)
+        self.step_done[buf] = done
+        self.ready = self._h2d(1 - buf)
         self.pin_loss[:1].copy_(self.net.loss_b[:1], non_blocking=True)  # the step's result read back
+        self.e2e_k += 1
 
     def cpu_prepare(self) -> None:
         from remora_b200 import crater
@@ -544,6 +642,85 @@ class CnnWorkload:
         return 32.0
 
     cpu_sample = "32 samples per SGD step (oracle CNN step: forward, backward, update; OpenMP over images)"
+
+
+class ScanWorkload:
+    """Inclusive + scan of 2^28 f32 ~ U[-1,1] along the leading axis (the
+    reference's rank-1 scan, remora/lowering/tensor_ops.py:2301-2482): 1 GiB
+    in and 1 GiB out, larger than L2.  `value` counts the algorithmic 8 B per
+    element (read once, write once); the reduce-then-scan implementation
+    reads the input twice (12 B per element), which the roofline counts."""
+
+    metric, unit, bound = METRIC_FOLD, "GB/s", "hbm"
+
+    def __init__(self, name: str) -> None:
+        self.name = name
+        self.n = 1 << 28
+        self.work_per_call = 8 * self.n
+        self.bytes_per_call = 12 * self.n
+        self.rotate = 1
+        self.desc = f"inclusive + scan f32[{self.n}] ~ U[-1,1]"
+
+    def setup(self, dev, rank: int) -> None:
+        import torch
+
+        from remora_b200 import _lib as L
+        from remora_b200.abi import tensor_descriptor
+        from remora_b200.codegen import scan_spec
+        from remora_b200.runtime import context
+
+        self.torch, self.L, self.lib, self.dev = torch, L, L.lib(), dev
+        g = torch.Generator(device=dev)
+        g.manual_seed(1729 + 1000 * rank)
+        self.x = torch.rand(self.n, generator=g, device=dev, dtype=torch.float32) * 2 - 1
+        self.out = torch.empty_like(self.x)
+        self.ctx = context(dev.index)
+        self.sptr = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        self._spec = scan_spec(op="+", init=0.0)
+        self.xd, self.od = tensor_descriptor(self.x), tensor_descriptor(self.out)
+
+    def call(self, k: int) -> None:
+        st = self.lib.remora_b200_scan(self.ctx.ptr, ctypes.byref(self._spec), ctypes.addressof(self.xd),
+                                       ctypes.addressof(self.od), 1, self.sptr)
+        if st:
+            self.L.check(st, "scan")
+
+    def check(self) -> None:
+        torch = self.torch
+        self.call(0)
+        torch.cuda.synchronize()
+        ref = torch.cumsum(self.x[: 1 << 20].double(), 0)
+        got = self.out[: 1 << 20].double()
+        err = float((got - ref).abs().max())
+        if not err <= 1e-5 * float(ref.abs().max()) + 1e-3:
+            raise SystemExit(f"benchmark output does not match the check (error {err:.3g})")
+
+    def e2e_setup(self) -> tuple[int, int]:
+        torch = self.torch
+        self.pin_in = self.x.cpu().pin_memory()
+        self.pin_out = torch.empty(self.n, dtype=torch.float32).pin_memory()
+        return self.n * 4, self.n * 4
+
+    def e2e_step(self) -> None:
+        L, lib = self.L, self.lib
+        L.check(lib.remora_b200_memcpy_h2d(self.ctx.ptr, ctypes.c_void_p(self.x.data_ptr()),
+                                           ctypes.c_void_p(self.pin_in.data_ptr()), self.n * 4, self.sptr))
+        self.call(0)
+        L.check(lib.remora_b200_memcpy_d2h(self.ctx.ptr, ctypes.c_void_p(self.pin_out.data_ptr()),
+                                           ctypes.c_void_p(self.out.data_ptr()), self.n * 4, self.sptr))
+
+    def cpu_prepare(self) -> None:
+        from remora_b200.codegen import scan_spec
+
+        self.cn = 1 << 24
+        self.cx = np.random.Generator(np.random.PCG64(1729)).uniform(-1, 1, self.cn).astype(np.float32)
+        self.cspec = scan_spec(op="+", init=0.0)
+        self.nt = 1
+        self.cpu_sample = f"{self.cn} elements per sample (oracle scan: the sequential f32 loop of the lowering, one thread)"
+
+    def cpu_step(self) -> float:
+        _oracle().scan(self.cspec, self.cx)
+        return 8.0 * self.cn
 
 
 class RuntimeWorkload:
@@ -668,12 +845,14 @@ class RuntimeWorkload:
 def make_workload(name: str):
     if name in ("chained", "row_norms"):
         return FoldWorkload(name)
-    if name in ("cnn", "cnn_tf32"):
+    if name in ("cnn", "cnn_3x", "cnn_tf32"):
         return CnnWorkload(name)
     if name.startswith("conv"):
         return ConvWorkload(name)
     if name in ("sort", "grade", "filter"):
         return RuntimeWorkload(name)
+    if name == "scan":
+        return ScanWorkload(name)
     return MatmulWorkload(name)
 
 
@@ -768,8 +947,14 @@ def run_ours(args) -> None:
             print(json.dumps({"profile_run": args.config, "ms": ms, "steps": args.steps}), flush=True)
         return
 
+    # each stage of a multi-kernel step timed alone: the dominant one gives
+    # the roofline (no collective inside a stage, so ranks need not agree)
+    stages = wl.stage_times(measured_peaks()) if hasattr(wl, "stage_times") else None
+
     h2d, d2h = wl.e2e_setup()
     e2e_steps = max(3, min(args.steps, 20))
+    begin = getattr(wl, "e2e_begin", lambda: None)
+    begin()
     for _ in range(2):
         wl.e2e_step()
     torch.cuda.synchronize()
@@ -778,6 +963,7 @@ def run_ours(args) -> None:
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    begin()
     for _ in range(e2e_steps):
         wl.e2e_step()
     e1.record(stream)
@@ -799,10 +985,12 @@ def run_ours(args) -> None:
         # roofline of the dominant kernel: algorithmic bytes for HBM-bound
         # work, algorithmic flops for tensor-bound work
         capped = bool(clocks) and "sw_power_cap" in clocks.get("reasons", [])
-        if wl.unit == "samples/s":
-            # the whole step against the dense TF32 rate: model flops per step
-            roof_unit, peak = "TFLOP/s", tf32_peak(peaks, capped)
-            achieved = wl.work_per_call * wl.FLOPS_PER_SAMPLE / (per_call_ms * 1e-3) / 1e12
+        dominant = None
+        if stages:
+            # the stage that takes longest when timed alone
+            dominant = max(stages, key=lambda k: stages[k]["ms"])
+            st = stages[dominant]
+            roof_unit, peak, achieved = st["unit"], st["peak"], st["achieved"]
         elif wl.bound == "hbm":
             roof_unit, peak = "GB/s", peaks["hbm_gbs"]
             achieved = getattr(wl, "bytes_per_call", wl.work_per_call) / (per_call_ms * 1e-3) / 1e9
@@ -828,16 +1016,27 @@ def run_ours(args) -> None:
                               if wl.unit == "GB/s" else "operands larger than the 126 MB L2"),
                        "parallelism": (f"dp{world} (NCCL gradient allreduce)" if wl.unit == "samples/s" else
                                        f"replicas x{world} (independent shards, no collective)")},
-            "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": roof_unit,
-                         "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
-                         "peak_source": peaks["source"] + (
-                             (" bf16 sustained / 2 (ran under sw_power_cap)" if capped else " bf16 burst / 2")
-                             if roof_unit == "TFLOP/s" else " HBM copy")},
+            "roofline": ({"kernel": dominant, "bound": stages[dominant]["bound"], "achieved": achieved,
+                          "peak": peak, "unit": roof_unit, "frac": stages[dominant]["frac"],
+                          "traffic": TRAFFIC.get(f"{args.config}:{dominant}"),
+                          "peak_source": peaks["source"] + (
+                              f" bf16 burst / 2 / {wl.tf32_products(dominant):g} (TF32 products per product)"
+                              if roof_unit == "TFLOP/s" else " HBM copy"),
+                          "timed": f"stage alone, {wl.B} images, CUDA graph of 10 calls, CUDA events"}
+                         if dominant else
+                         {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": roof_unit,
+                          "frac": round(achieved / peak, 4), "traffic": TRAFFIC.get(args.config),
+                          "peak_source": peaks["source"] + (
+                              (" bf16 sustained / 2 (ran under sw_power_cap)" if capped else " bf16 burst / 2")
+                              if roof_unit == "TFLOP/s" else " HBM copy")}),
             "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": n_launch,
             "clocks": clocks,
         }
+        if stages:
+            line["stages"] = {k: {f: v[f] for f in ("ms", "bound", "achieved", "unit", "frac")}
+                              for k, v in stages.items()}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -854,7 +1053,7 @@ TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms"
                                     "conv": 67_187_968 + 75_173_120, "conv_dgrad": 134_268_160 + 33_349_888,
                                     "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None,
                                     # a sort or filter call is several kernels: no single figure
-                                    "sort": None, "grade": None, "filter": None}
+                                    "sort": None, "grade": None, "filter": None, "scan": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
@@ -907,8 +1106,9 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-CONFIGS = ["chained", "row_norms", "matmul", "matmul_3x", "bmm", "conv", "conv_dgrad", "conv_wgrad", "cnn", "cnn_tf32",
-           "sort", "grade", "filter"]
+CONFIGS = ["cnn", "chained", "row_norms", "matmul", "matmul_3x", "bmm", "conv", "conv_dgrad", "conv_wgrad", "cnn_3x",
+           "cnn_tf32",
+           "scan", "sort", "grade", "filter"]
 
 
 def main() -> None:
@@ -916,7 +1116,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="chained", choices=CONFIGS)
+    ap.add_argument("--config", default="cnn", choices=CONFIGS)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

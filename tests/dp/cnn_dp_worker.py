@@ -45,7 +45,7 @@ def main() -> None:
         net.replay()                   # third step from the graph
         torch.cuda.synchronize()
         np.save(out_dir / f"params_rank{rank}.npy", net.params.cpu().numpy())
-        net.graph = None               # graphs holding NCCL calls go before the group
+        net.release_graphs()           # graphs holding NCCL calls go before the group
         dist.barrier()
         if rank == 0:
             ref = CraterCNN(dev, global_batch, global_batch, lr=0.05, precision=precision)
