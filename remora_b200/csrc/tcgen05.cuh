@@ -51,21 +51,27 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with `parity` to complete.  Returns false (and sets the
-// block's abort flag and *err) if it does not within kWaitCycles, or if
-// another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err,
-                                          int code) {
+// block's abort flag and *err) if it does not within `limit` clock cycles,
+// or if another role already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                              int code, long long limit) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       atomicCAS(err, 0, code);  // keep the first wait that ran out
       return false;
     }
   }
+}
+
+// The same with the kernels' limit, kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                          int code) {
+  return mbar_wait_for(bar, parity, abort_flag, err, code, kWaitCycles);
 }
 
 // ---------------------------------------------------------------- TMA
