@@ -23,14 +23,29 @@ _lib = None
 
 REF_DIR = HERE / "_ref"
 REF_RT_PATH = REF_DIR / "libremora_rt.so"
-REFERENCE = Path(os.environ.get("REMORA_REFERENCE", "/root/reference"))
+# where the last build() found the reference checkout (git-ignored, like _ref/)
+REF_RECORD = REF_DIR / "reference_root"
 
 
-def build() -> Path:
+def reference_root() -> Path | None:
+    """The reference checkout (the directory holding remora/): the
+    REMORA_REFERENCE environment variable, else the one the last build()
+    compiled the reference's C runtime from; None when neither names one."""
+    cand = os.environ.get("REMORA_REFERENCE") or (REF_RECORD.read_text().strip() if REF_RECORD.exists() else "")
+    if cand and (Path(cand) / "remora").is_dir():
+        return Path(cand)
+    return None
+
+
+def build(reference: str | os.PathLike | None = None) -> Path:
+    """Compile liboracle.so and, where a reference checkout is given (or
+    found by reference_root), the reference's own C runtime into _ref/."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
-    if (REFERENCE / "remora" / "remora_rt.c").exists():
+    root = Path(reference) if reference else reference_root()
+    if root is not None and (root / "remora" / "remora_rt.c").exists():
         # The reference's own C runtime, compiled from its source into _ref/.
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REMORA_REFERENCE={REFERENCE}"], check=True)
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REMORA_REFERENCE={root}"], check=True)
+        REF_RECORD.write_text(str(root.resolve()) + "\n")
     return LIB_PATH
 
 

@@ -21,6 +21,19 @@ for p in (str(ROOT), str(ROOT / "oracle")):
         sys.path.insert(0, p)
 
 
+def _reference() -> str | None:
+    import oracle
+
+    root = oracle.reference_root()
+    return str(root) if root is not None else None
+
+
+# The reference checkout for the tests that run its front end or read its
+# sources (REMORA_REFERENCE, else where the oracle's build found it); None
+# skips them.
+REFERENCE = _reference()
+
+
 def pytest_configure(config: pytest.Config) -> None:
     config.addinivalue_line("markers", "gpu: needs a B200 GPU and libremora_b200.so")
 

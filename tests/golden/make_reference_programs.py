@@ -27,7 +27,12 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
+sys.path.insert(0, str(Path(__file__).resolve().parents[2] / "oracle"))
+from oracle import reference_root  # noqa: E402  (REMORA_REFERENCE, or where the oracle's build found it)
+
+if reference_root() is None:
+    raise SystemExit("set REMORA_REFERENCE to the reference checkout (the directory holding remora/)")
+REF = str(reference_root())
 sys.path.insert(0, REF)
 sys.path.insert(0, str(ROOT))
 

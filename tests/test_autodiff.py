@@ -15,7 +15,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import REFERENCE, GOLDEN
 from remora_b200 import _lib as L
 from remora_b200.autodiff import derivative
 from remora_b200.codegen import spec_from_record
@@ -23,8 +23,8 @@ from remora_b200.errors import RemoraUnsupportedError
 from remora_b200.program import BinaryExpr, CmpExpr, ConstantExpr, InputExpr, SelectExpr, UnaryExpr
 
 
-REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
-needs_ref = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "remora")),
+REF = REFERENCE or ""
+needs_ref = pytest.mark.skipif(REFERENCE is None,
                                reason="the reference front end is not importable here")
 
 

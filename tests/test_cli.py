@@ -17,7 +17,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import REFERENCE, GOLDEN
 from remora_b200 import cli
 from remora_b200.codegen import meta_from_record, spec_from_record
 from remora_b200.program_plan import Plan
@@ -25,8 +25,8 @@ from remora_b200.program_plan import Plan
 from test_program_plan import run_plan_on_oracle
 from test_reference_codegen import oracle_run
 
-REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
-have_ref = os.path.isdir(os.path.join(REF, "remora"))
+REF = REFERENCE or ""
+have_ref = REFERENCE is not None
 needs_ref = pytest.mark.skipif(not have_ref, reason="the reference front end is not importable here")
 if have_ref and REF not in sys.path:
     sys.path.insert(0, REF)  # the CLI compiles through the reference's front end

@@ -17,12 +17,12 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import REFERENCE, GOLDEN
 from remora_b200 import _lib as L
 from remora_b200.program_plan import Plan
 
-REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
-have_ref = os.path.isdir(os.path.join(REF, "remora"))
+REF = REFERENCE or ""
+have_ref = REFERENCE is not None
 _NP = {0: np.float32, 1: np.int32, 2: np.bool_}
 
 

@@ -20,14 +20,14 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import REFERENCE, GOLDEN
 from remora_b200 import _lib as L
 from remora_b200.codegen import (AppendSpec, FoldSpec, MapSpec, RotateSpec, ScanSpec, SortSpec, meta_from_record,
                                  spec_from_record, spec_record)
 from remora_b200.errors import RemoraUnsupportedError
 
-REF = os.environ.get("REMORA_REFERENCE", "/root/reference")
-have_ref = os.path.isdir(os.path.join(REF, "remora"))
+REF = REFERENCE or ""
+have_ref = REFERENCE is not None
 
 
 def records():
