@@ -300,6 +300,10 @@ class _LossPlanner:
         # W's slot, input's slot); kind "vec" for W x, "batch" for X W^T
         self.layers: dict[tuple, tuple[str, int, int, int]] = {}
         self.computed: dict[int, Expr] = {}  # slots of computed layer inputs -> their expression
+        # convolution layers: slot of an im2col patch matrix -> (image slot,
+        # kh, kw, stride); slot of a flattened kernel -> the kernel's slot
+        self.im2col_of: dict[int, tuple[int, int, int, int]] = {}
+        self.ravel_of: dict[int, int] = {}
 
     def new_slot(self, shape: tuple[int, ...], b: int) -> int:
         k = max(self.buf) + 1
@@ -348,6 +352,9 @@ class _LossPlanner:
         f = node.func
         if len(node.arrays) != 1 or _kind(f) != "HIRLambda" or len(f.params) != 1:
             raise RemoraUnsupportedError("autodiff: maps over cells other than rows times a vector")
+        conv = self._conv_layer(node, env)
+        if conv is not None:
+            return conv
         batched = self._batched_layer(node, env)
         if batched is not None:
             return batched
@@ -375,6 +382,88 @@ class _LossPlanner:
             out = self.pl.buf((n,), L.F32)
             self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [self.buf[w.index], xv], "out": out})
             self.layers[key] = ("vec", self.new_slot((n,), out), w.index, xs)
+        return InputExpr(self.layers[key][1])
+
+    def _dot_leaves(self, body: object) -> tuple[list, float] | None:
+        """([leaf, leaf], init) when ``body`` is ``fold (+) init (map (*) a
+        b)``: each leaf is ("free", name) for a name bound outside the body,
+        or (node, names) for a computed operand; None for any other body."""
+        pl = self.pl
+        node, s = pl._resolve(body, {})
+        if _kind(node) != "HIRFold":
+            return None
+        f = node.func
+        if _kind(f) != "HIRPrimCallable" or _base_op(f.op) != "+" or f.left_arg is not None or \
+                f.right_arg is not None:
+            return None
+        init, _ = pl._resolve(node.init, s)
+        if _kind(init) != "HIRLit" or isinstance(init.value, bool):
+            return None
+        m, s2 = pl._resolve(node.array, s)
+        if _kind(m) not in ("HIRMap", "HIRApply") or m.cell_shape or len(m.arrays) != 2:
+            return None
+        g = m.func
+        if _kind(g) != "HIRPrimCallable" or _base_op(g.op) != "*" or g.left_arg is not None or \
+                g.right_arg is not None:
+            return None
+        return [pl._resolve(a, s2) for a in m.arrays], float(init.value)
+
+    def _conv_layer(self, node: object, env: dict) -> Expr | None:
+        """``map (\\p -> dot p (ravel K)) (im2col X [kh kw] s)``: the
+        reference's conv2d (examples/crater_train.py:30-36), every patch of
+        the image X times the flattened kernel K.  The forward runs im2col
+        once (the patch matrix stays for the backward) and then the rows of
+        the patch matrix times ravel(K), a linear layer whose matrix is
+        computed from X; the backward sends the layer's adjoint to K as
+        patches^T g and to X through col2im, the im2col VJP of
+        remora/ad.py:157-171.  None for a cell map over anything but im2col."""
+        f, arr = node.func, node.arrays[0]
+        if _kind(arr) != "HIRIm2col":
+            return None
+        img = _elementwise(arr.image, env)
+        if not isinstance(img, InputExpr) or img.index >= self.n_params or len(self.shapes[img.index]) != 2:
+            raise RemoraUnsupportedError("autodiff: im2col of a rank-2 image parameter")
+        kh, kw = (int(v) for v in arr.kernel_shape)
+        stride = int(arr.stride)
+        dot = self._dot_leaves(f.body)
+        if dot is None:
+            raise RemoraUnsupportedError("autodiff: a map over im2col patches other than a dot with a kernel")
+        (la, sa), (lb, sb) = dot[0]
+        p = f.params[0].name
+        if la == ("free", p):
+            other, osub = lb, sb
+        elif lb == ("free", p):
+            other, osub = la, sa
+        else:
+            raise RemoraUnsupportedError("autodiff: a dot of each patch with a kernel")
+        if not isinstance(other, tuple) and _kind(other) == "HIRRavel":
+            other, _ = self.pl._resolve(other.array, osub)
+            want = (kh, kw)
+        else:
+            want = (kh * kw,)
+        kern = env.get(other[1]) if isinstance(other, tuple) and other[0] == "free" else None
+        if not isinstance(kern, InputExpr) or kern.index >= self.n_params or self.shapes[kern.index] != want:
+            raise RemoraUnsupportedError("autodiff: the kernel of a conv layer is a parameter of the patch size")
+        key = ("conv", img.index, kern.index, kh, kw, stride, dot[1])
+        if key not in self.layers:
+            H, W = self.shapes[img.index]
+            n, c = ((H - kh) // stride + 1) * ((W - kw) // stride + 1), kh * kw
+            cols = self.pl.buf((n, c), L.F32)
+            self.pl.plan.steps.append({"op": "im2col", "in": self.buf[img.index], "out": cols, "kh": kh, "kw": kw,
+                                       "stride": stride})
+            ws = self.new_slot((n, c), cols)
+            self.im2col_of[ws] = (img.index, kh, kw, stride)
+            if want == (kh, kw):
+                xs = self.new_slot((c,), self.pl.view(self.buf[kern.index], (c,), 0, (1,)))  # ravel K
+                self.ravel_of[xs] = kern.index
+            else:
+                xs = kern.index
+            xv = self.pl.view(self.buf[xs], (n, c), 0, (0, 1))  # the kernel repeated for every patch
+            sp = fold_spec(op="+", init=dot[1], mode="cell", cell_rank=1, dtype=L.F32,
+                           premap=BinaryExpr("*", InputExpr(0), InputExpr(1)), n_inputs=2)
+            out = self.pl.buf((n,), L.F32)
+            self.pl.plan.steps.append({"op": "fold", "spec": sp, "ins": [cols, xv], "out": out})
+            self.layers[key] = ("vec", self.new_slot((n,), out), ws, xs)
         return InputExpr(self.layers[key][1])
 
     def _batched_layer(self, node: object, env: dict) -> Expr | None:
@@ -552,7 +641,20 @@ def value_and_grad_plan_from_hir(function: object):
                                      "out": dw, "precision": L.PREC_3XTF32})
             lp.pl.plan.steps.append({"op": "gemm", "a": gzb, "b": lp.buf[wk], "out": dx,
                                      "precision": L.PREC_3XTF32})
-        contrib.setdefault(wk, []).append(dw)
+        if wk in lp.im2col_of:
+            # a patch matrix: its adjoint reaches the image through col2im
+            img, kh, kw, stride = lp.im2col_of[wk]
+            dimg = lp.pl.buf(lp.shapes[img], L.F32)
+            lp.pl.plan.steps.append({"op": "col2im", "in": dw, "out": dimg, "kh": kh, "kw": kw, "stride": stride})
+            contrib.setdefault(img, []).append(dimg)
+        else:
+            contrib.setdefault(wk, []).append(dw)
+        if xk in lp.ravel_of:
+            # a flattened kernel: its adjoint is the kernel's, reshaped
+            k = lp.ravel_of[xk]
+            ks = lp.shapes[k]
+            contrib.setdefault(k, []).append(lp.pl.view(dx, ks, 0, (ks[1], 1)))
+            continue
         if xk not in lp.computed:
             contrib.setdefault(xk, []).append(dx)
             continue
@@ -576,7 +678,7 @@ def value_and_grad_plan_from_hir(function: object):
                 if fshape == shape:
                     g = _add(g, _mul(adj[i], derivative(e, k)))
             parts = contrib.get(k, [])
-            if _is(g, 0.0) and len(parts) == 1:
+            if _is(g, 0.0) and len(parts) == 1 and lp.pl.plan.buffers[parts[0]].view is None:
                 results.append(parts[0])
                 continue
             for b in parts:

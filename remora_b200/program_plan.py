@@ -1078,6 +1078,11 @@ class PlanRunner:
                 self._keep.append(spec)
                 call = (lib.remora_b200_gemm, (ctx, ctypes.byref(spec), desc(st["a"]), desc(st["b"]), desc(st["out"]),
                                                2, s))
+            elif op in ("im2col", "col2im"):
+                spec = L.RemoraIm2colSpec(int(st["kh"]), int(st["kw"]), int(st["stride"]), 0)
+                self._keep.append(spec)
+                fn = lib.remora_b200_im2col if op == "im2col" else lib.remora_b200_col2im
+                call = (fn, (ctx, ctypes.byref(spec), desc(st["in"]), desc(st["out"]), s))
             else:
                 raise _unsupported(f"plan step {op}")
             self.calls.append((op, *call))

@@ -198,8 +198,53 @@ def plan_losses(rng) -> None:
                         "shapes": [None if s is None else list(s) for s in shapes],
                         "plan": plan.to_record(), "steps": [s["op"] for s in plan.steps]})
         print(name, [s["op"] for s in plan.steps])
+    crater_plan(records, arrays)
     (HERE / "value_and_grad_plans.json").write_text(json.dumps(records, indent=1) + "\n")
     np.savez(HERE / "value_and_grad_plans.npz", **arrays)
+
+
+def crater_example():
+    """The reference's crater-CNN example module (examples/crater_train.py),
+    loaded from the reference tree: its model source, parameter types,
+    initial parameters, data and dropout masks."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("crater_train", os.path.join(REF, "examples", "crater_train.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["crater_train"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def crater_plan(records, arrays) -> None:
+    """The reference's own crater CNN loss (cnn-loss of
+    examples/crater_train.py:29-59: im2col conv, ReLU, dropout mask, a
+    900 -> 4 linear layer, ReLU, a 4 -> 1 layer, stable BCE) as ONE
+    value-and-grad plan, on the reference's initial parameters, its first
+    training image and a dropout mask it makes; value from the reference
+    interpreter, every gradient from its tape (remora/ad.py).  The model
+    source is not stored: the tests read it from the reference tree."""
+    from remora_b200.autodiff import compile_value_and_grad_plan_source
+
+    ct = crater_example()
+    ptypes = ct._parameter_types()
+    plan = compile_value_and_grad_plan_source(ct._CNN_FULL_LISP_SRC, "cnn-loss", ptypes, include_prelude=False,
+                                              syntax="lisp")
+    images, labels = ct.make_tiny_dataset(2)
+    args = [*ct.initialize_parameters(), ct.make_dropout_mask(seed=42), images[0], np.float32(labels[0])]
+    sp = specialise(ct._CNN_FULL_LISP_SRC, "cnn-loss", list(ptypes), FLOAT)
+    tape, idx = trace_via_tape_multi(sp.body, [np.asarray(a, np.float64) for a in args], [p[0] for p in sp.params])
+    adj = tape.reverse()
+    name = "crater_cnn"
+    arrays[f"{name}__value"] = np.asarray(_lambda_callable(sp, {})(*args), dtype=np.float64)
+    for k, (i, a) in enumerate(zip(idx, args)):
+        arrays[f"{name}__in{k}"] = np.asarray(a, np.float32)
+        arrays[f"{name}__grad{k}"] = np.asarray(adj[i], dtype=np.float64).reshape(np.shape(a))
+    shapes = [None if not np.shape(a) else list(np.shape(a)) for a in args]
+    records.append({"name": name, "source": None, "source_in_reference": "examples/crater_train.py:_CNN_FULL_LISP_SRC",
+                    "function": "cnn-loss", "include_prelude": False, "syntax": "lisp", "shapes": shapes,
+                    "plan": plan.to_record(), "steps": [s["op"] for s in plan.steps]})
+    print(name, [s["op"] for s in plan.steps])
 
 
 def main() -> None:

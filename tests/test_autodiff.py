@@ -215,8 +215,40 @@ def test_planner_reproduces_recorded_value_and_grad_plans():
     for rec in plan_records():
         ptypes = tuple(FLOAT if s is None else ArrayType(FLOAT, tuple(StaticDim(d) for d in s))
                        for s in rec["shapes"])
-        plan = compile_value_and_grad_plan_source(rec["source"], "loss", ptypes, syntax=rec.get("syntax", "lisp"))
+        if rec["source"] is None:
+            # the reference's own model source, read from its tree
+            sys.path.insert(0, str(GOLDEN))
+            from make_reference_gradients import crater_example
+
+            src = crater_example()._CNN_FULL_LISP_SRC
+        else:
+            src = rec["source"]
+        plan = compile_value_and_grad_plan_source(src, rec.get("function", "loss"), ptypes,
+                                                  include_prelude=rec.get("include_prelude", True),
+                                                  syntax=rec.get("syntax", "lisp"))
         assert plan.to_record() == rec["plan"], rec["name"]
+
+
+def test_the_reference_crater_model_is_one_value_and_grad_plan():
+    """The reference trains its crater CNN through six gradient functions,
+    each compiled and run on its own (examples/crater_train.py:169-198).
+    Here its loss (cnn-loss, examples/crater_train.py:29-59) is one plan:
+    im2col once, the forward, then one backward that reaches every
+    parameter, the kernel through the patch matrix's transpose and the image
+    through col2im.  Its value and nine gradients are checked against the
+    reference interpreter and tape by test_value_and_grad_plan_on_the_oracle
+    and, on the device, by test_gpu_autodiff."""
+    from remora_b200.program_plan import Plan
+
+    rec = next(r for r in plan_records() if r["name"] == "crater_cnn")
+    plan = Plan.from_record(rec["plan"])
+    steps = rec["steps"]
+    assert steps.count("im2col") == 1 and steps.count("col2im") == 1
+    assert steps.index("im2col") == 0 and len(plan.results) == 1 + 9
+    shapes = [plan.buffers[r].shape for r in plan.results]
+    assert shapes == [(), (3, 3), (), (4, 900), (4,), (4,), (), (900,), (32, 32), ()]
+    a = plan_arrays()
+    assert float(a["crater_cnn__value"]) > 0.0 and "crater_cnn__closed_form" not in a
 
 
 @needs_ref

@@ -88,6 +88,11 @@ def run_plan_on_oracle(orc, plan: Plan, inputs: list[np.ndarray] | None = None, 
             store[s["out"]] = orc.grade(get(s["in"]))
         elif op == "gemm":
             store[s["out"]] = orc.matmul(get(s["a"]), get(s["b"]))
+        elif op == "im2col":
+            store[s["out"]] = orc.im2col(get(s["in"]), s["kh"], s["kw"], s["stride"])
+        elif op == "col2im":
+            h, w = plan.buffers[s["out"]].shape
+            store[s["out"]] = orc.col2im(np.ascontiguousarray(get(s["in"])), h, w, s["kh"], s["kw"], s["stride"])
         else:
             raise AssertionError(op)
     def result(r: int) -> np.ndarray:
