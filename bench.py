@@ -478,6 +478,7 @@ class CnnWorkload:
     scaling = "strong"
     GLOBAL = 4096
     OVERLAP = None  # the step's own choice
+    RESERVE = None  # SMs left to the overlapped allreduce (None: the step's own choice)
     FLOPS_PER_SAMPLE = 33.8e6  # forward + backward, all layers
 
     # Algorithmic work per image of each stage of the step (CraterCNN.stages):
@@ -524,8 +525,9 @@ class CnnWorkload:
         self.xs = [torch.from_numpy(self.himg).to(dev) for _ in range(2)]
         self.ys = [torch.from_numpy(self.hlab).to(dev) for _ in range(2)]
         allreduce = process_group_allreduce() if world > 1 else None
+        kw = {} if self.RESERVE is None else {"reserve_sms": self.RESERVE}
         self.net = CraterCNN(dev, self.B, self.GLOBAL, lr=0.01, allreduce=allreduce, precision=self.precision,
-                             overlap_allreduce=self.OVERLAP)
+                             overlap_allreduce=self.OVERLAP, **kw)
         self.net.step(self.xs[0], self.ys[0])  # eager step: compiles map programs, sizes workspaces
         self.gid = [self.net.capture(self.xs[k], self.ys[k]) for k in range(2)]
         # library kernels in one replay of the step's graph, counted at capture
@@ -877,13 +879,19 @@ def run_ours(args) -> None:
     if world > 1:
         from datetime import timedelta
 
+        if args.config.startswith("cnn"):
+            # the gradient allreduce runs beside the conv backward, whose
+            # persistent kernels leave it 8 SMs: at most 8 NCCL channels
+            os.environ.setdefault("NCCL_MAX_NCHANNELS", "8")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     wl = make_workload(args.config)
     wl.world = world
     if isinstance(wl, CnnWorkload):
         wl.GLOBAL = args.cnn_batch
-        wl.OVERLAP = False if args.cnn_serial_allreduce else None
+        wl.OVERLAP = False if args.cnn_serial_allreduce else (True if args.cnn_overlap_allreduce else None)
+        if args.cnn_reserve_sms is not None:
+            wl.RESERVE = args.cnn_reserve_sms
     wl.setup(dev, rank)
     wl.check()
     stream = torch.cuda.current_stream(dev)
@@ -1014,7 +1022,10 @@ def run_ours(args) -> None:
             "config": {"workload": wl.desc, "calls_per_step": wl.rotate,
                        "l2": (f"{wl.rotate} rotating inputs, {wl.rotate * wl.work_per_call / 1e6:.0f} MB > 126 MB L2"
                               if wl.unit == "GB/s" else "operands larger than the 126 MB L2"),
-                       "parallelism": (f"dp{world} (NCCL gradient allreduce)" if wl.unit == "samples/s" else
+                       "parallelism": (f"dp{world} (NCCL gradient allreduce, "
+                                       f"{'overlapped with the conv backward' if getattr(wl, 'net', None) is not None and wl.net.overlap else 'after the backward'}"
+                                       f"{', NCCL_MAX_NCHANNELS=' + os.environ['NCCL_MAX_NCHANNELS'] if world > 1 and 'NCCL_MAX_NCHANNELS' in os.environ else ''})"
+                                       if wl.unit == "samples/s" else
                                        f"replicas x{world} (independent shards, no collective)")},
             "roofline": ({"kernel": dominant, "bound": stages[dominant]["bound"], "achieved": achieved,
                           "peak": peak, "unit": roof_unit, "frac": stages[dominant]["frac"],
@@ -1121,8 +1132,12 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cnn-serial-allreduce", action="store_true",
-                    help="CNN: always one gradient allreduce after the backward (by default the dense "
-                         "layers' bucket overlaps the conv backward when a rank holds >= 1024 images)")
+                    help="CNN: one gradient allreduce after the backward (by default the dense layers' "
+                         "bucket is reduced and applied while the conv backward runs)")
+    ap.add_argument("--cnn-overlap-allreduce", action="store_true",
+                    help="CNN: reduce the dense layers' bucket while the conv backward runs (the default)")
+    ap.add_argument("--cnn-reserve-sms", type=int, default=None,
+                    help="CNN, overlapped allreduce: SMs the backward's persistent kernels leave to the collective")
     ap.add_argument("--cnn-batch", type=int, default=4096,
                     help="global batch of the cnn configs (4096 is the benchmark; smaller ones show the per-rank "
                          "work of a larger data-parallel job)")

@@ -256,6 +256,15 @@ int remora_b200_synchronize(RemoraB200Ctx *ctx, remora_stream_t stream);
    is in flight during the wait (no copies, no MMAs, no tensor memory). */
 int remora_b200_wait_check(RemoraB200Ctx *ctx, int64_t limit_cycles,
                            int32_t signal, remora_stream_t stream);
+/* Caps the CTAs of this context's persistent kernels (GEMM, tensor-core
+   convolutions and their gradients) at n, one per SM (n <= 0: every SM),
+   for calls enqueued from now on.  A persistent CTA holds a whole SM
+   (shared memory, tensor memory); when a kernel on another stream, such as
+   a data-parallel gradient allreduce, holds some SMs, the CTAs scheduled
+   behind it wait until it ends and the whole launch ends late.  Leaving
+   those SMs free lets the two run side by side.  No counterpart in the
+   reference (one stream, no collectives). */
+int remora_b200_set_persistent_sms(RemoraB200Ctx *ctx, int32_t n);
 /* Pins a host buffer for asynchronous copies (cudaHostRegister). */
 int remora_b200_host_register(void *ptr, size_t nbytes);
 int remora_b200_host_unregister(void *ptr);

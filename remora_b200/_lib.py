@@ -145,6 +145,7 @@ _PROTOTYPES: dict[str, tuple] = {
     "remora_b200_memset_d32": (_I32, [_VP, _VP, ctypes.c_uint32, _SZ, _VP]),
     "remora_b200_synchronize": (_I32, [_VP, _VP]),
     "remora_b200_wait_check": (_I32, [_VP, ctypes.c_int64, _I32, _VP]),
+    "remora_b200_set_persistent_sms": (_I32, [_VP, _I32]),
     "remora_b200_host_register": (_I32, [_VP, _SZ]),
     "remora_b200_host_unregister": (_I32, [_VP]),
     "remora_b200_jit_check": (_I32, [ctypes.POINTER(RemoraMapProgram), _I32, ctypes.c_char_p, _SZ]),

@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -82,6 +83,10 @@ struct Workspace {
   // that every call may overwrite.
   int *err = nullptr;
   unsigned int *fold_ticket() const { return reinterpret_cast<unsigned int *>(err + 16); }
+  // Activations of a training step (remora_b200_cnn_step), kept apart from
+  // `buf`, which the kernels of the step use as their own scratch.
+  void *act = nullptr;
+  size_t act_bytes = 0;
 };
 
 }  // namespace remora
@@ -89,14 +94,24 @@ struct Workspace {
 struct RemoraB200Ctx {
   int device = 0;
   int sm_count = 148;
+  // SMs the persistent kernels (GEMM, tensor-core convolutions) may fill;
+  // 0: all of them (remora_b200_set_persistent_sms)
+  std::atomic<int> persistent_sms{0};
   std::mutex mu;
   std::map<cudaStream_t, remora::Workspace> ws;
+  // CTAs a persistent kernel launches at most: one per SM it may fill
+  int persistent_limit() const {
+    const int n = persistent_sms.load(std::memory_order_relaxed);
+    return n > 0 && n < sm_count ? n : sm_count;
+  }
 };
 
 namespace remora {
 // Returns a workspace of at least `bytes` for `stream` (grown on demand).
 int get_workspace(RemoraB200Ctx *ctx, cudaStream_t stream, size_t bytes,
                   Workspace **out);
+// The stream's activation buffer, at least `bytes` (grown on demand).
+int get_activations(RemoraB200Ctx *ctx, cudaStream_t stream, size_t bytes, void **out);
 int check_ctx(RemoraB200Ctx *ctx);
 
 constexpr int kMaxFoldBlocks = 1184;  // 148 SMs x 8

@@ -95,6 +95,24 @@ int get_workspace(RemoraB200Ctx *ctx, cudaStream_t stream, size_t bytes,
   return REMORA_OK;
 }
 
+int get_activations(RemoraB200Ctx *ctx, cudaStream_t stream, size_t bytes, void **out) {
+  Workspace *ws = nullptr;
+  REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  if (ws->act_bytes < bytes) {
+    if (ws->act) {
+      REMORA_CUDA_TRY(cudaStreamSynchronize(stream));
+      REMORA_CUDA_TRY(cudaFree(ws->act));
+      ws->act = nullptr;
+      ws->act_bytes = 0;
+    }
+    REMORA_CUDA_TRY(cudaMalloc(&ws->act, bytes));
+    ws->act_bytes = bytes;
+  }
+  *out = ws->act;
+  return REMORA_OK;
+}
+
 }  // namespace remora
 
 using namespace remora;
@@ -139,6 +157,7 @@ int remora_b200_shutdown(RemoraB200Ctx *ctx) {
     cudaStreamSynchronize(kv.first);
     if (kv.second.buf && cudaFree(kv.second.buf) != cudaSuccess) status = REMORA_ERR_CUDA;
     if (kv.second.err && cudaFree(kv.second.err) != cudaSuccess) status = REMORA_ERR_CUDA;
+    if (kv.second.act && cudaFree(kv.second.act) != cudaSuccess) status = REMORA_ERR_CUDA;
   }
   ctx->ws.clear();
   delete ctx;
@@ -203,6 +222,12 @@ int remora_b200_synchronize(RemoraB200Ctx *ctx, remora_stream_t stream) {
                   host_err);
     }
   }
+  return REMORA_OK;
+}
+
+int remora_b200_set_persistent_sms(RemoraB200Ctx *ctx, int32_t n) {
+  REMORA_TRY(check_ctx(ctx));
+  ctx->persistent_sms.store(n > 0 ? n : 0, std::memory_order_relaxed);
   return REMORA_OK;
 }
 

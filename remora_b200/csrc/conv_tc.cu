@@ -675,7 +675,7 @@ int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const flo
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, y, nullptr, g.N, g.H, g.K, 0, 0, ws->err};
-  return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, prec_code(precision), ctx->sm_count,
+  return dispatch(ConvIO{x, nullptr, y, nullptr}, p, g.C, g.W, prec_code(precision), ctx->persistent_limit(),
                   stream, handled);
 }
 
@@ -687,7 +687,7 @@ int conv_tc_fwd_relu_pool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x,
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, pooled, codes, g.N, g.H, g.K, 0, 0, ws->err};
   return dispatch_pool(ConvIO{x, nullptr, pooled, codes}, p, g.C, g.W, prec_code(precision),
-                       ctx->sm_count, stream, handled);
+                       ctx->persistent_limit(), stream, handled);
 }
 
 int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpooled, const uint8_t *codes,
@@ -698,7 +698,7 @@ int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpo
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
   return dispatch_unpool(ConvIO{dpooled, codes, dx, nullptr}, p, g.K, g.W, prec_code(precision),
-                         ctx->sm_count, stream, handled);
+                         ctx->persistent_limit(), stream, handled);
 }
 
 int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const float *w, float *dx, int precision,
@@ -709,7 +709,7 @@ int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const 
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights
   ConvTCParams p{w, nullptr, dx, nullptr, g.N, g.H, g.C, 1, 0, ws->err};
-  return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, prec_code(precision), ctx->sm_count,
+  return dispatch(ConvIO{dy, nullptr, dx, nullptr}, p, g.K, g.W, prec_code(precision), ctx->persistent_limit(),
                   stream, handled);
 }
 

@@ -380,7 +380,7 @@ int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const fl
   }
   const int tiles_per_img = (g.H + R - 1) / R;
   const int ntiles = g.N * tiles_per_img;
-  const int grid = std::min(ntiles, ctx->sm_count);
+  const int grid = std::min(ntiles, ctx->persistent_limit());
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, (size_t)grid * 32 * kWgOutCols * sizeof(float) + 256, &ws));
   WgParams p{g.N, g.H, g.K, tiles_per_img, reinterpret_cast<float *>(ws->buf), ws->err};

@@ -654,13 +654,13 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   p.part = take(kSplitPartBytes);  // null when the workspace has no room: no split
   const bool narrow = N <= 64;
   if (prep_split)
-    return narrow ? launch_gemm<true, 64, false>(a, b, al, bl, p, ctx->sm_count, stream)
-                  : launch_gemm<true, 256, false>(a, b, al, bl, p, ctx->sm_count, stream);
+    return narrow ? launch_gemm<true, 64, false>(a, b, al, bl, p, ctx->persistent_limit(), stream)
+                  : launch_gemm<true, 256, false>(a, b, al, bl, p, ctx->persistent_limit(), stream);
   if (split)
-    return narrow ? launch_gemm<true, 64, true>(a, b, a, b, p, ctx->sm_count, stream)
-                  : launch_gemm<true, 256, true>(a, b, a, b, p, ctx->sm_count, stream);
-  return narrow ? launch_gemm<false, 64, false>(a, b, a, b, p, ctx->sm_count, stream)
-                : launch_gemm<false, 256, false>(a, b, a, b, p, ctx->sm_count, stream);
+    return narrow ? launch_gemm<true, 64, true>(a, b, a, b, p, ctx->persistent_limit(), stream)
+                  : launch_gemm<true, 256, true>(a, b, a, b, p, ctx->persistent_limit(), stream);
+  return narrow ? launch_gemm<false, 64, false>(a, b, a, b, p, ctx->persistent_limit(), stream)
+                : launch_gemm<false, 256, false>(a, b, a, b, p, ctx->persistent_limit(), stream);
 }
 
 }  // namespace remora
