@@ -119,6 +119,57 @@ int remora_b200_conv2d_wgrad_bias(RemoraB200Ctx *ctx, const RemoraConvSpec *spec
                                   const RemoraMemRef4 *dy, RemoraMemRef4 *dw,
                                   RemoraMemRef1 *db, remora_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* One SGD step of the crater CNN in one call                                */
+/* ------------------------------------------------------------------------ */
+/* Tensor-core precision of the step.  MIXED: 3xTF32 for the second conv
+   layer's forward and every dense-layer GEMM, 2xTF32 for that conv layer's
+   two gradients (every gradient within 1e-3 of the f32 step).  3XTF32:
+   split precision everywhere.  TF32: single-pass TF32 everywhere, outside
+   the 1e-3 gradient tolerance (a speed reference). */
+enum { REMORA_CNN_MIXED = 0, REMORA_CNN_3XTF32 = 1, REMORA_CNN_TF32 = 2 };
+
+typedef struct {
+  int32_t batch;       /* images of this rank's shard                         */
+  int32_t batch_total; /* global batch: the loss is the mean over it          */
+  float lr;            /* SGD learning rate                                   */
+  int32_t precision;   /* REMORA_CNN_*                                        */
+} RemoraCnnStepSpec;
+
+/* One SGD step on this rank's shard: forward, backward, the gradient summed
+   over the data-parallel ranks, the update p <- p - lr * g; everything is
+   enqueued on `stream`.  The reference trains its CNN one example at a time
+   through six interpreted gradient functions (examples/crater_train.py:
+   169-198, 239-257); this is the batched step of its formulas (stable BCE
+   :50-54, ReLU as select :46-48, SGD :249-253).
+   params, grads: contiguous f32[529217] device buffers in the layout
+   w1[16,1,3,3] b1[16] w2[32,16,3,3] b2[32] w3[64,8192] b3[64] w4[64] b4[1];
+   params is updated in place, grads receives the step's gradient (summed
+   over the ranks).  images [B,1,64,64], labels [B] (1 crater, 0 none),
+   losses [B] (optional, may be NULL): each sample's BCE.
+   nccl_comm: an ncclComm_t over the data-parallel ranks, each calling this
+   entry point with its own shard (NULL for a single rank); the gradient is
+   summed with one ncclAllReduce on `stream`, through the NCCL library the
+   process has loaded (the one that made the communicator).  The
+   activations live in a device buffer the library keeps per stream (about
+   220 KB per image), grown on the first call: make that call before any
+   stream capture. */
+int remora_b200_cnn_step(RemoraB200Ctx *ctx, const RemoraCnnStepSpec *spec,
+                         RemoraMemRef1 *params, RemoraMemRef1 *grads,
+                         const RemoraMemRef4 *images, const RemoraMemRef1 *labels,
+                         RemoraMemRef1 *losses, void *nccl_comm,
+                         remora_stream_t stream);
+
+/* Communicator helpers for callers without NCCL plumbing of their own,
+   through the same NCCL as remora_b200_cnn_step: a unique id (128 bytes,
+   made by one rank and handed to the others by any host channel), a
+   communicator of rank `rank` of `nranks` (the device current on the
+   calling thread), and its release. */
+int remora_b200_nccl_unique_id(void *id_out);
+int remora_b200_nccl_comm_init(void **comm_out, int32_t nranks, const void *id,
+                               int32_t rank);
+int remora_b200_nccl_comm_destroy(void *comm);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,7 +41,61 @@ _CNN_PROTOS = {
     "remora_b200_conv2d_fwd_relu_pool": [ctypes.c_void_p] * 8,
     "remora_b200_conv2d_dgrad_unpool": [ctypes.c_void_p] * 7,
     "remora_b200_conv2d_wgrad_bias_unpool": [ctypes.c_void_p] * 8,
+    "remora_b200_cnn_step": [ctypes.c_void_p] * 9,
+    "remora_b200_nccl_unique_id": [ctypes.c_void_p],
+    "remora_b200_nccl_comm_init": [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32],
+    "remora_b200_nccl_comm_destroy": [ctypes.c_void_p],
 }
+
+# precision codes of remora_b200_cnn_step (REMORA_CNN_* of remora_b200_cnn.h)
+CNN_PRECISION = {"mixed": 0, "3xtf32": 1, "tf32": 2}
+
+
+class RemoraCnnStepSpec(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("batch_total", ctypes.c_int32), ("lr", ctypes.c_float),
+                ("precision", ctypes.c_int32)]
+
+
+def cnn_step(params, grads, images, labels, *, batch_total: int | None = None, lr: float = 0.01,
+             precision: str = "mixed", losses=None, comm: int | None = None) -> None:
+    """One SGD step through the single C entry point remora_b200_cnn_step
+    (the C-ABI form of CraterCNN.step): device tensors params / grads
+    f32[529217], images [B,1,64,64], labels [B], optional losses [B]; `comm`
+    an ncclComm_t address (nccl_comm_init) or None for one rank.  Enqueued
+    on the current stream."""
+    import torch
+
+    lib = _lib()
+    B = int(images.shape[0])
+    spec = RemoraCnnStepSpec(B, int(batch_total or B), float(lr), CNN_PRECISION[precision])
+    keep = [tensor_descriptor(t) for t in (params, grads, images, labels)]
+    ld = tensor_descriptor(losses) if losses is not None else None
+    stream = ctypes.c_void_p(torch.cuda.current_stream(params.device).cuda_stream)
+    L.check(lib.remora_b200_cnn_step(context(params.device.index).ptr, ctypes.byref(spec),
+                                     *[ctypes.addressof(d) for d in keep],
+                                     ctypes.addressof(ld) if ld is not None else None,
+                                     ctypes.c_void_p(comm) if comm else None, stream), "cnn_step")
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for nccl_comm_init, made by one rank
+    and handed to the others over any host channel."""
+    buf = ctypes.create_string_buffer(128)
+    L.check(_lib().remora_b200_nccl_unique_id(buf), "nccl_unique_id")
+    return buf.raw
+
+
+def nccl_comm_init(nranks: int, uid: bytes, rank: int) -> int:
+    """An ncclComm_t (as an address) of rank `rank` of `nranks` on the
+    current device."""
+    comm = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(uid), 128)
+    L.check(_lib().remora_b200_nccl_comm_init(ctypes.byref(comm), int(nranks), buf, int(rank)), "nccl_comm_init")
+    return int(comm.value)
+
+
+def nccl_comm_destroy(comm: int) -> None:
+    L.check(_lib().remora_b200_nccl_comm_destroy(ctypes.c_void_p(comm)), "nccl_comm_destroy")
 
 
 def shard(batch_total: int, world: int, rank: int) -> tuple[int, int]:
@@ -126,7 +180,7 @@ class CraterCNN:
 
     def __init__(self, device: Any, batch: int, batch_total: int | None = None, lr: float = 0.01,
                  params: np.ndarray | None = None, allreduce=None, precision: str = "mixed",
-                 overlap_allreduce: bool | None = None) -> None:
+                 overlap_allreduce: bool | None = None, reserve_sms: int = 8) -> None:
         import torch
 
         self.torch = torch
@@ -173,20 +227,26 @@ class CraterCNN:
         self.graphs: list = []
         self._keep: list = []
         # Two allreduce buckets: w3..b4 (the dense layers, 99 % of the
-        # gradient) is final once the dense1 weight-gradient GEMM is done and
-        # is reduced on a side stream while the conv layers' backward runs;
-        # w1..b2 follows at the end of the backward.
+        # gradient) is final once the dense layers' backward is done; it is
+        # reduced, and those parameters updated, on a side stream while the
+        # conv layers' backward runs.  w1..b2 follows at the end.
         o = crater.offsets()
         split = o["w3"][0]
         self.bucket_dense = self.grads[split:]
         self.bucket_conv = self.grads[:split]
+        self.params_dense = self.params[split:]
+        self.params_conv = self.params[:split]
         self.comm = torch.cuda.Stream(self.dev) if allreduce is not None else None
         # False: one allreduce of the whole gradient after the backward.  By
-        # default the dense bucket overlaps the conv backward only when a
-        # rank holds at least 1024 images: NCCL's kernels take SMs from the
-        # conv layers' persistent kernels, and with 512 images per rank on 8
-        # GPUs the serial form measured faster (0.354 against 0.368 ms).
-        self.overlap = self.B >= 1024 if overlap_allreduce is None else bool(overlap_allreduce)
+        # default the dense bucket overlaps the conv backward: on two B200s
+        # with 512 images per rank the step took 0.408 ms serial, 0.405 ms
+        # overlapped, 0.399 ms overlapped with 8 SMs left to the collective.
+        self.overlap = True if overlap_allreduce is None else bool(overlap_allreduce)
+        # With the overlapped allreduce, the persistent kernels of the
+        # backward that runs beside it (dense1's input gradient, conv2's two
+        # gradients) may leave `reserve_sms` SMs to the collective's blocks.
+        self.reserve_sms = int(reserve_sms) if self.overlap and allreduce is not None else 0
+        self.sm_count = torch.cuda.get_device_properties(self.dev).multi_processor_count
 
     # ------------------------------------------------------------ helpers
     @staticmethod
@@ -271,17 +331,28 @@ class CraterCNN:
                 ("conv2_wgrad", conv2_wgrad), ("conv2_dgrad", conv2_dgrad), ("conv1_wgrad", conv1_wgrad)]
 
     def forward_backward(self, images, labels) -> None:
-        """Loss and gradients of this rank's shard into self.grads (not yet
-        reduced over ranks)."""
+        """Loss and gradients of this rank's shard into self.grads.  With a
+        data-parallel allreduce and overlap (the default), the dense layers'
+        bucket is already reduced over the ranks and applied to the
+        parameters on the side stream; update() finishes the conv bucket."""
         self._keep = []
-        for name, run in self.stages(images, labels):
-            run()
-            if name == "dense1_wgrad" and self.allreduce is not None and self.overlap:
-                # the dense bucket is final: reduce it while the convs run
-                cur = self.torch.cuda.current_stream(self.dev)
-                self.comm.wait_stream(cur)
-                with self.torch.cuda.stream(self.comm):
-                    self.allreduce(self.bucket_dense)
+        try:
+            for name, run in self.stages(images, labels):
+                run()
+                if name == "dense1_dgrad" and self.allreduce is not None and self.overlap:
+                    # the dense bucket is final and nothing later reads the
+                    # dense parameters: reduce and apply it while the convs run
+                    cur = self.torch.cuda.current_stream(self.dev)
+                    self.comm.wait_stream(cur)
+                    with self.torch.cuda.stream(self.comm):
+                        self.allreduce(self.bucket_dense)
+                        self._map(self.prog_sgd, [self.params_dense, self.bucket_dense], self.params_dense)
+                    if self.reserve_sms:
+                        self._check(self.lib.remora_b200_set_persistent_sms(
+                            self.ctx.ptr, max(1, self.sm_count - self.reserve_sms)), "persistent SMs")
+        finally:
+            if self.reserve_sms:
+                self.lib.remora_b200_set_persistent_sms(self.ctx.ptr, 0)
 
     def update(self) -> None:
         if self.allreduce is not None:
@@ -290,7 +361,11 @@ class CraterCNN:
             with self.torch.cuda.stream(self.comm):
                 self.allreduce(self.bucket_conv if self.overlap else self.grads)
             cur.wait_stream(self.comm)
-        self._map(self.prog_sgd, [self.params, self.grads], self.params)
+        if self.allreduce is not None and self.overlap:
+            # the dense layers were updated beside the conv backward
+            self._map(self.prog_sgd, [self.params_conv, self.bucket_conv], self.params_conv)
+        else:
+            self._map(self.prog_sgd, [self.params, self.grads], self.params)
 
     def step(self, images, labels) -> None:
         self.forward_backward(images, labels)

@@ -74,9 +74,11 @@ def test_cnn_step_3xtf32_matches_oracle(cuda, oracle_mod, batch):
 def test_cnn_graph_step_matches_oracle_at_bench_sizes(cuda, oracle_mod, batch, batch_total, precision):
     """The step the benchmark times, at the sizes it times: 4096 images on
     one GPU, and the 512-image shard of one rank of an 8-GPU run (conv1
-    split over several blocks per image, one allreduce of the whole
-    gradient after the backward; on one GPU the sum over ranks is the
-    tensor itself).  capture() runs one eager step and records the next;
+    split over several blocks per image, the gradient allreduced in two
+    buckets; on one GPU the sum over ranks is the
+    tensor itself; the dense layers' bucket is reduced and applied on the
+    side stream beside the conv backward, as in a data-parallel run, with
+    8 SMs left free for it).  capture() runs one eager step and records the next;
     replay() runs it from the CUDA graph.  Loss, every gradient tensor and
     the parameters after both steps are compared with two oracle steps.
 
@@ -115,7 +117,8 @@ def test_cnn_graph_step_matches_oracle_at_bench_sizes(cuda, oracle_mod, batch, b
     _compare_from(grads, ref_grads, 1e-4, crater.offsets()["w3"][0])
     np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
     if batch < batch_total:
-        assert not net.overlap and reduced and reduced[-1] == crater.NPARAMS
+        # the dense layers' bucket beside the conv backward, then the conv bucket
+        assert net.overlap and reduced[-2:] == [net.bucket_dense.numel(), net.bucket_conv.numel()]
 
 
 def test_cnn_step_tf32_matches_oracle(cuda, oracle_mod):
@@ -372,3 +375,34 @@ def test_cnn_resume_from_checkpoint_matches_unbroken_run(cuda, tmp_path):
     assert c.restore(tmp_path / "cnn.npz") == 2
     c.replay()                   # step 3 from the graph, on the restored parameters
     np.testing.assert_array_equal(to_host(c.params), to_host(a.params))
+
+
+@pytest.mark.parametrize("precision", ["mixed", "3xtf32"])
+def test_cnn_step_entry_point_matches_the_python_step(cuda, precision):
+    """remora_b200_cnn_step, the step behind one C call, gives bit for bit
+    the parameters, gradients and per-sample losses of CraterCNN.step (the
+    same kernels in the same order), alone and with a one-rank NCCL
+    communicator (whose allreduce leaves the gradient as it is)."""
+    import torch
+
+    from remora_b200.cnn import CraterCNN, cnn_step, nccl_comm_destroy, nccl_comm_init, nccl_unique_id
+
+    B = 96
+    imgs, labels = crater.make_batch(B)
+    xi, yi = torch.from_numpy(imgs).to(cuda), torch.from_numpy(labels).to(cuda)
+    ref = CraterCNN(cuda, B, lr=0.05, precision=precision)
+    for _ in range(2):
+        ref.step(xi, yi)
+    p = torch.from_numpy(crater.init_params()).to(cuda)
+    g = torch.zeros(crater.NPARAMS, dtype=torch.float32, device=cuda)
+    losses = torch.empty(B, dtype=torch.float32, device=cuda)
+    cnn_step(p, g, xi, yi, lr=0.05, precision=precision, losses=losses)
+    comm = nccl_comm_init(1, nccl_unique_id(), 0)
+    try:
+        cnn_step(p, g, xi, yi, lr=0.05, precision=precision, losses=losses, comm=comm)
+        torch.cuda.synchronize()
+    finally:
+        nccl_comm_destroy(comm)
+    np.testing.assert_array_equal(to_host(p), to_host(ref.params))
+    np.testing.assert_array_equal(to_host(g), to_host(ref.grads))
+    np.testing.assert_array_equal(to_host(losses), to_host(ref.loss_b))
