@@ -613,7 +613,14 @@ void oracle_chained_fold_f32(const float *x, int64_t rows, int64_t L, float *out
     for (int64_t j = 0; j < L; ++j) {
       float y = row[j] * 2.5f;
       y = y + 1.0f;
-      float v = y > 0.5f ? y : 0.0f;
+      /* select(y > 0.5, y, 0.0) as LLVM lowers arith.select: no branch.
+         A 50/50 mask would mispredict half the time; the masked bits give
+         y or +0.0 exactly. */
+      uint32_t bits;
+      memcpy(&bits, &y, sizeof bits);
+      bits &= (uint32_t)0 - (uint32_t)(y > 0.5f);
+      float v;
+      memcpy(&v, &bits, sizeof v);
       acc = acc + v;
     }
     out[r] = acc;
