@@ -78,16 +78,59 @@ __device__ __forceinline__ T block_exclusive(T v, T *sh_warp, T *total) {
 
 __device__ __forceinline__ int64_t phys(int64_t q, int64_t n, int right) { return right ? n - 1 - q : q; }
 
+// The kItems (8) elements q = base .. base+7 of a tile row in scan order,
+// and their stores.  Where the 8 physical elements are one aligned 32-byte
+// run (whole tile slot, 16-byte aligned array, and for a right scan a
+// length divisible by 4) they move as two 16-byte vectors, so the lanes of
+// a warp cover 1 KB contiguously per pair of instructions; else one by one.
+template <typename T>
+__device__ __forceinline__ bool vec8(const T *p, int64_t base, int64_t n, int right) {
+  return base + kItems <= n && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (!right || (n & 3) == 0);
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ void load8(const T *__restrict__ x, int64_t base, int64_t n, int right, T (&v)[kItems]) {
+  if (vec8(x, base, n, right)) {
+    const int64_t p0 = right ? n - base - kItems : base;
+    const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(x + p0));
+    const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(x + p0 + 4));
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) v[k] = __builtin_bit_cast(T, w[right ? kItems - 1 - k : k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) v[k] = base + k < n ? x[phys(base + k, n, right)] : Op::ident();
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T *__restrict__ y, int64_t base, int64_t n, int right, const T (&v)[kItems]) {
+  if (vec8(y, base, n, right)) {
+    const int64_t p0 = right ? n - base - kItems : base;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) w[right ? kItems - 1 - k : k] = __builtin_bit_cast(uint32_t, v[k]);
+    __stcs(reinterpret_cast<uint4 *>(y + p0), make_uint4(w[0], w[1], w[2], w[3]));
+    __stcs(reinterpret_cast<uint4 *>(y + p0 + 4), make_uint4(w[4], w[5], w[6], w[7]));
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k)
+      if (base + k < n) y[phys(base + k, n, right)] = v[k];
+  }
+}
+
 template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) tile_aggregate(const T *__restrict__ x, int64_t n, int right,
                                                           T *__restrict__ agg) {
   __shared__ T sh[kThreads / 32];
   __shared__ T total;
   const int64_t base = (int64_t)blockIdx.x * kTile + (int64_t)threadIdx.x * kItems;
+  T v[kItems];
+  load8<T, Op>(x, base, n, right, v);
   T acc = Op::ident();
 #pragma unroll
   for (int k = 0; k < kItems; ++k)
-    if (base + k < n) acc = Op::apply(acc, x[phys(base + k, n, right)]);
+    if (base + k < n) acc = Op::apply(acc, v[k]);
   (void)block_exclusive<T, Op>(acc, sh, &total);
   if (threadIdx.x == 0) agg[blockIdx.x] = total;
 }
@@ -127,25 +170,23 @@ __global__ void __launch_bounds__(kThreads) tile_scan(const T *__restrict__ x, T
   __shared__ T total;
   const int64_t base = (int64_t)blockIdx.x * kTile + (int64_t)threadIdx.x * kItems;
   T v[kItems];
+  load8<T, Op>(x, base, n, right, v);
   T acc = Op::ident();
 #pragma unroll
-  for (int k = 0; k < kItems; ++k) {
-    v[k] = base + k < n ? x[phys(base + k, n, right)] : Op::ident();
-    acc = Op::apply(acc, v[k]);
-  }
+  for (int k = 0; k < kItems; ++k) acc = Op::apply(acc, v[k]);
   T run = Op::apply(carry[blockIdx.x], block_exclusive<T, Op>(acc, sh, &total));
+  T out[kItems];
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
-    if (base + k < n) {
-      if (exclusive) {
-        y[phys(base + k, n, right)] = run;
-        run = Op::apply(run, v[k]);
-      } else {
-        run = Op::apply(run, v[k]);
-        y[phys(base + k, n, right)] = run;
-      }
+    if (exclusive) {
+      out[k] = run;
+      run = Op::apply(run, v[k]);
+    } else {
+      run = Op::apply(run, v[k]);
+      out[k] = run;
     }
   }
+  store8<T>(y, base, n, right, out);
 }
 
 // ---- rank >= 2: columns t in [0, T), rows split into segments.

@@ -46,6 +46,31 @@ def test_rank1_scans(cuda, oracle_mod, n, kw):
                xf, right=kw.get("right", False))
 
 
+@pytest.mark.parametrize("kw", [{}, {"right": True, "exclusive": True}])
+@pytest.mark.parametrize("n", [100000, 100001])
+def test_rank1_scan_unaligned_views_equal_contiguous_copies(cuda, oracle_mod, n, kw):
+    """A view one element into its buffer (not 16-byte aligned: the tiles
+    read element by element) scans to the same bits as a contiguous copy
+    (read as 16-byte vectors): the combine order does not depend on how
+    the elements are loaded.  i32 results equal the oracle's."""
+    import torch
+
+    rng = np.random.default_rng(n + 7)
+    for dt, lo_hi in ((np.int32, (-1000, 1000)), (np.float32, None)):
+        host = (rng.integers(*lo_hi, n + 1) if lo_hi else rng.uniform(-1, 1, n + 1)).astype(dt)
+        buf = to_dev(host, cuda)
+        view = buf[1:]
+        assert view.data_ptr() % 16 != 0
+        a = to_host(ops.scan(view, **kw))
+        b = to_host(ops.scan(view.contiguous(), **kw))
+        np.testing.assert_array_equal(a, b)
+        if dt == np.int32:
+            np.testing.assert_array_equal(a, oracle_mod.scan(scan_spec(dtype="i32", **kw), host[1:]))
+        out = torch.zeros(n + 1, dtype=view.dtype, device=cuda)
+        ops.scan(view.contiguous(), out=out[1:], **kw)  # an unaligned output view
+        np.testing.assert_array_equal(to_host(out[1:]), b)
+
+
 @pytest.mark.parametrize("shape", [(5, 3), (1000, 1), (4096, 16), (3, 300000), (257, 7, 5)])
 def test_multirank_scans(cuda, oracle_mod, shape):
     rng = np.random.default_rng(len(shape))
