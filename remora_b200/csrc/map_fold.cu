@@ -27,6 +27,9 @@
 #ifndef REMORA_FOLD_U
 #define REMORA_FOLD_U 0
 #endif
+#ifndef REMORA_FOLD_KC
+#define REMORA_FOLD_KC 8
+#endif
 
 namespace remora {
 
@@ -229,10 +232,11 @@ struct FoldAllArgs {
 
 // Cell-fold module for cells of G lanes x U rows per lane group.  minb > 0
 // asks for at least that many resident 256-thread blocks per SM (register
-// budget); one = 1 when every lane of a group reads exactly one 16-byte
-// vector per row (L / 4 == G), in which case the vector kernel issues the
-// next pass's loads before this pass's butterfly.
-std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U, int minb = 0, int one = 0) {
+// budget); kc > 0 when every lane of a group reads exactly kc 16-byte
+// vectors per row (L / 4 == kc * G): the vector kernel then issues all of a
+// pass's loads at once and, when a pass holds at most 4 vectors per lane,
+// the next pass's loads before this pass's butterfly.
+std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U, int minb = 0, int kc = 0) {
   const bool f = sp.dtype == REMORA_F32;
   std::string s = kPrelude;
   RemoraMapProgram ident{};
@@ -289,22 +293,26 @@ std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U,
   }
   // ---- cell fold, 128-bit loads (L % 4 == 0, 16-byte aligned rows)
   const std::string lb = minb > 0 ? "__launch_bounds__(256, " + std::to_string(minb) + ")" : "__launch_bounds__(256)";
-  // loads of the U rows starting at row R into (VA, VB), vector column C
+  // loads of the U rows starting at row R into (VA, VB), vector columns
+  // C + k * G for k < KC (element u * KC + k)
   auto loads = [&](const std::string &VA, const std::string &VB, const std::string &R, const std::string &C) {
     std::string t = "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        const i64 r = " + R +
-                    " + u;\n        if (r < a.rows) {\n";
-    t += "          " + VA + "[u] = __ldcs((const " + inV + "*)a.in[0] + r * nv + " + C + ");\n";
-    if (n_in == 2) t += "          " + VB + "[u] = __ldcs((const " + inV1 + "*)a.in[1] + r * nv + " + C + ");\n";
-    else t += "          " + VB + "[u] = " + VA + "[u];\n";
-    t += "        }\n      }\n";
+                    " + u;\n        if (r < a.rows) {\n#pragma unroll\n          for (int k = 0; k < KC; ++k) {\n";
+    t += "            " + VA + "[u * KC + k] = __ldcs((const " + inV + "*)a.in[0] + r * nv + " + C + " + k * G);\n";
+    if (n_in == 2)
+      t += "            " + VB + "[u * KC + k] = __ldcs((const " + inV1 + "*)a.in[1] + r * nv + " + C + " + k * G);\n";
+    else t += "            " + VB + "[u * KC + k] = " + VA + "[u * KC + k];\n";
+    t += "          }\n        }\n      }\n";
     return t;
   };
+  // each lane adds its vectors of a row in column order
   auto accum = [&](const std::string &VA, const std::string &VB) {
-    std::string t = "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        if (r0 + u < a.rows) {\n";
+    std::string t = "#pragma unroll\n      for (int u = 0; u < U; ++u) {\n        if (r0 + u < a.rows) {\n"
+                    "#pragma unroll\n          for (int k = 0; k < KC; ++k) {\n";
     for (const char *c : {"x", "y", "z", "w"})
-      t += std::string("          acc[u] = acc_op(acc[u], ELEM(") + cvt + "(" + VA + "[u]." + c + "), " + cvt +
-           "(" + VB + "[u]." + c + ")));\n";
-    t += "        }\n      }\n";
+      t += std::string("            acc[u] = acc_op(acc[u], ELEM(") + cvt + "(" + VA + "[u * KC + k]." + c + "), " +
+           cvt + "(" + VB + "[u * KC + k]." + c + ")));\n";
+    t += "          }\n        }\n      }\n";
     return t;
   };
   const std::string butterfly = R"(
@@ -348,20 +356,36 @@ std::string fold_module_source(const RemoraFoldSpec &sp, int n_in, int G, int U,
   const i64 rows_per_warp = (32 / G) * U;
   const i64 nv = a.L >> 2;
 )";
-  if (one) {
-    // One vector per lane per row: pass k+1's loads are in flight while
+  if (kc > 0 && U * kc <= 4) {
+    // kc vectors per lane per row: pass k+1's loads are in flight while
     // pass k's butterfly and stores run.
+    s += "#define KC " + std::to_string(kc) + "\n";
     s += "  const i64 stride = nwarps * rows_per_warp;\n  i64 base = warp * rows_per_warp;\n";
-    s += "  " + inV + " va[U]; " + inV1 + " vb[U];\n  {\n    const i64 r0 = base + (i64)grp * U;\n";
+    s += "  " + inV + " va[U * KC]; " + inV1 + " vb[U * KC];\n  {\n    const i64 r0 = base + (i64)grp * U;\n";
     s += loads("va", "vb", "r0", "sub");
     s += "  }\n  for (; base < a.rows; base += stride) {\n    const i64 r0 = base + (i64)grp * U;\n";
-    s += "    " + inV + " na[U]; " + inV1 + " nb[U];\n    {\n      const i64 rn = r0 + stride;\n";
+    s += "    " + inV + " na[U * KC]; " + inV1 + " nb[U * KC];\n    {\n      const i64 rn = r0 + stride;\n";
     s += loads("na", "nb", "rn", "sub");
     s += "    }\n    ACC acc[U];\n#pragma unroll\n    for (int u = 0; u < U; ++u) acc[u] = IDENT;\n";
     s += accum("va", "vb");
     s += butterfly;
-    s += "#pragma unroll\n    for (int u = 0; u < U; ++u) { va[u] = na[u]; vb[u] = nb[u]; }\n  }\n}\n";
+    s += "#pragma unroll\n    for (int i = 0; i < U * KC; ++i) { va[i] = na[i]; vb[i] = nb[i]; }\n  }\n}\n";
+  } else if (kc > 0) {
+    // kc vectors per lane per row, all of a pass's loads issued at once
+    s += "#define KC " + std::to_string(kc) + "\n";
+    s += R"(  for (i64 base = warp * rows_per_warp; base < a.rows; base += nwarps * rows_per_warp) {
+    const i64 r0 = base + (i64)grp * U;
+    ACC acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] = IDENT;
+)";
+    s += "    " + inV + " va[U * KC]; " + inV1 + " vb[U * KC];\n";
+    s += loads("va", "vb", "r0", "sub");
+    s += accum("va", "vb");
+    s += butterfly;
+    s += "  }\n}\n";
   } else {
+    s += "#define KC 1\n";
     s += R"(  for (i64 base = warp * rows_per_warp; base < a.rows; base += nwarps * rows_per_warp) {
     const i64 r0 = base + (i64)grp * U;
     ACC acc[U];
@@ -732,7 +756,8 @@ int run_fold(RemoraB200Ctx *ctx, const RemoraFoldSpec &sp, const DescView *ins_i
     int U = 1;
     if (per_lane < 4) U = (int)std::max<int64_t>(1, 4 / std::max<int64_t>(per_lane, 1));
     if (REMORA_FOLD_U > 0 && per_lane < 4) U = REMORA_FOLD_U;
-    const int one = (vec && REMORA_FOLD_PF && units == G) ? 1 : 0;
+    // vectors per lane per row when they divide evenly (at most 8)
+    const int one = (vec && REMORA_FOLD_PF && units % G == 0 && units / G <= REMORA_FOLD_KC) ? (int)(units / G) : 0;
     const int minb = REMORA_FOLD_MINB;
     std::string key("fold");
     key_append(key, sp);
@@ -854,8 +879,10 @@ int remora_b200_jit_check(const RemoraMapProgram *prog, int32_t fold_op, char *s
     std::string fsrc = fold_module_source(sp, prog->n_inputs, 16, 4);
     REMORA_TRY(nvrtc_compile(fsrc, nullptr));
     src += fsrc;
-    // the form with the next pass's loads in flight (one vector per lane)
+    // the forms with a pass's loads issued at once (one vector per lane
+    // and row with the next pass in flight; eight per lane and row)
     REMORA_TRY(nvrtc_compile(fold_module_source(sp, prog->n_inputs, 16, 4, 4, 1), nullptr));
+    REMORA_TRY(nvrtc_compile(fold_module_source(sp, prog->n_inputs, 32, 1, 0, 8), nullptr));
   }
   if (src_out && n) std::snprintf(src_out, n, "%s", src.c_str());
   return REMORA_OK;
