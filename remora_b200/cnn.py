@@ -227,9 +227,11 @@ class CraterCNN:
         self.graphs: list = []
         self._keep: list = []
         # Two allreduce buckets: w3..b4 (the dense layers, 99 % of the
-        # gradient) is final once the dense layers' backward is done; it is
-        # reduced, and those parameters updated, on a side stream while the
-        # conv layers' backward runs.  w1..b2 follows at the end.
+        # gradient) is final once dense1's weight gradient is done; it is
+        # reduced on a side stream while dense1's input gradient and the conv
+        # layers' backward run, and applied there once dense1's input
+        # gradient, the last reader of those parameters, is done.  w1..b2
+        # follows at the end.
         o = crater.offsets()
         split = o["w3"][0]
         self.bucket_dense = self.grads[split:]
@@ -337,19 +339,27 @@ class CraterCNN:
         parameters on the side stream; update() finishes the conv bucket."""
         self._keep = []
         try:
+            overlap = self.allreduce is not None and self.overlap
             for name, run in self.stages(images, labels):
+                if name == "dense1_dgrad" and overlap and self.reserve_sms:
+                    # from here on the persistent kernels run beside the allreduce
+                    self._check(self.lib.remora_b200_set_persistent_sms(
+                        self.ctx.ptr, max(1, self.sm_count - self.reserve_sms)), "persistent SMs")
                 run()
-                if name == "dense1_dgrad" and self.allreduce is not None and self.overlap:
-                    # the dense bucket is final and nothing later reads the
-                    # dense parameters: reduce and apply it while the convs run
+                if name == "dense1_wgrad" and overlap:
+                    # the dense bucket is final: reduce it while the rest runs
                     cur = self.torch.cuda.current_stream(self.dev)
                     self.comm.wait_stream(cur)
                     with self.torch.cuda.stream(self.comm):
                         self.allreduce(self.bucket_dense)
+                elif name == "dense1_dgrad" and overlap:
+                    # the last reader of the dense parameters is done: apply
+                    # the reduced dense bucket beside the conv backward
+                    done = self.torch.cuda.Event()
+                    done.record(self.torch.cuda.current_stream(self.dev))
+                    self.comm.wait_event(done)
+                    with self.torch.cuda.stream(self.comm):
                         self._map(self.prog_sgd, [self.params_dense, self.bucket_dense], self.params_dense)
-                    if self.reserve_sms:
-                        self._check(self.lib.remora_b200_set_persistent_sms(
-                            self.ctx.ptr, max(1, self.sm_count - self.reserve_sms)), "persistent SMs")
         finally:
             if self.reserve_sms:
                 self.lib.remora_b200_set_persistent_sms(self.ctx.ptr, 0)
