@@ -59,8 +59,17 @@ def measured_peaks() -> dict:
     if p.exists():
         d = json.loads(p.read_text())
         return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
-                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "sm_max_mhz": float(d.get("sm_max_mhz", 1965.0)), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "sm_max_mhz": 1965.0,
+            "source": "fallback"}
+
+
+def simt_f32_peak(peaks: dict, sm_count: int) -> float:
+    """Nominal f32 rate of the CUDA cores in TFLOP/s: 128 f32 lanes per SM,
+    one fused multiply-add (2 flops) per lane and clock, at the maximum SM
+    clock."""
+    return sm_count * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12
 
 
 # ---------------------------------------------------------------- clocks
@@ -548,14 +557,16 @@ class CnnWorkload:
     def stage_times(self, peaks: dict, reps: int = 10) -> dict:
         """Each stage of the step timed alone on this rank (a CUDA graph of
         `reps` calls, CUDA events on the launching stream, after one warm-up
-        replay) with its roofline: the larger of the HBM time of its bytes and
-        the tensor time of its flops.  3xTF32 issues three TF32 products per
-        product and 2xTF32 two, so their tensor peaks are a third and a half
-        of the TF32 rate; the mixed step runs its forward and GEMMs in 3xTF32
-        and the conv layer's gradients in 2xTF32."""
+        replay) with its roofline: the largest of the HBM time of its bytes,
+        the tensor time of its flops (tensor-core stages) and their f32 time
+        on the CUDA cores (the others).  3xTF32 issues three TF32 products
+        per product and 2xTF32 two, so their tensor peaks are a third and a
+        half of the TF32 rate; the mixed step runs its forward and GEMMs in
+        3xTF32 and the conv layer's gradients in 2xTF32."""
         torch = self.torch
         stream = torch.cuda.current_stream(self.dev)
         tf32 = tf32_peak(peaks) * 1e12
+        simt = simt_f32_peak(peaks, torch.cuda.get_device_properties(self.dev).multi_processor_count) * 1e12
         out = {}
         for name, (fl, by, tensor) in self.STAGE_WORK.items():
             mult = self.tf32_products(name)
@@ -570,9 +581,12 @@ class CnnWorkload:
             flops, nbytes = fl * self.B, by * self.B
             t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
             t_tc = mult * flops / tf32 if tensor else 0.0
-            bound = "tensor" if t_tc > t_hbm else "hbm"
+            t_simt = 0.0 if tensor else flops / simt
+            bound = "tensor" if t_tc > t_hbm else "simt" if t_simt > t_hbm else "hbm"
             if bound == "tensor":
                 achieved, peak, unit = flops / (ms * 1e-3) / 1e12, tf32 / mult / 1e12, "TFLOP/s"
+            elif bound == "simt":
+                achieved, peak, unit = flops / (ms * 1e-3) / 1e12, simt / 1e12, "TFLOP/s"
             else:
                 achieved, peak, unit = nbytes / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
             out[name] = {"ms": round(ms, 5), "bound": bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
@@ -1032,7 +1046,9 @@ def run_ours(args) -> None:
                           "traffic": TRAFFIC.get(f"{args.config}:{dominant}"),
                           "peak_source": peaks["source"] + (
                               f" bf16 burst / 2 / {wl.tf32_products(dominant):g} (TF32 products per product)"
-                              if roof_unit == "TFLOP/s" else " HBM copy"),
+                              if stages[dominant]["bound"] == "tensor" else
+                              " f32 CUDA-core rate at the maximum SM clock" if stages[dominant]["bound"] == "simt"
+                              else " HBM copy"),
                           "timed": f"stage alone, {wl.B} images, CUDA graph of 10 calls, CUDA events"}
                          if dominant else
                          {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": roof_unit,

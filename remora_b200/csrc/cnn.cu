@@ -47,12 +47,51 @@ __device__ __forceinline__ void pool4(float v0, float v1, float v2, float v3, fl
 constexpr int kConv1Threads = 256;
 constexpr int kConv1MaxK = 32;
 
+// Stage the padded input rows 2*i0-1 .. 2*i0+IR-2 of one H x W image in
+// shared memory (row stride W + 2, zero outside the image).  With `vec` (the
+// image starts on a 16-byte boundary) each thread issues all of its 16-byte
+// reads before its first shared-memory write, so a block waits for one
+// memory latency rather than one per row chunk.
+template <int H, int W, int IR>
+__device__ __forceinline__ void stage_rows(const float *__restrict__ xb, int i0, float *img, bool vec) {
+  constexpr int PWD = W + 2, V4 = W / 4, NV = IR * V4;
+  constexpr int LPT = (NV + kConv1Threads - 1) / kConv1Threads;
+  static_assert(W % 4 == 0, "rows of whole 16-byte vectors");
+  if (vec) {
+    float4 v[LPT];
+#pragma unroll
+    for (int j = 0; j < LPT; ++j) {
+      const int e = threadIdx.x + j * kConv1Threads, r = 2 * i0 + e / V4 - 1;
+      v[j] = (e < NV && r >= 0 && r < H) ? __ldg(reinterpret_cast<const float4 *>(xb + r * W) + e % V4)
+                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int j = 0; j < LPT; ++j) {
+      const int e = threadIdx.x + j * kConv1Threads;
+      if (e < NV) {
+        float *d = img + (e / V4) * PWD + 1 + 4 * (e % V4);
+        d[0] = v[j].x;
+        d[1] = v[j].y;
+        d[2] = v[j].z;
+        d[3] = v[j].w;
+      }
+    }
+    for (int e = threadIdx.x; e < 2 * IR; e += kConv1Threads) img[(e >> 1) * PWD + (e & 1) * (W + 1)] = 0.0f;
+  } else {
+    for (int e = threadIdx.x; e < IR * PWD; e += kConv1Threads) {
+      const int r = 2 * i0 + e / PWD - 1, c = e % PWD - 1;
+      img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
+    }
+  }
+}
+
 template <int H, int W, int PARTS>
 __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const float *__restrict__ x,
                                                                         const float *__restrict__ w,
                                                                         const float *__restrict__ bias,
                                                                         float *__restrict__ p,
-                                                                        uint8_t *__restrict__ code, int K) {
+                                                                        uint8_t *__restrict__ code, int K,
+                                                                        bool vec) {
   // PARTS blocks share an image, each taking RP consecutive pooled rows (and
   // the 2 * RP + 2 padded input rows they read), so that small batches
   // still fill the GPU; every output is computed the same way for any PARTS.
@@ -64,11 +103,7 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const fl
   __shared__ float ws[kConv1MaxK * 10];
   const long long b = blockIdx.x / PARTS;
   const int i0 = (blockIdx.x % PARTS) * RP;  // first pooled row of this block
-  const float *xb = x + b * (long long)H * W;
-  for (int e = threadIdx.x; e < IR * PWD; e += kConv1Threads) {
-    const int r = 2 * i0 + e / PWD - 1, c = e % PWD - 1;
-    img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
-  }
+  stage_rows<H, W, IR>(x + b * (long long)H * W, i0, img, vec);
   for (int e = threadIdx.x; e < K * 10; e += kConv1Threads)
     ws[e] = (e % 10) < 9 ? __ldg(w + (e / 10) * 9 + e % 10) : __ldg(bias + e / 10);
   __syncthreads();
@@ -98,11 +133,12 @@ __global__ void __launch_bounds__(kConv1Threads) conv1_relu_pool_kernel(const fl
       for (int di = 0; di < 2; ++di)
 #pragma unroll
         for (int dj = 0; dj < 2; ++dj) {
-          float dot = 0.0f;
+          // 0 + p0*w0 only differs from p0*w0 by the sign of a zero, which no
+          // later sum keeps once 0 + dot is taken: the first add is skipped.
+          float dot = __fmul_rn(patch[u][di][dj], wk[0]);
 #pragma unroll
-          for (int a = 0; a < 3; ++a)
-#pragma unroll
-            for (int c = 0; c < 3; ++c) dot = __fadd_rn(dot, __fmul_rn(patch[u][di + a][dj + c], wk[a * 3 + c]));
+          for (int t = 1; t < 9; ++t)
+            dot = __fadd_rn(dot, __fmul_rn(patch[u][di + t / 3][dj + t % 3], wk[t]));
           v[di * 2 + dj] = __fadd_rn(__fadd_rn(0.0f, dot), bk);
         }
       if (pos < NPP) pool4(v[0], v[1], v[2], v[3], pb + (long long)k * NP + pos, cb + (long long)k * NP + pos);
@@ -244,49 +280,78 @@ __global__ void __launch_bounds__(256) dense_bwd_kernel(const float *__restrict_
 // pooled output with a recorded element (h, q) contributes
 // dp * x[h + a - 1, q + b - 1] to dw1[k][a][b] and dp to db1[k].  PARTS
 // blocks per image, each over RP consecutive pooled rows (its input rows in
-// shared memory with a zero border); the 16 lanes of a half-warp share a
-// channel k and stride its pooled positions, keep f32 sums, and combine them
+// shared memory with a zero border).  The 16 lanes of a half-warp share a
+// channel k; lane l reads pooled positions 64 j + 4 l .. 64 j + 4 l + 3 as one
+// 16-byte gradient vector and one 4-byte code word, four such groups in
+// flight at a time.  A group of 16 positions is summed in f32 (fused
+// multiply-adds), each group sum is added in f64, and the 16 lanes combine
 // with a fixed shuffle tree into
-// part[((b * PARTS + part) * K + k) * 10 + {0..8: taps, 9: bias}].  The
-// finish kernel adds the partials in (image, part) order in f64.
+// part[((b * PARTS + part) * K + k) * 10 + {0..8: taps, 9: bias}]: the weight
+// gradient adds every pixel of the batch with heavy cancellation, and f32
+// sums of whole rows lose about 1e-4 of the result.  The finish kernel adds
+// the partials in (image, part) order in f64.
 template <int H, int W, int PARTS>
 __global__ void __launch_bounds__(kConv1Threads) conv1_wgrad_pool_kernel(const float *__restrict__ x,
                                                                          const float *__restrict__ dp,
                                                                          const uint8_t *__restrict__ code,
-                                                                         double *__restrict__ part, int K) {
+                                                                         double *__restrict__ part, int K,
+                                                                         bool vec) {
   constexpr int OW = W / 2, NP = (H / 2) * OW, PWD = W + 2;
   constexpr int RP = (H / 2) / PARTS, NPP = RP * OW, IR = 2 * RP + 2;
+  constexpr int GROUPS = NPP / 64;  // 4-position groups per lane and channel
   static_assert((H / 2) % PARTS == 0, "parts split the pooled rows evenly");
+  static_assert(NPP % 256 == 0 && OW % 4 == 0, "whole batches of four groups, groups inside one row");
   __shared__ float img[IR * PWD];
   const long long b = blockIdx.x / PARTS;
   const int i0 = (blockIdx.x % PARTS) * RP;
-  const float *xb = x + b * (long long)H * W;
-  for (int e = threadIdx.x; e < IR * PWD; e += kConv1Threads) {
-    const int r = 2 * i0 + e / PWD - 1, c = e % PWD - 1;
-    img[e] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xb + r * W + c) : 0.0f;
-  }
+  stage_rows<H, W, IR>(x + b * (long long)H * W, i0, img, vec);
   __syncthreads();
   const int lane16 = threadIdx.x & 15;
   for (int k = threadIdx.x >> 4; k < K; k += kConv1Threads / 16) {
-    // f64 sums: the weight gradient adds every pixel of the batch with
-    // heavy cancellation, where f32 partials lose about 1e-4 of the result
     double acc[10];
 #pragma unroll
     for (int u = 0; u < 10; ++u) acc[u] = 0.0;
     const long long base = (b * K + k) * (long long)NP + i0 * OW;
-#pragma unroll 4
-    for (int pos = lane16; pos < NPP; pos += 16) {
-      const uint8_t c0 = code[base + pos];
-      if (c0 == kNoGrad) continue;
-      const int c = c0 & 3;  // window index; anything else is not a valid code
-      const float g = dp[base + pos];
-      const int h = 2 * (pos / OW) + (c >> 1), q = 2 * (pos % OW) + (c & 1);
+    const float *dpk = dp + base;
+    const uint8_t *ck = code + base;
+#pragma unroll 1
+    for (int j0 = 0; j0 < GROUPS; j0 += 4) {
+      float g[4][4];
+      uint32_t cw[4];
 #pragma unroll
-      for (int a = 0; a < 3; ++a)
+      for (int j = 0; j < 4; ++j) {
+        const int p0 = 64 * (j0 + j) + 4 * lane16;
+        if (vec) {
+          const float4 t = __ldg(reinterpret_cast<const float4 *>(dpk + p0));
+          g[j][0] = t.x, g[j][1] = t.y, g[j][2] = t.z, g[j][3] = t.w;
+          cw[j] = __ldg(reinterpret_cast<const unsigned int *>(ck + p0));
+        } else {
 #pragma unroll
-        for (int bb = 0; bb < 3; ++bb)
-          acc[a * 3 + bb] = fma((double)g, (double)img[(h + a) * PWD + q + bb], acc[a * 3 + bb]);
-      acc[9] += (double)g;
+          for (int e = 0; e < 4; ++e) g[j][e] = __ldg(dpk + p0 + e);
+          cw[j] = (uint32_t)ck[p0] | (uint32_t)ck[p0 + 1] << 8 | (uint32_t)ck[p0 + 2] << 16 |
+                  (uint32_t)ck[p0 + 3] << 24;
+        }
+      }
+      float sum[10];
+#pragma unroll
+      for (int u = 0; u < 10; ++u) sum[u] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int pos = 64 * (j0 + j) + 4 * lane16 + e;
+          const uint32_t c0 = (cw[j] >> (8 * e)) & 0xFFu;
+          const float gv = c0 == kNoGrad ? 0.0f : g[j][e];
+          const int c = (int)(c0 & 3u);  // window index; a no-gradient code still reads inside the border
+          const float *ip = img + (2 * (pos / OW) + (c >> 1)) * PWD + 2 * (pos % OW) + (c & 1);
+#pragma unroll
+          for (int a = 0; a < 3; ++a)
+#pragma unroll
+            for (int bb = 0; bb < 3; ++bb) sum[a * 3 + bb] = fmaf(gv, ip[a * PWD + bb], sum[a * 3 + bb]);
+          sum[9] += gv;
+        }
+#pragma unroll
+      for (int u = 0; u < 10; ++u) acc[u] += (double)sum[u];
     }
 #pragma unroll
     for (int u = 0; u < 10; ++u) {
@@ -329,6 +394,8 @@ __global__ void __launch_bounds__(256) conv1_wgrad_finish_kernel(const double *_
 int grid_for(long long n, int sm_count) {
   return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)sm_count * 32));
 }
+
+bool aligned(const void *p, uintptr_t bytes) { return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) == 0; }
 
 int need4(const void *desc, DescView *v, const char *what) {
   REMORA_TRY(read_desc(desc, 4, v, what));
@@ -373,7 +440,7 @@ int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, cons
   note_launch();
   kern<<<B * parts, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)Wd.data(4),
                                                       (const float *)Bd.data(4), (float *)P.data(4),
-                                                      (uint8_t *)C.data(1), K);
+                                                      (uint8_t *)C.data(1), K, aligned(X.data(4), 16));
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }
@@ -542,9 +609,10 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x, c
               : parts == 4 ? conv1_wgrad_pool_kernel<64, 64, 4>
               : parts == 2 ? conv1_wgrad_pool_kernel<64, 64, 2>
                            : conv1_wgrad_pool_kernel<64, 64, 1>;
+  const bool vec = aligned(X.data(4), 16) && aligned(P.data(4), 16) && aligned(C.data(1), 4);
   note_launch();
   kern<<<B * parts, kConv1Threads, 0, (cudaStream_t)stream>>>((const float *)X.data(4), (const float *)P.data(4),
-                                                              (const uint8_t *)C.data(1), part, K);
+                                                              (const uint8_t *)C.data(1), part, K, vec);
   note_launch();
   conv1_wgrad_finish_kernel<<<K * 10, 256, 0, (cudaStream_t)stream>>>(part, (float *)Dw.data(4),
                                                                       (float *)Db.data(4), B * parts, K);

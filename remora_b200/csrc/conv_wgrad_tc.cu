@@ -292,14 +292,21 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         const uint32_t dst = a0 + kc * Cf::A_CH + co * 16;
         wg_put<Cf::SPLIT_A>(dst, dst + 32 * 16, v);
       }
-      // B: x rows shifted by the tap, three column shifts from one read
+      // B: x rows shifted by the tap, three column shifts from one read.
+      // A warp's 32 items are whole groups of NCH consecutive chunks, so the
+      // pixels either side of a chunk are the neighbouring lanes' (one
+      // 16-byte read per lane, no 4-byte reads that share banks).
+      static_assert(Cf::ITEMS_B % kWgTransformThreads == 0 && 32 % Cf::NCH == 0,
+                    "every lane runs each pass; a warp covers whole chunk groups");
       for (int item = tt; item < Cf::ITEMS_B; item += kWgTransformThreads) {
         const int kc = item % Cf::NCH, rci = item / Cf::NCH, ci = rci % kWgCin, r = rci / kWgCin;
         const int hr = kc / Cf::CPR, w0 = 4 * (kc % Cf::CPR);
         const uint32_t row = rawx + (uint32_t)((ci * (R + 2) + hr + r) * W) * 4;
         const float4 L = wg_ld4(row + w0 * 4);
-        const float prev = w0 > 0 ? wg_ld1(row + (w0 - 1) * 4) : 0.0f;
-        const float next = w0 + 4 < W ? wg_ld1(row + (w0 + 4) * 4) : 0.0f;
+        const float left = __shfl_up_sync(0xffffffffu, L.w, 1);
+        const float right = __shfl_down_sync(0xffffffffu, L.x, 1);
+        const float prev = w0 > 0 ? left : 0.0f;
+        const float next = w0 + 4 < W ? right : 0.0f;
         const uint32_t dst = b0 + kc * Cf::B_CH + ((r * 3) * kWgCin + ci) * 16;
         wg_put<Cf::SPLIT_B>(dst, dst + Cf::B_BYTES, make_float4(prev, L.x, L.y, L.z));
         wg_put<Cf::SPLIT_B>(dst + kWgCin * 16, dst + kWgCin * 16 + Cf::B_BYTES, L);

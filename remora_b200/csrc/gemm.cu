@@ -61,6 +61,7 @@ struct Cfg {
   static constexpr uint32_t STAGE_BYTES = SPLIT3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
   static_assert(SMEM <= 227 * 1024, "shared memory per block");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "split_hi_lo walks 1 KB passes");
 };
 // Tile columns per group of the tile order (decode_tile).
 #ifndef REMORA_GEMM_GROUP_COLS
@@ -142,19 +143,34 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, 
 // x -> (hi, lo) for the `bytes` of one operand tile at shared address t
 // (hi in place, lo at t + bytes); 64 threads, 16 bytes each per step.
 __device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid) {
-  for (uint32_t off = (uint32_t)tid * 16; off < bytes; off += 64 * 16) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(t + off) : "memory");
-    const float h0 = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    const float h1 = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    const float h2 = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    const float h3 = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + off), "f"(h0), "f"(h1), "f"(h2), "f"(h3)
-                 : "memory");
-    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + bytes + off), "f"(__fsub_rn(v.x, h0)),
-                 "f"(__fsub_rn(v.y, h1)), "f"(__fsub_rn(v.z, h2)), "f"(__fsub_rn(v.w, h3))
-                 : "memory");
+  // Four 16-byte reads in flight before the eight writes: a thread's reads
+  // of one pass are 1 KB apart, and `bytes` is a multiple of 1 KB, so the
+  // bound check of each is the same for all 64 threads.
+  for (uint32_t off0 = (uint32_t)tid * 16; off0 < bytes; off0 += 4 * 64 * 16) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t off = off0 + j * 64 * 16;
+      if (off < bytes)
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(v[j].x), "=f"(v[j].y), "=f"(v[j].z), "=f"(v[j].w)
+                     : "r"(t + off)
+                     : "memory");
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t off = off0 + j * 64 * 16;
+      if (off >= bytes) break;
+      const float h0 = __uint_as_float(__float_as_uint(v[j].x) & 0xFFFFE000u);
+      const float h1 = __uint_as_float(__float_as_uint(v[j].y) & 0xFFFFE000u);
+      const float h2 = __uint_as_float(__float_as_uint(v[j].z) & 0xFFFFE000u);
+      const float h3 = __uint_as_float(__float_as_uint(v[j].w) & 0xFFFFE000u);
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + off), "f"(h0), "f"(h1), "f"(h2), "f"(h3)
+                   : "memory");
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + bytes + off), "f"(__fsub_rn(v[j].x, h0)),
+                   "f"(__fsub_rn(v[j].y, h1)), "f"(__fsub_rn(v[j].z, h2)), "f"(__fsub_rn(v[j].w, h3))
+                   : "memory");
+    }
   }
 }
 
