@@ -47,7 +47,14 @@
 // alone are split, their hi and lo halves stacked as the N = 2 * NOUT
 // columns of one MMA against the TF32 activations, and the epilogue adds
 // column c and column NOUT + c (one MMA of twice the width in place of
-// three: the activation operand is read once, not three times).
+// three: the activation operand is read once, not three times); 3 3xTF32
+// with stacked weights: the activation split into hi and lo copies, the
+// weights' hi and lo rows stacked as in 2, and per K step one MMA
+// act_hi x [w_hi; w_lo] (N = 2 * NOUT) and one act_lo x w_hi (N = NOUT, into
+// the first NOUT columns): the same three products as 1 from two reads of
+// the activation operand instead of three.  The 16 -> 32 channel forward on
+// 32-wide images (the crater CNN's conv2, plain and pooled) runs this form
+// with tiles of 12 rows (two 256-column accumulators fit TMEM).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -79,8 +86,10 @@ constexpr uint8_t kNoGradCode = 255;
 template <int CIN, int W, int TH, int NOUT, int PREC, int RAW_ST, int A_ST, int CG, int FUSE = kFuseNone,
           int CSPLIT = 1>
 struct ConvCfg {
-  static constexpr bool SPLIT3 = PREC == 1;            // hi / lo copies of both operands
-  static constexpr int NB = PREC == 2 ? 2 * NOUT : NOUT;  // MMA N: weight hi rows, then lo rows
+  static constexpr bool SPLIT_A = PREC == 1 || PREC == 3;  // hi / lo copies of the activation operand
+  static constexpr bool SPLIT_W = PREC == 1;               // hi / lo copies of the weights
+  static constexpr bool STACKED = PREC == 2 || PREC == 3;  // weight hi rows, then lo rows, in one operand
+  static constexpr int NB = STACKED ? 2 * NOUT : NOUT;     // MMA N
   static constexpr int CH = CIN / CSPLIT;              // channels of one stage
   static constexpr bool PAR = FUSE == kFusePool;       // operand split by input row parity
   static constexpr int NPAR = PAR ? 2 : 1;
@@ -95,7 +104,7 @@ struct ConvCfg {
   static constexpr int NPL = CIN / 4;            // weight planes (every channel)
   static constexpr int NPLS = CH / 4;            // operand planes of one stage
   static constexpr uint32_t A_COPY = NPLS * NPAR * PLANE;
-  static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT3 ? 2 : 1));
+  static constexpr uint32_t A_STAGE = align1k(A_COPY * (SPLIT_A ? 2 : 1));
   // kFuseUnpool: the raw stage holds pooled rows: values, then codes
   static constexpr int PROWS = TH / 2 + 2;
   static constexpr uint32_t RAW_F32 = FUSE == kFuseUnpool ? CH * PROWS * (W / 2) * 4 : CH * ROWS * W * 4;
@@ -105,7 +114,7 @@ struct ConvCfg {
   static constexpr uint32_t RAW_STAGE = align1k(RAW_CODE_OFF + RAW_CODES);
   static constexpr uint32_t BPLANE = NB * 16;
   static constexpr uint32_t W_COPY = 9 * NPL * BPLANE;
-  static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT3 ? 2 : 1));
+  static constexpr uint32_t W_REGION = align1k(W_COPY * (SPLIT_W ? 2 : 1));
   static constexpr uint32_t OFF_RAW = W_REGION;
   static constexpr uint32_t OFF_A = OFF_RAW + RAW_ST * RAW_STAGE;
   static constexpr size_t SMEM = (size_t)OFF_A + A_ST * A_STAGE + 1024;
@@ -209,7 +218,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   // tmx: input rows (kFuseUnpool: pooled gradient values), tmx2: their pool
   // codes (kFuseUnpool only)
   using Cf = ConvCfg<CIN, W, TH, NOUT, PREC, RAW_ST, A_ST, CG, FUSE, CSPLIT>;
-  constexpr bool SPLIT3 = Cf::SPLIT3;
+  constexpr bool SPLIT_A = Cf::SPLIT_A, SPLIT_W = Cf::SPLIT_W, STACKED = Cf::STACKED;
   constexpr int NB = Cf::NB;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -252,11 +261,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       v = p.mode == 0 ? __ldg(p.w + ((co * CIN + ci) * 3 + r) * 3 + s)
                       : __ldg(p.w + ((ci * p.COUT + co) * 3 + (2 - r)) * 3 + (2 - s));
     const uint32_t off = (uint32_t)(tap * Cf::NPL + (ci >> 2)) * Cf::BPLANE + co * 16 + (ci & 3) * 4;
-    if (SPLIT3) {
+    if (SPLIT_W) {
       const float h = tf32_hi(v);
       *reinterpret_cast<float *>(smem + off) = h;
       *reinterpret_cast<float *>(smem + Cf::W_COPY + off) = __fsub_rn(v, h);
-    } else if (PREC == 2) {
+    } else if (STACKED) {
       // hi in row co, lo in row NOUT + co of the same plane
       const float h = tf32_hi(v);
       *reinterpret_cast<float *>(smem + off) = h;
@@ -311,6 +320,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     if (lane == 0) {
       // ------------------------------------------------------ MMA issue
       const uint32_t idesc = tc::idesc_tf32(128, NB, 0, 0);
+      // stacked 3xTF32: the second MMA (activation lo x weight hi) reads
+      // the weight operand's first NOUT rows only
+      const uint32_t idesc_hi_rows = tc::idesc_tf32(128, NOUT, 0, 0);
       // Descriptors are built once; an operand at byte offset o from a base
       // is the base descriptor plus o >> 4 (start-address field, no carry:
       // shared-memory addresses are below 2^18).
@@ -350,7 +362,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
                     (uint32_t)((ro * Cf::PW + sc) * 16 + (2 * kk * Cf::NPAR + pp) * Cf::PLANE) >> 4;
                 const uint32_t b_off = ((uint32_t)(tap * Cf::NPL + cs * Cf::NPLS + 2 * kk) * Cf::BPLANE) >> 4;
                 tc::mma_tf32(d, ad_hi + a_off, bd_hi + b_off, idesc, (cs | tap | kk) != 0);
-                if (SPLIT3) {
+                if (PREC == 3) tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc_hi_rows, 1);
+                if (SPLIT_W) {
                   tc::mma_tf32(d, ad_hi + a_off, bd_lo + b_off, idesc, 1);
                   tc::mma_tf32(d, ad_lo + a_off, bd_hi + b_off, idesc, 1);
                 }
@@ -414,7 +427,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           uint32_t top[CG], bot[CG];
           tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NB, top);
           tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NB, bot);
-          if constexpr (PREC == 2) {
+          if constexpr (STACKED) {
             uint32_t tl[CG], bl[CG];
             tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NB + NOUT, tl);
             tmem_ld_cols<CG>(tacc + (mb * 2 + 1) * NB + NOUT, bl);
@@ -447,7 +460,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 + i) * W + col;
           uint32_t r[CG];
           tmem_ld_cols<CG>(tacc + mb * NB, r);
-          if constexpr (PREC == 2) {
+          if constexpr (STACKED) {
             uint32_t rl[CG];
             tmem_ld_cols<CG>(tacc + mb * NB + NOUT, rl);
             tc::tmem_ld_wait();
@@ -517,7 +530,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         for (int jj = 0; jj < 4; ++jj) {
           const uint32_t dst = a_hi + row0 + (uint32_t)((jj + rot) & 3) * 16;
           const float x0 = comp(v[0], jj), x1 = comp(v[1], jj), x2 = comp(v[2], jj), x3 = comp(v[3], jj);
-          if (SPLIT3) {
+          if (SPLIT_A) {
             const float h0 = tf32_hi(x0), h1 = tf32_hi(x1), h2 = tf32_hi(x2), h3 = tf32_hi(x3);
             st_shared_v4(dst, h0, h1, h2, h3);
             st_shared_v4(dst + Cf::A_COPY, __fsub_rn(x0, h0), __fsub_rn(x1, h1), __fsub_rn(x2, h2),
@@ -624,7 +637,7 @@ int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, int pr
          : prec == 2 ? launch_conv<32, 64, 8, 16, 2, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
                      : launch_conv<32, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
   if (cin == 16 && width == 32 && nout == 32)
-    return prec == 1 ? launch_conv<16, 32, 16, 32, 1, 1, 1, 16>(io, p, sm_count, stream, handled)
+    return prec == 1 ? launch_conv<16, 32, 12, 32, 3, 2, 1, 16>(io, p, sm_count, stream, handled)
          : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16>(io, p, sm_count, stream, handled)
                      : launch_conv<16, 32, 16, 32, 0, 2, 2, 16>(io, p, sm_count, stream, handled);
   if (cin == 32 && width == 32 && nout == 16)
@@ -640,7 +653,7 @@ int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, i
                   cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 16 && width == 32 && p.COUT > 16 && p.COUT <= 32 && p.H % 2 == 0)
-    return prec == 1 ? launch_conv<16, 32, 16, 32, 1, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
+    return prec == 1 ? launch_conv<16, 32, 12, 32, 3, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
          : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled)
                      : launch_conv<16, 32, 16, 32, 0, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
   return REMORA_OK;

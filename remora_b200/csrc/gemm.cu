@@ -18,8 +18,8 @@
 // cleared) and lo = x - hi (exact), and the MMA issues hi*hi + hi*lo +
 // lo*hi per K step into the same f32 accumulator.  Small GEMMs (at most
 // one tile per SM, or a short K) split in the kernel: TMA loads A and B as
-// they are and warps 2-3 split each stage in shared memory (hi in place, lo
-// beside it).  Large ones take operands split by a prep pass, whose cost is
+// they are and warps 2-3 write each stage's lo beside it in shared memory
+// (the raw tile is hi as the tensor core reads it).  Large ones take operands split by a prep pass, whose cost is
 // small against their MMAs and which keeps the transform off their
 // critical path.
 #include <cudaTypedefs.h>
@@ -140,10 +140,14 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, 
   nb = g * p.gn + (i - mb * gw);
 }
 
-// x -> (hi, lo) for the `bytes` of one operand tile at shared address t
-// (hi in place, lo at t + bytes); 64 threads, 16 bytes each per step.
+// x -> (hi, lo) for the `bytes` of one operand tile at shared address t:
+// lo = x - hi goes to t + bytes; hi stays where it is.  The tensor core
+// reads an f32 operand of a kind::tf32 MMA as its TF32 part by dropping the
+// low 13 mantissa bits, which is hi exactly, so the raw tile serves as hi
+// (results bit-identical to writing hi back).  64 threads, 16 bytes each per
+// step.
 __device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid) {
-  // Four 16-byte reads in flight before the eight writes: a thread's reads
+  // Four 16-byte reads in flight before the four writes: a thread's reads
   // of one pass are 1 KB apart, and `bytes` is a multiple of 1 KB, so the
   // bound check of each is the same for all 64 threads.
   for (uint32_t off0 = (uint32_t)tid * 16; off0 < bytes; off0 += 4 * 64 * 16) {
@@ -165,8 +169,6 @@ __device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid)
       const float h1 = __uint_as_float(__float_as_uint(v[j].y) & 0xFFFFE000u);
       const float h2 = __uint_as_float(__float_as_uint(v[j].z) & 0xFFFFE000u);
       const float h3 = __uint_as_float(__float_as_uint(v[j].w) & 0xFFFFE000u);
-      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + off), "f"(h0), "f"(h1), "f"(h2), "f"(h3)
-                   : "memory");
       asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(t + bytes + off), "f"(__fsub_rn(v[j].x, h0)),
                    "f"(__fsub_rn(v[j].y, h1)), "f"(__fsub_rn(v[j].z, h2)), "f"(__fsub_rn(v[j].w, h3))
                    : "memory");
@@ -303,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (INK && (warp == 2 || warp == 3)) {
     // ------------------------------------------------ 3xTF32 hi/lo split
-    // Elementwise and in place: hi keeps the raw tile's position (and so its
+    // Elementwise: the raw tile is hi where it lies (and keeps its
     // swizzle), lo goes to the same position of the lo slot.
     const int tid = threadIdx.x - 64;
     int s = 0;

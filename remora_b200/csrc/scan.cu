@@ -136,30 +136,92 @@ __global__ void __launch_bounds__(kThreads) tile_aggregate(const T *__restrict__
 }
 
 // One block turns the tile aggregates into per-tile carries: carry[0] = init,
-// carry[t] = carry[t-1] op agg[t-1].
+// carry[t] = carry[t-1] op agg[t-1].  Thread i owns the run of `per`
+// consecutive aggregates from i * per (per a multiple of 4, so runs start on
+// 16-byte boundaries): it reduces its run with 16-byte reads, eight in
+// flight, the block scans the 1024 run totals in thread order, and each
+// thread rescans its run from its prefix.  The combine order is fixed, so
+// results are reproducible run to run.
+constexpr int kCarryThreads = 1024;
+
+template <typename T>
+__device__ __forceinline__ void load4(const T *__restrict__ p, T (&v)[4]) {
+  const uint4 w = *reinterpret_cast<const uint4 *>(p);
+  v[0] = __builtin_bit_cast(T, w.x), v[1] = __builtin_bit_cast(T, w.y);
+  v[2] = __builtin_bit_cast(T, w.z), v[3] = __builtin_bit_cast(T, w.w);
+}
+
 template <typename T, typename Op>
-__global__ void __launch_bounds__(kThreads) carries_rank1(const T *__restrict__ agg, T *__restrict__ carry,
-                                                         int64_t ntiles, T init) {
-  __shared__ T sh[kThreads / 32];
-  __shared__ T total;
-  T run = init;
-  for (int64_t b = 0; b < ntiles; b += kTile) {
-    T v[kItems];
-    T acc = Op::ident();
-    const int64_t base = b + (int64_t)threadIdx.x * kItems;
+__global__ void __launch_bounds__(kCarryThreads) carries_rank1(const T *__restrict__ agg, T *__restrict__ carry,
+                                                              int64_t ntiles, T init) {
+  __shared__ T sh[kCarryThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t per = ((ntiles + kCarryThreads - 1) / kCarryThreads + 3) & ~int64_t(3);
+  const int64_t b0 = min(ntiles, (int64_t)threadIdx.x * per), b1 = min(ntiles, b0 + per);
+  T acc = Op::ident();
+  bool any = false;
+  for (int64_t i = b0; i < b1; i += 32) {
+    T v[8][4];
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      v[k] = base + k < ntiles ? agg[base + k] : Op::ident();
-      acc = Op::apply(acc, v[k]);
-    }
-    T pre = Op::apply(run, block_exclusive<T, Op>(acc, sh, &total));
+    for (int j = 0; j < 8; ++j) {
+      const int64_t q = i + 4 * j;
+      if (q + 4 <= b1) {
+        load4(agg + q, v[j]);
+      } else {
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      if (base + k < ntiles) carry[base + k] = pre;
-      pre = Op::apply(pre, v[k]);
+        for (int e = 0; e < 4; ++e) v[j][e] = q + e < b1 ? agg[q + e] : Op::ident();
+      }
     }
-    run = Op::apply(run, total);
-    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (i + 4 * j + e < b1) {
+          acc = any ? Op::apply(acc, v[j][e]) : v[j][e];
+          any = true;
+        }
+  }
+  // exclusive scan of the run totals in thread order: lanes, then warps
+  T inc = acc;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T up = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc = Op::apply(up, inc);
+  }
+  if (lane == 31) sh[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    T w = sh[lane], winc = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T up = __shfl_up_sync(0xffffffffu, winc, o);
+      if (lane >= o) winc = Op::apply(up, winc);
+    }
+    T wex = __shfl_up_sync(0xffffffffu, winc, 1);
+    sh[lane] = lane == 0 ? init : Op::apply(init, wex);
+  }
+  __syncthreads();
+  T ex = __shfl_up_sync(0xffffffffu, inc, 1);
+  T run = lane == 0 ? sh[warp] : Op::apply(sh[warp], ex);
+  for (int64_t i = b0; i < b1; i += 4) {
+    T v[4];
+    if (i + 4 <= b1) {
+      load4(agg + i, v);
+      T c[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        c[e] = run;
+        run = Op::apply(run, v[e]);
+      }
+      *reinterpret_cast<uint4 *>(carry + i) =
+          make_uint4(__builtin_bit_cast(uint32_t, c[0]), __builtin_bit_cast(uint32_t, c[1]),
+                     __builtin_bit_cast(uint32_t, c[2]), __builtin_bit_cast(uint32_t, c[3]));
+    } else {
+      for (int64_t q = i; q < b1; ++q) {
+        carry[q] = run;
+        run = Op::apply(run, agg[q]);
+      }
+    }
   }
 }
 
@@ -241,7 +303,7 @@ int scan_impl(const T *x, T *y, int64_t N, int64_t C, int right, int exclusive, 
     note_launch();
     tile_aggregate<T, Op><<<(unsigned)ntiles, kThreads, 0, stream>>>(x, N, right, agg);
     note_launch();
-    carries_rank1<T, Op><<<1, kThreads, 0, stream>>>(agg, carry, ntiles, init);
+    carries_rank1<T, Op><<<1, kCarryThreads, 0, stream>>>(agg, carry, ntiles, init);
     note_launch();
     tile_scan<T, Op><<<(unsigned)ntiles, kThreads, 0, stream>>>(x, y, N, right, exclusive, carry);
   } else {
