@@ -14,7 +14,7 @@
 // Pixels are consumed in tiles of R image rows.  Per tile:
 //   warp 0 lane 0   TMA: x rows h0-1 .. h0+R (zero outside the image) and
 //                   dy rows h0 .. h0+R-1, raw NCHW, into a raw stage
-//   warps 6-13      transform: the K-major interleaved operands, 4 pixels
+//   warps 2-13      transform: the K-major interleaved operands, 4 pixels
 //                   (16 bytes) per row and K chunk: A[chunk][co] from dy
 //                   rows, B[chunk][tap * 16 + ci] from x rows shifted by the
 //                   tap (left/right image borders read as zero)
@@ -25,7 +25,8 @@
 //                   two 32-row halves the epilogue adds.  2xTF32 keeps the
 //                   split rows of dy and the first MMA only:
 //                   [dy_hi; dy_lo] x x (x as TF32).
-//   warps 2-5       epilogue, once at the end: TMEM -> shared -> partials.
+//   warps 2-5       epilogue, once after their last transform tile:
+//                   TMEM -> shared -> partials.
 // Chunks of the operands are 16 bytes longer than their rows so that the
 // lanes of the transform, which walk consecutive chunks, hit different
 // shared-memory banks.
@@ -48,7 +49,7 @@ constexpr int kWgRowsB = 9 * kWgCin + 16;   // N = 160
 constexpr int kWgOnesRow = 9 * kWgCin;      // B row of ones: column 144 of D is db
 constexpr int kWgOutCols = 9 * kWgCin + 1;  // 145 columns kept per partial
 constexpr int kWgThreads = 448;
-constexpr int kWgTransformWarp0 = 6, kWgTransformWarps = 8;
+constexpr int kWgTransformWarp0 = 2, kWgTransformWarps = 12;  // warps 2-5 also run the epilogue
 constexpr int kWgTransformThreads = kWgTransformWarps * 32;
 
 // UNPOOL: dy is given as a pooled gradient and its 2x2 max-pool codes
@@ -221,45 +222,9 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       }
       if (issued) tc::mma_commit(&drain);
     }
-  } else if (warp < kWgTransformWarp0) {
-    // ------------------------------------------------------------- epilogue
-    // D row m (M = 64, one CTA) lives in TMEM lane (m % 16) + 32 * (m / 16):
-    // warp quarter q holds rows 16q .. 16q+15 in its first 16 lanes.
-    const int q = warp & 3;
-    bool ok = ntiles > (int)blockIdx.x;
-    if (ok) ok = tc::mbar_wait(&drain, 0, abort_v, p.err, 213);
-    if (ok) {
-      tc::fence_after_sync();
-      const uint32_t dsm = s_base;  // operand stage 0, idle now
-#pragma unroll 1
-      for (int c = 0; c < kWgRowsB / 32; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld_32x32b_x32(tbase + c * 32 + ((uint32_t)(q * 32) << 16), r);
-        tc::tmem_ld_wait();
-        if (lane < 16) {
-          const int m = 16 * q + lane;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            asm volatile("st.shared.f32 [%0], %1;" ::"r"(dsm + (uint32_t)(m * kWgRowsB + c * 32 + j) * 4),
-                         "r"(r[j])
-                         : "memory");
-        }
-      }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&efull);
-      ok = tc::mbar_wait(&efull, 0, abort_v, p.err, 214);
-      if (ok) {
-        float *pb = p.part + (long long)blockIdx.x * 32 * kWgOutCols;
-        for (int idx = (warp - 2) * 32 + lane; idx < 32 * kWgOutCols; idx += 128) {
-          const int co = idx / kWgOutCols, n = idx % kWgOutCols;
-          const float v = __fadd_rn(wg_ld1(dsm + (uint32_t)(co * kWgRowsB + n) * 4),
-                                    wg_ld1(dsm + (uint32_t)((32 + co) * kWgRowsB + n) * 4));
-          pb[idx] = v;
-        }
-      }
-    }
   } else {
+    // Warps 2-13 build the operands of every tile; after the last one,
+    // warps 2-5 also run the epilogue (they are idle until then).
     // ------------------------------------------------------------ transform
     const int tt = threadIdx.x - kWgTransformWarp0 * 32;
     int it = 0;
@@ -318,6 +283,45 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       if (lane == 0) {
         tc::mbar_arrive(&ofull[os]);
         tc::mbar_arrive(&rempty[rs]);
+      }
+    }
+    if (warp < kWgTransformWarp0 + 4) {
+      // ------------------------------------------------------------- epilogue
+      // D row m (M = 64, one CTA) lives in TMEM lane (m % 16) + 32 * (m / 16):
+      // warp quarter q holds rows 16q .. 16q+15 in its first 16 lanes.
+      const int q = warp & 3;
+      bool ok = ntiles > (int)blockIdx.x;
+      if (ok) ok = tc::mbar_wait(&drain, 0, abort_v, p.err, 213);
+      if (ok) {
+        tc::fence_after_sync();
+        const uint32_t dsm = s_base;  // operand stage 0, idle now
+#pragma unroll 1
+        for (int c = 0; c < kWgRowsB / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld_32x32b_x32(tbase + c * 32 + ((uint32_t)(q * 32) << 16), r);
+          tc::tmem_ld_wait();
+          if (lane < 16) {
+            const int m = 16 * q + lane;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(dsm + (uint32_t)(m * kWgRowsB + c * 32 + j) * 4),
+                           "r"(r[j])
+                           : "memory");
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&efull);
+        ok = tc::mbar_wait(&efull, 0, abort_v, p.err, 214);
+        if (ok) {
+          float *pb = p.part + (long long)blockIdx.x * 32 * kWgOutCols;
+          for (int idx = (warp - 2) * 32 + lane; idx < 32 * kWgOutCols; idx += 128) {
+            const int co = idx / kWgOutCols, n = idx % kWgOutCols;
+            const float v = __fadd_rn(wg_ld1(dsm + (uint32_t)(co * kWgRowsB + n) * 4),
+                                      wg_ld1(dsm + (uint32_t)((32 + co) * kWgRowsB + n) * 4));
+            pb[idx] = v;
+          }
+        }
       }
     }
   }
