@@ -10,8 +10,9 @@
 //                  stage; 2 accumulators of 256 columns (all 512 TMEM
 //                  columns) so the epilogue of tile i overlaps tile i+1
 //   warp 2         TMEM allocator
-//   warps 4-7      epilogue: tcgen05.ld 32 lanes x 32 columns, 128-byte
-//                  row segments straight to global memory
+//   warps 4-7      epilogue: tcgen05.ld 32 lanes x 32 columns into a
+//                  per-warp staging tile in shared memory, stored row by
+//                  row as 128-byte runs of 32 columns (coalesced)
 // Operands may be K-major (SWIZZLE_128B tiles) or M/N-major
 // (SWIZZLE_128B_BASE32B tiles); both are native UMMA layouts.
 // 3xTF32: each operand is split into hi = tf32(x) (low 13 mantissa bits
@@ -60,7 +61,7 @@ struct Cfg {
   static constexpr int STAGES = SPLIT3 ? (BN == 256 ? 2 : 4) : (BN == 256 ? 4 : 8);
   static constexpr uint32_t STAGE_BYTES = SPLIT3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
-  static_assert(SMEM <= 227 * 1024, "shared memory per block");
+  static_assert(SMEM + 4 * 32 * 36 * 4 + 1024 <= 227 * 1024, "shared memory per block (dynamic + the epilogue's staging)");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "split_hi_lo walks 1 KB passes");
 };
 // Tile columns per group of the tile order (decode_tile).
@@ -191,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], xfull[STAGES], tfull[2], tempty[2], drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ __align__(16) float epi_stage[4 * 32 * 36];  // one 32 x 32 block per epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -329,8 +331,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // --------------------------------------------------------- epilogue
     const int e = warp - 4;
     int local = 0;
-    const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && ((p.ldc & 3) == 0) &&
-                        ((p.c_bstride & 3) == 0);
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++local) {
       int t, kb0, kb1, slot;
       decode_unit(u, p, t, kb0, kb1, slot);
@@ -340,34 +340,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       int b, mb, nb;
       decode_tile(t, p, b, mb, nb);
-      const int row = mb * BM + e * 32 + lane;
-      float *crow = p.C + (long long)b * p.c_bstride + (long long)row * p.ldc;
+      // Each 32 x 32 block goes through the warp's staging tile: lane l
+      // writes row l (its TMEM lane), then the warp stores the block row by
+      // row, 32 consecutive columns per store (128 contiguous bytes) rather
+      // than 32 rows of 16 bytes each.  Rows are padded to 36 floats, so the
+      // 16-byte writes and the column reads are both free of bank conflicts.
+      const uint32_t stg_s = tc::smem_u32(epi_stage + e * 32 * 36);
+      const float *stg = epi_stage + e * 32 * 36;
+      const int row0 = mb * BM + e * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tc::tmem_ld_32x32b_x32(tbase + buf * BN + c * 32 + ((uint32_t)(e * 32) << 16), r);
         tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg_s + (uint32_t)(lane * 36 + 4 * j) * 4),
+                       "r"(r[4 * j]), "r"(r[4 * j + 1]), "r"(r[4 * j + 2]), "r"(r[4 * j + 3])
+                       : "memory");
+        __syncwarp();
         const int col0 = nb * BN + c * 32;
         if (slot >= 0) {
           // one K range of a split tile: the whole BM x BN partial, unguarded
-          float4 *dst = reinterpret_cast<float4 *>(p.part + ((long long)slot * BM + e * 32 + lane) * BN + c * 32);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-        } else if (row < p.M && col0 < p.N) {
-          if (vec_ok && col0 + 32 <= p.N) {
-            float4 *dst = reinterpret_cast<float4 *>(crow + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) crow[col0 + j] = __uint_as_float(r[j]);
-          }
+          float *dst = p.part + ((long long)slot * BM + e * 32) * BN + c * 32 + lane;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) dst[(long long)rr * BN] = stg[rr * 36 + lane];
+        } else if (col0 + lane < p.N) {
+          float *dst = p.C + (long long)b * p.c_bstride + (long long)row0 * p.ldc + col0 + lane;
+          const int rows = min(32, p.M - row0);
+#pragma unroll 4
+          for (int rr = 0; rr < rows; ++rr) dst[(long long)rr * p.ldc] = stg[rr * 36 + lane];
         }
+        __syncwarp();
       }
       tc::fence_before_sync();
       __syncwarp();
