@@ -348,7 +348,8 @@ int remora_b200_scan_noalloc(RemoraB200Ctx *ctx, const RemoraScanSpec *spec,
    C[i,j] = fold(+, 0, map(*, A[i,:], B[:,j])) (stdlib/prelude.rem:14,
    examples/crater_train.py:38-44), rank 2 or batched rank 3, f32 storage,
    TF32 or 3xTF32 tcgen05 tensor-core arithmetic with f32 accumulation.
-   A may be K-major or M-major and B K-major or N-major, as their strides say. */
+   A may be K-major or M-major and B K-major or N-major, as their strides say;
+   C may have any strides (rows or columns contiguous store at full speed). */
 int remora_b200_gemm(RemoraB200Ctx *ctx, const RemoraGemmSpec *spec,
                      const void *a_desc, const void *b_desc, void *c_desc,
                      int32_t rank, remora_stream_t stream);

@@ -309,8 +309,8 @@ class CraterCNN:
             chk(lib.remora_b200_dense_relu_bwd(c, d(self.h), d(p["w4"]), d(self.dz), d(self.dh), d(g["w4"]),
                                                d(g["b4"]), d(g["b3"]), self._stream()), "dense2 bwd")
 
-        def dense1_wgrad():
-            self._gemm(self.dh.t(), p2flat, g["w3"])
+        def dense1_wgrad():  # as its transpose, [8192, 64] = p2^T dh: 64 row blocks, not 1
+            self._gemm(p2flat.t(), self.dh, g["w3"].t())
 
         def dense1_dgrad():
             self._gemm(self.dh, p["w3"], self.dp2.view(B, 8192))

@@ -160,14 +160,16 @@ int remora_b200_cnn_step(RemoraB200Ctx *ctx, const RemoraCnnStepSpec *spec, Remo
   RemoraMemRef4 gw1 = d4(gb, kW1, 16, 1, 3, 3), gw2 = d4(gb, kW2, 32, 16, 3, 3);
   RemoraMemRef1 gb1 = d1(gb, kB1, 16), gb2 = d1(gb, kB2, 32), gb3 = d1(gb, kB3, 64), gw4 = d1(gb, kW4, 64),
                 gb4 = d1(gb, kB4, 1);
-  RemoraMemRef2 gw3 = d2(gb, kW3, 64, 8192, 8192, 1);
+  // dense1's weight gradient as its transpose [8192, 64] (column-major in
+  // the flat buffer): 64 row blocks of 128 over the 8192 features
+  RemoraMemRef2 gw3t = d2(gb, kW3, 8192, 64, 1, 8192);
   // activations
   RemoraMemRef4 P1 = d4(p1, 0, B, 16, 32, 32), C1 = d4(c1, 0, B, 16, 32, 32);
   RemoraMemRef4 P2 = d4(p2, 0, B, 32, 16, 16), C2 = d4(c2, 0, B, 32, 16, 16);
-  RemoraMemRef2 P2f = d2(p2, 0, B, 8192, 8192, 1), DP2f = d2(dp2, 0, B, 8192, 8192, 1);
+  RemoraMemRef2 P2f = d2(p2, 0, B, 8192, 8192, 1), DP2f = d2(dp2, 0, B, 8192, 8192, 1),
+                P2ft = d2(p2, 0, 8192, B, 1, 8192);
   RemoraMemRef4 DP2 = d4(dp2, 0, B, 32, 16, 16), DP1 = d4(dp1, 0, B, 16, 32, 32);
-  RemoraMemRef2 Hpre = d2(hpre, 0, B, 64, 64, 1), H = d2(h, 0, B, 64, 64, 1), DH = d2(dh, 0, B, 64, 64, 1),
-                DHt = d2(dh, 0, 64, B, 1, 64);
+  RemoraMemRef2 Hpre = d2(hpre, 0, B, 64, 64, 1), H = d2(h, 0, B, 64, 64, 1), DH = d2(dh, 0, B, 64, 64, 1);
   RemoraMemRef1 Z = d1(z, 0, B), DZ = d1(dz, 0, B);
   RemoraMemRef1 LB = losses != nullptr ? *losses : d1(lossb, 0, B);
 
@@ -184,7 +186,7 @@ int remora_b200_cnn_step(RemoraB200Ctx *ctx, const RemoraCnnStepSpec *spec, Remo
                                              1.0f / (float)BT, stream));
   // backward
   REMORA_TRY(remora_b200_dense_relu_bwd(ctx, &H, &w4, &DZ, &DH, &gw4, &gb4, &gb3, stream));
-  REMORA_TRY(remora_b200_gemm(ctx, &gs, &DHt, &P2f, &gw3, 2, stream));
+  REMORA_TRY(remora_b200_gemm(ctx, &gs, &P2ft, &DH, &gw3t, 2, stream));
   REMORA_TRY(remora_b200_gemm(ctx, &gs, &DH, &w3, &DP2f, 2, stream));
   REMORA_TRY(remora_b200_conv2d_wgrad_bias_unpool(ctx, &cb, &P1, &DP2, &C2, &gw2, &gb2, stream));
   REMORA_TRY(remora_b200_conv2d_dgrad_unpool(ctx, &cb, &DP2, &C2, &w2, &DP1, stream));

@@ -77,7 +77,8 @@ struct GemmParams {
   int a_mn, b_mn;
   int mt, nt, kt;
   float *C;
-  long long ldc;
+  long long ldc;  // C's row stride: element (row, col) at row * ldc + col * c_cs
+  long long c_cs;  // C's column stride (1: rows contiguous)
   long long c_bstride;
   int *err;
   // Tiles from `split_from` on are split along K into `split` ranges; their
@@ -365,6 +366,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           float *dst = p.part + ((long long)slot * BM + e * 32) * BN + c * 32 + lane;
 #pragma unroll 4
           for (int rr = 0; rr < 32; ++rr) dst[(long long)rr * BN] = stg[rr * 36 + lane];
+        } else if (p.c_cs != 1) {
+          // columns not contiguous (a column-major C: lanes hold consecutive
+          // rows, so each store of the 32 lanes is one contiguous run)
+          if (row0 + lane < p.M) {
+            float *dst = p.C + (long long)b * p.c_bstride + (long long)(row0 + lane) * p.ldc;
+            const int cols = min(32, p.N - col0);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < cols) dst[(long long)(col0 + j) * p.c_cs] = __uint_as_float(r[j]);
+          }
         } else if (col0 + lane < p.N) {
           float *dst = p.C + (long long)b * p.c_bstride + (long long)row0 * p.ldc + col0 + lane;
           const int rows = min(32, p.M - row0);
@@ -419,7 +430,9 @@ __global__ void __launch_bounds__(256) gemm_split_fixup(const float *__restrict_
   const long long step = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
     const int st = (int)(i / per);  // index among the split tiles
-    const int r = (int)((i % per) / BN), c = (int)(i % BN);
+    // consecutive threads walk C's contiguous direction
+    const int r = p.c_cs == 1 ? (int)((i % per) / BN) : (int)(i % BM);
+    const int c = p.c_cs == 1 ? (int)(i % BN) : (int)((i % per) / BM);
     int b, mb, nb;
     decode_tile(p.split_from + st, p, b, mb, nb);
     const int row = mb * BM + r, col = nb * BN + c;
@@ -427,16 +440,16 @@ __global__ void __launch_bounds__(256) gemm_split_fixup(const float *__restrict_
     const float *src = part + ((long long)st * p.split) * per + (long long)r * BN + c;
     float v = src[0];
     for (int s = 1; s < p.split; ++s) v = __fadd_rn(v, src[(long long)s * per]);
-    p.C[(long long)b * p.c_bstride + (long long)row * p.ldc + col] = v;
+    p.C[(long long)b * p.c_bstride + (long long)row * p.ldc + (long long)col * p.c_cs] = v;
   }
 }
 
-__global__ void fill_zero_kernel(float *c, long long ldc, long long bs, int batch, int M, int N) {
+__global__ void fill_zero_kernel(float *c, long long ldc, long long cs, long long bs, int batch, int M, int N) {
   const long long n = (long long)batch * M * N;
   const long long step = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
     const long long j = i % N, r = (i / N) % M, b = i / ((long long)N * M);
-    c[b * bs + r * ldc + j] = 0.0f;
+    c[b * bs + r * ldc + j * cs] = 0.0f;
   }
 }
 
@@ -577,13 +590,13 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   if (M > (1LL << 30) || N > (1LL << 30) || K > (1LL << 30) || batch > 65535)
     return fail(REMORA_ERR_LIMIT, "gemm: dimension beyond the supported range");
   if (M == 0 || N == 0 || batch == 0) return REMORA_OK;
-  if (Cd.strides[o + 1] != 1 && N > 1)
-    return fail(REMORA_ERR_UNSUPPORTED, "gemm: C must have unit column stride");
   float *cptr = reinterpret_cast<float *>(Cd.data(4));
-  const long long ldc = Cd.strides[o], cbs = rank == 3 ? Cd.strides[0] : 0;
+  // any strides for C; rows contiguous (column stride 1) is the fast path,
+  // columns contiguous (a column-major C) stores as fast
+  const long long ldc = Cd.strides[o], ccs = N > 1 ? Cd.strides[o + 1] : 1, cbs = rank == 3 ? Cd.strides[0] : 0;
   if (K == 0) {
     note_launch();
-    fill_zero_kernel<<<grid_for((long long)batch * M * N, ctx->sm_count), 256, 0, stream>>>(cptr, ldc, cbs, batch,
+    fill_zero_kernel<<<grid_for((long long)batch * M * N, ctx->sm_count), 256, 0, stream>>>(cptr, ldc, ccs, cbs, batch,
                                                                                               (int)M, (int)N);
     REMORA_CUDA_TRY(cudaGetLastError());
     return REMORA_OK;
@@ -671,6 +684,7 @@ int run_gemm(RemoraB200Ctx *ctx, int precision, const DescView &A, const DescVie
   p.kt = (int)((K + BK - 1) / BK);
   p.C = cptr;
   p.ldc = ldc;
+  p.c_cs = ccs;
   p.c_bstride = cbs;
   p.err = err;
   p.part = take(kSplitPartBytes);  // null when the workspace has no room: no split

@@ -83,6 +83,32 @@ def test_gemm_batched_and_views(cuda, oracle_mod):
     assert float(out[:3].abs().sum()) == 0.0 and float(out[:, :7].abs().sum()) == 0.0
 
 
+@pytest.mark.parametrize("mnk", [(8192, 64, 512), (300, 70, 96), (130, 260, 68)])
+@pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
+def test_gemm_output_any_strides(cuda, oracle_mod, mnk, prec):
+    """C given as a column-major view (the transpose of a row-major array,
+    as the CNN writes its dense layer's weight gradient), as a view with both
+    strides above 1, and with a zero K: the same values as a row-major C."""
+    import torch
+
+    M, N, K = mnk
+    rng = np.random.default_rng(M + N + K)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ref, ex = oracle_mod.matmul(a, b), exact(a, b)
+    ct = torch.full((N, M), 5.0, dtype=torch.float32, device=cuda)
+    ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec, out=ct.t())
+    check(to_host(ct).T, ref, prec, ex)
+    big = torch.full((2 * M + 1, 3 * N + 2), 5.0, dtype=torch.float32, device=cuda)
+    view = big[1::2, 2::3]
+    ops.gemm(to_dev(a, cuda), to_dev(b, cuda), precision=prec, out=view)
+    check(to_host(view), ref, prec, ex)
+    assert float((big[0::2] - 5.0).abs().sum()) == 0.0  # rows between the view's rows untouched
+    z = torch.full((N, M), 5.0, dtype=torch.float32, device=cuda)
+    ops.gemm(to_dev(a[:, :0], cuda), to_dev(b[:0], cuda), precision=prec, out=z.t())
+    assert float(z.abs().sum()) == 0.0
+
+
 def test_gemm_k_zero(cuda):
     import torch
 
