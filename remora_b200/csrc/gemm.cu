@@ -62,7 +62,7 @@ struct Cfg {
   static constexpr uint32_t STAGE_BYTES = SPLIT3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024;
   static_assert(SMEM + 4 * 32 * 36 * 4 + 1024 <= 227 * 1024, "shared memory per block (dynamic + the epilogue's staging)");
-  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "split_hi_lo walks 1 KB passes");
+  static_assert(A_BYTES % 16 == 0 && B_BYTES % 16 == 0, "split_hi_lo moves 16-byte vectors");
 };
 // Tile columns per group of the tile order (decode_tile).
 #ifndef REMORA_GEMM_GROUP_COLS
@@ -146,17 +146,17 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams &p, int &b, 
 // lo = x - hi goes to t + bytes; hi stays where it is.  The tensor core
 // reads an f32 operand of a kind::tf32 MMA as its TF32 part by dropping the
 // low 13 mantissa bits, which is hi exactly, so the raw tile serves as hi
-// (results bit-identical to writing hi back).  64 threads, 16 bytes each per
-// step.
-__device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid) {
-  // Four 16-byte reads in flight before the four writes: a thread's reads
-  // of one pass are 1 KB apart, and `bytes` is a multiple of 1 KB, so the
-  // bound check of each is the same for all 64 threads.
-  for (uint32_t off0 = (uint32_t)tid * 16; off0 < bytes; off0 += 4 * 64 * 16) {
+// (results bit-identical to writing hi back).  `nthreads` threads, 16 bytes
+// each per pass.
+__device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid, int nthreads) {
+  // Four 16-byte reads in flight per thread before its four writes; a
+  // thread's reads are one pass (nthreads * 16 bytes) apart.
+  const uint32_t pass = (uint32_t)nthreads * 16;
+  for (uint32_t off0 = (uint32_t)tid * 16; off0 < bytes; off0 += 4 * pass) {
     float4 v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t off = off0 + j * 64 * 16;
+      const uint32_t off = off0 + j * pass;
       if (off < bytes)
         asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                      : "=f"(v[j].x), "=f"(v[j].y), "=f"(v[j].z), "=f"(v[j].w)
@@ -165,7 +165,7 @@ __device__ __forceinline__ void split_hi_lo(uint32_t t, uint32_t bytes, int tid)
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t off = off0 + j * 64 * 16;
+      const uint32_t off = off0 + j * pass;
       if (off >= bytes) break;
       const float h0 = __uint_as_float(__float_as_uint(v[j].x) & 0xFFFFE000u);
       const float h1 = __uint_as_float(__float_as_uint(v[j].y) & 0xFFFFE000u);
@@ -196,11 +196,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(16) float epi_stage[4 * 32 * 36];  // one 32 x 32 block per epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // A CTA with a single work unit runs its epilogue once, at the end: its
+  // four epilogue warps split stages with warps 2-3 until then.
+  const int ntiles = p.batch * p.mt * p.nt;
+  const int nunits = p.split == 1 ? ntiles : p.split_from + (ntiles - p.split_from) * p.split;
+  const bool epi_split = INK && (nunits - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x == 1;
+  const int split_warps = epi_split ? 6 : 2;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
-      tc::mbar_init(&xfull[s], 2);
+      tc::mbar_init(&xfull[s], split_warps);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
@@ -222,9 +228,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_base;
-  const int ntiles = p.batch * p.mt * p.nt;
-  const int nunits = p.split == 1 ? ntiles : p.split_from + (ntiles - p.split_from) * p.split;
   volatile int *abort_v = &abort_flag;
+
+  // ------------------------------------------------ 3xTF32 hi/lo split
+  // Elementwise: the raw tile is hi where it lies (and keeps its swizzle), lo
+  // goes to the same position of the lo slot.
+  auto split_stages = [&]() {
+    const int tid = threadIdx.x - 64, nthreads = split_warps * 32;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < nunits && !*abort_v; u += gridDim.x) {
+      int t, kb0, kb1, slot;
+      decode_unit(u, p, t, kb0, kb1, slot);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 105)) return;
+        const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
+        split_hi_lo(sa, A_BYTES, tid, nthreads);
+        split_hi_lo(sa + 2 * A_BYTES, B_BYTES, tid, nthreads);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&xfull[s]);
+        if (++s == STAGES) s = 0, ph ^= 1;
+      }
+    }
+  };
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------ TMA producer
@@ -307,28 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (INK && (warp == 2 || warp == 3)) {
-    // ------------------------------------------------ 3xTF32 hi/lo split
-    // Elementwise: the raw tile is hi where it lies (and keeps its
-    // swizzle), lo goes to the same position of the lo slot.
-    const int tid = threadIdx.x - 64;
-    int s = 0;
-    uint32_t ph = 0;
-    for (int u = blockIdx.x; u < nunits && !*abort_v; u += gridDim.x) {
-      int t, kb0, kb1, slot;
-      decode_unit(u, p, t, kb0, kb1, slot);
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!tc::mbar_wait(&full[s], ph, abort_v, p.err, 105)) goto split_done;
-        const uint32_t sa = tc::smem_u32(smem + (size_t)s * C::STAGE_BYTES);
-        split_hi_lo(sa, A_BYTES, tid);
-        split_hi_lo(sa + 2 * A_BYTES, B_BYTES, tid);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&xfull[s]);
-        if (++s == STAGES) s = 0, ph ^= 1;
-      }
-    }
-  split_done:;
+    split_stages();
   } else if (warp >= 4) {
+    if (epi_split) split_stages();
     // --------------------------------------------------------- epilogue
     const int e = warp - 4;
     int local = 0;
