@@ -140,6 +140,9 @@ struct ConvTCParams {
   int mode;  // 0: forward, w is [COUT][CIN][3][3]; 1: input gradient, w is [CIN][COUT][3][3] (forward weights)
   int tiles_per_img;
   int *err;
+  // output channels co0 .. co0 + COUT - 1 of ctot (0: COUT, one group): a
+  // layer with more than 32 output channels runs one launch per group
+  int co0, ctot;
 };
 
 // warp roles
@@ -247,7 +250,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     abort_flag = 0;
     tc::fence_barrier_init();
   }
-  if (threadIdx.x < 32) bias_s[threadIdx.x] = (p.bias && (int)threadIdx.x < p.COUT) ? p.bias[threadIdx.x] : 0.0f;
+  const int ctot = p.ctot > 0 ? p.ctot : p.COUT;
+  if (threadIdx.x < 32)
+    bias_s[threadIdx.x] = (p.bias && (int)threadIdx.x < p.COUT) ? p.bias[p.co0 + threadIdx.x] : 0.0f;
   // Operand stages start all zero: pad columns and the tail past the last
   // row are never written again.
   for (uint32_t off = threadIdx.x * 16; off < A_ST * Cf::A_STAGE; off += kConvThreads * 16)
@@ -258,8 +263,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const int r = tap / 3, s = tap % 3;
     float v = 0.0f;
     if (co < p.COUT)
-      v = p.mode == 0 ? __ldg(p.w + ((co * CIN + ci) * 3 + r) * 3 + s)
-                      : __ldg(p.w + ((ci * p.COUT + co) * 3 + (2 - r)) * 3 + (2 - s));
+      v = p.mode == 0 ? __ldg(p.w + (((p.co0 + co) * CIN + ci) * 3 + r) * 3 + s)
+                      : __ldg(p.w + ((ci * ctot + p.co0 + co) * 3 + (2 - r)) * 3 + (2 - s));
     const uint32_t off = (uint32_t)(tap * Cf::NPL + (ci >> 2)) * Cf::BPLANE + co * 16 + (ci & 3) * 4;
     if (SPLIT_W) {
       const float h = tf32_hi(v);
@@ -422,7 +427,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           // The even-column lane of each pair stores.  H is even, so conv
           // row 2i + 1 exists whenever row 2i does.
           const bool store = col < W && !(col & 1) && i < TH / 2 && h0 + 2 * i < p.H;
-          const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 / 2 + i) * (W / 2) +
+          const long long o = ((long long)n * ctot + p.co0 + cg * CG) * plane_px + (long long)(h0 / 2 + i) * (W / 2) +
                               col / 2;
           uint32_t top[CG], bot[CG];
           tmem_ld_cols<CG>(tacc + (mb * 2 + 0) * NB, top);
@@ -457,7 +462,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           }
         } else {
           const bool store = col < W && i < TH && h0 + i < p.H;
-          const long long o = ((long long)n * p.COUT + cg * CG) * plane_px + (long long)(h0 + i) * W + col;
+          const long long o = ((long long)n * ctot + p.co0 + cg * CG) * plane_px + (long long)(h0 + i) * W + col;
           uint32_t r[CG];
           tmem_ld_cols<CG>(tacc + mb * NB, r);
           if constexpr (STACKED) {
@@ -620,30 +625,116 @@ int launch_conv(const ConvIO &io, const ConvTCParams &p, int sm_count, cudaStrea
   return REMORA_OK;
 }
 
-// Picks the instantiation for (input channels, width, output channels,
-// precision); *handled = false if there is none.  prec: 0 TF32, 1 3xTF32,
-// 2 2xTF32 (weights split).
-int dispatch(const ConvIO &io, const ConvTCParams &p, int cin, int width, int prec, int sm_count,
-             cudaStream_t stream, bool *handled) {
+using ConvLauncher = int (*)(const ConvIO &, const ConvTCParams &, int, cudaStream_t, bool *);
+
+// The instantiation for (input channels, width, output channels of a group
+// (16: at most 16, 32: at most 32), precision 0 TF32 / 1 3xTF32 / 2 2xTF32),
+// or null.  Tile rows, stages and channel slices per shape: the largest
+// share of useful GEMM rows (rows of PW = W + 1 positions in 128-row blocks)
+// over the image's ragged last tile that fits shared memory and two TMEM
+// accumulators; the 16 -> 32 channel 3xTF32 forward on 32-wide images (the
+// crater CNN's conv2) runs the stacked-weight form.
+#define REMORA_UNPAREN(...) __VA_ARGS__
+#define C(ci, wd, no, pr, args) \
+  if (cin == ci && width == wd && nout == no && prec == pr) return &launch_conv<REMORA_UNPAREN args>;
+ConvLauncher pick(int cin, int width, int nout, int prec) {
+  C(16, 16, 16, 0, (16, 16, 6, 16, 0, 2, 2, 8, kFuseNone, 1))
+  C(16, 16, 16, 1, (16, 16, 6, 16, 1, 2, 2, 8, kFuseNone, 1))
+  C(16, 16, 16, 2, (16, 16, 6, 16, 2, 2, 2, 8, kFuseNone, 1))
+  C(16, 16, 32, 0, (16, 16, 6, 32, 0, 2, 2, 16, kFuseNone, 1))
+  C(16, 16, 32, 1, (16, 16, 6, 32, 1, 2, 2, 16, kFuseNone, 1))
+  C(16, 16, 32, 2, (16, 16, 6, 32, 2, 2, 2, 16, kFuseNone, 1))
+  C(16, 32, 16, 0, (16, 32, 32, 16, 0, 2, 1, 8, kFuseNone, 1))
+  C(16, 32, 16, 1, (16, 32, 16, 16, 1, 2, 1, 8, kFuseNone, 1))
+  C(16, 32, 16, 2, (16, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 1))
+  C(16, 32, 32, 0, (16, 32, 16, 32, 0, 2, 2, 16, kFuseNone, 1))
+  C(16, 32, 32, 1, (16, 32, 12, 32, 3, 2, 1, 16, kFuseNone, 1))
+  C(16, 32, 32, 2, (16, 32, 8, 32, 2, 2, 2, 16, kFuseNone, 1))
+  C(16, 64, 16, 0, (16, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 1))
+  C(16, 64, 16, 1, (16, 64, 8, 16, 1, 2, 1, 8, kFuseNone, 1))
+  C(16, 64, 16, 2, (16, 64, 8, 16, 2, 2, 2, 8, kFuseNone, 1))
+  C(16, 64, 32, 0, (16, 64, 8, 32, 0, 2, 2, 16, kFuseNone, 1))
+  C(16, 64, 32, 1, (16, 64, 8, 32, 1, 2, 1, 16, kFuseNone, 1))
+  C(16, 64, 32, 2, (16, 64, 4, 32, 2, 2, 2, 16, kFuseNone, 1))
+  C(16, 128, 16, 0, (16, 128, 4, 16, 0, 2, 2, 8, kFuseNone, 1))
+  C(16, 128, 16, 1, (16, 128, 4, 16, 1, 1, 1, 8, kFuseNone, 1))
+  C(16, 128, 16, 2, (16, 128, 6, 16, 2, 2, 1, 8, kFuseNone, 1))
+  C(16, 128, 32, 0, (16, 128, 6, 32, 0, 2, 1, 16, kFuseNone, 1))
+  C(16, 128, 32, 1, (16, 128, 4, 32, 1, 1, 1, 16, kFuseNone, 1))
+  C(16, 128, 32, 2, (16, 128, 2, 32, 2, 2, 2, 16, kFuseNone, 1))
+  C(32, 16, 16, 0, (32, 16, 6, 16, 0, 2, 2, 8, kFuseNone, 2))
+  C(32, 16, 16, 1, (32, 16, 6, 16, 1, 2, 2, 8, kFuseNone, 2))
+  C(32, 16, 16, 2, (32, 16, 6, 16, 2, 2, 2, 8, kFuseNone, 2))
+  C(32, 16, 32, 0, (32, 16, 6, 32, 0, 2, 2, 16, kFuseNone, 2))
+  C(32, 16, 32, 1, (32, 16, 6, 32, 1, 2, 2, 16, kFuseNone, 2))
+  C(32, 16, 32, 2, (32, 16, 6, 32, 2, 2, 2, 16, kFuseNone, 2))
+  C(32, 32, 16, 0, (32, 32, 16, 16, 0, 2, 2, 8, kFuseNone, 2))
+  C(32, 32, 16, 1, (32, 32, 8, 16, 1, 2, 2, 8, kFuseNone, 2))
+  C(32, 32, 16, 2, (32, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 2))
+  C(32, 32, 32, 0, (32, 32, 16, 32, 0, 2, 2, 16, kFuseNone, 2))
+  C(32, 32, 32, 1, (32, 32, 16, 32, 1, 1, 1, 16, kFuseNone, 2))
+  C(32, 32, 32, 2, (32, 32, 6, 32, 2, 2, 2, 16, kFuseNone, 2))
+  C(32, 64, 16, 0, (32, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 2))
+  C(32, 64, 16, 1, (32, 64, 4, 16, 1, 2, 2, 8, kFuseNone, 2))
+  C(32, 64, 16, 2, (32, 64, 8, 16, 2, 2, 2, 8, kFuseNone, 2))
+  C(32, 64, 32, 0, (32, 64, 8, 32, 0, 2, 2, 16, kFuseNone, 2))
+  C(32, 64, 32, 1, (32, 64, 8, 32, 1, 1, 1, 16, kFuseNone, 2))
+  C(32, 64, 32, 2, (32, 64, 6, 32, 2, 2, 2, 16, kFuseNone, 2))
+  C(32, 128, 16, 0, (32, 128, 8, 16, 0, 1, 1, 8, kFuseNone, 2))
+  C(32, 128, 16, 1, (32, 128, 4, 16, 1, 1, 1, 8, kFuseNone, 2))
+  C(32, 128, 16, 2, (32, 128, 4, 16, 2, 2, 1, 8, kFuseNone, 2))
+  C(32, 128, 32, 0, (32, 128, 4, 32, 0, 2, 1, 16, kFuseNone, 2))
+  C(32, 128, 32, 1, (32, 128, 2, 32, 1, 2, 1, 16, kFuseNone, 2))
+  C(32, 128, 32, 2, (32, 128, 2, 32, 2, 2, 2, 16, kFuseNone, 2))
+  C(64, 16, 16, 0, (64, 16, 6, 16, 0, 2, 2, 8, kFuseNone, 4))
+  C(64, 16, 16, 1, (64, 16, 6, 16, 1, 2, 2, 8, kFuseNone, 4))
+  C(64, 16, 16, 2, (64, 16, 6, 16, 2, 2, 2, 8, kFuseNone, 4))
+  C(64, 16, 32, 0, (64, 16, 6, 32, 0, 2, 2, 16, kFuseNone, 4))
+  C(64, 16, 32, 1, (64, 16, 6, 32, 1, 2, 2, 16, kFuseNone, 4))
+  C(64, 16, 32, 2, (64, 16, 6, 32, 2, 2, 2, 16, kFuseNone, 4))
+  C(64, 32, 16, 0, (64, 32, 16, 16, 0, 2, 2, 8, kFuseNone, 4))
+  C(64, 32, 16, 1, (64, 32, 16, 16, 1, 1, 1, 8, kFuseNone, 4))
+  C(64, 32, 16, 2, (64, 32, 16, 16, 2, 2, 1, 8, kFuseNone, 4))
+  C(64, 32, 32, 0, (64, 32, 16, 32, 0, 2, 1, 16, kFuseNone, 4))
+  C(64, 32, 32, 1, (64, 32, 6, 32, 1, 2, 1, 16, kFuseNone, 4))
+  C(64, 32, 32, 2, (64, 32, 6, 32, 2, 2, 2, 16, kFuseNone, 4))
+  C(64, 64, 16, 0, (64, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 4))
+  C(64, 64, 16, 1, (64, 64, 8, 16, 1, 1, 1, 8, kFuseNone, 4))
+  C(64, 64, 16, 2, (64, 64, 8, 16, 2, 2, 1, 8, kFuseNone, 4))
+  C(64, 64, 32, 0, (64, 64, 8, 32, 0, 2, 1, 16, kFuseNone, 4))
+  C(64, 64, 32, 1, (64, 64, 1, 32, 1, 2, 1, 16, kFuseNone, 4))
+  C(64, 64, 32, 2, (64, 64, 6, 32, 2, 1, 1, 16, kFuseNone, 4))
+  C(64, 128, 16, 0, (64, 128, 8, 16, 0, 1, 1, 8, kFuseNone, 4))
+  C(64, 128, 16, 1, (64, 128, 2, 16, 1, 2, 1, 8, kFuseNone, 4))
+  C(64, 128, 16, 2, (64, 128, 4, 16, 2, 2, 1, 8, kFuseNone, 4))
+  C(64, 128, 32, 0, (64, 128, 4, 32, 0, 2, 1, 16, kFuseNone, 4))
+  C(64, 128, 32, 2, (64, 128, 2, 32, 2, 1, 1, 16, kFuseNone, 4))
+  return nullptr;
+}
+#undef C
+#undef REMORA_UNPAREN
+
+// One launch per group of at most 32 output channels (groups of equal
+// size); *handled = false (the direct kernels run instead) if no
+// instantiation exists, if TMA cannot address the operands, or for fewer
+// than 8 output channels.
+int dispatch(const ConvIO &io, ConvTCParams p, int cin, int width, int prec, int sm_count, cudaStream_t stream,
+             bool *handled) {
   *handled = false;
-  const int nout = p.COUT <= 16 ? 16 : 32;
-  if (cin == 16 && width == 64 && nout == 32)
-    return prec == 1 ? launch_conv<16, 64, 8, 32, 1, 2, 1, 16>(io, p, sm_count, stream, handled)
-         : prec == 2 ? launch_conv<16, 64, 4, 32, 2, 2, 2, 16>(io, p, sm_count, stream, handled)
-                     : launch_conv<16, 64, 8, 32, 0, 2, 2, 16>(io, p, sm_count, stream, handled);
-  // 32 input channels: two 16-channel stages per tile, double-buffered
-  if (cin == 32 && width == 64 && nout == 16)
-    return prec == 1 ? launch_conv<32, 64, 4, 16, 1, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-         : prec == 2 ? launch_conv<32, 64, 8, 16, 2, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-                     : launch_conv<32, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
-  if (cin == 16 && width == 32 && nout == 32)
-    return prec == 1 ? launch_conv<16, 32, 12, 32, 3, 2, 1, 16>(io, p, sm_count, stream, handled)
-         : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16>(io, p, sm_count, stream, handled)
-                     : launch_conv<16, 32, 16, 32, 0, 2, 2, 16>(io, p, sm_count, stream, handled);
-  if (cin == 32 && width == 32 && nout == 16)
-    return prec == 1 ? launch_conv<32, 32, 8, 16, 1, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-         : prec == 2 ? launch_conv<32, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled)
-                     : launch_conv<32, 32, 16, 16, 0, 2, 2, 8, kFuseNone, 2>(io, p, sm_count, stream, handled);
+  const int total = p.COUT;
+  // fewer than 8 output channels would leave most of an N = 16 MMA empty:
+  // the direct kernels (exact f32 order) take those
+  if (total < 8) return REMORA_OK;
+  const int ng = (total + 31) / 32, gs = (total + ng - 1) / ng;
+  const ConvLauncher launch = pick(cin, width, gs <= 16 ? 16 : 32, prec);
+  if (launch == nullptr) return REMORA_OK;
+  p.ctot = total;
+  for (int co0 = 0; co0 < total; co0 += gs) {
+    p.co0 = co0;
+    p.COUT = std::min(gs, total - co0);
+    REMORA_TRY(launch(io, p, sm_count, stream, handled));
+    if (!*handled) return REMORA_OK;  // only the first group can decline (alignment)
+  }
   return REMORA_OK;
 }
 
@@ -684,7 +775,7 @@ bool shape_ok(const ConvGeom &g, const void *x, int precision) {
 int conv_tc_fwd(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *w, const float *bias, float *y,
                 int precision, cudaStream_t stream, bool *handled) {
   *handled = false;
-  if (!shape_ok(g, x, precision) || g.K > 32) return REMORA_OK;
+  if (!shape_ok(g, x, precision)) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   ConvTCParams p{w, bias, y, nullptr, g.N, g.H, g.K, 0, 0, ws->err};
@@ -717,7 +808,7 @@ int conv_tc_dgrad_unpool(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dpo
 int conv_tc_dgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *dy, const float *w, float *dx, int precision,
                   cudaStream_t stream, bool *handled) {
   *handled = false;
-  if (!shape_ok(g, dy, precision) || g.C > 32) return REMORA_OK;
+  if (!shape_ok(g, dy, precision)) return REMORA_OK;
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, 0, &ws));
   // forward conv of dy (K channels) into dx (C channels) with flipped weights

@@ -85,10 +85,14 @@ struct WgCfg {
 };
 
 struct WgParams {
-  int N, H, COUT;
+  int N, H, COUT;  // COUT: the output channels of this launch (at most 32)
   int tiles_per_img;
   float *part;  // [gridDim.x][32][kWgOutCols]
   int *err;
+  // this launch's channels: input channels ci0 .. ci0 + 15 of cin_total and
+  // output channels co0 .. co0 + COUT - 1 of cout_total (a layer with more
+  // channels runs one launch per group)
+  int ci0, cin_total, co0, cout_total;
 };
 
 __device__ __forceinline__ void wg_st4(uint32_t addr, float a, float b, float c, float d) {
@@ -180,12 +184,12 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         const int n = t / p.tiles_per_img, h0 = (t % p.tiles_per_img) * R;
         uint8_t *raw = smem + Cf::OFF_RAW + st * Cf::RAW_STAGE;
         tc::mbar_arrive_expect_tx(&rfull[st], raw_bytes);
-        tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, n * kWgCin);
+        tc::tma_load_3d(&tmx, &rfull[st], raw, 0, h0 - 1, n * p.cin_total + p.ci0);
         if (UNPOOL) {
-          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0 / 2, n * p.COUT);
-          tc::tma_load_3d(&tmc, &rfull[st], raw + Cf::RAWC_OFF, 0, h0 / 2, n * p.COUT);
+          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0 / 2, n * p.cout_total + p.co0);
+          tc::tma_load_3d(&tmc, &rfull[st], raw + Cf::RAWC_OFF, 0, h0 / 2, n * p.cout_total + p.co0);
         } else {
-          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0, n * p.COUT);
+          tc::tma_load_3d(&tmd, &rfull[st], raw + Cf::RAWX_AL, 0, h0, n * p.cout_total + p.co0);
         }
         ++issued;
       }
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 // per value, lane l adding partials l, l+32, ... in order, then a fixed
 // shuffle tree (deterministic).
 __global__ void __launch_bounds__(256) wgrad_tc_finish(const float *__restrict__ part, int nblocks, int cout,
-                                                       float *__restrict__ dw, float *__restrict__ db) {
+                                                       int cin_total, float *__restrict__ dw, float *__restrict__ db) {
   const int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (e >= cout * kWgOutCols) return;
   const int co = e / kWgOutCols, n = e % kWgOutCols;
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(256) wgrad_tc_finish(const float *__restrict__
     if (db) db[co] = (float)s;
   } else {
     const int tap = n / kWgCin, ci = n % kWgCin;
-    dw[(co * kWgCin + ci) * 9 + tap] = (float)s;
+    dw[((long long)co * cin_total + ci) * 9 + tap] = (float)s;
   }
 }
 
@@ -370,6 +374,9 @@ int wg_encode(const void *x, int N, int C, int H, int W, int box_rows, int box_c
   return REMORA_OK;
 }
 
+// One launch per group of 16 input channels and at most 32 output
+// channels (groups of equal size); each writes its block of dw (and, the
+// first input-channel group, of db).
 template <int W, int R, int PREC, int RAW_ST, int OP_ST, bool UNPOOL = false>
 int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const float *dy, const uint8_t *codes,
                  float *dw, float *db, cudaStream_t stream) {
@@ -380,26 +387,33 @@ int launch_wgrad(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, const fl
     REMORA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM));
     attr = true;
   }
-  CUtensorMap mx, md, mc;
-  REMORA_TRY(wg_encode(x, g.N, kWgCin, g.H, W, R + 2, kWgCin, &mx));
-  if (UNPOOL) {
-    REMORA_TRY(wg_encode(dy, g.N, g.K, g.H / 2, W / 2, R / 2, g.K, &md));
-    REMORA_TRY(wg_encode(codes, g.N, g.K, g.H / 2, W / 2, R / 2, g.K, &mc, true));
-  } else {
-    REMORA_TRY(wg_encode(dy, g.N, g.K, g.H, W, R, g.K, &md));
-    mc = md;
-  }
+  const int ng = (g.K + 31) / 32, gs = (g.K + ng - 1) / ng;
   const int tiles_per_img = (g.H + R - 1) / R;
   const int ntiles = g.N * tiles_per_img;
   const int grid = std::min(ntiles, ctx->persistent_limit());
   Workspace *ws = nullptr;
   REMORA_TRY(get_workspace(ctx, stream, (size_t)grid * 32 * kWgOutCols * sizeof(float) + 256, &ws));
-  WgParams p{g.N, g.H, g.K, tiles_per_img, reinterpret_cast<float *>(ws->buf), ws->err};
-  note_launch();
-  kern<<<grid, kWgThreads, Cf::SMEM, stream>>>(mx, md, mc, p);
-  const int outs = g.K * kWgOutCols;
-  note_launch();
-  wgrad_tc_finish<<<(outs * 32 + 255) / 256, 256, 0, stream>>>(p.part, grid, g.K, dw, db);
+  CUtensorMap mx, md, mc;
+  REMORA_TRY(wg_encode(x, g.N, g.C, g.H, W, R + 2, kWgCin, &mx));
+  for (int co0 = 0; co0 < g.K; co0 += gs) {
+    const int cout = std::min(gs, g.K - co0);
+    if (UNPOOL) {
+      REMORA_TRY(wg_encode(dy, g.N, g.K, g.H / 2, W / 2, R / 2, cout, &md));
+      REMORA_TRY(wg_encode(codes, g.N, g.K, g.H / 2, W / 2, R / 2, cout, &mc, true));
+    } else {
+      REMORA_TRY(wg_encode(dy, g.N, g.K, g.H, W, R, cout, &md));
+      mc = md;
+    }
+    for (int ci0 = 0; ci0 < g.C; ci0 += kWgCin) {
+      WgParams p{g.N, g.H, cout, tiles_per_img, reinterpret_cast<float *>(ws->buf), ws->err, ci0, g.C, co0, g.K};
+      note_launch();
+      kern<<<grid, kWgThreads, Cf::SMEM, stream>>>(mx, md, mc, p);
+      const int outs = cout * kWgOutCols;
+      note_launch();
+      wgrad_tc_finish<<<(outs * 32 + 255) / 256, 256, 0, stream>>>(
+          p.part, grid, cout, g.C, dw + ((long long)co0 * g.C + ci0) * 9, ci0 == 0 && db ? db + co0 : nullptr);
+    }
+  }
   REMORA_CUDA_TRY(cudaGetLastError());
   return REMORA_OK;
 }
@@ -415,11 +429,18 @@ int conv_tc_wgrad_bias(RemoraB200Ctx *ctx, const ConvGeom &g, const float *x, co
                        int precision, cudaStream_t stream, bool *handled) {
   *handled = false;
   const int prec = wg_prec(precision);
-  if (prec < 0 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 ||
-      g.C != kWgCin || g.K < 1 || g.K > 32 || g.N < 1 || g.H < 1 || g.OH != g.H || g.OW != g.W)
+  if (prec < 0 || g.R != 3 || g.S != 3 || g.pad != 1 || g.stride != 1 || g.C < kWgCin || g.C % kWgCin ||
+      g.K < 1 || g.N < 1 || g.H < 1 || g.OH != g.H || g.OW != g.W)
     return REMORA_OK;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(dy) & 15)) return REMORA_OK;
   *handled = true;
+  if (g.W == 16)
+    return prec == 1 ? launch_wgrad<16, 4, 1, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+         : prec == 2 ? launch_wgrad<16, 4, 2, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
+                     : launch_wgrad<16, 4, 0, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream);
+  if (g.W == 128 && prec != 1)  // 3xTF32's hi and lo copies of x do not fit a 128-wide row
+    return prec == 2 ? launch_wgrad<128, 1, 2, 2, 1>(ctx, g, x, dy, nullptr, dw, db, stream)
+                     : launch_wgrad<128, 1, 0, 2, 1>(ctx, g, x, dy, nullptr, dw, db, stream);
   if (g.W == 32)
     return prec == 1 ? launch_wgrad<32, 2, 1, 1, 2>(ctx, g, x, dy, nullptr, dw, db, stream)
          : prec == 2 ? launch_wgrad<32, 2, 2, 2, 2>(ctx, g, x, dy, nullptr, dw, db, stream)

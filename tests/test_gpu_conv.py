@@ -66,6 +66,31 @@ def test_conv_fwd_dgrad_tensor_core_shapes(cuda, oracle_mod, shape, prec):
     close(dw, oracle_mod.conv2d_wgrad(x, dy, sw, nthreads=oracle_mod.max_threads()), prec == "3xtf32")
 
 
+@pytest.mark.parametrize("shape", [((2, 16, 16, 16), (48, 16, 3, 3)), ((2, 32, 20, 128), (40, 32, 3, 3)),
+                                   ((2, 64, 32, 32), (64, 64, 3, 3)), ((1, 64, 24, 64), (16, 64, 3, 3)),
+                                   ((2, 16, 10, 16), (100, 16, 3, 3)), ((1, 32, 9, 128), (16, 32, 3, 3))])
+@pytest.mark.parametrize("prec", ["tf32", "3xtf32", "2xtf32"])
+def test_conv_wider_shapes(cuda, oracle_mod, shape, prec):
+    """3x3 / pad 1 layers beyond the crater CNN's: 16-, 64- and 128-wide
+    images, 16, 32 or 64 input channels, and output channels past 32, which
+    the tensor-core kernels take in launches of at most 32 output channels
+    each (weight gradient: 16 input channels per launch as well).  Where no
+    tensor-core form exists (48 or 100 reduction channels in the input
+    gradient, 3xTF32 weight gradient of 128-wide rows) the direct kernels
+    run, and the same tolerances hold."""
+    sx, sw = shape
+    x, w, b = data(sx, sw, 21)
+    dx_, dw_ = to_dev(x, cuda), to_dev(w, cuda)
+    nt = oracle_mod.max_threads()
+    y = to_host(ops.conv2d_fwd(dx_, dw_, to_dev(b, cuda), precision=prec))
+    close(y, oracle_mod.conv2d_fwd(x, w, b, nthreads=nt), prec == "3xtf32")
+    dy = np.random.Generator(np.random.PCG64(22)).standard_normal(y.shape).astype(np.float32)
+    dx = to_host(ops.conv2d_dgrad(to_dev(dy, cuda), dw_, sx, precision=prec))
+    close(dx, oracle_mod.conv2d_dgrad(dy, w, sx, nthreads=nt), prec == "3xtf32")
+    dw = to_host(ops.conv2d_wgrad(dx_, to_dev(dy, cuda), sw, precision=prec))
+    close(dw, oracle_mod.conv2d_wgrad(x, dy, sw, nthreads=nt), prec == "3xtf32")
+
+
 @pytest.mark.parametrize("shape", [((2, 16, 64, 64), (32, 16, 3, 3)), ((3, 16, 32, 32), (32, 16, 3, 3)),
                                    ((2, 32, 32, 32), (16, 32, 3, 3)), ((2, 32, 64, 64), (16, 32, 3, 3))])
 def test_conv_2xtf32_between_tf32_and_3xtf32(cuda, oracle_mod, shape):
