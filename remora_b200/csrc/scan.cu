@@ -203,23 +203,37 @@ __global__ void __launch_bounds__(kCarryThreads) carries_rank1(const T *__restri
   __syncthreads();
   T ex = __shfl_up_sync(0xffffffffu, inc, 1);
   T run = lane == 0 ? sh[warp] : Op::apply(sh[warp], ex);
-  for (int64_t i = b0; i < b1; i += 4) {
-    T v[4];
-    if (i + 4 <= b1) {
-      load4(agg + i, v);
+  // the run again, eight 16-byte reads in flight, carries written 16 bytes
+  // at a time
+  for (int64_t i = b0; i < b1; i += 32) {
+    T v[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t q = i + 4 * j;
+      if (q + 4 <= b1) {
+        load4(agg + q, v[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[j][e] = q + e < b1 ? agg[q + e] : Op::ident();
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t q = i + 4 * j;
       T c[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         c[e] = run;
-        run = Op::apply(run, v[e]);
+        if (q + e < b1) run = Op::apply(run, v[j][e]);
       }
-      *reinterpret_cast<uint4 *>(carry + i) =
-          make_uint4(__builtin_bit_cast(uint32_t, c[0]), __builtin_bit_cast(uint32_t, c[1]),
-                     __builtin_bit_cast(uint32_t, c[2]), __builtin_bit_cast(uint32_t, c[3]));
-    } else {
-      for (int64_t q = i; q < b1; ++q) {
-        carry[q] = run;
-        run = Op::apply(run, agg[q]);
+      if (q + 4 <= b1) {
+        *reinterpret_cast<uint4 *>(carry + q) =
+            make_uint4(__builtin_bit_cast(uint32_t, c[0]), __builtin_bit_cast(uint32_t, c[1]),
+                       __builtin_bit_cast(uint32_t, c[2]), __builtin_bit_cast(uint32_t, c[3]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (q + e < b1) carry[q + e] = c[e];
       }
     }
   }
