@@ -1074,13 +1074,19 @@ def run_ours(args) -> None:
 
 
 # Per-call DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel, from ncu captures of the same bench commands.
-TRAFFIC: dict[str, float | None] = {"chained": 67_127_040 + 637_952, "row_norms": None,
-                                    "matmul": 335_706_368 + 61_118_208, "matmul_3x": None, "bmm": None,
-                                    "conv": 67_187_968 + 75_173_120, "conv_dgrad": 134_268_160 + 33_349_888,
-                                    "conv_wgrad": 201_346_304 + 4_110_848, "cnn": None, "cnn_tf32": None,
-                                    # a sort or filter call is several kernels: no single figure
-                                    "sort": None, "grade": None, "filter": None, "scan": None}
+# dominant kernel, from ncu captures of the same bench commands (for the CNN
+# per stage, "cnn:<stage>"; for the scan, the three kernels of one call).
+TRAFFIC: dict[str, float | None] = {
+    "chained": 67_117_312 + 713_728, "row_norms": 33_560_832 + 0,
+    "matmul": 279_432_192 + 53_611_264, "matmul_3x": None, "bmm": None,
+    "conv": 67_158_528 + 76_917_504, "conv_dgrad": 134_289_664 + 33_810_432, "conv_wgrad": 201_347_072 + 3_692_288,
+    "cnn:conv1_fwd": 67_196_928 + 277_051_392, "cnn:conv2_fwd": 268_837_888 + 129_799_936,
+    "cnn:dense1_fwd": 136_367_616 + 3_971_584, "cnn:dense1_wgrad": 135_338_240 + 4_023_040,
+    "cnn:dense1_dgrad": 3_313_664 + 74_428_672, "cnn:conv2_wgrad": 436_544_256 + 4_085_504,
+    "cnn:conv2_dgrad": 167_825_408 + 212_258_816, "cnn:conv1_wgrad": 402_680_320 + 7_718_912,
+    "scan": 1_073_750_000 + 3_587_000 + 539_000 + 1_074_945_000 + 1_021_055_000,
+    # a sort or filter call is several kernels: no single figure
+    "sort": None, "grade": None, "filter": None}
 
 
 def cpu_baseline(wl, budget_s: float = 8.0) -> dict:
