@@ -357,7 +357,12 @@ int remora_b200_gemm(RemoraB200Ctx *ctx, const RemoraGemmSpec *spec,
 /* Multi-channel NCHW convolution, cross-correlation as the reference's
    conv2d = map(dot-patch p (ravel k)) (im2col image) + b
    (examples/crater_train.py:30-36), extended with channels, batch and zero
-   padding.  bias may be NULL. */
+   padding.  bias may be NULL.  3x3 / pad 1 / stride 1 layers with 16, 32
+   or 64 reduction channels on 16-, 32-, 64- or 128-wide rows and at least
+   8 output channels run on the tensor cores in the spec's precision (more
+   than 32 output channels: one launch per group of at most 32); every
+   other shape runs on CUDA-core kernels in the reference's f32 order,
+   whatever the precision. */
 int remora_b200_conv2d_fwd(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                            const RemoraMemRef4 *x, const RemoraMemRef4 *w,
                            const RemoraMemRef1 *bias, RemoraMemRef4 *y,
@@ -368,7 +373,9 @@ int remora_b200_conv2d_dgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                              const RemoraMemRef4 *dy, const RemoraMemRef4 *w,
                              RemoraMemRef4 *dx, remora_stream_t stream);
 /* Reverse mode w.r.t. the weights: the mul VJP adj*other summed over the
-   patches (remora/ad.py:88-92 with the fold VJP at :106-110). */
+   patches (remora/ad.py:88-92 with the fold VJP at :106-110).  On the
+   tensor cores for 3x3 / pad 1 / stride 1 layers whose input channels are a
+   multiple of 16, on 16-, 32-, 64- or 128-wide rows (128: TF32 and 2XTF32). */
 int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                              const RemoraMemRef4 *x, const RemoraMemRef4 *dy,
                              RemoraMemRef4 *dw, remora_stream_t stream);
