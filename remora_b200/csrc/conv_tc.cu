@@ -54,7 +54,7 @@
 // the first NOUT columns): the same three products as 1 from two reads of
 // the activation operand instead of three.  The 16 -> 32 channel forward on
 // 32-wide images (the crater CNN's conv2, plain and pooled) runs this form
-// with tiles of 12 rows (two 256-column accumulators fit TMEM).
+// with tiles of 14 rows (two 256-column accumulators fit TMEM).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -338,6 +338,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
         const int acc = ti & 1;
         const uint32_t aph = (ti >> 1) & 1;
+        // 128-row blocks that hold rows of this tile: the image's last tile
+        // may have fewer rows (the epilogue stores none of the others)
+        const int rows_here = min(TH, p.H - (t % p.tiles_per_img) * TH);
+        const int mb_n = min(Cf::MB, ((Cf::PAR ? (rows_here + 1) / 2 : rows_here) * Cf::PW + 127) / 128);
         for (int cs = 0; cs < CSPLIT; ++cs, ++it) {
         const int st = it % A_ST;
         const uint32_t ph = (it / A_ST) & 1;
@@ -349,7 +353,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const uint64_t ad_hi0 = desc_interleaved(a_hi, Cf::NPAR * Cf::PLANE);
         const uint64_t ad_lo0 = desc_interleaved(a_hi + Cf::A_COPY, Cf::NPAR * Cf::PLANE);
 #pragma unroll 1
-        for (int mb = 0; mb < Cf::MB; ++mb) {
+        for (int mb = 0; mb < mb_n; ++mb) {
           const uint64_t ad_hi = ad_hi0 + (uint64_t)(mb * 128), ad_lo = ad_lo0 + (uint64_t)(mb * 128);
 #pragma unroll
           for (int a = 0; a < Cf::NPAR; ++a) {
@@ -648,7 +652,7 @@ ConvLauncher pick(int cin, int width, int nout, int prec) {
   C(16, 32, 16, 1, (16, 32, 16, 16, 1, 2, 1, 8, kFuseNone, 1))
   C(16, 32, 16, 2, (16, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 1))
   C(16, 32, 32, 0, (16, 32, 16, 32, 0, 2, 2, 16, kFuseNone, 1))
-  C(16, 32, 32, 1, (16, 32, 12, 32, 3, 2, 1, 16, kFuseNone, 1))
+  C(16, 32, 32, 1, (16, 32, 14, 32, 3, 2, 1, 16, kFuseNone, 1))
   C(16, 32, 32, 2, (16, 32, 8, 32, 2, 2, 2, 16, kFuseNone, 1))
   C(16, 64, 16, 0, (16, 64, 8, 16, 0, 2, 2, 8, kFuseNone, 1))
   C(16, 64, 16, 1, (16, 64, 8, 16, 1, 2, 1, 8, kFuseNone, 1))
@@ -744,7 +748,7 @@ int dispatch_pool(const ConvIO &io, const ConvTCParams &p, int cin, int width, i
                   cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 16 && width == 32 && p.COUT > 16 && p.COUT <= 32 && p.H % 2 == 0)
-    return prec == 1 ? launch_conv<16, 32, 12, 32, 3, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
+    return prec == 1 ? launch_conv<16, 32, 14, 32, 3, 2, 1, 16, kFusePool>(io, p, sm_count, stream, handled)
          : prec == 2 ? launch_conv<16, 32, 8, 32, 2, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled)
                      : launch_conv<16, 32, 16, 32, 0, 2, 2, 16, kFusePool>(io, p, sm_count, stream, handled);
   return REMORA_OK;
