@@ -1080,7 +1080,7 @@ TRAFFIC: dict[str, float | None] = {
     "chained": 67_117_312 + 713_728, "row_norms": 33_560_832 + 0,
     "matmul": 279_432_192 + 53_611_264, "matmul_3x": None, "bmm": None,
     "conv": 67_158_528 + 76_917_504, "conv_dgrad": 134_289_664 + 33_810_432, "conv_wgrad": 201_347_072 + 3_692_288,
-    "cnn:conv1_fwd": 67_196_928 + 277_051_392, "cnn:conv2_fwd": 268_837_888 + 129_799_936,
+    "cnn:conv1_fwd": 67_196_928 + 277_051_392, "cnn:conv2_fwd": 268_548_608 + 131_713_792,
     "cnn:dense1_fwd": 136_367_616 + 3_971_584, "cnn:dense1_wgrad": 135_338_240 + 4_023_040,
     "cnn:dense1_dgrad": 3_313_664 + 74_428_672, "cnn:conv2_wgrad": 436_544_256 + 4_085_504,
     "cnn:conv2_dgrad": 167_825_408 + 212_258_816, "cnn:conv1_wgrad": 402_680_320 + 7_718_912,
