@@ -54,7 +54,8 @@
 // the first NOUT columns): the same three products as 1 from two reads of
 // the activation operand instead of three.  The 16 -> 32 channel forward on
 // 32-wide images (the crater CNN's conv2, plain and pooled) runs this form
-// with tiles of 14 rows (two 256-column accumulators fit TMEM).
+// with tiles of 14 rows (two 256-column accumulators fit TMEM), and so does
+// the 32 -> 16 channel 3xTF32 input gradient on 32-wide images.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -673,7 +674,7 @@ ConvLauncher pick(int cin, int width, int nout, int prec) {
   C(32, 16, 32, 1, (32, 16, 6, 32, 1, 2, 2, 16, kFuseNone, 2))
   C(32, 16, 32, 2, (32, 16, 6, 32, 2, 2, 2, 16, kFuseNone, 2))
   C(32, 32, 16, 0, (32, 32, 16, 16, 0, 2, 2, 8, kFuseNone, 2))
-  C(32, 32, 16, 1, (32, 32, 8, 16, 1, 2, 2, 8, kFuseNone, 2))
+  C(32, 32, 16, 1, (32, 32, 16, 16, 3, 2, 1, 8, kFuseNone, 2))
   C(32, 32, 16, 2, (32, 32, 16, 16, 2, 2, 2, 8, kFuseNone, 2))
   C(32, 32, 32, 0, (32, 32, 16, 32, 0, 2, 2, 16, kFuseNone, 2))
   C(32, 32, 32, 1, (32, 32, 16, 32, 1, 1, 1, 16, kFuseNone, 2))
@@ -758,7 +759,7 @@ int dispatch_unpool(const ConvIO &io, const ConvTCParams &p, int cin, int width,
                     cudaStream_t stream, bool *handled) {
   *handled = false;
   if (cin == 32 && width == 32 && p.COUT <= 16 && p.H % 2 == 0)
-    return prec == 1 ? launch_conv<32, 32, 8, 16, 1, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
+    return prec == 1 ? launch_conv<32, 32, 16, 16, 3, 2, 1, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
          : prec == 2 ? launch_conv<32, 32, 16, 16, 2, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled)
                      : launch_conv<32, 32, 16, 16, 0, 2, 2, 8, kFuseUnpool, 2>(io, p, sm_count, stream, handled);
   return REMORA_OK;
