@@ -1,6 +1,8 @@
 // conv_tc.cu — tcgen05 implicit-GEMM convolution for 3x3 / pad 1 / stride 1
-// (the benchmark layer [256,16,64,64] * [32,16,3,3] and the crater CNN's
-// second layer), forward and input gradient, TF32 and 3xTF32.
+// (among them the benchmark layer [256,16,64,64] * [32,16,3,3] and the
+// crater CNN's second layer), forward and input gradient, TF32, 3xTF32 and
+// 2xTF32; 16, 32 or 64 input channels on 16- to 128-wide images, output
+// channels in launches of at most 32 (a table of instantiations below).
 //
 // GEMM view of one tile: M = output pixels of TH rows of one image, N = the
 // output channels (16 or 32, zero-padded weights above COUT), K = input

@@ -1,7 +1,7 @@
 // conv_wgrad_tc.cu — tcgen05 weight (and bias) gradient of a 3x3 / pad 1 /
-// stride 1 convolution with 16 input channels and at most 32 output
-// channels (the benchmark layer and the crater CNN's second layer), TF32 or
-// 3xTF32:
+// stride 1 convolution, one launch per group of 16 input channels and at
+// most 32 output channels (the benchmark layer and the crater CNN's second
+// layer are one group each), TF32, 3xTF32 or 2xTF32:
 //   dw[co][ci][r][s] = sum_pixels dy[co][p] * x[ci][p + (r - 1, s - 1)]
 //   db[co]           = sum_pixels dy[co][p]
 // GEMM view: M = 64 rows (dy channels 0..31, then 32 more rows: zero for
