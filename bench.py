@@ -102,6 +102,12 @@ class ClockSampler:
 
         self._thread = threading.Thread(target=pump, daemon=True)
         self._thread.start()
+        # nvidia-smi can take a second or more to print its first line on a
+        # fresh box: wait (bounded) for it, so that a short timed region
+        # still falls inside the sampled window
+        t0 = time.perf_counter()
+        while not self.rows and time.perf_counter() - t0 < 5.0 and self._proc.poll() is None:
+            time.sleep(0.05)
 
     def stop(self) -> dict | None:
         if self._proc is None:
@@ -113,6 +119,16 @@ class ClockSampler:
             self._proc.kill()
         if self._thread:
             self._thread.join(timeout=2)
+        if not self.rows:
+            # the sampler printed nothing in the window: one query right
+            # after the timed region is the closest record left
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=10).stdout
+                self.rows = [[c.strip() for c in line.split(",")] for line in out.splitlines() if line.strip()]
+            except (FileNotFoundError, OSError, subprocess.TimeoutExpired):
+                pass
         busy = [r for r in self.rows if len(r) >= 10 and _num(r[4]) > 0]
         use = busy or self.rows
         if not use:
