@@ -224,10 +224,12 @@ int remora_b200_init(int device, RemoraB200Ctx **ctx);
 int remora_b200_shutdown(RemoraB200Ctx *ctx);
 /* replaces the CUDAError message path (remora/runtime.py:477-491) */
 int remora_b200_last_error(char *buf, size_t n);
+/* The library's version string (no counterpart in the reference). */
 const char *remora_b200_version(void);
 /* Number of kernels the library has enqueued in this process (launched, or
    recorded into a CUDA graph under stream capture): the difference over a
-   captured region is the kernel count of one replay. */
+   captured region is the kernel count of one replay.  No counterpart in the
+   reference. */
 unsigned long long remora_b200_launch_count(void);
 /* replaces CUDARuntime.alloc / free (remora/runtime.py:270-281) */
 int remora_b200_malloc(RemoraB200Ctx *ctx, size_t nbytes, void **dptr);
@@ -265,7 +267,9 @@ int remora_b200_wait_check(RemoraB200Ctx *ctx, int64_t limit_cycles,
    those SMs free lets the two run side by side.  No counterpart in the
    reference (one stream, no collectives). */
 int remora_b200_set_persistent_sms(RemoraB200Ctx *ctx, int32_t n);
-/* Pins a host buffer for asynchronous copies (cudaHostRegister). */
+/* Pins a host buffer for asynchronous copies (cudaHostRegister), and
+   releases it.  No counterpart in the reference, whose copies are
+   synchronous (remora/runtime.py:283-300). */
 int remora_b200_host_register(void *ptr, size_t nbytes);
 int remora_b200_host_unregister(void *ptr);
 
@@ -373,7 +377,7 @@ int remora_b200_conv2d_dgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                              const RemoraMemRef4 *dy, const RemoraMemRef4 *w,
                              RemoraMemRef4 *dx, remora_stream_t stream);
 /* Reverse mode w.r.t. the weights: the mul VJP adj*other summed over the
-   patches (remora/ad.py:88-92 with the fold VJP at :106-110).  On the
+   patches (remora/ad.py:91-95 with the fold VJP at :106-110).  On the
    tensor cores for 3x3 / pad 1 / stride 1 layers whose input channels are a
    multiple of 16, on 16-, 32-, 64- or 128-wide rows (128: TF32 and 2XTF32). */
 int remora_b200_conv2d_wgrad(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,

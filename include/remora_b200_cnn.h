@@ -35,7 +35,9 @@ int remora_b200_conv1_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *x,
                                 RemoraMemRef4 *pooled, RemoraMemRef4 *code,
                                 remora_stream_t stream);
 
-/* pooled = maxpool2x2(relu(a)) for a [N,C,H,W] (H, W even). */
+/* pooled = maxpool2x2(relu(a)) for a [N,C,H,W] (H, W even); ReLU is the
+   select form of examples/crater_train.py:46-48, the pooling has no
+   reference counterpart. */
 int remora_b200_relu_pool(RemoraB200Ctx *ctx, const RemoraMemRef4 *a,
                           RemoraMemRef4 *pooled, RemoraMemRef4 *code,
                           remora_stream_t stream);
@@ -70,7 +72,10 @@ int remora_b200_dense_bias_relu_bce(RemoraB200Ctx *ctx, const RemoraMemRef2 *hpr
    dw[o] = sum_b dz[b] h[b,o], db = sum_b dz[b],
    dh[b,o] = h[b,o] > 0 ? dz[b] * w[o] : 0, and, when dh_colsum is not
    NULL, dh_colsum[o] = sum_b dh[b,o] (the gradient of the hidden layer's
-   bias).  Sums in f64, fixed order. */
+   bias).  Sums in f64, fixed order.  The dot, fold and select VJPs of
+   remora/ad.py (:91-95, :106-110, :172-179) batched over the samples, in
+   place of the reference's per-parameter gradient functions
+   (examples/crater_train.py:169-198). */
 int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h,
                                const RemoraMemRef1 *w, const RemoraMemRef1 *dz,
                                RemoraMemRef2 *dh, RemoraMemRef1 *dw,
@@ -79,7 +84,10 @@ int remora_b200_dense_relu_bwd(RemoraB200Ctx *ctx, const RemoraMemRef2 *h,
 
 /* conv1's weight and bias gradients straight from the pooled gradient and
    the pool codes (the unpooled gradient is never materialised):
-   x [B,1,H,W], dpooled/code [B,K,H/2,W/2], dw [K,1,3,3], db [K]. */
+   x [B,1,H,W], dpooled/code [B,K,H/2,W/2], dw [K,1,3,3], db [K].  The
+   select VJP (remora/ad.py:172-179) composed with the conv weight and bias
+   VJPs (:91-95, :106-110), in place of the reference's per-parameter
+   gradient functions (examples/crater_train.py:169-198). */
 int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x,
                                    const RemoraMemRef4 *dpooled,
                                    const RemoraMemRef4 *code, RemoraMemRef4 *dw,
@@ -89,7 +97,9 @@ int remora_b200_conv1_wgrad_pooled(RemoraB200Ctx *ctx, const RemoraMemRef4 *x,
    on the tensor cores (TF32 or 3xTF32 per spec), x [B,C,H,W] (C = 16,
    W = 32), w [K,C,3,3] (K = 17..32), pooled and code [B,K,H/2,W/2]; the
    full-resolution activation is never written.  Other shapes return
-   REMORA_ERR_UNSUPPORTED. */
+   REMORA_ERR_UNSUPPORTED.  The reference's conv2d (examples/crater_train.py:
+   30-36, a dot over each im2col patch) and ReLU (:46-48) for many channels
+   at once; the pooling has no reference counterpart. */
 int remora_b200_conv2d_fwd_relu_pool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                                      const RemoraMemRef4 *x, const RemoraMemRef4 *w,
                                      const RemoraMemRef1 *bias, RemoraMemRef4 *pooled,
@@ -98,14 +108,18 @@ int remora_b200_conv2d_fwd_relu_pool(RemoraB200Ctx *ctx, const RemoraConvSpec *s
 /* Input gradient of that layer from the pooled gradient: dx = conv2d_dgrad(
    unpool(dpooled, code), w) with the unpooled gradient formed on the fly
    (dpooled/code [B,K,H/2,W/2], K = 32; w [K,C,3,3], C <= 16; dx [B,C,H,W],
-   W = 32). */
+   W = 32).  The select VJP (remora/ad.py:172-179) composed with the conv
+   input VJP (:157-171). */
 int remora_b200_conv2d_dgrad_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                                     const RemoraMemRef4 *dpooled,
                                     const RemoraMemRef4 *code, const RemoraMemRef4 *w,
                                     RemoraMemRef4 *dx, remora_stream_t stream);
 
 /* Weight and bias gradients of that layer from the pooled gradient
-   (x [B,16,H,W], W = 32; dpooled/code [B,K,H/2,W/2]; dw [K,16,3,3]; db [K]). */
+   (x [B,16,H,W], W = 32; dpooled/code [B,K,H/2,W/2]; dw [K,16,3,3]; db [K]).
+   The select VJP (remora/ad.py:172-179) composed with the conv weight and
+   bias VJPs (:91-95, :106-110), in place of the reference's per-parameter
+   gradient functions (examples/crater_train.py:169-198). */
 int remora_b200_conv2d_wgrad_bias_unpool(RemoraB200Ctx *ctx, const RemoraConvSpec *spec,
                                          const RemoraMemRef4 *x,
                                          const RemoraMemRef4 *dpooled,
@@ -164,7 +178,8 @@ int remora_b200_cnn_step(RemoraB200Ctx *ctx, const RemoraCnnStepSpec *spec,
    through the same NCCL as remora_b200_cnn_step: a unique id (128 bytes,
    made by one rank and handed to the others by any host channel), a
    communicator of rank `rank` of `nranks` (the device current on the
-   calling thread), and its release. */
+   calling thread), and its release.  No counterpart in the reference,
+   which trains on one device. */
 int remora_b200_nccl_unique_id(void *id_out);
 int remora_b200_nccl_comm_init(void **comm_out, int32_t nranks, const void *id,
                                int32_t rank);
