@@ -4,7 +4,7 @@ The reference differentiates a program by generating one gradient function
 per input and compiling each separately (examples/crater_train.py:169-198;
 its fused single-kernel form for ``fold + lit (elementwise expr of x)`` is
 compile_gradient_function_source_to_supported_gpu_artifacts, exercised by
-remora/tests/test_ad_source.py:553-605).  Here, for a loss
+tests/test_ad_source.py:553-605).  Here, for a loss
 
     loss(x_1 .. x_n) = fold (+) init (E(x_1 .. x_n))
 

@@ -1,5 +1,5 @@
 """Generate tests/golden/program_plans.{json,npz}: whole Remora programs —
-the reference's own acceptance programs (remora/tests/acceptance/pass/
+the reference's own acceptance programs (tests/acceptance/pass/
 *.remora) plus a few more — compiled by the reference's front end and
 planned by remora_b200.program_plan, with the result the reference
 interpreter gives (remora/runtime.py:evaluate_source).  Where the acceptance

@@ -7,7 +7,7 @@ value_and_grad_plans.{json,npz}: wider losses (scalar parameters, several
 folds, rank-2 and rank-3 arrays) as value-and-grad plans, with the
 interpreter's value and the tape's gradients.  The first three losses and their
 closed-form gradients are the reference's own GPU gradient tests
-(remora/tests/test_ad_source.py:569-605).  Regenerate with:
+(tests/test_ad_source.py:569-605).  Regenerate with:
 
     REMORA_REFERENCE=/path/to/remorac python tests/golden/make_reference_gradients.py
 """

@@ -9,7 +9,7 @@ reference nor its front end.  The reference is only needed to regenerate:
     REMORA_REFERENCE=/path/to/remorac python tests/golden/make_reference_programs.py
 
 The first programs are the ones the reference's GPU executor tests compile
-(remora/tests/test_executor.py: scale, add, sum, dot, inc); the rest cover
+(tests/test_executor.py: scale, add, sum, dot, inc); the rest cover
 the other shapes the codegen accepts.  tests/golden/function_plans.{json,npz}
 hold functions no single kernel computes, planned by
 remora_b200.program_plan.plan_from_function, with seeded inputs and the

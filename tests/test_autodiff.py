@@ -3,7 +3,7 @@ without a GPU: the symbolic derivative against central differences in f64,
 and the recorded specs (tests/golden/reference_gradients.json, made from the
 reference's front end) on the oracle against the reference's tape AD and,
 for its three GPU cases, its closed forms (rtol 1e-5, the reference's own
-tolerance, remora/tests/test_ad_source.py:605)."""
+tolerance, tests/test_ad_source.py:605)."""
 
 from __future__ import annotations
 

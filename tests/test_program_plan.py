@@ -1,7 +1,7 @@
 """Whole-program plans (remora_b200.program_plan) without a GPU.
 
 tests/golden/program_plans.{json,npz} holds the reference's acceptance
-programs (remora/tests/acceptance/pass/*.remora) and a few more, planned from
+programs (tests/acceptance/pass/*.remora) and a few more, planned from
 the reference front end's HIR, with the reference's result for each.  Here a
 CPU interpreter of plans, built on the oracle, runs every recorded plan and
 must give those results: the plan means what the program says.  Where the
