@@ -203,7 +203,7 @@ typedef struct {
 /* Filter predicate fused into the compaction: keep x where `x op literal`
    (op one of REMORA_OP_LT .. REMORA_OP_NE; f32 comparisons are ordered, so
    NaN compares false), the mask the reference's lowering builds with
-   arith.cmpi / arith.cmpf (remora/lowering/tensor_ops.py:2655-2706). */
+   arith.cmpi / arith.cmpf (remora/lowering/tensor_ops.py:2657-2706). */
 typedef struct {
   int32_t op;
   float lit_f;   /* literal of an f32 filter */
@@ -220,7 +220,7 @@ typedef struct RemoraB200Ctx RemoraB200Ctx;
 /* ------------------------------------------------------------------------ */
 /* replaces CUDARuntime.__init__ (remora/runtime.py:246-260) */
 int remora_b200_init(int device, RemoraB200Ctx **ctx);
-/* replaces CUDARuntime.close (remora/runtime.py:316-320) */
+/* replaces CUDARuntime.close (remora/runtime.py:315-319) */
 int remora_b200_shutdown(RemoraB200Ctx *ctx);
 /* replaces the CUDAError message path (remora/runtime.py:477-491) */
 int remora_b200_last_error(char *buf, size_t n);
@@ -395,7 +395,7 @@ int remora_b200_col2im(RemoraB200Ctx *ctx, const RemoraIm2colSpec *spec,
                        remora_stream_t stream);
 
 /* Rank-2 transpose, the swapaxes(0,1) of remora/runtime.py:1052-1056 and
-   its VJP (remora/ad.py:113-114). */
+   its VJP (remora/ad.py:116-117). */
 int remora_b200_transpose(RemoraB200Ctx *ctx, int32_t dtype,
                           const RemoraMemRef2 *in, RemoraMemRef2 *out,
                           remora_stream_t stream);

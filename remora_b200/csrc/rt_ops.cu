@@ -500,7 +500,7 @@ int sort_or_grade(RemoraB200Ctx *ctx, int32_t dtype, const void *in_desc, void *
 // Keep flags: an i32 mask (remora_rt.c's form), a one-byte bool mask, or a
 // comparison of the value against a literal evaluated in the kernel (the
 // lowering's mask program, tensor_ops.py:2697-2706, fused away).  Float
-// comparisons are ordered, like arith.cmpf o** (tensor_ops.py:2655-2662):
+// comparisons are ordered, like arith.cmpf o** (tensor_ops.py:2657-2663):
 // NaN compares false, `!=` included.
 enum { kMaskI32 = 0, kMaskU8 = 1, kMaskPred = 2 };
 
