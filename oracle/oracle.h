@@ -18,7 +18,7 @@
  *   sort / grade     remora/remora_rt.c:17-121 (interpreter: stable np.sort /
  *                    np.argsort, remora/runtime.py:1171-1177)
  *   filter           remora/remora_rt.c:125-163 (+ the comparison mask of
- *                    remora/lowering/tensor_ops.py:2655-2706)
+ *                    remora/lowering/tensor_ops.py:2657-2706)
  *   replicate        remora/remora_rt.c:167-285
  * f32 arithmetic is done as separate IEEE multiplies and adds (the file is
  * compiled with -ffp-contract=off), matching arith.mulf/arith.addf.

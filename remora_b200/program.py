@@ -155,7 +155,7 @@ def compile_program(
 def from_reference_expr(node: object) -> Expr:
     """Convert the reference's F32Expr dataclasses (F32InputExpr,
     F32ConstantExpr, F32BinaryExpr, F32CmpExpr, F32SelectExpr of
-    remora/_gpu_map_support.py:28-60) into this module's nodes."""
+    remora/_gpu_map_support.py:29-60) into this module's nodes."""
     name = type(node).__name__
     if name == "F32InputExpr":
         return InputExpr(int(node.index))

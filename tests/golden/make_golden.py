@@ -107,7 +107,7 @@ def main() -> None:
     # typechecks (prefix agreement), but the interpreter evaluates it with
     # numpy's suffix broadcasting and raises; the CPU MLIR lowering keeps the
     # first k result dims for a rank-k operand
-    # (remora/lowering/tensor_ops.py:707-715), which is the rule restated
+    # (remora/lowering/tensor_ops.py:708-715), which is the rule restated
     # here: out[i, j] = p[i, j] + q[i], one f32 add.
     p = rng.standard_normal((3, 4)).astype(np.float32)
     q = rng.standard_normal((3,)).astype(np.float32)

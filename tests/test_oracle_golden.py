@@ -168,7 +168,7 @@ def test_bce_formula(orc):
 
 
 def test_cnn_step_gradient_fd(orc):
-    """Central finite differences (the reference's remora/ad_testing.py:13-37
+    """Central finite differences (the reference's remora/ad_testing.py:15-37
     method) on a few parameters of the batch CNN oracle."""
     rng = np.random.default_rng(2718)
     from remora_b200.crater import init_params, make_batch
