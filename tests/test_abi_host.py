@@ -142,3 +142,55 @@ def test_jit_check_rejects_bad_programs():
     assert "before it is written" in L.last_error()
     p = compile_program(UnaryExpr("exp", x(0)), 1, compute="i32")
     assert L.lib().remora_b200_jit_check(ctypes.byref(p), -1, None, 0) == L.ERR_UNSUPPORTED
+
+
+def _c_member(cname: str, field: str) -> str:
+    m = re.fullmatch(r"(size|stride)(\d+)", field)
+    if cname.startswith("RemoraMemRef") and m:
+        return f"{m.group(1)}s[{m.group(2)}]"
+    return field
+
+
+def test_headers_compile_as_c_and_cxx_with_the_ctypes_layouts(tmp_path):
+    """include/*.h is plain C (what a cgo or C caller includes) and C++, and a
+    C compiler lays every struct out exactly as the ctypes mirrors the Python
+    binding passes by pointer: same size, same offset for every field."""
+    import shutil
+    import subprocess
+
+    from remora_b200 import abi
+    from remora_b200.cnn import RemoraCnnStepSpec
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = [abi.DESCRIPTORS[r] for r in range(abi.MAX_RANK + 1)] + [
+        L.RemoraMapInstr, L.RemoraMapProgram, L.RemoraFoldSpec, L.RemoraScanSpec, L.RemoraGemmSpec,
+        L.RemoraConvSpec, L.RemoraIm2colSpec, L.RemoraFilterPred, RemoraCnnStepSpec]
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "remora_b200.h"', '#include "remora_b200_cnn.h"',
+             "int main(void) {"]
+    for s in structs:
+        c = s.__name__
+        lines.append(f'  printf("{c} %zu\\n", sizeof({c}));')
+        for f, _ in s._fields_:
+            lines.append(f'  printf("{c}.{f} %zu\\n", offsetof({c}, {_c_member(c, f)}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", f"-I{ROOT / 'include'}",
+                        str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for s in structs:
+        c = s.__name__
+        assert int(got[c]) == ctypes.sizeof(s), c
+        for f, _ in s._fields_:
+            assert int(got[f"{c}.{f}"]) == getattr(s, f).offset, f"{c}.{f}"
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is not None:
+        for h in sorted((ROOT / "include").glob("*.h")):
+            r = subprocess.run([cxx, "-std=c++11", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", "c++",
+                                f"-I{ROOT / 'include'}", str(h)], capture_output=True, text=True)
+            assert r.returncode == 0, (h.name, r.stderr)
