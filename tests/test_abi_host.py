@@ -194,3 +194,41 @@ def test_headers_compile_as_c_and_cxx_with_the_ctypes_layouts(tmp_path):
             r = subprocess.run([cxx, "-std=c++11", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", "c++",
                                 f"-I{ROOT / 'include'}", str(h)], capture_output=True, text=True)
             assert r.returncode == 0, (h.name, r.stderr)
+
+
+def test_a_c_caller_links_and_calls_the_library(tmp_path):
+    """The library as a C (or cgo) binding sees it: linked by name, no Python
+    in between.  Calls that need no GPU: the version, a call rejected before
+    any work (no context) with its status and message."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    so = L.library_path()
+    src = tmp_path / "caller.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "remora_b200.h"
+int main(void) {
+  char msg[512];
+  int st;
+  printf("version %s\n", remora_b200_version());
+  st = remora_b200_memset_d32(NULL, NULL, 0u, 16, NULL);
+  remora_b200_last_error(msg, sizeof msg);
+  printf("status %d\n", st);
+  printf("message %s\n", msg);
+  return 0;
+}
+""")
+    exe = tmp_path / "caller"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(src), "-o", str(exe),
+                        f"-L{so.parent}", f"-l:{so.name}", f"-Wl,-rpath,{so.parent}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True, timeout=60).stdout
+    lines = dict(line.split(" ", 1) for line in out.splitlines())
+    assert "sm_100a" in lines["version"]
+    assert int(lines["status"]) == L.ERR_ARG
+    assert lines["message"].strip()
